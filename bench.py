@@ -1,0 +1,429 @@
+"""Benchmark of the B200 rasterizer hot path (one JSON line on rank 0).
+
+Metric: fwd+bwd ms at 4096^2 x 64K splats and Gsplat-px evals/s.
+A step is one training pass over one view of the headline config c3
+(B=1, 4096x4096, G=65,536 uniform 2D splats): depth sort + binning + forward
+compositing + backward with a N(0,1) grad_image, through the public API.
+Work unit E = sum over tiles of valid_pixels x pairs(tile) (the reference's
+tiled_scan_work). Multi-GPU: one process per GPU (torchrun), each rank renders its
+own view (seed = rank), no data-path collective: weak scaling.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "fast-mac-gsplat_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "Gsplat-px evals/s, fwd+bwd at 4096x4096 x 65,536 splats (ms_per_step = fwd+bwd ms)"
+UNIT = "Gsplat-px evals/s"
+CONFIG_NAME = "c3"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def tiled_work(tile_offsets: torch.Tensor, B: int, H: int, W: int) -> int:
+    """E = sum_t valid_px(t) * count(t) for a flat [B*tiles+1] offsets array."""
+    off = tile_offsets.to("cpu", torch.int64)
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    counts = (off[1:] - off[:-1]).view(B, ty, tx)
+    h = torch.full((ty,), 16, dtype=torch.int64)
+    h[-1] = H - (ty - 1) * 16
+    w = torch.full((tx,), 16, dtype=torch.int64)
+    w[-1] = W - (tx - 1) * 16
+    return int((counts * (h[:, None] * w[None, :])[None]).sum())
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(kernel: str, config: str):
+    """Per-launch DRAM bytes from the committed ncu summary (profiles/traffic.txt,
+    lines `kernel config bytes_per_launch`), or None."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 3 and parts[0] == kernel and parts[1] == config and not line.startswith("#"):
+            try:
+                return float(parts[2])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"gsb_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+class KernelTimer:
+    """CUDA events around each C-ABI call, on the current (launching) stream."""
+
+    def __init__(self):
+        self.events = {}
+
+    def begin(self, name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.events.setdefault(name, []).append([e, None])
+
+    def end(self, name):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.events[name][-1][1] = e
+
+    def summary(self):
+        torch.cuda.synchronize()
+        return {k: [a.elapsed_time(b) for a, b in v] for k, v in self.events.items()}
+
+
+def algorithmic_bytes(kernel: str, B: int, H: int, W: int, G: int, P: int) -> int:
+    """Bytes one launch must move at minimum (reads + writes)."""
+    px = B * H * W
+    tiles = B * ((H + 15) // 16) * ((W + 15) // 16)
+    rec = 36 * B * G  # 9 floats of splat params
+    if kernel == "render_fwd":  # rgb + final_T + last_idx out, ids + ranges + params in
+        return px * (12 + 4 + 4) + P * 4 + tiles * 8 + rec
+    if kernel == "render_bwd":  # grad rgb + state in, ids + ranges + params in, 9 grads out
+        return px * (12 + 4 + 4) + P * 4 + tiles * 8 + rec + 36 * B * G
+    if kernel == "bin_emit":  # params in, pairs out, sort read+write per pass (2 passes), ranges
+        return rec + P * 12 * (1 + 2 * 2) + tiles * 4
+    if kernel == "bin_prepare":  # params+depth in, keys, sort passes, records out, offsets
+        return B * G * (40 + 12 * (1 + 2 * 4) + 48 + 4)
+    if kernel == "unsort":
+        return B * G * (48 + 36 + 4)
+    return 0
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    import torch_gsplat_bridge_fast as tgb
+    from torch_gsplat_bridge_fast import _native
+    from torch_gsplat_bridge_fast.rasterize import _bin, set_kernel_timer
+    from workloads import config_2d, grad_image
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    s = config_2d(args.config, seed=rank)
+    B, G, H, W = s.B, s.G, s.height, s.width
+    cfg = tgb.RasterConfig(H, W)
+    base = [t.to(dev) for t in s.tensors()]
+    gimg = grad_image(B, H, W, seed=1000 + rank).to(dev)
+    st = _bin(cfg, *base)
+    E = tiled_work(st.tile_offsets, B, H, W)
+    P = st.P
+    del st
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step():
+        ins = [t.detach().requires_grad_(i < 4) for i, t in enumerate(base)]
+        out = tgb.rasterize_projected_gaussians(*ins, cfg)
+        out.backward(gimg)
+        return ins
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    L = _native.load()
+    timer = KernelTimer()
+    step_ms = []
+    with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = L.gsb_kernel_launches()
+        t_bracket = time.perf_counter()
+        set_kernel_timer(timer)
+        for _ in range(args.steps):
+            flush.zero_()  # L2 flush between timed steps (outside the step events)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            e1.synchronize()
+            step_ms.append(e0.elapsed_time(e1))
+        set_kernel_timer(None)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        bracket_ms = (time.perf_counter() - t_bracket) * 1e3
+        launches = L.gsb_kernel_launches() - launches0
+    clock = clocks.summary()
+    ms = statistics.mean(step_ms)
+    ms_med = statistics.median(step_ms)
+    kt = timer.summary()
+
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * E / (ms_max * 1e-3) / 1e9
+
+    # Dominant kernel roofline (HBM-bound compositing / binning kernels).
+    totals = {k: sum(v) for k, v in kt.items()}
+    dom = max(totals, key=totals.get)
+    dom_ms = statistics.mean(kt[dom])
+    alg = algorithmic_bytes(dom, B, H, W, G, P)
+    peak, peak_kind = load_peaks()
+    achieved = alg / (dom_ms * 1e-3) / 1e9
+    traffic = load_traffic("k_" + dom, args.config)
+    kernels = {k: {"launches_per_step": len(v) / args.steps, "avg_ms": statistics.mean(v),
+                   "share": totals[k] / max(sum(totals.values()), 1e-9)} for k, v in kt.items()}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(tgb, s, gimg.cpu(), cfg, dev, E, steps=min(args.steps, 10))
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config, seed=0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms_max, 4),
+            "ms_per_step_median": round(ms_med, 4),
+            "bracket_ms": round(bracket_ms, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp32",
+            "data": "synthetic (seeded; BASELINE config distributions)",
+            "config": {"workload": f"{args.config}: B={B}, {W}x{H}, G={G} 2D splats per GPU, fwd+bwd",
+                       "pairs_per_view": P, "evals_per_view_E": E, "l2": "flushed (256 MB write) between steps",
+                       "parallelism": f"views sharded, {world} rank(s), no collective"},
+            "gpu_launches": int(launches),
+            "kernels": kernels,
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": f"{peak_kind} copy bandwidth", "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "algorithmic_bytes_per_launch": alg,
+                         "traffic": traffic, "avg_launch_ms": round(dom_ms, 4)},
+            "clocks": clock,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measure_e2e(tgb, s, gimg_cpu, cfg, dev, E, steps):
+    """Same metric through the public API from pinned host buffers: H2D of the
+    splat tensors and grad_image, fwd+bwd, D2H of the four gradients, every step."""
+    host = [t.contiguous().pin_memory() for t in s.tensors()]
+    ghost = gimg_cpu.contiguous().pin_memory()
+    outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in host[:4]]
+    h2d = sum(t.numel() * t.element_size() for t in host) + ghost.numel() * ghost.element_size()
+    d2h = sum(t.numel() * t.element_size() for t in outs)
+
+    def step():
+        ins = [t.to(dev, non_blocking=True).requires_grad_(i < 4) for i, t in enumerate(host)]
+        g = ghost.to(dev, non_blocking=True)
+        out = tgb.rasterize_projected_gaussians(*ins, cfg)
+        out.backward(g)
+        for o, t in zip(outs, ins[:4]):
+            o.copy_(t.grad, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.mean(times)
+    return {"value": round(E / (ms * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+
+def cpu_baseline(config: str, seed: int, steps: int = 1):
+    """The C oracle (a restatement of the reference's algorithm; the reference
+    itself is Metal-only) timed on this host's cores on one full step of the
+    same workload: binning + forward + backward."""
+    import numpy as np
+
+    from oracle import oracle as O
+    from workloads import config_2d, grad_image
+
+    s = config_2d(config, seed=seed)
+    g = grad_image(s.B, s.height, s.width, seed=1000).numpy()
+    arrs = [t.numpy() for t in s.tensors()]
+    meta = O.Meta(s.height, s.width, s.B, s.G)
+    times = []
+    E = 0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        r = O.full_forward_backward(meta, *arrs, g)
+        times.append(time.perf_counter() - t0)
+        cnt = np.diff(r["tile_offsets"]).astype(np.int64)
+        E = tiled_work(torch.from_numpy(r["tile_offsets"]), s.B, s.height, s.width)
+    t = statistics.mean(times)
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": round(E / t / 1e9, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "seconds_per_step": round(t, 3),
+            "sample": f"one full {config} fwd+bwd step (C oracle: binning + composite + reverse backward)"}
+
+
+def run_reference(args):
+    """Reference arm: the reference is Metal-only (no CPU or CUDA build), so its
+    algorithm runs as the C oracle port on this host's cores, same config/metric."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import oracle as O
+    from workloads import config_2d, grad_image
+
+    s = config_2d(args.config, seed=0)
+    g = grad_image(s.B, s.height, s.width, seed=1000).numpy()
+    arrs = [t.numpy() for t in s.tensors()]
+    meta = O.Meta(s.height, s.width, s.B, s.G)
+    for _ in range(max(args.warmup, 3)):
+        r = O.full_forward_backward(meta, *arrs, g)
+    E = tiled_work(torch.from_numpy(r["tile_offsets"]), s.B, s.height, s.width)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.full_forward_backward(meta, *arrs, g)
+        times.append(time.perf_counter() - t0)
+    t = statistics.mean(times)
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    value = E / t / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": round(t * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic (seeded; BASELINE config distributions)",
+        "config": {"workload": f"{args.config}: B={s.B}, {s.width}x{s.height}, G={s.G} 2D splats, fwd+bwd",
+                   "evals_per_view_E": E},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"one full {args.config} fwd+bwd step per timed step"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        sys.exit(1)
+    run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

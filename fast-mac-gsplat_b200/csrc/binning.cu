@@ -1,0 +1,363 @@
+// Tile binning on sm_100a: depth sort, exact tile-overlap counts, decoupled
+// look-back scan, deterministic pair emission, stable tile sort, tile ranges.
+//
+// Reference behaviour (nbardy/fast-mac-gsplat):
+//   depth sort + gathers   variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:708-717
+//   count_tiles            variants/v8_project3d/csrc/metal/gsplat_v8_project3d_kernels.metal:697-741
+//   cumsum + .item()       variants/v8_project3d/csrc/metal/gsplat_metal.mm:358-364
+//   emit_binned_ids        …/gsplat_v8_project3d_kernels.metal:743-780 (atomic cursors)
+//   bitonic_sort_ids       …/gsplat_v8_project3d_kernels.metal:594-617
+// The B200 design replaces the per-tile atomic cursors + per-tile bitonic sort
+// with deterministic scan offsets in depth-rank order followed by a stable
+// radix sort on the tile bits, so every output is bit-reproducible.
+#include "gsb_common.cuh"
+#include "gsb_host.cuh"
+#include "radix_sort.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 8;
+constexpr int kScanTile = kScanThreads * kScanItems;
+constexpr unsigned long long kScanAgg = 1ull << 62;
+constexpr unsigned long long kScanInc = 2ull << 62;
+constexpr unsigned long long kScanMask = (1ull << 62) - 1ull;
+
+// Per splat in input order: depth-sort key (view in the high word) and the
+// exact number of tiles its support ellipse touches.
+__global__ void __launch_bounds__(256)
+    k_prepare(Meta m, const float2* __restrict__ means2d, const float* __restrict__ conics,
+              const float* __restrict__ opacities, const float* __restrict__ depths,
+              uint64_t* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
+              uint32_t* __restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= m.BG) return;
+  const int b = i / m.G;
+  sort_keys[i] = ((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]);
+  sort_vals[i] = (uint32_t)i;
+  const float2 mu = means2d[i];
+  const float a = conics[3 * i + 0], bq = conics[3 * i + 1], c = conics[3 * i + 2];
+  uint32_t n = 0;
+  for_each_tile(mu.x, mu.y, a, bq, c, opacities[i], m, [&](int, int) { ++n; });
+  counts[i] = n;
+}
+
+// Gathers splats into depth-rank order (packed 48-byte records), and turns the
+// per-splat tile counts into exclusive pair offsets with a single-pass chained
+// scan (dynamic partition ids + decoupled look-back).
+__global__ void __launch_bounds__(kScanThreads)
+    k_gather_scan(Meta m, const uint64_t* __restrict__ sorted_keys,
+                  const uint32_t* __restrict__ sorted_vals, const float2* __restrict__ means2d,
+                  const float* __restrict__ conics, const float* __restrict__ colors,
+                  const float* __restrict__ opacities, const uint32_t* __restrict__ counts,
+                  float4* __restrict__ rec, int32_t* __restrict__ perm,
+                  int32_t* __restrict__ pair_offsets, unsigned long long* __restrict__ lookback,
+                  uint32_t* __restrict__ part_counter, uint32_t* __restrict__ status) {
+  __shared__ uint32_t s_part;
+  __shared__ unsigned long long s_warp[kScanThreads / 32];
+  __shared__ unsigned long long s_exclusive;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_part = atomicAdd(part_counter, 1u);
+  __syncthreads();
+  const int64_t part = s_part;
+  const int64_t r0 = part * kScanTile + (int64_t)tid * kScanItems;
+
+  uint32_t c[kScanItems];
+  unsigned long long tsum = 0;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    const int64_t r = r0 + i;
+    c[i] = 0;
+    if (r < m.BG) {
+      const uint32_t orig = sorted_vals[r];
+      const int b = (int)(r / m.G);
+      c[i] = counts[orig];
+      tsum += c[i];
+      const float2 mu = means2d[orig];
+      const float4 p0 = make_float4(mu.x, mu.y, conics[3 * orig + 0], conics[3 * orig + 1]);
+      const float4 p1 = make_float4(conics[3 * orig + 2], opacities[orig], colors[3 * orig + 0],
+                                    colors[3 * orig + 1]);
+      const float4 p2 = make_float4(colors[3 * orig + 2], __uint_as_float((uint32_t)sorted_keys[r]),
+                                    0.0f, 0.0f);
+      rec[3 * r + 0] = p0;
+      rec[3 * r + 1] = p1;
+      rec[3 * r + 2] = p2;
+      perm[r] = (int32_t)(orig - (uint32_t)b * (uint32_t)m.G);
+    }
+  }
+  // Block-wide exclusive scan of the thread sums.
+  unsigned long long x = tsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  unsigned long long warp_off = 0, block_total = 0;
+#pragma unroll
+  for (int w = 0; w < kScanThreads / 32; ++w) {
+    const unsigned long long v = s_warp[w];
+    if (w < warp) warp_off += v;
+    block_total += v;
+  }
+  const unsigned long long thread_excl = warp_off + x - tsum;
+
+  if (tid == 0) {
+    unsigned long long excl = 0;
+    if (part == 0) {
+      st_volatile_u64(&lookback[0], kScanInc | block_total);
+    } else {
+      st_volatile_u64(&lookback[part], kScanAgg | block_total);
+      int64_t j = part - 1;
+      int spins = 0;
+      bool failed = false;
+      while (j >= 0) {
+        const unsigned long long w = ld_volatile_u64(&lookback[j]);
+        if (w & kScanInc) {
+          excl += w & kScanMask;
+          break;
+        }
+        if (w & kScanAgg) {
+          excl += w & kScanMask;
+          --j;
+          continue;
+        }
+        if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
+          failed = true;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteScanLookback);
+      st_volatile_u64(&lookback[part], kScanInc | ((excl + block_total) & kScanMask));
+    }
+    s_exclusive = excl;
+  }
+  __syncthreads();
+  unsigned long long run = s_exclusive + thread_excl;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    const int64_t r = r0 + i;
+    if (r < m.BG) {
+      pair_offsets[r] = (int32_t)run;
+      run += c[i];
+      if (r == (int64_t)m.BG - 1) {
+        if (run > 0x7fffffffull) {
+          raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteScanTotal);
+          pair_offsets[m.BG] = 0;
+          status[GSB_STATUS_TOTAL_PAIRS] = 0;
+        } else {
+          pair_offsets[m.BG] = (int32_t)run;
+          status[GSB_STATUS_TOTAL_PAIRS] = (uint32_t)run;
+        }
+      }
+    }
+  }
+}
+
+// Re-runs the tile loop per splat in depth-rank order and writes its pairs at
+// its scan slot: key = (global_tile << 32) | depth_key, value = rank index.
+__global__ void __launch_bounds__(256)
+    k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
+           uint64_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= m.BG) return;
+  const int start = pair_offsets[r];
+  const int n = pair_offsets[r + 1] - start;
+  if (n <= 0) return;
+  const float4 p0 = rec[3 * r + 0];
+  const float4 p1 = rec[3 * r + 1];
+  const float4 p2 = rec[3 * r + 2];
+  const uint32_t dk = __float_as_uint(p2.y);
+  const uint32_t tile_base = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
+  int k = 0;
+  for_each_tile(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m, [&](int tx, int ty) {
+    if (k < n) {
+      const uint32_t tile = tile_base + (uint32_t)(ty * m.tiles_x + tx);
+      keys[start + k] = ((uint64_t)tile << 32) | dk;
+      vals[start + k] = (uint32_t)r;
+    }
+    ++k;
+  });
+  if (k != n) raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteEmit);
+}
+
+// tile_offsets[t] = index of the first sorted pair of tile t (= exclusive
+// prefix of per-tile counts); every entry is written by exactly one thread.
+__global__ void __launch_bounds__(256)
+    k_ranges(const uint64_t* __restrict__ keys, int64_t n_pairs, int total_tiles,
+             int32_t* __restrict__ tile_offsets) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_pairs) return;
+  const int64_t t = (int64_t)(keys[i] >> 32);
+  const int64_t tp = (i == 0) ? -1 : (int64_t)(keys[i - 1] >> 32);
+  for (int64_t s = tp + 1; s <= t; ++s) tile_offsets[s] = (int32_t)i;
+  if (i == n_pairs - 1)
+    for (int64_t s = t + 1; s <= total_tiles; ++s) tile_offsets[s] = (int32_t)n_pairs;
+}
+
+__global__ void k_fill_i32(int32_t* __restrict__ p, int64_t n, int32_t v) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+__global__ void __launch_bounds__(256)
+    k_tile_max(const int32_t* __restrict__ tile_offsets, int total_tiles, uint32_t* __restrict__ status) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  uint32_t c = 0;
+  if (t < total_tiles) c = (uint32_t)(tile_offsets[t + 1] - tile_offsets[t]);
+  c = __reduce_max_sync(kFullMask, c);
+  if ((threadIdx.x & 31) == 0 && c) atomicMax(&status[GSB_STATUS_MAX_TILE_COUNT], c);
+}
+
+// Workspace carve of gsb_bin_prepare (shared by size query and run).
+struct PrepareWs {
+  uint64_t* keys_in;
+  uint32_t* vals_in;
+  uint64_t* keys_sorted;
+  uint32_t* vals_sorted;
+  uint32_t* counts;
+  unsigned long long* lookback;
+  uint32_t* counter;
+};
+
+void carve_prepare(Carver& c, const Meta& m, PrepareWs* w) {
+  const size_t n = (size_t)m.BG;
+  w->keys_in = c.take<uint64_t>(n);
+  w->vals_in = c.take<uint32_t>(n);
+  w->keys_sorted = c.take<uint64_t>(n);
+  w->vals_sorted = c.take<uint32_t>(n);
+  w->counts = c.take<uint32_t>(n);
+  w->lookback = c.take<unsigned long long>((n + kScanTile - 1) / kScanTile + 1);
+  w->counter = c.take<uint32_t>(1);
+}
+
+int depth_sort_end_bit(const Meta& m) { return 32 + (m.B > 1 ? bits_for(m.B - 1) : 0); }
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+extern "C" size_t gsb_bin_prepare_workspace_size(const gsb_raster_meta* meta) {
+  Meta m;
+  if (make_meta(meta, &m) != GSB_OK) return 0;
+  Carver c(nullptr);
+  PrepareWs w;
+  carve_prepare(c, m, &w);
+  radix_sort_pairs(c, nullptr, nullptr, nullptr, nullptr, m.BG, 0, depth_sort_end_bit(m), nullptr, 0);
+  return c.off + 256;
+}
+
+extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                               const float* colors, const float* opacities, const float* depths,
+                               int32_t* perm, float* rec, int32_t* pair_offsets, uint32_t* status,
+                               void* workspace, size_t workspace_bytes, void* stream_) {
+  Meta m;
+  int rc = make_meta(meta, &m);
+  if (rc != GSB_OK) return rc;
+  if (!status || !pair_offsets) return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG > 0 && (!means2d || !conics || !colors || !opacities || !depths || !perm || !rec))
+    return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG >= kSortMaxN) return GSB_ERR_CAPACITY;
+  if (workspace_bytes < gsb_bin_prepare_workspace_size(meta) || (m.BG > 0 && !workspace))
+    return GSB_ERR_WORKSPACE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t) * GSB_STATUS_WORDS, stream);
+  if (e != cudaSuccess) return GSB_ERR_CUDA;
+  if (m.BG == 0) return cuda_status(cudaMemsetAsync(pair_offsets, 0, sizeof(int32_t), stream));
+
+  Carver c(workspace);
+  PrepareWs w;
+  carve_prepare(c, m, &w);
+  const int parts = (m.BG + kScanTile - 1) / kScanTile;
+  e = cudaMemsetAsync(w.lookback, 0, sizeof(unsigned long long) * (parts + 1), stream);
+  if (e != cudaSuccess) return GSB_ERR_CUDA;
+  e = cudaMemsetAsync(w.counter, 0, sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return GSB_ERR_CUDA;
+
+  k_prepare<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
+                                                   opacities, depths, w.keys_in, w.vals_in, w.counts);
+
+  note_launches(1);
+  e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0,
+                       depth_sort_end_bit(m), status, stream);
+  if (e != cudaSuccess) return GSB_ERR_CUDA;
+  k_gather_scan<<<parts, kScanThreads, 0, stream>>>(
+      m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors,
+      opacities, w.counts, reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter,
+      status);
+  note_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+namespace {
+struct EmitWs {
+  uint64_t* keys;
+  uint32_t* vals;
+};
+void carve_emit(Carver& c, int64_t P, EmitWs* w) {
+  w->keys = c.take<uint64_t>((size_t)P);
+  w->vals = c.take<uint32_t>((size_t)P);
+}
+int tile_end_bit(const Meta& m) { return 32 + (m.total_tiles > 1 ? bits_for(m.total_tiles - 1) : 0); }
+}  // namespace
+
+extern "C" size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64_t total_pairs) {
+  Meta m;
+  if (make_meta(meta, &m) != GSB_OK || total_pairs < 0) return 0;
+  Carver c(nullptr);
+  EmitWs w;
+  carve_emit(c, total_pairs, &w);
+  radix_sort_pairs(c, nullptr, nullptr, nullptr, nullptr, total_pairs, 32, tile_end_bit(m), nullptr, 0);
+  return c.off + 256;
+}
+
+extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
+                            int64_t total_pairs, uint64_t* keys, int32_t* binned_ids,
+                            int32_t* tile_offsets, uint32_t* status, void* workspace,
+                            size_t workspace_bytes, void* stream_) {
+  Meta m;
+  int rc = make_meta(meta, &m);
+  if (rc != GSB_OK) return rc;
+  if (total_pairs < 0 || !tile_offsets || !status) return GSB_ERR_INVALID_ARGUMENT;
+  if (total_pairs >= kSortMaxN) return GSB_ERR_CAPACITY;
+  if (total_pairs > 0 && (!rec || !pair_offsets || !keys || !binned_ids)) return GSB_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < gsb_bin_emit_workspace_size(meta, total_pairs) || (total_pairs > 0 && !workspace))
+    return GSB_ERR_WORKSPACE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int64_t T1 = (int64_t)m.total_tiles + 1;
+  if (total_pairs == 0) {
+    k_fill_i32<<<grid1d(T1, 256), 256, 0, stream>>>(tile_offsets, T1, 0);
+    note_launches(1);
+    return cuda_status(cudaGetLastError());
+  }
+  Carver c(workspace);
+  EmitWs w;
+  carve_emit(c, total_pairs, &w);
+  k_emit<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float4*>(rec), pair_offsets,
+                                                w.keys, w.vals, status);
+  note_launches(1);
+  cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, keys, reinterpret_cast<uint32_t*>(binned_ids),
+                                   total_pairs, 32, tile_end_bit(m), status, stream);
+  if (e != cudaSuccess) return GSB_ERR_CUDA;
+  k_ranges<<<grid1d(total_pairs, 256), 256, 0, stream>>>(keys, total_pairs, m.total_tiles, tile_offsets);
+  note_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int gsb_tile_stats(const gsb_raster_meta* meta, const int32_t* tile_offsets, uint32_t* status,
+                              void* stream_) {
+  Meta m;
+  int rc = make_meta(meta, &m);
+  if (rc != GSB_OK) return rc;
+  if (!tile_offsets || !status) return GSB_ERR_INVALID_ARGUMENT;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  cudaError_t e = cudaMemsetAsync(&status[GSB_STATUS_MAX_TILE_COUNT], 0, sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return GSB_ERR_CUDA;
+  k_tile_max<<<grid1d(m.total_tiles, 256), 256, 0, stream>>>(tile_offsets, m.total_tiles, status);
+  note_launches(1);
+  return cuda_status(cudaGetLastError());
+}

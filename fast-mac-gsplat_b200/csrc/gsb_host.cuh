@@ -1,0 +1,61 @@
+// Host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+#include "gsb_common.cuh"
+
+namespace gsb {
+
+// Process-wide count of kernel launches issued by this library.
+void note_launches(uint64_t n);
+
+// Validates a gsb_raster_meta and expands it into the kernel-side Meta.
+inline int make_meta(const gsb_raster_meta* in, Meta* m) {
+  if (in == nullptr || m == nullptr) return GSB_ERR_INVALID_ARGUMENT;
+  if (in->tile_size != kTile) return GSB_ERR_UNSUPPORTED;
+  if (in->height <= 0 || in->width <= 0 || in->batch_size <= 0 || in->gaussians_per_batch < 0)
+    return GSB_ERR_INVALID_ARGUMENT;
+  const int64_t tiles_x = (in->width + kTile - 1) / kTile;
+  const int64_t tiles_y = (in->height + kTile - 1) / kTile;
+  const int64_t tpi = tiles_x * tiles_y;
+  const int64_t total_tiles = tpi * in->batch_size;
+  const int64_t bg = (int64_t)in->batch_size * in->gaussians_per_batch;
+  const int64_t pixels = (int64_t)in->batch_size * in->height * in->width;
+  if (total_tiles >= (int64_t(1) << 31) - 1 || bg >= (int64_t(1) << 31) - 1 || pixels >= (int64_t(1) << 40))
+    return GSB_ERR_INVALID_ARGUMENT;
+  m->H = in->height;
+  m->W = in->width;
+  m->tiles_x = (int)tiles_x;
+  m->tiles_y = (int)tiles_y;
+  m->tiles_per_image = (int)tpi;
+  m->B = in->batch_size;
+  m->G = in->gaussians_per_batch;
+  m->BG = (int)bg;
+  m->total_tiles = (int)total_tiles;
+  m->alpha_thr = in->alpha_threshold;
+  m->T_thr = in->transmittance_threshold;
+  m->bg_r = in->background[0];
+  m->bg_g = in->background[1];
+  m->bg_b = in->background[2];
+  m->eps = in->eps;
+  m->max_alpha = in->max_alpha;
+  return GSB_OK;
+}
+
+inline int bits_for(int64_t max_value) {
+  int b = 0;
+  while (b < 63 && (int64_t(1) << b) <= max_value) ++b;
+  return b;
+}
+
+inline int grid1d(int64_t n, int threads) {
+  int64_t b = (n + threads - 1) / threads;
+  return (int)(b < 1 ? 1 : b);
+}
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? GSB_OK : GSB_ERR_CUDA; }
+
+}  // namespace gsb

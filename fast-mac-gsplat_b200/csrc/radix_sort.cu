@@ -1,0 +1,252 @@
+// Onesweep LSD radix sort for (uint64 key, uint32 value) pairs on sm_100a.
+//
+// Replaces the per-tile threadgroup bitonic sort of the reference
+// (variants/v8_project3d/csrc/metal/gsplat_v8_project3d_kernels.metal:594-617, capped at
+// GSP_FAST_CAP entries per tile) with one global, stable, uncapped sort.
+#include "gsb_common.cuh"
+#include "gsb_host.cuh"
+#include "radix_sort.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr uint32_t kFlagAgg = 0x40000000u;  // partition aggregate published
+constexpr uint32_t kFlagInc = 0x80000000u;  // inclusive prefix published
+constexpr uint32_t kValueMask = 0x3fffffffu;
+constexpr int kMaxPasses = 8;
+
+// Histograms of every digit pass in one read of the keys.
+__global__ void __launch_bounds__(kSortThreads)
+    rs_histogram(const uint64_t* __restrict__ keys, int64_t n, int begin_bit, int passes,
+                 int last_bits, uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[kMaxPasses][kRadix];
+  for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) s_hist[i / kRadix][i % kRadix] = 0;
+  __syncthreads();
+  const int64_t stride = (int64_t)gridDim.x * kSortThreads;
+  for (int64_t i = (int64_t)blockIdx.x * kSortThreads + threadIdx.x; i < n; i += stride) {
+    const uint64_t k = keys[i];
+    for (int p = 0; p < passes; ++p) {
+      const int bits = (p == passes - 1) ? last_bits : kRadixBits;
+      const uint32_t d = (uint32_t)(k >> (begin_bit + p * kRadixBits)) & ((1u << bits) - 1u);
+      atomicAdd(&s_hist[p][d], 1u);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) {
+    const uint32_t v = s_hist[i / kRadix][i % kRadix];
+    if (v) atomicAdd(&hist[i], v);
+  }
+}
+
+// Exclusive scan of each pass's 256-bin histogram (one block per pass).
+__global__ void __launch_bounds__(kRadix) rs_digit_base(const uint32_t* __restrict__ hist,
+                                                        uint32_t* __restrict__ base) {
+  __shared__ uint32_t s_warp[kRadix / 32];
+  const int p = blockIdx.x;
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const uint32_t v = hist[p * kRadix + t];
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  uint32_t wsum = 0;
+  for (int w = 0; w < warp; ++w) wsum += s_warp[w];
+  base[p * kRadix + t] = wsum + x - v;
+}
+
+// One digit pass. Keys are held warp-striped: warp w owns the contiguous
+// segment [tile + w*32*ITEMS, +32*ITEMS) and lane l holds its items i*32+l, so
+// (item, lane) order is input order and the match_any ranking is stable.
+__global__ void __launch_bounds__(kSortThreads)
+    rs_onesweep(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+                uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
+                int shift, int bits, const uint32_t* __restrict__ digit_base,
+                uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter,
+                uint32_t* __restrict__ status) {
+  __shared__ uint32_t s_part;
+  __shared__ uint32_t s_warp_hist[kSortWarps][kRadix];
+  __shared__ uint32_t s_prefix[kRadix];
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_part = atomicAdd(part_counter, 1u);
+  for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&s_warp_hist[0][0])[i] = 0u;
+  __syncthreads();
+  const uint32_t part = s_part;
+  const uint32_t dmask = (1u << bits) - 1u;
+
+  const int64_t seg = (int64_t)part * kSortTile + (int64_t)warp * (32 * kSortItems);
+  uint64_t k[kSortItems];
+  uint32_t v[kSortItems];
+  uint32_t rank[kSortItems];
+  const uint32_t lt_mask = (1u << lane) - 1u;
+
+#pragma unroll
+  for (int i = 0; i < kSortItems; ++i) {
+    const int64_t idx = seg + i * 32 + lane;
+    const bool valid = idx < n;
+    k[i] = valid ? keys_in[idx] : 0ull;
+    v[i] = valid ? vals_in[idx] : 0u;
+    const uint32_t d = valid ? ((uint32_t)(k[i] >> shift) & dmask) : kRadix;  // sentinel group
+    const uint32_t peers = __match_any_sync(kFullMask, d);
+    uint32_t cnt_before = 0;
+    if (valid) cnt_before = s_warp_hist[warp][d];
+    __syncwarp();
+    rank[i] = cnt_before + __popc(peers & lt_mask);
+    const int leader = 31 - __clz(peers);
+    if (valid && lane == leader) s_warp_hist[warp][d] = cnt_before + __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Digit t: exclusive scan over warps, partition total, decoupled look-back.
+  {
+    const int t = tid;
+    uint32_t sum = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      const uint32_t c = s_warp_hist[w][t];
+      s_warp_hist[w][t] = sum;
+      sum += c;
+    }
+    uint32_t* my = lookback + (size_t)part * kRadix + t;
+    uint32_t exclusive = 0;
+    if (part == 0) {
+      st_volatile_u32(my, kFlagInc | sum);
+    } else {
+      st_volatile_u32(my, kFlagAgg | sum);
+      int64_t j = (int64_t)part - 1;
+      int spins = 0;
+      bool failed = false;
+      while (j >= 0) {
+        const uint32_t w = ld_volatile_u32(lookback + (size_t)j * kRadix + t);
+        if (w & kFlagInc) {
+          exclusive += w & kValueMask;
+          break;
+        }
+        if (w & kFlagAgg) {
+          exclusive += w & kValueMask;
+          --j;
+          continue;
+        }
+        if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
+          failed = true;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteSortLookback);
+      st_volatile_u32(my, kFlagInc | ((exclusive + sum) & kValueMask));
+    }
+    s_prefix[t] = digit_base[t] + exclusive;
+  }
+  __syncthreads();
+
+#pragma unroll
+  for (int i = 0; i < kSortItems; ++i) {
+    const int64_t idx = seg + i * 32 + lane;
+    if (idx < n) {
+      const uint32_t d = (uint32_t)(k[i] >> shift) & dmask;
+      const uint32_t pos = s_prefix[d] + s_warp_hist[warp][d] + rank[i];
+      keys_out[pos] = k[i];
+      vals_out[pos] = v[i];
+    }
+  }
+}
+
+__global__ void rs_copy(const uint64_t* __restrict__ ki, const uint32_t* __restrict__ vi,
+                        uint64_t* __restrict__ ko, uint32_t* __restrict__ vo, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    ko[i] = ki[i];
+    vo[i] = vi[i];
+  }
+}
+
+int grid_for(int64_t n, int threads, int max_blocks) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return (int)b;
+}
+
+}  // namespace
+
+cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in,
+                             uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
+                             int end_bit, uint32_t* status, cudaStream_t stream) {
+  const int passes = sort_passes(begin_bit, end_bit);
+  const int64_t parts = sort_partitions(n);
+  // Scratch layout (identical in measuring and running mode).
+  uint64_t* k_tmp = ws.take<uint64_t>(passes > 1 ? (size_t)n : 0);
+  uint32_t* v_tmp = ws.take<uint32_t>(passes > 1 ? (size_t)n : 0);
+  uint32_t* hist = ws.take<uint32_t>((size_t)kMaxPasses * kRadix);
+  uint32_t* base = ws.take<uint32_t>((size_t)kMaxPasses * kRadix);
+  uint32_t* counters = ws.take<uint32_t>(kMaxPasses);
+  uint32_t* lookback = ws.take<uint32_t>((size_t)passes * (size_t)parts * kRadix);
+  if (ws.base == nullptr) return cudaSuccess;
+  if (n <= 0) return cudaSuccess;
+  if (passes == 0) {
+    rs_copy<<<grid_for(n, 256, 148 * 8), 256, 0, stream>>>(keys_in, vals_in, keys_out, vals_out, n);
+    note_launches(1);
+    return cudaGetLastError();
+  }
+  const int last_bits = (end_bit - begin_bit) - (passes - 1) * kRadixBits;
+  cudaError_t e = cudaMemsetAsync(hist, 0, sizeof(uint32_t) * kMaxPasses * kRadix, stream);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(counters, 0, sizeof(uint32_t) * kMaxPasses, stream);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(lookback, 0, sizeof(uint32_t) * (size_t)passes * (size_t)parts * kRadix, stream);
+  if (e != cudaSuccess) return e;
+  rs_histogram<<<grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream>>>(keys_in, n, begin_bit,
+                                                                                passes, last_bits, hist);
+  note_launches(1);
+  rs_digit_base<<<passes, kRadix, 0, stream>>>(hist, base);
+  note_launches(1);
+  // Ping-pong so the last pass writes keys_out: pass p writes out when
+  // (passes-1-p) is even, else tmp.
+  const uint64_t* ki = keys_in;
+  const uint32_t* vi = vals_in;
+  for (int p = 0; p < passes; ++p) {
+    const bool to_out = ((passes - 1 - p) % 2) == 0;
+    uint64_t* ko = to_out ? keys_out : k_tmp;
+    uint32_t* vo = to_out ? vals_out : v_tmp;
+    const int bits = (p == passes - 1) ? last_bits : kRadixBits;
+    rs_onesweep<<<(unsigned)parts, kSortThreads, 0, stream>>>(
+        ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, base + p * kRadix,
+        lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status);
+    note_launches(1);
+    ki = ko;
+    vi = vo;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace gsb
+
+extern "C" size_t gsb_radix_sort_pairs_workspace_size(int64_t n, int begin_bit, int end_bit) {
+  gsb::Carver c(nullptr);
+  gsb::radix_sort_pairs(c, nullptr, nullptr, nullptr, nullptr, n, begin_bit, end_bit, nullptr, 0);
+  return c.off + 256;
+}
+
+extern "C" int gsb_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in,
+                                    uint64_t* keys_out, uint32_t* vals_out, int64_t n,
+                                    int begin_bit, int end_bit, uint32_t* status, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  if (n < 0 || begin_bit < 0 || end_bit > 64 || end_bit < begin_bit) return GSB_ERR_INVALID_ARGUMENT;
+  if (n > gsb::kSortMaxN) return GSB_ERR_CAPACITY;
+  if (n > 0 && (!keys_in || !vals_in || !keys_out || !vals_out || !status)) return GSB_ERR_INVALID_ARGUMENT;
+  if (keys_in == keys_out && n > 0) return GSB_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < gsb_radix_sort_pairs_workspace_size(n, begin_bit, end_bit)) return GSB_ERR_WORKSPACE;
+  if (n > 0 && workspace == nullptr) return GSB_ERR_WORKSPACE;
+  gsb::Carver c(workspace);
+  const cudaError_t e = gsb::radix_sort_pairs(c, keys_in, vals_in, keys_out, vals_out, n, begin_bit,
+                                              end_bit, status, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}

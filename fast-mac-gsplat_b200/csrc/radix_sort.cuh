@@ -1,0 +1,49 @@
+// Stable LSD radix sort of (uint64 key, uint32 value) pairs, onesweep style:
+// one kernel builds the histograms of every digit pass at once, then each
+// 8-bit digit pass ranks a 4096-key partition in shared memory, resolves its
+// global per-digit offsets with decoupled look-back, and scatters.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+namespace gsb {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortItems = 16;
+constexpr int kSortTile = kSortThreads * kSortItems;  // 4096 keys per partition
+constexpr int kRadix = 256;
+constexpr int kRadixBits = 8;
+constexpr int64_t kSortMaxN = (int64_t(1) << 30) - 1;  // 30-bit look-back payload
+
+inline int sort_passes(int begin_bit, int end_bit) {
+  return end_bit > begin_bit ? (end_bit - begin_bit + kRadixBits - 1) / kRadixBits : 0;
+}
+inline int64_t sort_partitions(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+// Bump allocator over a caller-provided workspace. With base == nullptr it only
+// measures (the *_workspace_size queries run the same carve sequence).
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+// Carves the sort's scratch: temp key/value buffers, histograms, partition
+// counters and per-pass look-back tiles. Returns the status of the launches
+// when running (base != nullptr); measuring mode launches nothing.
+cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in,
+                             uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
+                             int end_bit, uint32_t* status, cudaStream_t stream);
+
+}  // namespace gsb

@@ -1,0 +1,678 @@
+"""Drop-in torch API of the B200 Gaussian-splat rasterizer.
+
+Mirrors the public surface of nbardy/fast-mac-gsplat:
+  torch_gsplat_bridge_fast/rasterize.py:15-184 (RasterConfig, rasterize_projected_gaussians,
+      ProjectedGaussianRasterizer; [G,...] inputs)
+  variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:16-1105 ([B,G,...] inputs,
+      RuntimeShaderConfig, project_pinhole_gaussians, rasterize_pinhole_gaussians,
+      profile_projected_gaussians)
+with the same argument meaning, defaults, exception types and messages (CUDA
+replaces MPS). Every op runs the sm_100a kernels of libgsplat_b200.so through its
+C ABI on the current CUDA stream; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import os
+import threading
+from dataclasses import dataclass
+from typing import Any, Dict, Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from . import _native as N
+
+
+# ---------------------------------------------------------------------------
+# Configuration
+# ---------------------------------------------------------------------------
+@dataclass(frozen=True)
+class RuntimeShaderConfig:
+    """Runtime kernel configuration (…/v8_project3d/…/rasterize.py:16-52). The B200
+    kernels are compiled for 16x16 tiles; chunk_size/fast_cap are validated and
+    reported for compatibility (the global sort has no per-tile capacity)."""
+
+    tile_size: int
+    threads: int
+    chunk_size: int
+    fast_cap: int
+    simdgroups: int
+
+
+def _env_int(name: str, default: int) -> int:
+    raw = os.environ.get(name)
+    if raw is None or raw == "":
+        return int(default)
+    return int(raw)
+
+
+def get_runtime_shader_config() -> RuntimeShaderConfig:
+    tile_size = _env_int("GSP_TILE_SIZE", 16)
+    chunk_size = _env_int("GSP_CHUNK", 64)
+    fast_cap = _env_int("GSP_FAST_CAP", 2048)
+    if tile_size not in (8, 16, 32):
+        raise ValueError(f"GSP_TILE_SIZE must be one of 8, 16, 32; got {tile_size}")
+    threads = tile_size * tile_size
+    if threads > 1024:
+        raise ValueError(f"tile_size={tile_size} implies {threads} threads, which exceeds 1024")
+    if chunk_size <= 0:
+        raise ValueError("GSP_CHUNK must be positive")
+    if fast_cap <= 0:
+        raise ValueError("GSP_FAST_CAP must be positive")
+    return RuntimeShaderConfig(tile_size=tile_size, threads=threads, chunk_size=chunk_size, fast_cap=fast_cap,
+                               simdgroups=(threads + 31) // 32)
+
+
+@dataclass(frozen=True)
+class RasterConfig:
+    """Superset of the reference configs (root rasterize.py:15-23; v8_project3d
+    rasterize.py:55-67; v8 rasterize.py:65-82). `max_tile_pairs` is the root API's
+    name for the per-tile cap and overrides `max_fast_pairs` when given. Tiles
+    over the cap are rendered exactly (what the reference's overflow fallback
+    produces); with `enable_overflow_fallback=False` the reference's error is
+    raised instead. The v8 scheduling knobs (active tiles, stop-count mode,
+    pair budgets) are accepted and have no effect: they tune Metal launch
+    overhead, which the B200 pipeline does not have."""
+
+    height: int
+    width: int
+    tile_size: int = 16
+    max_fast_pairs: int = 2048
+    alpha_threshold: float = 1.0 / 255.0
+    transmittance_threshold: float = 1e-4
+    background: Tuple[float, float, float] = (0.0, 0.0, 0.0)
+    enable_overflow_fallback: bool = True
+    batch_strategy: str = "auto"  # auto | flatten | serial
+    batch_launch_limit_tiles: int = 262144
+    batch_launch_limit_gaussians: int = 262144
+    max_tile_pairs: Optional[int] = None
+    use_active_tiles: bool = False
+    active_policy: str = "off"
+    sort_active_tiles_by_count: bool = True
+    stop_count_mode: str = "adaptive"
+    stop_count_dense_threshold: int = 64
+    max_pairs_per_launch: int = 0
+
+    @property
+    def pair_cap(self) -> int:
+        return int(self.max_tile_pairs if self.max_tile_pairs is not None else self.max_fast_pairs)
+
+
+def _runtime_validate(config: RasterConfig) -> RuntimeShaderConfig:
+    rt = get_runtime_shader_config()
+    if config.tile_size != rt.tile_size:
+        raise ValueError(
+            f"RasterConfig.tile_size={config.tile_size} does not match runtime shader tile size {rt.tile_size}. "
+            "Set GSP_TILE_SIZE before importing/running the extension, or adjust RasterConfig."
+        )
+    if config.tile_size != 16:
+        raise ValueError("The B200 kernels are specialized for 16x16 tiles.")
+    if config.max_tile_pairs is None and config.max_fast_pairs > rt.fast_cap:
+        raise ValueError(
+            f"RasterConfig.max_fast_pairs={config.max_fast_pairs} exceeds compiled fast cap {rt.fast_cap}. "
+            "Lower the runtime cap or set GSP_FAST_CAP before import."
+        )
+    if config.batch_strategy not in ("auto", "flatten", "serial"):
+        raise ValueError("batch_strategy must be one of: auto, flatten, serial")
+    if config.height <= 0 or config.width <= 0:
+        raise ValueError("height and width must be positive")
+    return rt
+
+
+# ---------------------------------------------------------------------------
+# Input checks (…/v8_project3d/…/rasterize.py:128-240)
+# ---------------------------------------------------------------------------
+def _normalize_inputs(means2d, conics, colors, opacities, depths):
+    if means2d.ndim == 2:
+        return (means2d.unsqueeze(0), conics.unsqueeze(0), colors.unsqueeze(0), opacities.unsqueeze(0),
+                depths.unsqueeze(0), False)
+    if means2d.ndim != 3:
+        raise ValueError("means2d must have shape [G,2] or [B,G,2]")
+    return means2d, conics, colors, opacities, depths, True
+
+
+def _check_inputs(means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor, depths: Tensor) -> None:
+    tensors = {"means2d": means2d, "conics": conics, "colors": colors, "opacities": opacities, "depths": depths}
+    if len({t.device for t in tensors.values()}) != 1:
+        raise ValueError("means2d/conics/colors/opacities/depths must be on the same device")
+    if means2d.device.type != "cuda":
+        raise ValueError("B200 rasterizer inputs must be on CUDA")
+    for name, t in tensors.items():
+        if t.dtype != torch.float32:
+            raise ValueError(f"{name} must be float32")
+    if means2d.ndim not in (2, 3):
+        raise ValueError("means2d must have shape [G,2] or [B,G,2]")
+    if conics.ndim != means2d.ndim or colors.ndim != means2d.ndim:
+        raise ValueError("conics/colors rank must match means2d rank")
+    if opacities.ndim != means2d.ndim - 1 or depths.ndim != means2d.ndim - 1:
+        raise ValueError("opacities/depths rank must be one less than means2d rank")
+    if means2d.shape[-1] != 2:
+        raise ValueError("means2d must have last dim = 2")
+    if conics.shape[-1] != 3:
+        raise ValueError("conics must have last dim = 3")
+    if colors.shape[-1] != 3:
+        raise ValueError("colors must have last dim = 3")
+    if means2d.shape[:-1] != conics.shape[:-1] or means2d.shape[:-1] != colors.shape[:-1]:
+        raise ValueError("means2d/conics/colors batch/G dimensions must match")
+    if means2d.shape[:-1] != opacities.shape or means2d.shape[:-1] != depths.shape:
+        raise ValueError("means2d/opacities/depths batch/G dimensions must match")
+
+
+def _normalize_3d_inputs(means3d, scales, quats, opacities):
+    if opacities.ndim >= 1 and opacities.shape[-1:] == (1,):
+        opacities = opacities.squeeze(-1)
+    if means3d.ndim == 2:
+        return means3d.unsqueeze(0), scales.unsqueeze(0), quats.unsqueeze(0), opacities.unsqueeze(0), False
+    if means3d.ndim != 3:
+        raise ValueError("means3d must have shape [G,3] or [B,G,3]")
+    return means3d, scales, quats, opacities, True
+
+
+def _normalize_colors(colors: Tensor, batch_size: int, gaussians: int, was_batched: bool) -> Tensor:
+    if colors.ndim == 2:
+        colors_b = colors.unsqueeze(0)
+    elif colors.ndim == 3:
+        colors_b = colors
+    else:
+        raise ValueError("colors must have shape [G,3] or [B,G,3]")
+    if colors_b.shape != (batch_size, gaussians, 3):
+        expected = "[B,G,3]" if was_batched else "[G,3]"
+        raise ValueError(f"colors must match Gaussian shape {expected}; got {tuple(colors.shape)}")
+    return colors_b
+
+
+def _check_3d_inputs(means3d: Tensor, scales: Tensor, quats: Tensor, opacities: Tensor) -> None:
+    tensors = {"means3d": means3d, "scales": scales, "quats": quats, "opacities": opacities}
+    if len({t.device for t in tensors.values()}) != 1:
+        raise ValueError("means3d/scales/quats/opacities must be on the same device")
+    if means3d.device.type != "cuda":
+        raise ValueError("B200 projection inputs must be on CUDA")
+    for name, t in tensors.items():
+        if t.dtype != torch.float32:
+            raise ValueError(f"{name} must be float32")
+    if means3d.ndim not in (2, 3) or means3d.shape[-1] != 3:
+        raise ValueError("means3d must have shape [G,3] or [B,G,3]")
+    if scales.shape != means3d.shape:
+        raise ValueError("scales must match means3d shape")
+    if quats.shape[:-1] != means3d.shape[:-1] or quats.shape[-1] != 4:
+        raise ValueError("quats must have shape [G,4] or [B,G,4]")
+    op_shape = opacities.shape[:-1] if opacities.ndim >= 1 and opacities.shape[-1:] == (1,) else opacities.shape
+    if op_shape != means3d.shape[:-1]:
+        raise ValueError("opacities must have shape [G], [G,1], [B,G], or [B,G,1]")
+
+
+# ---------------------------------------------------------------------------
+# Native pipeline helpers
+# ---------------------------------------------------------------------------
+_tls = threading.local()
+_kernel_timer = None
+
+
+def set_kernel_timer(timer) -> None:
+    """Installs an object with begin(name)/end(name) methods that bench code uses
+    to bracket each C-ABI call with CUDA events on the launching stream
+    (names: bin_prepare, bin_emit, render_fwd, render_bwd, unsort). None removes it."""
+    global _kernel_timer
+    _kernel_timer = timer
+
+
+def _timed(name: str, fn):
+    t = _kernel_timer
+    if t is None:
+        return fn()
+    t.begin(name)
+    rc = fn()
+    t.end(name)
+    return rc
+
+
+def _debug_checks() -> bool:
+    return os.environ.get("GSPLAT_B200_CHECK", "0") not in ("", "0")
+
+
+def _pinned_status() -> Tensor:
+    buf = getattr(_tls, "status_host", None)
+    if buf is None:
+        buf = torch.empty(N.GSB_STATUS_WORDS, dtype=torch.int32, pin_memory=True)
+        _tls.status_host = buf
+    return buf
+
+
+def _read_status(status: Tensor) -> list:
+    host = _pinned_status()
+    host.copy_(status, non_blocking=True)
+    torch.cuda.current_stream(status.device).synchronize()
+    vals = [int(v) & 0xFFFFFFFF for v in host.tolist()]
+    if vals[N.GSB_STATUS_ERROR]:
+        raise RuntimeError(N.decode_device_error(vals[N.GSB_STATUS_ERROR], vals[N.GSB_STATUS_ERROR_SITE]))
+    return vals
+
+
+def _aligned(t: Tensor, align: int = 16) -> Tensor:
+    t = t.contiguous()
+    if t.data_ptr() % align:
+        t = t.clone()
+    return t
+
+
+def _meta_for(config: RasterConfig, B: int, G: int) -> N.GsbRasterMeta:
+    return N.make_meta(config.height, config.width, B, G, config.alpha_threshold, config.transmittance_threshold,
+                       config.background)
+
+
+class _BinState:
+    __slots__ = ("meta", "perm", "rec", "pair_offsets", "P", "keys", "binned_ids", "tile_offsets", "status")
+
+
+def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Tensor, opacities_b: Tensor,
+         depths_b: Tensor) -> _BinState:
+    """Depth sort, exact tile counts, scan, emit, stable tile sort, tile ranges
+    (replaces metal_bin, variants/v8_project3d/csrc/metal/gsplat_metal.mm:317-379)."""
+    L = N.load()
+    B, G = means2d_b.shape[:2]
+    dev = means2d_b.device
+    meta = _meta_for(config, B, G)
+    BG = B * G
+    st = _BinState()
+    st.meta = meta
+    st.status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
+    st.perm = torch.empty((B, G), dtype=torch.int32, device=dev)
+    st.rec = torch.empty((BG, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
+    st.pair_offsets = torch.empty(BG + 1, dtype=torch.int32, device=dev)
+    stream = N.stream_ptr(dev)
+    ws_bytes = L.gsb_bin_prepare_workspace_size(meta)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
+    # Locals keep every (possibly copied) input alive until the launch returns.
+    m2 = _aligned(means2d_b, 8)
+    q2, c2, o2, d2 = (t.contiguous() for t in (conics_b, colors_b, opacities_b, depths_b))
+    N.check(
+        _timed("bin_prepare", lambda: L.gsb_bin_prepare(
+            meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm), N.ptr(st.rec),
+            N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes, stream)),
+        "gsb_bin_prepare",
+    )
+    vals = _read_status(st.status)
+    P = vals[N.GSB_STATUS_TOTAL_PAIRS]
+    st.P = P
+    T = B * ((config.height + 15) // 16) * ((config.width + 15) // 16)
+    st.keys = torch.empty(max(P, 1), dtype=torch.int64, device=dev)[:P]
+    st.binned_ids = torch.empty(max(P, 1), dtype=torch.int32, device=dev)[:P]
+    st.tile_offsets = torch.empty(T + 1, dtype=torch.int32, device=dev)
+    ws2_bytes = L.gsb_bin_emit_workspace_size(meta, P)
+    ws2 = torch.empty(max(int(ws2_bytes), 1), dtype=torch.uint8, device=dev)
+    N.check(
+        _timed("bin_emit", lambda: L.gsb_bin_emit(
+            meta, N.ptr(st.rec), N.ptr(st.pair_offsets), P, N.ptr(st.keys), N.ptr(st.binned_ids),
+            N.ptr(st.tile_offsets), N.ptr(st.status), N.ptr(ws2), ws2_bytes, stream)),
+        "gsb_bin_emit",
+    )
+    if _debug_checks():
+        _read_status(st.status)
+    return st
+
+
+def _check_overflow(st: _BinState, config: RasterConfig) -> None:
+    """Reference overflow error when the fallback is disabled
+    (…/v8_project3d/…/rasterize.py:756-760, 902-906)."""
+    if config.enable_overflow_fallback:
+        return
+    L = N.load()
+    dev = st.status.device
+    N.check(L.gsb_tile_stats(st.meta, N.ptr(st.tile_offsets), N.ptr(st.status), N.stream_ptr(dev)), "gsb_tile_stats")
+    vals = _read_status(st.status)
+    if vals[N.GSB_STATUS_MAX_TILE_COUNT] > config.pair_cap:
+        raise RuntimeError(
+            f"Tile overflow detected with max_fast_pairs={config.pair_cap}. "
+            "Enable overflow fallback or increase the runtime cap."
+        )
+
+
+def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: bool):
+    L = N.load()
+    dev = st.status.device
+    out = torch.empty((B, config.height, config.width, 3), dtype=torch.float32, device=dev)
+    final_T = last_idx = None
+    if save_state:
+        final_T = torch.empty((B, config.height, config.width), dtype=torch.float32, device=dev)
+        last_idx = torch.empty((B, config.height, config.width), dtype=torch.int32, device=dev)
+    N.check(
+        _timed("render_fwd", lambda: L.gsb_render_forward(
+            st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out), N.ptr(final_T),
+            N.ptr(last_idx), N.ptr(st.status), N.stream_ptr(dev))),
+        "gsb_render_forward",
+    )
+    if _debug_checks():
+        _read_status(st.status)
+    return out, final_T, last_idx
+
+
+class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
+    """Training path (…/v8_project3d/…/rasterize.py:691-852; root rasterize.py:26-106).
+    Saves the per-pixel final transmittance and last-contributor index instead of
+    per-tile stop counts; backward un-sorts into input order; depth grad is zero."""
+
+    @staticmethod
+    def forward(ctx, means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig):
+        B, G = means2d_b.shape[:2]
+        st = _bin(config, means2d_b, conics_b, colors_b, opacities_b, depths_b)
+        _check_overflow(st, config)
+        out, final_T, last_idx = _render_forward(st, config, B, save_state=True)
+        ctx.save_for_backward(st.perm, st.rec, st.tile_offsets, st.binned_ids, final_T, last_idx, st.status)
+        ctx.meta = st.meta
+        ctx.shape = (B, G)
+        ctx.depths_shape = depths_b.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out: Tensor):
+        perm, rec, tile_offsets, binned_ids, final_T, last_idx, status = ctx.saved_tensors
+        L = N.load()
+        B, G = ctx.shape
+        dev = rec.device
+        stream = N.stream_ptr(dev)
+        g = _aligned(grad_out.to(torch.float32))
+        grad_rec = torch.empty((B * G, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
+        N.check(
+            _timed("render_bwd", lambda: L.gsb_render_backward(
+                ctx.meta, N.ptr(rec), N.ptr(tile_offsets), N.ptr(binned_ids), N.ptr(final_T), N.ptr(last_idx),
+                N.ptr(g), N.ptr(grad_rec), N.ptr(status), stream)),
+            "gsb_render_backward",
+        )
+        need = ctx.needs_input_grad
+        g_means = torch.empty((B, G, 2), dtype=torch.float32, device=dev) if need[0] else None
+        g_conics = torch.empty((B, G, 3), dtype=torch.float32, device=dev) if need[1] else None
+        g_colors = torch.empty((B, G, 3), dtype=torch.float32, device=dev) if need[2] else None
+        g_opac = torch.empty((B, G), dtype=torch.float32, device=dev) if need[3] else None
+        N.check(
+            _timed("unsort", lambda: L.gsb_unsort_grads(
+                ctx.meta, N.ptr(perm), N.ptr(grad_rec), N.ptr(g_means), N.ptr(g_conics), N.ptr(g_colors),
+                N.ptr(g_opac), stream)),
+            "gsb_unsort_grads",
+        )
+        if _debug_checks():
+            _read_status(status)
+        g_depths = torch.zeros(ctx.depths_shape, dtype=torch.float32, device=dev) if need[4] else None
+        return g_means, g_conics, g_colors, g_opac, g_depths, None
+
+
+def _rasterize_chunk_eval(means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig) -> Tensor:
+    """No-grad path (…/v8_project3d/…/rasterize.py:855-907): no saved state."""
+    B = means2d_b.shape[0]
+    st = _bin(config, means2d_b, conics_b, colors_b, opacities_b, depths_b)
+    _check_overflow(st, config)
+    out, _, _ = _render_forward(st, config, B, save_state=False)
+    return out
+
+
+def _should_use_training_path(means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor) -> bool:
+    if not torch.is_grad_enabled():
+        return False
+    return bool(means2d.requires_grad or conics.requires_grad or colors.requires_grad or opacities.requires_grad)
+
+
+def _choose_batch_chunk_size(config: RasterConfig, batch_size: int, gaussians_per_batch: int,
+                             tiles_per_image: int) -> int:
+    """Same chunking policy as …/v8_project3d/…/rasterize.py:681-688 (outputs do not
+    depend on it; it bounds per-launch memory)."""
+    if config.batch_strategy == "flatten":
+        return batch_size
+    if config.batch_strategy == "serial":
+        return 1
+    by_tiles = max(1, config.batch_launch_limit_tiles // max(tiles_per_image, 1))
+    by_gaussians = max(1, config.batch_launch_limit_gaussians // max(gaussians_per_batch, 1))
+    return max(1, min(batch_size, by_tiles, by_gaussians))
+
+
+def _rasterize_batched(means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig) -> Tensor:
+    B, G = means2d_b.shape[:2]
+    tiles_y = (config.height + config.tile_size - 1) // config.tile_size
+    tiles_x = (config.width + config.tile_size - 1) // config.tile_size
+    chunk_b = _choose_batch_chunk_size(config, B, G, tiles_y * tiles_x)
+    train_mode = _should_use_training_path(means2d_b, conics_b, colors_b, opacities_b)
+    outs = []
+    for b0 in range(0, B, chunk_b):
+        b1 = min(B, b0 + chunk_b)
+        args = [t[b0:b1].contiguous() for t in (means2d_b, conics_b, colors_b, opacities_b, depths_b)]
+        if train_mode:
+            outs.append(_RasterizeProjectedGaussiansB200.apply(*args, config))
+        else:
+            with torch.no_grad():
+                outs.append(_rasterize_chunk_eval(*args, config))
+    return torch.cat(outs, dim=0) if len(outs) > 1 else outs[0]
+
+
+def rasterize_projected_gaussians(means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor,
+                                  depths: Tensor, config: RasterConfig) -> Tensor:
+    """[G,...] -> [H,W,3] or [B,G,...] -> [B,H,W,3] (root rasterize.py:144-175;
+    …/v8_project3d/…/rasterize.py:941-955)."""
+    _check_inputs(means2d, conics, colors, opacities, depths)
+    means2d_b, conics_b, colors_b, opacities_b, depths_b, was_batched = _normalize_inputs(
+        means2d, conics, colors, opacities, depths)
+    _runtime_validate(config)
+    out = _rasterize_batched(means2d_b, conics_b, colors_b, opacities_b, depths_b, config)
+    return out if was_batched else out[0]
+
+
+# ---------------------------------------------------------------------------
+# Pinhole projection (…/v8_project3d/…/rasterize.py:243-572, 958-1003)
+# ---------------------------------------------------------------------------
+def _camera_scalar_batch(value, batch_size: int, device: torch.device, dtype: torch.dtype, name: str) -> Tensor:
+    if torch.is_tensor(value):
+        value = value.to(device=device, dtype=dtype)
+        if value.ndim == 0:
+            return value.expand(batch_size)
+        if value.numel() == batch_size:
+            return value.reshape(batch_size)
+        raise ValueError(f"{name} must be scalar or have {batch_size} values")
+    return torch.full((batch_size,), float(value), device=device, dtype=dtype)
+
+
+def _camera_to_world_batch(camera_to_world, batch_size: int, device: torch.device, dtype: torch.dtype) -> Tensor:
+    if camera_to_world is None:
+        return torch.eye(4, device=device, dtype=dtype).unsqueeze(0).expand(batch_size, -1, -1).contiguous()
+    camera_to_world = camera_to_world.to(device=device, dtype=dtype)
+    if camera_to_world.shape == (4, 4):
+        return camera_to_world.unsqueeze(0).expand(batch_size, -1, -1).contiguous()
+    if camera_to_world.shape == (batch_size, 4, 4):
+        return camera_to_world.contiguous()
+    raise ValueError(f"camera_to_world must be [4,4] or [{batch_size},4,4]")
+
+
+def _projection_backward_requested(*values) -> bool:
+    if not torch.is_grad_enabled():
+        return False
+    return any(torch.is_tensor(v) and v.requires_grad for v in values)
+
+
+def _project_forward_native(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params, near_plane):
+    L = N.load()
+    B, G = means3d_b.shape[:2]
+    dev = means3d_b.device
+    out_m = torch.empty((B, G, 2), dtype=torch.float32, device=dev)
+    out_c = torch.empty((B, G, 3), dtype=torch.float32, device=dev)
+    out_o = torch.empty((B, G), dtype=torch.float32, device=dev)
+    out_d = torch.empty((B, G), dtype=torch.float32, device=dev)
+    m3, s3, o3 = means3d_b.contiguous(), scales_b.contiguous(), opacities_b.contiguous()
+    q4, k16, k4 = _aligned(quats_b), _aligned(c2w_b), _aligned(camera_params)
+    N.check(
+        L.gsb_project_forward(B, G, N.ptr(m3), N.ptr(s3), N.ptr(q4), N.ptr(o3), N.ptr(k16), N.ptr(k4),
+                              float(near_plane), N.ptr(out_m), N.ptr(out_c), N.ptr(out_o), N.ptr(out_d),
+                              N.stream_ptr(dev)),
+        "gsb_project_forward",
+    )
+    return out_m, out_c, out_o, out_d
+
+
+class _ProjectPinholeGaussiansB200(torch.autograd.Function):
+    """…/v8_project3d/…/rasterize.py:371-481."""
+
+    @staticmethod
+    def forward(ctx, means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params, near_plane: float):
+        outs = _project_forward_native(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params, near_plane)
+        ctx.save_for_backward(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params)
+        ctx.near_plane = float(near_plane)
+        return outs
+
+    @staticmethod
+    def backward(ctx, g_m2d, g_con, g_op, g_depth):
+        means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params = ctx.saved_tensors
+        if not any(ctx.needs_input_grad[:6]):
+            return (None,) * 7
+        L = N.load()
+        B, G = means3d_b.shape[:2]
+        dev = means3d_b.device
+
+        def opt(g):
+            return None if g is None else _aligned(g.to(torch.float32))
+
+        g_m2d, g_con, g_op, g_depth = opt(g_m2d), opt(g_con), opt(g_op), opt(g_depth)
+        gm3 = torch.empty_like(means3d_b)
+        gs = torch.empty_like(scales_b)
+        gq = torch.empty((B, G, 4), dtype=torch.float32, device=dev)
+        go = torch.empty_like(opacities_b)
+        gc2w = torch.empty((B, 4, 4), dtype=torch.float32, device=dev)
+        gcam = torch.empty((B, 4), dtype=torch.float32, device=dev)
+        m3, s3, o3 = means3d_b.contiguous(), scales_b.contiguous(), opacities_b.contiguous()
+        q4, k16, k4 = _aligned(quats_b), _aligned(c2w_b), _aligned(camera_params)
+        N.check(
+            L.gsb_project_backward(B, G, N.ptr(g_m2d), N.ptr(g_con), N.ptr(g_op), N.ptr(g_depth), N.ptr(m3),
+                                   N.ptr(s3), N.ptr(q4), N.ptr(o3), N.ptr(k16), N.ptr(k4), ctx.near_plane,
+                                   N.ptr(gm3), N.ptr(gs), N.ptr(gq), N.ptr(go), N.ptr(gc2w), N.ptr(gcam),
+                                   N.stream_ptr(dev)),
+            "gsb_project_backward",
+        )
+        grads = [gm3, gs, gq, go, gc2w, gcam]
+        for i, need in enumerate(ctx.needs_input_grad[:6]):
+            if not need:
+                grads[i] = None
+        return (*grads, None)
+
+
+def _project_pinhole_gaussians_batched(means3d_b, scales_b, quats_b, opacities_b, fx, fy, cx, cy, camera_to_world,
+                                       near_plane: float):
+    B = means3d_b.shape[0]
+    dev, dt = means3d_b.device, means3d_b.dtype
+    camera_params = torch.stack(
+        [_camera_scalar_batch(v, B, dev, dt, n) for v, n in ((fx, "fx"), (fy, "fy"), (cx, "cx"), (cy, "cy"))], dim=1
+    ).contiguous()
+    c2w_b = _camera_to_world_batch(camera_to_world, B, dev, dt)
+    if _projection_backward_requested(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params):
+        return _ProjectPinholeGaussiansB200.apply(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params,
+                                                  float(near_plane))
+    with torch.no_grad():
+        return _project_forward_native(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params, near_plane)
+
+
+def project_pinhole_gaussians(means3d: Tensor, scales: Tensor, quats: Tensor, opacities: Tensor, fx, fy, cx, cy,
+                              camera_to_world=None, near_plane: float = 1e-4):
+    """-> (means2d, conics, projected_opacities, depths) (…/rasterize.py:544-572)."""
+    _check_3d_inputs(means3d, scales, quats, opacities)
+    m, s, q, o, was_batched = _normalize_3d_inputs(means3d, scales, quats, opacities)
+    out = _project_pinhole_gaussians_batched(m.contiguous(), s.contiguous(), q.contiguous(), o.contiguous(), fx, fy,
+                                             cx, cy, camera_to_world, near_plane)
+    if was_batched:
+        return out
+    return tuple(t[0] for t in out)
+
+
+def rasterize_pinhole_gaussians(means3d: Tensor, scales: Tensor, quats: Tensor, opacities: Tensor, colors: Tensor,
+                                fx, fy, cx, cy, camera_to_world=None, near_plane: float = 1e-4,
+                                config: RasterConfig | None = None) -> Tensor:
+    """Project then rasterize (…/rasterize.py:958-1003)."""
+    if config is None:
+        raise ValueError("config is required")
+    _check_3d_inputs(means3d, scales, quats, opacities)
+    m, s, q, o, was_batched = _normalize_3d_inputs(means3d, scales, quats, opacities)
+    B, G = m.shape[:2]
+    colors_b = _normalize_colors(colors, B, G, was_batched)
+    if colors_b.device != m.device:
+        raise ValueError("colors must be on the same device as means3d")
+    if colors_b.dtype != torch.float32:
+        raise ValueError("colors must be float32")
+    means2d, conics, proj_op, depths = _project_pinhole_gaussians_batched(
+        m.contiguous(), s.contiguous(), q.contiguous(), o.contiguous(), fx, fy, cx, cy, camera_to_world, near_plane)
+    _runtime_validate(config)
+    out = _rasterize_batched(means2d.contiguous(), conics.contiguous(), colors_b.contiguous(), proj_op.contiguous(),
+                             depths.contiguous(), config)
+    return out if was_batched else out[0]
+
+
+# ---------------------------------------------------------------------------
+# Profiling (…/v8_project3d/…/rasterize.py:1006-1096)
+# ---------------------------------------------------------------------------
+def _tile_stop_counts(final_T: Tensor, last_idx: Tensor, counts: Tensor, config: RasterConfig) -> Tensor:
+    """Reference per-tile stop count from per-pixel state: max over valid pixels
+    of (saturated ? break index + 1 : tile count) (…kernels.metal:899-923)."""
+    B, H, W = final_T.shape
+    ty, tx = (H + 15) // 16, (W + 15) // 16
+    cnt = counts.view(B, ty, tx).to(torch.int64)
+    cnt_px = cnt.repeat_interleave(16, 1).repeat_interleave(16, 2)[:, :H, :W]
+    stop = torch.where(final_T <= config.transmittance_threshold, last_idx.to(torch.int64), cnt_px)
+    pad = torch.zeros((B, ty * 16, tx * 16), dtype=torch.int64, device=stop.device)
+    pad[:, :H, :W] = stop
+    return pad.view(B, ty, 16, tx, 16).amax(dim=(2, 4)).reshape(-1)
+
+
+@torch.no_grad()
+def profile_projected_gaussians(means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor, depths: Tensor,
+                                config: RasterConfig, *, run_forward: bool = False,
+                                return_image: bool = False) -> Dict[str, Any]:
+    _check_inputs(means2d, conics, colors, opacities, depths)
+    means2d_b, conics_b, colors_b, opacities_b, depths_b, was_batched = _normalize_inputs(
+        means2d, conics, colors, opacities, depths)
+    B, G = means2d_b.shape[:2]
+    _runtime_validate(config)
+    tiles_y = (config.height + config.tile_size - 1) // config.tile_size
+    tiles_x = (config.width + config.tile_size - 1) // config.tile_size
+    chunk_b = _choose_batch_chunk_size(config, B, G, tiles_y * tiles_x)
+    all_counts, all_stops, images = [], [], []
+    for b0 in range(0, B, chunk_b):
+        b1 = min(B, b0 + chunk_b)
+        args = [t[b0:b1].contiguous() for t in (means2d_b, conics_b, colors_b, opacities_b, depths_b)]
+        st = _bin(config, *args)
+        counts = (st.tile_offsets[1:] - st.tile_offsets[:-1])
+        all_counts.append(counts.cpu().to(torch.float32))
+        if run_forward or return_image:
+            out, final_T, last_idx = _render_forward(st, config, b1 - b0, save_state=True)
+            if return_image:
+                images.append(out)
+            all_stops.append(_tile_stop_counts(final_T, last_idx, counts, config).cpu().to(torch.float32))
+    counts_cpu = torch.cat(all_counts) if all_counts else torch.zeros(0)
+    stats: Dict[str, Any] = {
+        "batch_size": int(B),
+        "gaussians_per_batch": int(G),
+        "height": int(config.height),
+        "width": int(config.width),
+        "tile_size": int(config.tile_size),
+        "tiles": int(counts_cpu.numel()),
+        "total_pairs": int(counts_cpu.sum().item()) if counts_cpu.numel() else 0,
+        "mean_pairs_per_tile": float(counts_cpu.mean().item()) if counts_cpu.numel() else 0.0,
+        "p95_pairs_per_tile": float(torch.quantile(counts_cpu, 0.95).item()) if counts_cpu.numel() else 0.0,
+        "max_pairs_per_tile": int(counts_cpu.max().item()) if counts_cpu.numel() else 0,
+        "overflow_tile_count": int((counts_cpu > int(config.pair_cap)).sum().item()) if counts_cpu.numel() else 0,
+        "chosen_batch_chunk": int(chunk_b),
+    }
+    if all_stops:
+        stop_cpu = torch.cat(all_stops)
+        denom = torch.clamp(counts_cpu, min=1.0)
+        ratio = torch.where(counts_cpu > 0, stop_cpu / denom, torch.zeros_like(stop_cpu))
+        stats.update({
+            "mean_stop_count": float(stop_cpu.mean().item()),
+            "p95_stop_count": float(torch.quantile(stop_cpu, 0.95).item()),
+            "max_stop_count": int(stop_cpu.max().item()),
+            "mean_stop_ratio": float(ratio.mean().item()),
+            "p95_stop_ratio": float(torch.quantile(ratio, 0.95).item()),
+        })
+    if return_image:
+        out = torch.cat(images, dim=0) if len(images) > 1 else images[0]
+        return {"image": out if was_batched else out[0], "stats": stats}
+    return stats
+
+
+class ProjectedGaussianRasterizer(torch.nn.Module):
+    def __init__(self, config: RasterConfig):
+        super().__init__()
+        self.config = config
+
+    def forward(self, means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor, depths: Tensor) -> Tensor:
+        return rasterize_projected_gaussians(means2d, conics, colors, opacities, depths, self.config)

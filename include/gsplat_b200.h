@@ -1,0 +1,173 @@
+/*
+ * gsplat_b200.h — C ABI of the B200 (sm_100a) differentiable Gaussian-splat rasterizer.
+ *
+ * Every entry point takes raw device pointers, element counts and a CUDA stream
+ * (passed as `void*`, a `cudaStream_t`; NULL means the legacy default stream),
+ * enqueues its kernels on that stream and returns an `int` status (GSB_OK == 0).
+ * Nothing here allocates memory: outputs, the per-call workspace (sized by the
+ * matching `*_workspace_size` query) and the status block are caller-owned.
+ * No call synchronises the device; the caller reads the status block when it
+ * needs a device-side result (the pair total, error flags, the max tile count).
+ *
+ * Layouts (all row-major, fp32 unless stated):
+ *   2D splats   means2d [B*G,2], conics [B*G,3] (a,b,c of the inverse 2D covariance),
+ *               colors [B*G,3], opacities [B*G], depths [B*G]  (view-major: index b*G+g)
+ *   records     rec [B*G,12]: splat params in depth-rank order (see GSB_REC_* below)
+ *   pair keys   keys [P] uint64 = (global_tile << 32) | depth_key, sorted ascending
+ *   binned ids  binned_ids [P] int32 = depth-rank index b*G+rank, tile-major
+ *   tile ranges tile_offsets [B*tiles+1] int32 (exclusive prefix of per-tile counts)
+ *   image       out_rgb [B,H,W,3]; per-pixel state final_T [B,H,W], last_idx [B,H,W] int32
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * nbardy/fast-mac-gsplat).
+ */
+#ifndef GSPLAT_B200_H
+#define GSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define GSB_OK 0
+#define GSB_ERR_INVALID_ARGUMENT 1 /* bad pointer / shape / config */
+#define GSB_ERR_UNSUPPORTED 2      /* e.g. tile_size != 16 */
+#define GSB_ERR_WORKSPACE 3        /* workspace smaller than *_workspace_size */
+#define GSB_ERR_CAPACITY 4         /* pair count exceeds the int32 index range */
+#define GSB_ERR_DEVICE_TIMEOUT 5   /* a bounded device-side wait ran out */
+#define GSB_ERR_CUDA 6             /* a CUDA runtime call failed */
+#define GSB_ERR_DEVICE_BOUNDS 7    /* a device-side bounds check fired */
+
+/* ---- device status block (caller-owned, GSB_STATUS_WORDS x uint32) ------ */
+#define GSB_STATUS_TOTAL_PAIRS 0    /* written by gsb_bin_prepare */
+#define GSB_STATUS_ERROR 1          /* OR of GSB_DEVERR_* flags */
+#define GSB_STATUS_MAX_TILE_COUNT 2 /* written by gsb_tile_stats */
+#define GSB_STATUS_ERROR_SITE 3     /* first kernel site that raised an error */
+#define GSB_STATUS_WORDS 8
+
+#define GSB_DEVERR_LOOKBACK_TIMEOUT 1u /* decoupled look-back spin limit hit */
+#define GSB_DEVERR_PAIR_OVERFLOW 2u    /* emit wrote past its scan slot / P >= 2^31 */
+#define GSB_DEVERR_BOUNDS 4u           /* index outside its buffer */
+
+/* ---- packed splat record (12 floats, 48 B, 16-B aligned) --------------- */
+#define GSB_REC_FLOATS 12
+/* rec[r*12 + ...]: 0 mean_x, 1 mean_y, 2 conic_a, 3 conic_b,
+ *                  4 conic_c, 5 opacity, 6 color_r, 7 color_g,
+ *                  8 color_b, 9 depth_key (uint32 bits), 10,11 unused (0) */
+/* grad record (same 12-float stride, depth-rank order):
+ *   0 g_mean_x, 1 g_mean_y, 2 g_a, 3 g_b, 4 g_c, 5 g_opacity, 6 g_r, 7 g_g, 8 g_b_color */
+
+/* ---- raster meta (replaces the meta_i32 / meta_f32 tensors) ------------ */
+typedef struct gsb_raster_meta {
+  int32_t height;
+  int32_t width;
+  int32_t tile_size;           /* must be 16 */
+  int32_t batch_size;          /* B (views) */
+  int32_t gaussians_per_batch; /* G */
+  float alpha_threshold;       /* 1/255 */
+  float transmittance_threshold; /* 1e-4 */
+  float background[3];
+  float eps;       /* 1e-8 */
+  float max_alpha; /* 0.99 */
+} gsb_raster_meta;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int gsb_version(void);
+/* Human-readable text for a status code. */
+const char* gsb_status_string(int code);
+/* Number of kernels this library has launched in this process (all devices);
+ * a diagnostic for launch accounting, no reference counterpart. */
+uint64_t gsb_kernel_launches(void);
+
+/* ---- binning, phase 1 ---------------------------------------------------
+ * Replaces: the depth sort + gathers of
+ *   torch_gsplat_bridge_fast/rasterize.py:43-47 and
+ *   variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:708-717,
+ * `count_tiles` (variants/v8_project3d/csrc/metal/gsplat_v8_project3d_kernels.metal:697-741)
+ * and the cumsum + `.item()` of metal_bin
+ *   (variants/v8_project3d/csrc/metal/gsplat_metal.mm:341-364).
+ * Stable per-view depth sort, gather into packed records, exact per-splat tile
+ * counts, exclusive scan of those counts in depth-rank order.
+ * Outputs: perm [B*G] int32 (perm[b*G+rank] = original index g within view b),
+ *          rec [B*G*12], pair_offsets [B*G+1] int32,
+ *          status[GSB_STATUS_TOTAL_PAIRS] = total pair count P. */
+size_t gsb_bin_prepare_workspace_size(const gsb_raster_meta* meta);
+int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                    const float* colors, const float* opacities, const float* depths,
+                    int32_t* perm, float* rec, int32_t* pair_offsets, uint32_t* status,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- binning, phase 2 ---------------------------------------------------
+ * Replaces: `emit_binned_ids` (…/gsplat_v8_project3d_kernels.metal:743-780), the per-tile
+ * `bitonic_sort_ids` (…:594-617) and the tile offsets of metal_bin (…/gsplat_metal.mm:358-361).
+ * Emits (tile<<32 | depth_key, rank) pairs at the scan offsets, stable radix-sorts them
+ * by tile, and writes tile ranges. `total_pairs` is status[GSB_STATUS_TOTAL_PAIRS]. */
+size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64_t total_pairs);
+int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
+                 int64_t total_pairs, uint64_t* keys, int32_t* binned_ids, int32_t* tile_offsets,
+                 uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Max pairs over tiles -> status[GSB_STATUS_MAX_TILE_COUNT] (overflow check of
+ * variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:756-760). */
+int gsb_tile_stats(const gsb_raster_meta* meta, const int32_t* tile_offsets, uint32_t* status,
+                   void* stream);
+
+/* ---- compositing ---------------------------------------------------------
+ * Replaces `tile_fast_forward_eval` / `tile_fast_forward_state`
+ * (…/gsplat_v8_project3d_kernels.metal:783-929; root csrc/metal/gsplat_fast_kernels.metal:221-294).
+ * final_T and last_idx may both be NULL (eval: no saved state). */
+int gsb_render_forward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
+                       const int32_t* binned_ids, float* out_rgb, float* final_T,
+                       int32_t* last_idx, uint32_t* status, void* stream);
+
+/* Replaces `tile_fast_backward_saved` (…/gsplat_v8_project3d_kernels.metal:931-1063; root
+ * csrc/metal/gsplat_fast_kernels.metal:296-395). Zeroes and accumulates grad_rec [B*G*12]. */
+int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
+                        const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
+                        const float* grad_rgb, float* grad_rec, uint32_t* status, void* stream);
+
+/* Replaces the un-sort scatter of the autograd backward
+ * (torch_gsplat_bridge_fast/rasterize.py:96-105; …/v8_project3d/…/rasterize.py:583-591, 847-851).
+ * Any output pointer may be NULL (that gradient is skipped). */
+int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm, const float* grad_rec,
+                     float* g_means2d, float* g_conics, float* g_colors, float* g_opacities,
+                     void* stream);
+
+/* ---- pinhole projection --------------------------------------------------
+ * Replaces `project_pinhole_forward` (…/gsplat_v8_project3d_kernels.metal:66-174).
+ * camera_to_world [B,4,4] row-major, camera_params [B,4] = (fx, fy, cx, cy). */
+int gsb_project_forward(int32_t batch_size, int32_t gaussians_per_batch, const float* means3d,
+                        const float* scales, const float* quats, const float* opacities,
+                        const float* camera_to_world, const float* camera_params, float near_plane,
+                        float* out_means2d, float* out_conics, float* out_opacities,
+                        float* out_depths, void* stream);
+
+/* Replaces `project_pinhole_backward` (…/gsplat_v8_project3d_kernels.metal:217-501).
+ * Any incoming gradient pointer may be NULL (treated as zeros). g_camera_to_world [B,16]
+ * and g_camera_params [B,4] are zeroed and accumulated. */
+int gsb_project_backward(int32_t batch_size, int32_t gaussians_per_batch,
+                         const float* grad_means2d, const float* grad_conics,
+                         const float* grad_opacities, const float* grad_depths,
+                         const float* means3d, const float* scales, const float* quats,
+                         const float* opacities, const float* camera_to_world,
+                         const float* camera_params, float near_plane, float* g_means3d,
+                         float* g_scales, float* g_quats, float* g_opacities,
+                         float* g_camera_to_world, float* g_camera_params, void* stream);
+
+/* ---- building blocks, exported for parity tests -------------------------
+ * Stable LSD radix sort of (uint64 key, uint32 value) pairs on key bits
+ * [begin_bit, end_bit) (onesweep: one histogram pass + one pass per 8-bit digit).
+ * keys_in/vals_in are read only; the result lands in keys_out/vals_out. */
+size_t gsb_radix_sort_pairs_workspace_size(int64_t n, int begin_bit, int end_bit);
+int gsb_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
+                         uint32_t* vals_out, int64_t n, int begin_bit, int end_bit,
+                         uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSPLAT_B200_H */

@@ -1,0 +1,176 @@
+"""Torch fp32 restatements of the reference's own torch oracles (test infrastructure).
+
+Each function follows a reference function line by line (paths inside
+nbardy/fast-mac-gsplat); tests pin them to golden vectors made by the originals.
+"""
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+
+def _batched(*xs: Tensor):
+    squeeze = xs[0].ndim == 2
+    if squeeze:
+        xs = tuple(x.unsqueeze(0) for x in xs)
+    return squeeze, xs
+
+
+def dense_reference(means2d, conics, colors, opacities, depths, H, W, bg=(0.0, 0.0, 0.0),
+                    alpha_threshold=1.0 / 255.0, max_alpha=0.99):
+    """No early stop. Restates benchmarks/benchmark_full_matrix.py:128-152 and
+    variants/v8_project3d/tests/reference_check.py:15-50."""
+    squeeze, (means2d, conics, colors, opacities, depths) = _batched(means2d, conics, colors, opacities, depths)
+    dev, dt = means2d.device, means2d.dtype
+    bg_t = torch.tensor(bg, dtype=dt, device=dev)
+    ys = torch.arange(H, dtype=dt, device=dev) + 0.5
+    xs = torch.arange(W, dtype=dt, device=dev) + 0.5
+    yy, xx = torch.meshgrid(ys, xs, indexing="ij")
+    outs = []
+    for b in range(means2d.shape[0]):
+        perm = torch.argsort(depths[b].detach(), stable=True)
+        m, q, c, o = means2d[b][perm], conics[b][perm], colors[b][perm], opacities[b][perm]
+        out = torch.zeros(H, W, 3, dtype=dt, device=dev)
+        T = torch.ones(H, W, dtype=dt, device=dev)
+        for i in range(m.shape[0]):
+            dx = xx - m[i, 0]
+            dy = yy - m[i, 1]
+            power = -0.5 * (q[i, 0] * dx * dx + 2 * q[i, 1] * dx * dy + q[i, 2] * dy * dy)
+            alpha = torch.clamp(o[i] * torch.exp(power), max=max_alpha)
+            alpha = torch.where((power <= 0) & (alpha >= alpha_threshold), alpha, torch.zeros_like(alpha))
+            out = out + (T * alpha)[..., None] * c[i]
+            T = T * (1.0 - alpha)
+        outs.append(out + T[..., None] * bg_t)
+    out = torch.stack(outs, 0)
+    return out[0] if squeeze else out
+
+
+def saturating_reference(means2d, conics, colors, opacities, depths, H, W, bg=(0.0, 0.0, 0.0),
+                         alpha_threshold=1.0 / 255.0, transmittance_threshold=1.0e-4, max_alpha=0.99,
+                         pixel_mask: Tensor | None = None):
+    """Early-stop oracle with the kernel's exact semantics. Restates
+    variants/v8_project3d/tests/reference_check.py:53-104 (there `bg` defaults to
+    white; here it is an explicit argument). `pixel_mask` [H,W] bool optionally
+    restricts the evaluation to a subset of pixels (others render background and
+    carry no gradient) for tile-sampled parity on large frames."""
+    squeeze, (means2d, conics, colors, opacities, depths) = _batched(means2d, conics, colors, opacities, depths)
+    dev, dt = means2d.device, means2d.dtype
+    bg_t = torch.tensor(bg, dtype=dt, device=dev)
+    ys = torch.arange(H, dtype=dt, device=dev) + 0.5
+    xs = torch.arange(W, dtype=dt, device=dev) + 0.5
+    yy, xx = torch.meshgrid(ys, xs, indexing="ij")
+    if pixel_mask is not None:
+        sel = pixel_mask.to(dev).reshape(-1)
+        yy = yy.reshape(-1)[sel]
+        xx = xx.reshape(-1)[sel]
+        shape = (int(sel.sum()),)
+    else:
+        shape = (H, W)
+    outs = []
+    for b in range(means2d.shape[0]):
+        perm = torch.argsort(depths[b].detach(), stable=True)
+        m, q, c, o = means2d[b][perm], conics[b][perm], colors[b][perm], opacities[b][perm]
+        out = torch.zeros(*shape, 3, dtype=dt, device=dev)
+        T = torch.ones(*shape, dtype=dt, device=dev)
+        for i in range(m.shape[0]):
+            active = T > transmittance_threshold
+            dx = xx - m[i, 0]
+            dy = yy - m[i, 1]
+            power = -0.5 * (q[i, 0] * dx * dx + 2 * q[i, 1] * dx * dy + q[i, 2] * dy * dy)
+            alpha = torch.clamp(o[i] * torch.exp(power), max=max_alpha)
+            alpha = torch.where((power <= 0) & (alpha >= alpha_threshold) & active, alpha, torch.zeros_like(alpha))
+            out = out + (T * alpha)[..., None] * c[i]
+            T = T * (1.0 - alpha)
+        outs.append(out + T[..., None] * bg_t)
+    out = torch.stack(outs, 0)
+    return out[0] if squeeze else out
+
+
+def project_pinhole(means3d_b, scales_b, quats_b, opacities_b, camera_to_world_b, camera_params, near_plane):
+    """Restates _torch_project_pinhole_gaussians_batched
+    (variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:288-358)."""
+    B, G = means3d_b.shape[:2]
+    qr, qi, qj, qk = quats_b[..., 0], quats_b[..., 1], quats_b[..., 2], quats_b[..., 3]
+    R = torch.stack(
+        [
+            torch.stack([1 - 2 * (qj * qj + qk * qk), 2 * (qi * qj - qr * qk), 2 * (qi * qk + qr * qj)], -1),
+            torch.stack([2 * (qi * qj + qr * qk), 1 - 2 * (qi * qi + qk * qk), 2 * (qj * qk - qr * qi)], -1),
+            torch.stack([2 * (qi * qk - qr * qj), 2 * (qj * qk + qr * qi), 1 - 2 * (qi * qi + qj * qj)], -1),
+        ],
+        -2,
+    )
+    M = R * scales_b[..., None, :]
+    cov3d = M @ M.transpose(-1, -2)
+    Rcw = camera_to_world_b[:, :3, :3]
+    t = camera_to_world_b[:, :3, 3]
+    mc = (means3d_b - t[:, None, :]) @ Rcw
+    covc = Rcw.transpose(1, 2).unsqueeze(1) @ cov3d @ Rcw.unsqueeze(1)
+    x, y, z = mc[..., 0], mc[..., 1], mc[..., 2]
+    front = z > float(near_plane)
+    zs = torch.where(front, torch.clamp(z, min=float(near_plane)), torch.ones_like(z))
+    xp = torch.where(front, x, torch.zeros_like(x))
+    yp = torch.where(front, y, torch.zeros_like(y))
+    fx, fy, cx, cy = (camera_params[:, k : k + 1] for k in range(4))
+    zero = torch.zeros_like(zs)
+    J = torch.stack(
+        [torch.stack([fx / zs, zero, -(fx * xp) / zs.square()], -1),
+         torch.stack([zero, fy / zs, -(fy * yp) / zs.square()], -1)],
+        -2,
+    )
+    cov2d = J @ covc @ J.transpose(-1, -2)
+    c00 = cov2d[..., 0, 0] + 0.3
+    c01 = cov2d[..., 0, 1]
+    c11 = cov2d[..., 1, 1] + 0.3
+    det = torch.clamp(c00 * c11 - c01 * c01, min=1.0e-6)
+    conics = torch.stack([c11 / det, -c01 / det, c00 / det], -1)
+    means2d = torch.stack([(fx * xp) / zs + cx, (fy * yp) / zs + cy], -1)
+    opac = torch.where(front, opacities_b, torch.zeros_like(opacities_b))
+    return means2d, conics, opac, z
+
+
+def tiled_scan_work(tile_offsets: Tensor, *, height: int, width: int, tile_size: int = 16, batch: int = 1) -> int:
+    """E = sum over tiles of valid_pixels(tile) * count(tile); restates
+    variants/v7_tiled_capture/torch_gsplat_bridge_v72/reference.py:288-302 for a flat
+    [B*tiles+1] offsets array."""
+    off = tile_offsets.detach().to("cpu", torch.int64)
+    tx = (width + tile_size - 1) // tile_size
+    ty = (height + tile_size - 1) // tile_size
+    counts = (off[1:] - off[:-1]).view(batch, ty, tx)
+    h = torch.full((ty,), tile_size, dtype=torch.int64)
+    h[-1] = height - (ty - 1) * tile_size
+    w = torch.full((tx,), tile_size, dtype=torch.int64)
+    w[-1] = width - (tx - 1) * tile_size
+    return int((counts * (h[:, None] * w[None, :])[None]).sum())
+
+
+def saturating_reference_pixels(means2d, conics, colors, opacities, depths, px, py, bg=(0.0, 0.0, 0.0),
+                                alpha_threshold=1.0 / 255.0, transmittance_threshold=1.0e-4, max_alpha=0.99,
+                                chunk=256):
+    """saturating_reference (variants/v8_project3d/tests/reference_check.py:53-104) for
+    one view, evaluated only at the pixel-centre samples (px+0.5, py+0.5), with the
+    per-splat loop replaced by a cumulative product over the depth-sorted splats:
+    T_before_i = prod_{j<i} (1 - alpha_j); active_i = T_before_i > T_thr. T is
+    non-increasing, so once a pixel stops every later splat is inactive, exactly as
+    in the loop. Splats are processed in chunks to bound memory. -> [N,3]."""
+    dev, dt = means2d.device, means2d.dtype
+    perm = torch.argsort(depths.detach(), stable=True)
+    m, q, c, o = means2d[perm], conics[perm], colors[perm], opacities[perm]
+    xs = px.to(dev, dt)[:, None] + 0.5
+    ys = py.to(dev, dt)[:, None] + 0.5
+    T = torch.ones(xs.shape[0], 1, dtype=dt, device=dev)
+    out = torch.zeros(xs.shape[0], 3, dtype=dt, device=dev)
+    for s in range(0, m.shape[0], chunk):
+        e = min(m.shape[0], s + chunk)
+        dx = xs - m[s:e, 0][None]
+        dy = ys - m[s:e, 1][None]
+        power = -0.5 * (q[s:e, 0][None] * dx * dx + 2 * q[s:e, 1][None] * dx * dy + q[s:e, 2][None] * dy * dy)
+        alpha = torch.clamp(o[s:e][None] * torch.exp(power), max=max_alpha)
+        alpha = torch.where((power <= 0) & (alpha >= alpha_threshold), alpha, torch.zeros_like(alpha))
+        one_minus = 1.0 - alpha
+        t_incl = T * torch.cumprod(one_minus, dim=1)
+        t_before = torch.cat([T, t_incl[:, :-1]], dim=1)
+        active = (t_before > transmittance_threshold).detach()
+        a_eff = torch.where(active, alpha, torch.zeros_like(alpha))
+        out = out + (t_before * a_eff) @ c[s:e]
+        T = T * torch.prod(1.0 - a_eff, dim=1, keepdim=True)
+    return out + T * torch.tensor(bg, dtype=dt, device=dev)

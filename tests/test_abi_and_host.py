@@ -1,0 +1,124 @@
+"""CPU-side checks: the C-ABI library loads and exports every declared symbol,
+argument validation needs no GPU, and the host API mirrors the reference's
+configuration and error behaviour."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import torch_gsplat_bridge_fast as tgb
+from torch_gsplat_bridge_fast import _native as N
+from torch_gsplat_bridge_fast.rasterize import _choose_batch_chunk_size
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "gsplat_b200.h"
+
+
+def _declared_symbols():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(gsb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = N.load()
+    declared = _declared_symbols()
+    assert declared, "no declarations parsed"
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(declared) == set(N.EXPORTED)
+
+
+def test_version_and_status_strings():
+    L = N.load()
+    assert L.gsb_version() >= 100
+    assert L.gsb_status_string(0) == b"ok"
+    assert b"tile_size" in L.gsb_status_string(2)
+
+
+def _meta(**kw):
+    d = dict(height=64, width=80, batch_size=2, gaussians_per_batch=100, alpha_threshold=1 / 255,
+             transmittance_threshold=1e-4, background=(0, 0, 0))
+    d.update(kw)
+    return N.make_meta(**d)
+
+
+def test_workspace_queries_without_gpu():
+    L = N.load()
+    m = _meta()
+    assert L.gsb_bin_prepare_workspace_size(C.byref(m)) > 100 * 2 * 8
+    assert L.gsb_bin_emit_workspace_size(C.byref(m), 1000) > 1000 * 12
+    assert L.gsb_bin_emit_workspace_size(C.byref(m), 0) >= 0
+    assert L.gsb_radix_sort_pairs_workspace_size(1 << 20, 32, 48) > (1 << 20) * 12
+    bad = _meta(tile_size=8)
+    assert L.gsb_bin_prepare_workspace_size(C.byref(bad)) == 0
+
+
+def test_argument_validation_without_gpu():
+    L = N.load()
+    bad = _meta(tile_size=8)
+    rc = L.gsb_bin_prepare(C.byref(bad), *([None] * 9), None, 0, None)
+    assert rc == 2  # GSB_ERR_UNSUPPORTED
+    m = _meta()
+    rc = L.gsb_bin_prepare(C.byref(m), *([None] * 9), None, 0, None)
+    assert rc == 1  # null pointers
+    rc = L.gsb_render_forward(C.byref(_meta(height=0)), None, None, None, None, None, None, None, None)
+    assert rc == 1
+    rc = L.gsb_radix_sort_pairs(None, None, None, None, -1, 0, 8, None, None, 0, None)
+    assert rc == 1
+    rc = L.gsb_radix_sort_pairs(None, None, None, None, 1 << 31, 0, 8, None, None, 0, None)
+    assert rc == 4  # capacity
+    with pytest.raises(N.NativeError, match="status 2"):
+        N.check(2, "x")
+
+
+def test_raster_config_defaults_and_aliases():
+    cfg = tgb.RasterConfig(height=32, width=48)
+    assert cfg.tile_size == 16 and cfg.max_fast_pairs == 2048 and cfg.enable_overflow_fallback
+    assert cfg.pair_cap == 2048
+    assert tgb.RasterConfig(32, 48, 16, 4096).pair_cap == 4096  # root positional order
+    assert tgb.RasterConfig(32, 48, max_tile_pairs=4096).pair_cap == 4096
+    tgb.RasterConfig(32, 48, use_active_tiles=True, active_policy="auto", stop_count_mode="always")
+
+
+def test_runtime_shader_config_env(monkeypatch):
+    rt = tgb.get_runtime_shader_config()
+    assert (rt.tile_size, rt.threads, rt.chunk_size, rt.fast_cap, rt.simdgroups) == (16, 256, 64, 2048, 8)
+    monkeypatch.setenv("GSP_TILE_SIZE", "12")
+    with pytest.raises(ValueError, match="GSP_TILE_SIZE"):
+        tgb.get_runtime_shader_config()
+    monkeypatch.setenv("GSP_TILE_SIZE", "16")
+    monkeypatch.setenv("GSP_CHUNK", "0")
+    with pytest.raises(ValueError, match="GSP_CHUNK"):
+        tgb.get_runtime_shader_config()
+
+
+def _inputs(B=None, G=8, device="cpu"):
+    shp = (G,) if B is None else (B, G)
+    return (torch.zeros(*shp, 2, device=device), torch.zeros(*shp, 3, device=device),
+            torch.zeros(*shp, 3, device=device), torch.zeros(*shp, device=device), torch.zeros(*shp, device=device))
+
+
+def test_input_validation_messages():
+    cfg = tgb.RasterConfig(16, 16)
+    with pytest.raises(ValueError, match="must be on CUDA"):
+        tgb.rasterize_projected_gaussians(*_inputs(), cfg)
+    m, q, c, o, d = _inputs()
+    with pytest.raises(ValueError, match="same device"):
+        tgb.rasterize_projected_gaussians(m.to("meta"), q, c, o, d, cfg)
+    with pytest.raises(ValueError, match="must be on CUDA"):
+        tgb.project_pinhole_gaussians(torch.zeros(4, 3), torch.zeros(4, 3), torch.zeros(4, 4), torch.zeros(4),
+                                      1.0, 1.0, 0.0, 0.0)
+    with pytest.raises(ValueError, match="config is required"):
+        tgb.rasterize_pinhole_gaussians(torch.zeros(4, 3), torch.zeros(4, 3), torch.zeros(4, 4), torch.zeros(4),
+                                        torch.zeros(4, 3), 1.0, 1.0, 0.0, 0.0)
+
+
+def test_batch_chunk_policy_matches_reference():
+    cfg = tgb.RasterConfig(4096, 4096)
+    assert _choose_batch_chunk_size(cfg, 1, 65536, 65536) == 1
+    assert _choose_batch_chunk_size(tgb.RasterConfig(512, 1024), 4, 2048, 2048) == 4
+    assert _choose_batch_chunk_size(tgb.RasterConfig(512, 1024, batch_strategy="serial"), 4, 2048, 2048) == 1
+    assert _choose_batch_chunk_size(cfg, 8, 65536, 65536) == 4

@@ -1,0 +1,145 @@
+"""GPU binning parity through the C ABI: depth permutation, packed records, scan
+offsets, 64-bit pair keys, sorted intersection lists and tile ranges must be
+bit-identical to the C oracle (oracle/gsplat_oracle.c)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import torch_gsplat_bridge_fast as tgb
+from torch_gsplat_bridge_fast import _native as N
+from torch_gsplat_bridge_fast.rasterize import _bin
+from oracle import oracle as O
+from workloads import Splats2D, config_2d, make_2d
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def gpu_bin(s: Splats2D):
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV).contiguous() for t in s.tensors()))
+    torch.cuda.synchronize()
+    return dict(perm=st.perm.cpu().numpy().reshape(-1), rec=st.rec.cpu().numpy(),
+                pair_offsets=st.pair_offsets.cpu().numpy(), P=st.P,
+                keys=st.keys.cpu().numpy().view(np.uint64), ids=st.binned_ids.cpu().numpy(),
+                tile_offsets=st.tile_offsets.cpu().numpy())
+
+
+def cpu_bin(s: Splats2D):
+    meta = O.Meta(s.height, s.width, s.B, s.G)
+    perm, rec, off, P = O.bin_prepare(meta, *(t.numpy() for t in s.tensors()))
+    keys, ids, toff = O.bin_emit(meta, rec, off, P)
+    return dict(perm=perm, rec=rec, pair_offsets=off, P=P, keys=keys, ids=ids, tile_offsets=toff)
+
+
+def assert_bin_equal(g, c):
+    assert g["P"] == c["P"]
+    assert np.array_equal(g["perm"], c["perm"])
+    assert np.array_equal(g["rec"].view(np.uint32), c["rec"].view(np.uint32))
+    assert np.array_equal(g["pair_offsets"], c["pair_offsets"])
+    assert np.array_equal(g["keys"], c["keys"])
+    assert np.array_equal(g["ids"], c["ids"])
+    assert np.array_equal(g["tile_offsets"], c["tile_offsets"])
+
+
+@pytest.mark.parametrize("name", ["c0", "c1", "c2", "c3"])
+def test_binning_bit_exact_configs(name):
+    s = config_2d(name, seed=0)
+    assert_bin_equal(gpu_bin(s), cpu_bin(s))
+
+
+@pytest.mark.parametrize("B,G,H,W,sigma", [
+    (1, 1, 16, 16, (2.0, 3.0)),
+    (1, 7, 17, 33, (0.5, 30.0)),
+    (3, 513, 70, 90, (0.5, 12.0)),
+    (2, 4097, 129, 257, (1.0, 40.0)),
+    (5, 3000, 31, 47, (0.5, 8.0)),
+])
+def test_binning_bit_exact_ragged(B, G, H, W, sigma):
+    s = make_2d(B, G, H, W, seed=B * 1000 + G, sigma=sigma)
+    assert_bin_equal(gpu_bin(s), cpu_bin(s))
+
+
+def test_binning_edge_values():
+    """Ties, signed zeros, NaN/inf depths, degenerate conics, zero/over-unit
+    opacities and off-screen or non-finite means bin identically."""
+    s = make_2d(2, 600, 64, 96, seed=77, sigma=(0.5, 20.0))
+    d = s.depths
+    d[0, :50] = 1.0  # ties
+    d[0, 50:60] = -0.0
+    d[0, 60:70] = 0.0
+    d[0, 70] = float("nan")
+    d[0, 71] = float("inf")
+    d[0, 72] = -float("inf")
+    d[1, :100] = -torch.rand(100) * 10
+    o = s.opacities
+    o[0, 100:120] = 0.0
+    o[0, 120:130] = 1.0 / 255.0
+    o[0, 130:140] = 1.7
+    o[1, 200:210] = float("nan")
+    q = s.conics
+    q[0, 150:160] = torch.tensor([1.0, 2.0, 1.0])  # det < 0
+    q[0, 160:170] = torch.tensor([0.0, 0.0, 0.0])
+    q[0, 170:175] = torch.tensor([1e-12, 0.0, 1e-12])  # huge support
+    m = s.means2d
+    m[0, 180:190] = torch.tensor([-500.0, 30.0])
+    m[0, 190:200] = torch.tensor([5e9, -5e9])
+    m[1, 300:305] = float("nan")
+    m[1, 305:310] = float("inf")
+    assert_bin_equal(gpu_bin(s), cpu_bin(s))
+
+
+def test_binning_empty_and_zero_pairs():
+    s = make_2d(1, 64, 32, 32, seed=1)
+    s.opacities.zero_()  # nothing visible -> P = 0
+    g = gpu_bin(s)
+    assert g["P"] == 0 and np.all(g["tile_offsets"] == 0)
+    assert_bin_equal(g, cpu_bin(s))
+
+
+def test_binning_is_deterministic():
+    s = config_2d("c1", seed=3)
+    a, b = gpu_bin(s), gpu_bin(s)
+    for k in ("perm", "pair_offsets", "keys", "ids", "tile_offsets"):
+        assert np.array_equal(a[k], b[k]), k
+
+
+def _sort(keys: np.ndarray, vals: np.ndarray, begin: int, end: int):
+    L = N.load()
+    n = keys.size
+    k_in = torch.from_numpy(keys.view(np.int64)).to(DEV)
+    v_in = torch.from_numpy(vals.view(np.int32)).to(DEV)
+    k_out = torch.empty_like(k_in)
+    v_out = torch.empty_like(v_in)
+    status = torch.zeros(8, dtype=torch.int32, device=DEV)
+    ws_n = L.gsb_radix_sort_pairs_workspace_size(n, begin, end)
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=DEV)
+    rc = L.gsb_radix_sort_pairs(N.ptr(k_in), N.ptr(v_in), N.ptr(k_out), N.ptr(v_out), n, begin, end, N.ptr(status),
+                                N.ptr(ws), ws_n, N.stream_ptr(DEV))
+    N.check(rc, "sort")
+    torch.cuda.synchronize()
+    assert int(status[1]) == 0
+    return k_out.cpu().numpy().view(np.uint64), v_out.cpu().numpy().view(np.uint32)
+
+
+@pytest.mark.parametrize("n,begin,end", [(1, 0, 8), (4095, 0, 32), (4096, 32, 48), (4097, 5, 19),
+                                         (100_000, 0, 64), (1_000_003, 32, 45), (300_000, 0, 0)])
+def test_radix_sort_is_stable_and_exact(n, begin, end):
+    rng = np.random.default_rng(n + begin)
+    keys = rng.integers(0, 2**63, n, dtype=np.uint64) | (rng.integers(0, 2, n, dtype=np.uint64) << np.uint64(63))
+    keys[: n // 3] &= np.uint64(0xFFFF0000FFFF00FF)  # many ties
+    vals = np.arange(n, dtype=np.uint32)
+    k, v = _sort(keys, vals, begin, end)
+    width = end - begin
+    if width == 0:
+        assert np.array_equal(k, keys) and np.array_equal(v, vals)
+        return
+    mask = np.uint64((1 << width) - 1) if width < 64 else np.uint64(0xFFFFFFFFFFFFFFFF)
+    digit = (keys >> np.uint64(begin)) & mask
+    order = np.argsort(digit, kind="stable")
+    assert np.array_equal(v, vals[order])
+    assert np.array_equal(k, keys[order])

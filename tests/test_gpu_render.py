@@ -1,0 +1,226 @@
+"""GPU compositing parity (forward image + saved state, backward gradients)
+through the C ABI, against the C oracle and the torch restatement of the
+reference's early-stop oracle, plus the reference's own fixtures through the
+public API. Gates: image max-abs <= 1e-4; gradients <= 1e-3 relative."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import torch_gsplat_bridge_fast as tgb
+from helpers import GRAD_RTOL, IMAGE_ATOL, REF_FIXTURE_ATOL, golden, max_abs, np_, rel_err, upstream_grad
+from oracle import oracle as O
+from oracle import torch_ref as TR
+from workloads import config_2d, grad_image, make_2d
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+GRAD_KEYS = ("g_means2d", "g_conics", "g_colors", "g_opacities")
+
+
+def gpu_fwd_bwd(s, gimg, bg=(0.0, 0.0, 0.0), batched=True):
+    cfg = tgb.RasterConfig(s.height, s.width, background=bg)
+    ins = [t.to(DEV).clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+    args = ins if batched else [t[0] for t in ins]
+    out = tgb.rasterize_projected_gaussians(*args, cfg)
+    g = gimg.to(DEV) if batched else gimg[0].to(DEV)
+    out.backward(g)
+    torch.cuda.synchronize()
+    grads = [np_(t.grad).reshape(s.B, s.G, -1).squeeze(-1) if t.grad is not None else None for t in ins[:4]]
+    return np_(out).reshape(s.B, s.height, s.width, 3), grads
+
+
+def cpu_oracle(s, gimg, bg=(0.0, 0.0, 0.0)):
+    meta = O.Meta(s.height, s.width, s.B, s.G, background=bg)
+    return O.full_forward_backward(meta, *(t.numpy() for t in s.tensors()), gimg.numpy())
+
+
+@pytest.mark.parametrize("name", ["c0", "c1", "c2", "c3"])
+def test_forward_backward_match_c_oracle(name):
+    s = config_2d(name, seed=0)
+    gimg = grad_image(s.B, s.height, s.width, seed=1)
+    img, grads = gpu_fwd_bwd(s, gimg)
+    ref = cpu_oracle(s, gimg)
+    assert max_abs(img, ref["image"]) <= IMAGE_ATOL
+    for got, want, key in zip(grads, ref["grads"], GRAD_KEYS):
+        assert rel_err(got, want) <= GRAD_RTOL, key
+
+
+def test_saved_state_matches_c_oracle():
+    from torch_gsplat_bridge_fast.rasterize import _bin, _render_forward
+
+    s = config_2d("c1", seed=2)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV) for t in s.tensors()))
+    out, T, last = _render_forward(st, cfg, s.B, save_state=True)
+    meta = O.Meta(s.height, s.width, s.B, s.G)
+    ref = cpu_oracle(s, torch.zeros(s.B, s.height, s.width, 3))
+    assert max_abs(np_(T), ref["final_T"]) <= 1e-5
+    agree = np.mean(np_(last) == ref["last_idx"])
+    assert agree >= 0.9999, agree
+
+
+def test_c0_full_frame_matches_torch_saturating_reference():
+    """Config 0 against the reference's early-stop oracle (torch fp32 restatement,
+    evaluated by torch on the GPU), full frame, N(0,1) upstream gradient."""
+    s = config_2d("c0", seed=0)
+    gimg = grad_image(1, 512, 512, seed=1)
+    img, grads = gpu_fwd_bwd(s, gimg)
+    ins = [t.to(DEV).clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+    ref = TR.saturating_reference(*ins, 512, 512)
+    ref.backward(gimg.to(DEV))
+    assert max_abs(img, np_(ref)) <= IMAGE_ATOL
+    for got, t, key in zip(grads, ins[:4], GRAD_KEYS):
+        assert rel_err(got, np_(t.grad).reshape(got.shape)) <= GRAD_RTOL, key
+
+
+@pytest.mark.parametrize("name,n_tiles", [("c1", 24), ("c2", 12), ("c3", 24)])
+def test_tile_sampled_parity_with_torch_reference(name, n_tiles):
+    """Large frames: the reference oracle on sampled tiles (all splats, no
+    binning), upstream gradient zero elsewhere, so both sides differentiate the
+    same restricted loss."""
+    s = config_2d(name, seed=0)
+    H, W, B = s.height, s.width, s.B
+    gen = torch.Generator().manual_seed(5)
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    # Half of the sampled tiles are the busiest ones (per the C oracle), half random.
+    meta = O.Meta(H, W, B, s.G)
+    _, rec, off, P = O.bin_prepare(meta, *(t.numpy() for t in s.tensors()))
+    _, _, toff = O.bin_emit(meta, rec, off, P)
+    counts = torch.tensor(toff[1:] - toff[:-1]).view(B, ty * tx)
+    gimg = torch.zeros(B, H, W, 3)
+    full = grad_image(B, H, W, seed=1)
+    picks = []
+    for b in range(B):
+        busy = torch.argsort(counts[b], descending=True)[: n_tiles // 2]
+        rnd = torch.randint(0, ty * tx, (n_tiles - busy.numel(),), generator=gen)
+        tiles = torch.unique(torch.cat([busy, rnd]))
+        ys, xs = [], []
+        for t in tiles.tolist():
+            y0, x0 = (t // tx) * 16, (t % tx) * 16
+            yy, xx = torch.meshgrid(torch.arange(y0, min(y0 + 16, H)), torch.arange(x0, min(x0 + 16, W)),
+                                    indexing="ij")
+            ys.append(yy.reshape(-1))
+            xs.append(xx.reshape(-1))
+        py, px = torch.cat(ys), torch.cat(xs)
+        gimg[b, py, px] = full[b, py, px]
+        picks.append((px, py))
+    img, grads = gpu_fwd_bwd(s, gimg)
+    ins = [t.to(DEV).clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+    loss = 0.0
+    for b, (px, py) in enumerate(picks):
+        ref = TR.saturating_reference_pixels(ins[0][b], ins[1][b], ins[2][b], ins[3][b], ins[4][b], px, py)
+        assert max_abs(img[b, py.numpy(), px.numpy()], np_(ref)) <= IMAGE_ATOL
+        loss = loss + (ref * gimg[b, py, px].to(DEV)).sum()
+    loss.backward()
+    for got, t, key in zip(grads, ins[:4], GRAD_KEYS):
+        assert rel_err(got, np_(t.grad).reshape(got.shape)) <= GRAD_RTOL, key
+
+
+@pytest.mark.parametrize("name,bg,batched", [
+    ("check_case_b1", (0.0, 0.0, 0.0), False),
+    ("check_case_b2", (0.0, 0.0, 0.0), True),
+    ("saturated_many_splats", (1.0, 1.0, 1.0), True),
+    ("c0like_saturating", (0.0, 0.0, 0.0), True),
+])
+def test_reference_fixtures_through_public_api(name, bg, batched):
+    """The reference's own test cases (reference_check.py:114-214) against the
+    outputs its torch oracles produced, at its tolerance (1e-5)."""
+    c = golden(name)
+    H, W = int(c["H"]), int(c["W"])
+    ins = [torch.tensor(c[k], device=DEV) for k in ("means2d", "conics", "colors", "opacities", "depths")]
+    ins = [t.requires_grad_(i < 4) for i, t in enumerate(ins)]
+    args = ins if batched else [t[0] for t in ins]
+    cfg = tgb.RasterConfig(height=H, width=W, tile_size=16, max_fast_pairs=2048, background=bg)
+    out = tgb.rasterize_projected_gaussians(*args, cfg)
+    up = torch.tensor(upstream_grad(c), device=DEV)
+    out.backward(up if batched else up[0])
+    assert max_abs(np_(out).reshape(c["image"].shape), c["image"]) <= REF_FIXTURE_ATOL
+    for t, key in zip(ins[:4], GRAD_KEYS):
+        assert max_abs(np_(t.grad), c[key]) <= REF_FIXTURE_ATOL, key
+
+
+def test_eval_overflow_disabled_raises():
+    """reference_check.py:217-235."""
+    G, H, W = 4, 16, 16
+    means2d = torch.full((G, 2), 8.0, device=DEV)
+    conics = torch.tensor([[0.05, 0.0, 0.05]], device=DEV).expand(G, 3).contiguous()
+    colors = torch.rand(G, 3, device=DEV)
+    opacities = torch.full((G,), 0.5, device=DEV)
+    depths = torch.arange(G, device=DEV, dtype=torch.float32)
+    cfg = tgb.RasterConfig(height=H, width=W, tile_size=16, max_fast_pairs=1, enable_overflow_fallback=False)
+    with torch.no_grad():
+        with pytest.raises(RuntimeError, match="Tile overflow detected"):
+            tgb.rasterize_projected_gaussians(means2d, conics, colors, opacities, depths, cfg)
+    # With the fallback on, over-cap tiles render exactly.
+    cfg_ok = tgb.RasterConfig(height=H, width=W, max_fast_pairs=1)
+    out = tgb.rasterize_projected_gaussians(means2d, conics, colors, opacities, depths, cfg_ok)
+    ref = TR.saturating_reference(means2d, conics, colors, opacities, depths, H, W)
+    assert max_abs(np_(out), np_(ref)) <= 1e-5
+
+
+def test_eval_and_train_paths_agree_and_are_deterministic():
+    s = config_2d("c2", seed=4)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    ins = [t.to(DEV) for t in s.tensors()]
+    with torch.no_grad():
+        ev = tgb.rasterize_projected_gaussians(*ins, cfg)
+    tr_ins = [t.clone().requires_grad_(i < 4) for i, t in enumerate(ins)]
+    tr = tgb.rasterize_projected_gaussians(*tr_ins, cfg)
+    tr2 = tgb.rasterize_projected_gaussians(*tr_ins, cfg)
+    assert torch.equal(ev, tr.detach())
+    assert torch.equal(tr, tr2)
+
+
+def test_serial_and_flatten_batches_agree():
+    s = make_2d(3, 700, 48, 80, seed=12, sigma=(1.0, 15.0))
+    ins = [t.to(DEV) for t in s.tensors()]
+    a = tgb.rasterize_projected_gaussians(*ins, tgb.RasterConfig(48, 80, batch_strategy="serial"))
+    b = tgb.rasterize_projected_gaussians(*ins, tgb.RasterConfig(48, 80, batch_strategy="flatten"))
+    assert torch.equal(a, b)
+
+
+def test_empty_and_tiny_inputs():
+    cfg = tgb.RasterConfig(20, 36, background=(0.25, 0.5, 0.75))
+    z2, z3, z1 = (torch.zeros(0, 2, device=DEV), torch.zeros(0, 3, device=DEV), torch.zeros(0, device=DEV))
+    out = tgb.rasterize_projected_gaussians(z2, z3, z3, z1, z1, cfg)
+    assert out.shape == (20, 36, 3)
+    assert torch.allclose(out, torch.tensor([0.25, 0.5, 0.75], device=DEV).expand(20, 36, 3))
+    m = torch.tensor([[10.0, 5.0]], device=DEV, requires_grad=True)
+    q = torch.tensor([[0.3, 0.0, 0.3]], device=DEV, requires_grad=True)
+    c = torch.tensor([[1.0, 0.0, 0.0]], device=DEV, requires_grad=True)
+    o = torch.tensor([0.9], device=DEV, requires_grad=True)
+    d = torch.tensor([1.0], device=DEV)
+    out = tgb.rasterize_projected_gaussians(m, q, c, o, d, cfg)
+    ref = TR.saturating_reference(m, q, c, o, d, 20, 36, bg=(0.25, 0.5, 0.75))
+    assert max_abs(np_(out), np_(ref)) <= 1e-6
+
+
+def test_input_validation_on_cuda():
+    cfg = tgb.RasterConfig(16, 16)
+    m, q, c, o, d = (torch.zeros(4, 2, device=DEV), torch.zeros(4, 3, device=DEV), torch.zeros(4, 3, device=DEV),
+                     torch.zeros(4, device=DEV), torch.zeros(4, device=DEV))
+    with pytest.raises(ValueError, match="float32"):
+        tgb.rasterize_projected_gaussians(m.double(), q, c, o, d, cfg)
+    with pytest.raises(ValueError, match="rank"):
+        tgb.rasterize_projected_gaussians(m, q[None], c, o, d, cfg)
+    with pytest.raises(ValueError, match="tile"):
+        tgb.rasterize_projected_gaussians(m, q, c, o, d, tgb.RasterConfig(16, 16, tile_size=8))
+
+
+def test_profile_stats():
+    s = config_2d("c2", seed=0)
+    ins = [t.to(DEV) for t in s.tensors()]
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = tgb.profile_projected_gaussians(*ins, cfg, run_forward=True)
+    meta = O.Meta(s.height, s.width, s.B, s.G)
+    _, rec, off, P = O.bin_prepare(meta, *(t.numpy() for t in s.tensors()))
+    _, _, toff = O.bin_emit(meta, rec, off, P)
+    counts = np.diff(toff)
+    assert st["total_pairs"] == P and st["max_pairs_per_tile"] == counts.max()
+    assert st["tiles"] == counts.size
+    assert st["overflow_tile_count"] == int((counts > 2048).sum())
+    assert 0 < st["mean_stop_ratio"] <= 1.0
+    r = tgb.profile_projected_gaussians(*ins, cfg, return_image=True)
+    assert r["image"].shape == (4, 512, 1024, 3)
