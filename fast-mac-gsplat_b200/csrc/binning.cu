@@ -78,8 +78,10 @@ __global__ void __launch_bounds__(kScanThreads)
       const float4 p0 = make_float4(mu.x, mu.y, conics[3 * orig + 0], conics[3 * orig + 1]);
       const float4 p1 = make_float4(conics[3 * orig + 2], opacities[orig], colors[3 * orig + 0],
                                     colors[3 * orig + 1]);
+      const float op = opacities[orig];
       const float4 p2 = make_float4(colors[3 * orig + 2], __uint_as_float((uint32_t)sorted_keys[r]),
-                                    0.0f, 0.0f);
+                                    vis_log_threshold(op, m.alpha_thr, m.max_alpha),
+                                    sat_log_threshold(op, m.max_alpha));
       rec[3 * r + 0] = p0;
       rec[3 * r + 1] = p1;
       rec[3 * r + 2] = p2;

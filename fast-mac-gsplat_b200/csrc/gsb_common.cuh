@@ -119,6 +119,33 @@ __device__ __forceinline__ bool support_tau(float opacity, float thr, float eps,
   return isfinite(t) && (t > 0.0f);
 }
 
+// Visibility and saturation thresholds of a splat, in `power` units. A splat is
+// visible at a pixel iff power <= 0 && power >= vis (the reference gate
+// min(max_alpha, op*exp(power)) >= alpha_thr, …metal:586-591, restated as
+// power >= ln(alpha_thr/op)); its alpha saturates iff power >= sat (the
+// backward gate raw < max_alpha, …metal:1022, is power < ln(max_alpha/op)).
+// Both logs go through det_log, so every evaluator makes identical decisions.
+__device__ __forceinline__ float vis_log_threshold(float op, float thr, float max_alpha) {
+  if (!(op >= thr) || !(max_alpha >= thr)) return __int_as_float(0x7f800000);
+  const double ratio = __ddiv_rn((double)thr, (double)op);
+  if (!(ratio > 0.0)) return __int_as_float(0xff800000);
+  return __double2float_rn(det_log(ratio));
+}
+__device__ __forceinline__ float sat_log_threshold(float op, float max_alpha) {
+  if (!(op > 0.0f)) return __int_as_float(0x7f800000);
+  const double ratio = __ddiv_rn((double)max_alpha, (double)op);
+  if (!(ratio > 0.0)) return __int_as_float(0xff800000);
+  return __double2float_rn(det_log(ratio));
+}
+
+// power = -0.5 (a dx dx + 2 b dx dy + c dy dy) in the reference's operation
+// order (…metal:587) with round-to-nearest ops only. ta = (a dx) dx and
+// tb = (2 b) dx are shared by all pixels of a column.
+__device__ __forceinline__ float power_rn(float ta, float tb, float c, float dy) {
+  const float q = __fadd_rn(__fadd_rn(ta, __fmul_rn(tb, dy)), __fmul_rn(__fmul_rn(c, dy), dy));
+  return __fmul_rn(-0.5f, q);
+}
+
 // float -> int after clamping into int range (the clamp keeps NaN/huge means
 // deterministic; every in-range value converts exactly as int(x) would).
 __device__ __forceinline__ int clamp_f2i(float x) {

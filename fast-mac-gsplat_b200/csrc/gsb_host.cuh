@@ -1,6 +1,7 @@
 // Host-side helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <stddef.h>
 #include <stdint.h>
 
 #include <cuda_runtime.h>
@@ -8,6 +9,21 @@
 #include "gsb_common.cuh"
 
 namespace gsb {
+
+// Bump allocator over a caller-provided workspace. With base == nullptr it only
+// measures (the *_workspace_size queries run the same carve sequence).
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += count * sizeof(T);
+    return p;
+  }
+};
 
 // Process-wide count of kernel launches issued by this library.
 void note_launches(uint64_t n);

@@ -9,6 +9,8 @@
 
 #include <cuda_runtime.h>
 
+#include "gsb_host.cuh"
+
 namespace gsb {
 
 constexpr int kSortThreads = 256;
@@ -23,21 +25,6 @@ inline int sort_passes(int begin_bit, int end_bit) {
   return end_bit > begin_bit ? (end_bit - begin_bit + kRadixBits - 1) / kRadixBits : 0;
 }
 inline int64_t sort_partitions(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
-
-// Bump allocator over a caller-provided workspace. With base == nullptr it only
-// measures (the *_workspace_size queries run the same carve sequence).
-struct Carver {
-  char* base;
-  size_t off = 0;
-  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
-  template <typename T>
-  T* take(size_t count) {
-    off = (off + 255) & ~size_t(255);
-    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
-    off += count * sizeof(T);
-    return p;
-  }
-};
 
 // Carves the sort's scratch: temp key/value buffers, histograms, partition
 // counters and per-pass look-back tiles. Returns the status of the launches

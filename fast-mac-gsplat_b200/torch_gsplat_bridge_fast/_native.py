@@ -37,6 +37,7 @@ EXPORTED = (
     "gsb_bin_emit_workspace_size",
     "gsb_bin_emit",
     "gsb_tile_stats",
+    "gsb_render_workspace_size",
     "gsb_render_forward",
     "gsb_render_backward",
     "gsb_unsort_grads",
@@ -92,8 +93,9 @@ def load() -> C.CDLL:
         "gsb_bin_emit_workspace_size": (sz, [M, i64]),
         "gsb_bin_emit": (C.c_int, [M, p, p, i64, p, p, p, p, p, sz, p]),
         "gsb_tile_stats": (C.c_int, [M, p, p, p]),
-        "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p]),
-        "gsb_render_backward": (C.c_int, [M, p, p, p, p, p, p, p, p, p]),
+        "gsb_render_workspace_size": (sz, [M]),
+        "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, sz, p]),
+        "gsb_render_backward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_unsort_grads": (C.c_int, [M, p, p, p, p, p, p, p]),
         "gsb_project_forward": (C.c_int, [i32, i32, p, p, p, p, p, p, f32, p, p, p, p, p]),
         "gsb_project_backward": (C.c_int, [i32, i32] + [p] * 10 + [f32] + [p] * 7),

@@ -335,10 +335,12 @@ def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: boo
     if save_state:
         final_T = torch.empty((B, config.height, config.width), dtype=torch.float32, device=dev)
         last_idx = torch.empty((B, config.height, config.width), dtype=torch.int32, device=dev)
+    ws_bytes = L.gsb_render_workspace_size(st.meta)
+    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
     N.check(
         _timed("render_fwd", lambda: L.gsb_render_forward(
             st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out), N.ptr(final_T),
-            N.ptr(last_idx), N.ptr(st.status), N.stream_ptr(dev))),
+            N.ptr(last_idx), N.ptr(st.status), N.ptr(ws), ws_bytes, N.stream_ptr(dev))),
         "gsb_render_forward",
     )
     if _debug_checks():
@@ -372,10 +374,12 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         stream = N.stream_ptr(dev)
         g = _aligned(grad_out.to(torch.float32))
         grad_rec = torch.empty((B * G, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
+        ws_bytes = L.gsb_render_workspace_size(ctx.meta)
+        ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
         N.check(
             _timed("render_bwd", lambda: L.gsb_render_backward(
                 ctx.meta, N.ptr(rec), N.ptr(tile_offsets), N.ptr(binned_ids), N.ptr(final_T), N.ptr(last_idx),
-                N.ptr(g), N.ptr(grad_rec), N.ptr(status), stream)),
+                N.ptr(g), N.ptr(grad_rec), N.ptr(status), N.ptr(ws), ws_bytes, stream)),
             "gsb_render_backward",
         )
         need = ctx.needs_input_grad

@@ -56,7 +56,9 @@ extern "C" {
 #define GSB_REC_FLOATS 12
 /* rec[r*12 + ...]: 0 mean_x, 1 mean_y, 2 conic_a, 3 conic_b,
  *                  4 conic_c, 5 opacity, 6 color_r, 7 color_g,
- *                  8 color_b, 9 depth_key (uint32 bits), 10,11 unused (0) */
+ *                  8 color_b, 9 depth_key (uint32 bits),
+ *                  10 ln(alpha_threshold/opacity)  (visible iff power in [this, 0]),
+ *                  11 ln(max_alpha/opacity)        (alpha saturates iff power >= this) */
 /* grad record (same 12-float stride, depth-rank order):
  *   0 g_mean_x, 1 g_mean_y, 2 g_a, 3 g_b, 4 g_c, 5 g_opacity, 6 g_r, 7 g_g, 8 g_b_color */
 
@@ -116,18 +118,24 @@ int gsb_tile_stats(const gsb_raster_meta* meta, const int32_t* tile_offsets, uin
                    void* stream);
 
 /* ---- compositing ---------------------------------------------------------
- * Replaces `tile_fast_forward_eval` / `tile_fast_forward_state`
+ * Workspace of gsb_render_forward / gsb_render_backward (a list of the tiles
+ * with long pair lists, which get a CTA each; the others get a warp each). */
+size_t gsb_render_workspace_size(const gsb_raster_meta* meta);
+
+/* Replaces `tile_fast_forward_eval` / `tile_fast_forward_state`
  * (…/gsplat_v8_project3d_kernels.metal:783-929; root csrc/metal/gsplat_fast_kernels.metal:221-294).
  * final_T and last_idx may both be NULL (eval: no saved state). */
 int gsb_render_forward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                        const int32_t* binned_ids, float* out_rgb, float* final_T,
-                       int32_t* last_idx, uint32_t* status, void* stream);
+                       int32_t* last_idx, uint32_t* status, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /* Replaces `tile_fast_backward_saved` (…/gsplat_v8_project3d_kernels.metal:931-1063; root
  * csrc/metal/gsplat_fast_kernels.metal:296-395). Zeroes and accumulates grad_rec [B*G*12]. */
 int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                         const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
-                        const float* grad_rgb, float* grad_rec, uint32_t* status, void* stream);
+                        const float* grad_rgb, float* grad_rec, uint32_t* status, void* workspace,
+                        size_t workspace_bytes, void* stream);
 
 /* Replaces the un-sort scatter of the autograd backward
  * (torch_gsplat_bridge_fast/rasterize.py:96-105; …/v8_project3d/…/rasterize.py:583-591, 847-851).

@@ -106,6 +106,28 @@ static int support_tau(float op, float thr, float eps, float* tau) {
   return isfinite(t) && t > 0.0f;
 }
 
+/* Visibility of a splat at a pixel, decided on `power` instead of on the
+ * rounded product op*exp(power): alpha = min(max_alpha, op*e^power) >= thr
+ * <=> power >= ln(thr/op) (when max_alpha >= thr). The threshold is computed
+ * once per splat with det_log and rounded to float, so the decision is the
+ * same bit-for-bit wherever it is evaluated. +inf: never visible; -inf: always
+ * (op = +inf). */
+float orc_vis_log_threshold(float op, float thr, float max_alpha) {
+  if (!(op >= thr) || !(max_alpha >= thr)) return INFINITY;
+  const double ratio = (double)thr / (double)op;
+  if (!(ratio > 0.0)) return -INFINITY;
+  return (float)orc_det_log(ratio);
+}
+
+/* Saturation gate of the backward (raw < max_alpha) decided as power <
+ * ln(max_alpha/op); +inf when op <= 0 (never saturates). */
+float orc_sat_log_threshold(float op, float max_alpha) {
+  if (!(op > 0.0f)) return INFINITY;
+  const double ratio = (double)max_alpha / (double)op;
+  if (!(ratio > 0.0)) return -INFINITY;
+  return (float)orc_det_log(ratio);
+}
+
 static int clamp_f2i(float x) {
   x = fminf(fmaxf(x, -1073741824.0f), 1073741824.0f);
   return (int)x;
@@ -213,8 +235,8 @@ int64_t orc_bin_prepare(const orc_meta* m, const float* means2d, const float* co
       R[7] = colors[3 * o + 1];
       R[8] = colors[3 * o + 2];
       R[9] = u2f(kv[r].key);
-      R[10] = 0.0f;
-      R[11] = 0.0f;
+      R[10] = orc_vis_log_threshold(opacities[o], m->alpha_threshold, m->max_alpha);
+      R[11] = orc_sat_log_threshold(opacities[o], m->max_alpha);
     }
   }
 #pragma omp parallel for schedule(dynamic, 256)
@@ -307,9 +329,8 @@ void orc_render_forward(const orc_meta* m, const float* rec, const int32_t* tile
             const float* R = rec + (int64_t)ids[start + j] * REC;
             const float dx = fx - R[0], dy = fy - R[1];
             const float power = -0.5f * (R[2] * dx * dx + 2.0f * R[3] * dx * dy + R[4] * dy * dy);
-            if (power > 0.0f) continue;
+            if (!(power <= 0.0f && power >= R[10])) continue; /* eval_alpha gate, see orc_vis_log_threshold */
             const float alpha = fminf(m->max_alpha, R[5] * expf(power));
-            if (!(alpha >= m->alpha_threshold)) continue;
             const float w = T * alpha;
             cr += w * R[6];
             cg += w * R[7];
@@ -358,9 +379,8 @@ void orc_render_backward(const orc_meta* m, const float* rec, const int32_t* til
               const float* R = rec + (int64_t)ids[start + j] * REC;
               const float dx = fx - R[0], dy = fy - R[1];
               const float power = -0.5f * (R[2] * dx * dx + 2.0f * R[3] * dx * dy + R[4] * dy * dy);
-              if (power > 0.0f) continue;
+              if (!(power <= 0.0f && power >= R[10])) continue;
               const float alpha = fminf(m->max_alpha, R[5] * expf(power));
-              if (!(alpha >= m->alpha_threshold)) continue;
               T_final *= (1.0f - alpha);
               if (T_final <= m->transmittance_threshold) {
                 end_i = j + 1;
@@ -378,15 +398,14 @@ void orc_render_backward(const orc_meta* m, const float* rec, const int32_t* til
             const float dx = fx - R[0], dy = fy - R[1];
             const float a = R[2], bq = R[3], c = R[4], op = R[5];
             const float power = -0.5f * (a * dx * dx + 2.0f * bq * dx * dy + c * dy * dy);
-            if (power > 0.0f) continue;
+            if (!(power <= 0.0f && power >= R[10])) continue;
             const float raw = op * expf(power);
             const float alpha = fminf(m->max_alpha, raw);
-            if (!(alpha >= m->alpha_threshold)) continue;
             const float T_prev = T_cur / fmaxf(1.0f - alpha, m->eps);
             const float dot_gc = gr * R[6] + gg * R[7] + gb * R[8];
             const float g_alpha = T_prev * (dot_gc - gT);
             const float wc = T_prev * alpha;
-            const float g_raw = (raw < m->max_alpha) ? g_alpha : 0.0f;
+            const float g_raw = (power < R[11]) ? g_alpha : 0.0f; /* raw < max_alpha */
             const float g_power = g_raw * raw;
             double* A = loc + (int64_t)gi * 9;
             A[0] += g_power * (a * dx + bq * dy);

@@ -47,3 +47,15 @@ def upstream_grad(case: dict) -> np.ndarray:
         img = case["image"].astype(np.float32)
         return (2.0 * img / img.size).astype(np.float32)
     return case["grad_image"].astype(np.float32)
+
+
+def rel_err_finite(g, ref) -> float:
+    """rel_err over entries finite on both sides; the non-finite pattern must agree
+    (near-plane splats overflow to inf/nan identically in kernel and reference)."""
+    g = np.asarray(g, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    fin_g, fin_r = np.isfinite(g), np.isfinite(ref)
+    mismatch = np.mean(fin_g != fin_r) if g.size else 0.0
+    assert mismatch <= 1e-5, f"finite pattern differs on {mismatch:.2e} of entries"
+    both = fin_g & fin_r
+    return rel_err(g[both], ref[both])

@@ -52,6 +52,7 @@ def test_workspace_queries_without_gpu():
     assert L.gsb_bin_emit_workspace_size(C.byref(m), 1000) > 1000 * 12
     assert L.gsb_bin_emit_workspace_size(C.byref(m), 0) >= 0
     assert L.gsb_radix_sort_pairs_workspace_size(1 << 20, 32, 48) > (1 << 20) * 12
+    assert L.gsb_render_workspace_size(C.byref(m)) >= 4 * m.batch_size * 4 * 5
     bad = _meta(tile_size=8)
     assert L.gsb_bin_prepare_workspace_size(C.byref(bad)) == 0
 
@@ -64,7 +65,7 @@ def test_argument_validation_without_gpu():
     m = _meta()
     rc = L.gsb_bin_prepare(C.byref(m), *([None] * 9), None, 0, None)
     assert rc == 1  # null pointers
-    rc = L.gsb_render_forward(C.byref(_meta(height=0)), None, None, None, None, None, None, None, None)
+    rc = L.gsb_render_forward(C.byref(_meta(height=0)), None, None, None, None, None, None, None, None, 0, None)
     assert rc == 1
     rc = L.gsb_radix_sort_pairs(None, None, None, None, -1, 0, 8, None, None, 0, None)
     assert rc == 1

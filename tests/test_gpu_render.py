@@ -27,7 +27,8 @@ def gpu_fwd_bwd(s, gimg, bg=(0.0, 0.0, 0.0), batched=True):
     g = gimg.to(DEV) if batched else gimg[0].to(DEV)
     out.backward(g)
     torch.cuda.synchronize()
-    grads = [np_(t.grad).reshape(s.B, s.G, -1).squeeze(-1) if t.grad is not None else None for t in ins[:4]]
+    grads = [np_(t.grad).reshape(s.B, s.G, -1) for t in ins[:4]]
+    grads[3] = grads[3][..., 0]
     return np_(out).reshape(s.B, s.height, s.width, 3), grads
 
 
@@ -138,7 +139,10 @@ def test_reference_fixtures_through_public_api(name, bg, batched):
     out.backward(up if batched else up[0])
     assert max_abs(np_(out).reshape(c["image"].shape), c["image"]) <= REF_FIXTURE_ATOL
     for t, key in zip(ins[:4], GRAD_KEYS):
-        assert max_abs(np_(t.grad), c[key]) <= REF_FIXTURE_ATOL, key
+        if name.startswith("c0like"):  # N(0,1) upstream: gradients up to ~20, relative gate
+            assert rel_err(np_(t.grad), c[key]) <= GRAD_RTOL, key
+        else:  # the reference's own fixtures, at its absolute tolerance
+            assert max_abs(np_(t.grad), c[key]) <= REF_FIXTURE_ATOL, key
 
 
 def test_eval_overflow_disabled_raises():
