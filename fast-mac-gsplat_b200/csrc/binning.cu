@@ -23,6 +23,7 @@ constexpr int kScanTile = kScanThreads * kScanItems;
 constexpr unsigned long long kScanAgg = 1ull << 62;
 constexpr unsigned long long kScanInc = 2ull << 62;
 constexpr unsigned long long kScanMask = (1ull << 62) - 1ull;
+constexpr int kLookWin = 8;  // predecessors read per look-back step
 
 // Per splat in input order: depth-sort key (view in the high word) and the
 // exact number of tiles its support ellipse touches.
@@ -30,7 +31,7 @@ __global__ void __launch_bounds__(256)
     k_prepare(Meta m, const float2* __restrict__ means2d, const float* __restrict__ conics,
               const float* __restrict__ opacities, const float* __restrict__ depths,
               uint64_t* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
-              uint32_t* __restrict__ counts) {
+              uint32_t* __restrict__ counts, uint32_t* __restrict__ status) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= m.BG) return;
   const int b = i / m.G;
@@ -41,6 +42,10 @@ __global__ void __launch_bounds__(256)
   uint32_t n = 0;
   for_each_tile(mu.x, mu.y, a, bq, c, opacities[i], m, [&](int, int) { ++n; });
   counts[i] = n;
+  // Pair total (64-bit, order-independent integer sum) for the host's early read.
+  const unsigned long long wsum = __reduce_add_sync(__activemask(), n);
+  if ((threadIdx.x & 31) == __ffs(__activemask()) - 1 && wsum)
+    atomicAdd(reinterpret_cast<unsigned long long*>(status + GSB_STATUS_PAIR_TOTAL64), wsum);
 }
 
 // Gathers splats into depth-rank order (packed 48-byte records), and turns the
@@ -112,25 +117,31 @@ __global__ void __launch_bounds__(kScanThreads)
       st_volatile_u64(&lookback[0], kScanInc | block_total);
     } else {
       st_volatile_u64(&lookback[part], kScanAgg | block_total);
+      // Windowed look-back (kLookWin predecessors per L2 round trip).
       int64_t j = part - 1;
       int spins = 0;
-      bool failed = false;
-      while (j >= 0) {
-        const unsigned long long w = ld_volatile_u64(&lookback[j]);
-        if (w & kScanInc) {
-          excl += w & kScanMask;
-          break;
+      bool failed = false, done = false;
+      while (!done && !failed) {
+        unsigned long long w[kLookWin];
+#pragma unroll
+        for (int q = 0; q < kLookWin; ++q) w[q] = (j - q >= 0) ? ld_volatile_u64(&lookback[j - q]) : kScanInc;
+#pragma unroll
+        for (int q = 0; q < kLookWin; ++q) {
+          if (done || failed) break;
+          unsigned long long x = w[q];
+          while (!(x & (kScanAgg | kScanInc))) {
+            if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
+              failed = true;
+              break;
+            }
+            __nanosleep(32);
+            x = ld_volatile_u64(&lookback[j - q]);
+          }
+          if (failed) break;
+          excl += x & kScanMask;
+          if (x & kScanInc) done = true;
         }
-        if (w & kScanAgg) {
-          excl += w & kScanMask;
-          --j;
-          continue;
-        }
-        if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
-          failed = true;
-          break;
-        }
-        __nanosleep(64);
+        j -= kLookWin;
       }
       if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteScanLookback);
       st_volatile_u64(&lookback[part], kScanInc | ((excl + block_total) & kScanMask));
@@ -253,10 +264,33 @@ extern "C" size_t gsb_bin_prepare_workspace_size(const gsb_raster_meta* meta) {
   return c.off + 256;
 }
 
-extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const float* conics,
-                               const float* colors, const float* opacities, const float* depths,
-                               int32_t* perm, float* rec, int32_t* pair_offsets, uint32_t* status,
-                               void* workspace, size_t workspace_bytes, void* stream_) {
+extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                             const float* opacities, const float* depths, uint32_t* status, void* workspace,
+                             size_t workspace_bytes, void* stream_) {
+  Meta m;
+  int rc = make_meta(meta, &m);
+  if (rc != GSB_OK) return rc;
+  if (!status) return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG > 0 && (!means2d || !conics || !opacities || !depths)) return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG >= kSortMaxN) return GSB_ERR_CAPACITY;
+  if (workspace_bytes < gsb_bin_prepare_workspace_size(meta) || (m.BG > 0 && !workspace))
+    return GSB_ERR_WORKSPACE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (cudaMemsetAsync(status, 0, sizeof(uint32_t) * GSB_STATUS_WORDS, stream) != cudaSuccess) return GSB_ERR_CUDA;
+  if (m.BG == 0) return GSB_OK;
+  Carver c(workspace);
+  PrepareWs w;
+  carve_prepare(c, m, &w);
+  k_prepare<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics, opacities,
+                                                   depths, w.keys_in, w.vals_in, w.counts, status);
+  note_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                                 const float* colors, const float* opacities, const float* depths, int32_t* perm,
+                                 float* rec, int32_t* pair_offsets, uint32_t* status, void* workspace,
+                                 size_t workspace_bytes, void* stream_) {
   Meta m;
   int rc = make_meta(meta, &m);
   if (rc != GSB_OK) return rc;
@@ -267,32 +301,33 @@ extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d
   if (workspace_bytes < gsb_bin_prepare_workspace_size(meta) || (m.BG > 0 && !workspace))
     return GSB_ERR_WORKSPACE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t) * GSB_STATUS_WORDS, stream);
-  if (e != cudaSuccess) return GSB_ERR_CUDA;
   if (m.BG == 0) return cuda_status(cudaMemsetAsync(pair_offsets, 0, sizeof(int32_t), stream));
-
   Carver c(workspace);
   PrepareWs w;
   carve_prepare(c, m, &w);
   const int parts = (m.BG + kScanTile - 1) / kScanTile;
-  e = cudaMemsetAsync(w.lookback, 0, sizeof(unsigned long long) * (parts + 1), stream);
+  cudaError_t e = cudaMemsetAsync(w.lookback, 0, sizeof(unsigned long long) * (parts + 1), stream);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
   e = cudaMemsetAsync(w.counter, 0, sizeof(uint32_t), stream);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-
-  k_prepare<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
-                                                   opacities, depths, w.keys_in, w.vals_in, w.counts);
-
-  note_launches(1);
-  e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0,
-                       depth_sort_end_bit(m), status, stream);
+  e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
+                       status, stream);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
   k_gather_scan<<<parts, kScanThreads, 0, stream>>>(
-      m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors,
-      opacities, w.counts, reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter,
-      status);
+      m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
+      w.counts, reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
   note_launches(1);
   return cuda_status(cudaGetLastError());
+}
+
+extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                               const float* colors, const float* opacities, const float* depths, int32_t* perm,
+                               float* rec, int32_t* pair_offsets, uint32_t* status, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  int rc = gsb_bin_count(meta, means2d, conics, opacities, depths, status, workspace, workspace_bytes, stream);
+  if (rc != GSB_OK) return rc;
+  return gsb_bin_sort_scan(meta, means2d, conics, colors, opacities, depths, perm, rec, pair_offsets, status,
+                           workspace, workspace_bytes, stream);
 }
 
 namespace {

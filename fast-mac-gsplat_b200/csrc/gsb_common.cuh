@@ -138,12 +138,38 @@ __device__ __forceinline__ float sat_log_threshold(float op, float max_alpha) {
   return __double2float_rn(det_log(ratio));
 }
 
-// power = -0.5 (a dx dx + 2 b dx dy + c dy dy) in the reference's operation
-// order (…metal:587) with round-to-nearest ops only. ta = (a dx) dx and
-// tb = (2 b) dx are shared by all pixels of a column.
-__device__ __forceinline__ float power_rn(float ta, float tb, float c, float dy) {
-  const float q = __fadd_rn(__fadd_rn(ta, __fmul_rn(tb, dy)), __fmul_rn(__fmul_rn(c, dy), dy));
-  return __fmul_rn(-0.5f, q);
+// Gaussian exponent -0.5 (a dx^2 + 2 b dx dy + c dy^2) (…metal:587), evaluated as
+// fma(ch dy, dy, fma(tb, dy, ta)) with ta = ((-a/2) dx) dx, tb = (-b) dx,
+// ch = -c/2. Each step is one correctly rounded IEEE operation, matching the CPU
+// oracle bit for bit. ta and tb are shared by every pixel of a column.
+struct PowerCol {
+  float ta, tb, ch;
+};
+__device__ __forceinline__ PowerCol power_col(float a, float b, float c, float dx) {
+  PowerCol p;
+  p.ta = __fmul_rn(__fmul_rn(__fmul_rn(-0.5f, a), dx), dx);
+  p.tb = __fmul_rn(-b, dx);
+  p.ch = __fmul_rn(-0.5f, c);
+  return p;
+}
+__device__ __forceinline__ float power_at(const PowerCol& p, float dy) {
+  return __fmaf_rn(__fmul_rn(p.ch, dy), dy, __fmaf_rn(p.tb, dy, p.ta));
+}
+
+// cp.async (LDGSTS) helpers: asynchronous global -> shared copies, tracked per
+// thread in commit groups.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 // float -> int after clamping into int range (the clamp keeps NaN/huge means

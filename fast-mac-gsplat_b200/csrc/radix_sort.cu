@@ -14,6 +14,7 @@ constexpr uint32_t kFlagAgg = 0x40000000u;  // partition aggregate published
 constexpr uint32_t kFlagInc = 0x80000000u;  // inclusive prefix published
 constexpr uint32_t kValueMask = 0x3fffffffu;
 constexpr int kMaxPasses = 8;
+constexpr int kLookWin = 8;  // predecessors read per look-back step
 
 // Histograms of every digit pass in one read of the keys.
 __global__ void __launch_bounds__(kSortThreads)
@@ -120,25 +121,34 @@ __global__ void __launch_bounds__(kSortThreads)
       st_volatile_u32(my, kFlagInc | sum);
     } else {
       st_volatile_u32(my, kFlagAgg | sum);
+      // Windowed look-back: read kLookWin predecessors at once, consume them
+      // nearest-first until an inclusive prefix is found (one L2 round trip per
+      // window instead of one per predecessor).
       int64_t j = (int64_t)part - 1;
       int spins = 0;
-      bool failed = false;
-      while (j >= 0) {
-        const uint32_t w = ld_volatile_u32(lookback + (size_t)j * kRadix + t);
-        if (w & kFlagInc) {
-          exclusive += w & kValueMask;
-          break;
+      bool failed = false, done = false;
+      while (!done && !failed) {
+        uint32_t w[kLookWin];
+#pragma unroll
+        for (int q = 0; q < kLookWin; ++q)
+          w[q] = (j - q >= 0) ? ld_volatile_u32(lookback + (size_t)(j - q) * kRadix + t) : kFlagInc;
+#pragma unroll
+        for (int q = 0; q < kLookWin; ++q) {
+          if (done || failed) break;
+          uint32_t x = w[q];
+          while (!(x & (kFlagAgg | kFlagInc))) {
+            if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
+              failed = true;
+              break;
+            }
+            __nanosleep(32);
+            x = ld_volatile_u32(lookback + (size_t)(j - q) * kRadix + t);
+          }
+          if (failed) break;
+          exclusive += x & kValueMask;
+          if (x & kFlagInc) done = true;
         }
-        if (w & kFlagAgg) {
-          exclusive += w & kValueMask;
-          --j;
-          continue;
-        }
-        if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
-          failed = true;
-          break;
-        }
-        __nanosleep(64);
+        j -= kLookWin;
       }
       if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteSortLookback);
       st_volatile_u32(my, kFlagInc | ((exclusive + sum) & kValueMask));

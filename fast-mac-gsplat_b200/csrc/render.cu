@@ -8,21 +8,28 @@
 // and alpha = min(max_alpha, op*exp(power)) >= alpha_thr; C += T*alpha*c;
 // T *= 1-alpha; the pixel stops once T <= T_thr. The visibility and saturation
 // gates are decided on `power` against per-splat log thresholds stored in the
-// record (see vis_log_threshold), with `power` evaluated in the reference's
-// operation order by round-to-nearest ops, so the CPU oracle makes the same
-// decisions bit for bit.
+// record (vis_log_threshold / sat_log_threshold), with `power` evaluated by a
+// fixed sequence of correctly rounded ops (power_at), so the CPU oracle makes
+// the same decisions bit for bit.
 //
-// The forward saves per pixel the final transmittance and last_idx = 1 + index
-// (within the tile list) of the last visible splat, so the backward starts from
-// the exact per-pixel state without recompositing.
+// The forward saves per pixel the final transmittance and last_idx = the number
+// of list entries the pixel consumed (the saturation index + 1, or the tile's
+// count when it never saturates: the reference's per-pixel stop), so the
+// backward starts from the exact per-pixel state without recompositing.
 //
 // Work split. Most tiles carry short lists (c3: 6 pairs on average), where a
 // CTA per tile is dominated by barriers and per-splat overheads. Tiles with at
 // most kShortMax pairs are processed by ONE WARP each (8 pixels per lane, the
-// column's dx terms shared by the lane's 8 rows, backward gradients summed over
-// the lane's pixels before a single warp reduction). Longer lists are appended
-// to a device list and processed by a CTA per tile (one pixel per thread), so a
-// hot tile is spread over 8 warps. Both kernels are persistent grids.
+// column terms of the exponent shared by the lane's 8 rows, backward gradients
+// summed over the lane's pixels before a single warp reduction). Longer lists
+// are appended to a device list and processed by a CTA per tile (one pixel per
+// thread), so a hot tile is spread over 8 warps. All kernels are persistent.
+//
+// The training forward also copies each short tile's records, in list order,
+// into pair_rec [P,12] (a by-product of its gather). The backward warp kernel
+// then prefetches a tile's records, ids and per-pixel state with cp.async one
+// tile ahead (double-buffered shared memory), so its per-tile load latency
+// overlaps the previous tile's arithmetic.
 #include "gsb_common.cuh"
 #include "gsb_host.cuh"
 
@@ -30,9 +37,10 @@ namespace gsb {
 namespace {
 
 constexpr int kShortMax = 64;   // pairs per tile handled by one warp
-constexpr int kWarpBatch = 32;  // records staged per warp round
+constexpr int kWarpBatch = 32;  // records staged per warp round (forward)
 constexpr int kLanePx = 8;      // pixels per lane in the warp kernels: rows py0 + 2i
-constexpr int kWarps = 8;       // warps per CTA
+constexpr int kWarps = 8;       // warps per CTA (forward warp kernel, CTA kernels)
+constexpr int kBwdWarps = 4;    // warps per CTA (backward warp kernel)
 constexpr int kBatch = 256;     // records staged per CTA round (long kernels)
 constexpr int kGradComps = 9;
 
@@ -59,21 +67,26 @@ __device__ __forceinline__ int load_gi(const int32_t* __restrict__ ids, int k, i
   return gi;
 }
 
+// A record that is never visible (used for out-of-range ids).
+__device__ __forceinline__ void invisible_rec(float4* r) {
+  const float inf = __int_as_float(0x7f800000);
+  r[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  r[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  r[2] = make_float4(0.f, 0.f, inf, inf);
+}
+
 __device__ __forceinline__ void load_rec(const float4* __restrict__ rec, int gi, float4* dst) {
   if (gi >= 0) {
     dst[0] = __ldg(&rec[3 * gi + 0]);
     dst[1] = __ldg(&rec[3 * gi + 1]);
     dst[2] = __ldg(&rec[3 * gi + 2]);
-  } else {  // bad index: a record that is never visible
-    const float inf = __int_as_float(0x7f800000);
-    dst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-    dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    dst[2] = make_float4(0.f, 0.f, inf, inf);
+  } else {
+    invisible_rec(dst);
   }
 }
 
-// Warp-wide sum of v[0..15]; on return lane L holds the total of v[L >> 1] in
-// v[0] (recursive halving: 16 shuffles instead of 5 per value).
+// Warp-wide sum of v[0..15]; on return lane L holds the total of v[L >> 1]
+// (recursive halving: 16 shuffles instead of 5 per value).
 __device__ __forceinline__ float warp_reduce_scatter16(float (&v)[16], int lane) {
 #pragma unroll
   for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
@@ -95,8 +108,9 @@ template <bool kSave>
 __global__ void __launch_bounds__(kWarps * 32, 3)
     k_render_fwd_warp(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, float* __restrict__ out, float* __restrict__ final_T,
-                      int32_t* __restrict__ last_idx, int32_t* __restrict__ long_tiles,
-                      uint32_t* __restrict__ long_count, uint32_t* __restrict__ status) {
+                      int32_t* __restrict__ last_idx, float4* __restrict__ pair_rec,
+                      int32_t* __restrict__ long_tiles, uint32_t* __restrict__ long_count,
+                      uint32_t* __restrict__ status) {
   __shared__ float4 s_rec[kWarps][kWarpBatch][3];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float4(*my)[3] = s_rec[warp];
@@ -113,41 +127,56 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
     const int py0 = tc.ty * kTile + (lane >> 4);
     const float fx = (float)px + 0.5f;
     const float fy0 = (float)py0 + 0.5f;  // row i is at fy0 + 2i (exact)
+    // T[i] > T_thr marks a live pixel; pixels outside the image start dead (T = 0).
+    // last_idx (the number of list entries the pixel consumed, as the reference's
+    // per-pixel stop) is the saturation index + 1, or n for a pixel that never
+    // saturates; byte i&3 of last4[i>>2] records the saturation (n <= kShortMax < 256).
     float T[kLanePx], cr[kLanePx], cg[kLanePx], cb[kLanePx];
-    uint32_t last4[2] = {0u, 0u};  // last_idx of pixel i in byte i&3 of last4[i>>2] (n <= kShortMax < 256)
-    uint32_t alive = 0;
+    uint32_t last4[2] = {0u, 0u};
 #pragma unroll
     for (int i = 0; i < kLanePx; ++i) {
-      T[i] = 1.0f;
+      T[i] = (px < m.W && py0 + 2 * i < m.H) ? 1.0f : 0.0f;
       cr[i] = cg[i] = cb[i] = 0.0f;
-      if (px < m.W && py0 + 2 * i < m.H && 1.0f > m.T_thr) alive |= 1u << i;
     }
     for (int base = 0; base < n; base += kWarpBatch) {
-      if (!__any_sync(kFullMask, alive)) break;
+      bool live = false;
+#pragma unroll
+      for (int i = 0; i < kLanePx; ++i) live |= T[i] > m.T_thr;
+      if (!__any_sync(kFullMask, live)) break;
       const int cnt = min(kWarpBatch, n - base);
       __syncwarp();
-      if (lane < cnt) load_rec(rec, load_gi(ids, start + base + lane, m.BG, status, kSiteRender), my[lane]);
+      if (lane < cnt) {
+        float4 r[3];
+        load_rec(rec, load_gi(ids, start + base + lane, m.BG, status, kSiteRender), r);
+        my[lane][0] = r[0];
+        my[lane][1] = r[1];
+        my[lane][2] = r[2];
+        if (kSave) {
+          float4* dst = pair_rec + 3 * (size_t)(start + base + lane);
+          dst[0] = r[0];
+          dst[1] = r[1];
+          dst[2] = r[2];
+        }
+      }
       __syncwarp();
-      if (alive) {
+      if (live) {
         for (int j = 0; j < cnt; ++j) {
           const float4 p0 = my[j][0];
           const float4 p1 = my[j][1];
           const float4 p2 = my[j][2];
-          const float dx = __fsub_rn(fx, p0.x);
-          const float ta = __fmul_rn(__fmul_rn(p0.z, dx), dx);
-          const float tb = __fmul_rn(__fmul_rn(2.0f, p0.w), dx);
+          const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
 #pragma unroll
           for (int i = 0; i < kLanePx; ++i) {
-            const float power = power_rn(ta, tb, p1.x, __fsub_rn(fy0 + (float)(2 * i), p0.y));
-            if (((alive >> i) & 1u) && power <= 0.0f && power >= p2.z) {
+            const float power = power_at(pc, __fsub_rn(fy0 + (float)(2 * i), p0.y));
+            if (T[i] > m.T_thr && power <= 0.0f && power >= p2.z) {
               const float alpha = fminf(m.max_alpha, p1.y * __expf(power));
               const float w = T[i] * alpha;
               cr[i] = fmaf(w, p1.z, cr[i]);
               cg[i] = fmaf(w, p1.w, cg[i]);
               cb[i] = fmaf(w, p2.x, cb[i]);
               T[i] *= 1.0f - alpha;
-              last4[i >> 2] = (last4[i >> 2] & ~(0xffu << (8 * (i & 3)))) | ((uint32_t)(base + j + 1) << (8 * (i & 3)));
-              if (T[i] <= m.T_thr) alive &= ~(1u << i);
+              if (T[i] <= m.T_thr)  // saturated: the pixel consumed entries [0, base + j]
+                last4[i >> 2] |= (uint32_t)(base + j + 1) << (8 * (i & 3));
             }
           }
         }
@@ -163,8 +192,9 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
           out[3 * pix + 1] = fmaf(T[i], m.bg_g, cg[i]);
           out[3 * pix + 2] = fmaf(T[i], m.bg_b, cb[i]);
           if (kSave) {
+            const int sat = (int)((last4[i >> 2] >> (8 * (i & 3))) & 0xffu);
             final_T[pix] = T[i];
-            last_idx[pix] = (int32_t)((last4[i >> 2] >> (8 * (i & 3))) & 0xffu);
+            last_idx[pix] = sat ? sat : (1.0f > m.T_thr ? n : 0);
           }
         }
       }
@@ -191,8 +221,9 @@ __global__ void __launch_bounds__(kTilePixels)
     const int n = toff[tile + 1] - start;
     const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
     float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-    int last = 0;
+    int last = n;  // entries consumed: n unless the pixel saturates
     bool alive = valid && (T > m.T_thr);
+    if (!alive) last = 0;
     for (int base = 0; base < n; base += kBatch) {
       if (__syncthreads_count(alive) == 0) break;
       const int cnt = min(kBatch, n - base);
@@ -203,9 +234,7 @@ __global__ void __launch_bounds__(kTilePixels)
         for (int j = 0; j < cnt; ++j) {
           const float4 p0 = s_rec[j][0];
           const float4 p1 = s_rec[j][1];
-          const float dx = __fsub_rn(fx, p0.x);
-          const float power = power_rn(__fmul_rn(__fmul_rn(p0.z, dx), dx), __fmul_rn(__fmul_rn(2.0f, p0.w), dx),
-                                       p1.x, __fsub_rn(fy, p0.y));
+          const float power = power_at(power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x)), __fsub_rn(fy, p0.y));
           const float4 p2 = s_rec[j][2];
           if (!(power <= 0.0f && power >= p2.z)) continue;
           const float alpha = fminf(m.max_alpha, p1.y * __expf(power));
@@ -214,8 +243,8 @@ __global__ void __launch_bounds__(kTilePixels)
           cg = fmaf(w, p1.w, cg);
           cb = fmaf(w, p2.x, cb);
           T *= 1.0f - alpha;
-          last = base + j + 1;
           if (T <= m.T_thr) {
+            last = base + j + 1;
             alive = false;
             break;
           }
@@ -240,11 +269,16 @@ __global__ void __launch_bounds__(kTilePixels)
 // Backward
 // ---------------------------------------------------------------------------
 
-// Per-pixel VJP of one visible splat (…metal:1017-1034). Adds the pixel's 9
-// partials to v and advances the reverse recurrence (T_cur, gT).
-__device__ __forceinline__ void pixel_vjp(const Meta& m, float dx, float dy, float power, const float4& p0,
-                                          const float4& p1, const float4& p2, float gr, float gg, float gb,
-                                          float& T_cur, float& gT, float* v) {
+// Per-pixel VJP of one visible splat (…metal:1017-1034), advancing the reverse
+// recurrence (T_cur, gT). The splat's geometric gradients of all pixels that
+// share dx (one lane's column) are accumulated as moments of g_power:
+// S[0] = sum gp, S[1] = sum gp dy, S[2] = sum gp dy^2, expanded once per
+// splat by vjp_expand (g_mean = gp (a dx + b dy, b dx + c dy), g_conic =
+// gp (-dx^2/2, -dx dy, -dy^2/2)). S[3] = d opacity, S[4..6] = d color.
+// For a visible splat op >= alpha_thr > eps, so raw / max(op, eps) = exp(power).
+__device__ __forceinline__ void pixel_vjp(const Meta& m, float dy, float power, const float4& p1,
+                                          const float4& p2, float gr, float gg, float gb, float& T_cur, float& gT,
+                                          float* S) {
   const float e = __expf(power);
   const float raw = p1.y * e;
   const float alpha = fminf(m.max_alpha, raw);
@@ -253,108 +287,183 @@ __device__ __forceinline__ void pixel_vjp(const Meta& m, float dx, float dy, flo
   const float g_alpha = T_prev * (dot_gc - gT);
   const float wc = T_prev * alpha;
   const float g_raw = (power < p2.w) ? g_alpha : 0.0f;  // raw < max_alpha
-  const float g_power = g_raw * raw;
-  const float a = p0.z, b = p0.w, c = p1.x;
-  v[0] += g_power * (a * dx + b * dy);
-  v[1] += g_power * (b * dx + c * dy);
-  v[2] += g_power * (-0.5f) * dx * dx;
-  v[3] += g_power * (-1.0f) * dx * dy;
-  v[4] += g_power * (-0.5f) * dy * dy;
-  v[5] += g_raw * __fdividef(raw, fmaxf(p1.y, m.eps));
-  v[6] += gr * wc;
-  v[7] += gg * wc;
-  v[8] += gb * wc;
+  const float gp = g_raw * raw;
+  S[0] += gp;
+  const float gpdy = gp * dy;
+  S[1] += gpdy;
+  S[2] = fmaf(gpdy, dy, S[2]);
+  S[3] = fmaf(g_raw, e, S[3]);
+  S[4] = fmaf(gr, wc, S[4]);
+  S[5] = fmaf(gg, wc, S[5]);
+  S[6] = fmaf(gb, wc, S[6]);
   gT = alpha * dot_gc + (1.0f - alpha) * gT;
   T_cur = T_prev;
 }
 
-__global__ void __launch_bounds__(kWarps * 32, 2)
-    k_render_bwd_warp(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
+// Expands one lane's moments S into the 9 gradient components (grad record order).
+__device__ __forceinline__ void vjp_expand(const float* S, float dx, float a, float b, float c, float (&v)[16]) {
+  v[0] = a * dx * S[0] + b * S[1];
+  v[1] = b * dx * S[0] + c * S[1];
+  v[2] = -0.5f * dx * dx * S[0];
+  v[3] = -dx * S[1];
+  v[4] = -0.5f * S[2];
+  v[5] = S[3];
+  v[6] = S[4];
+  v[7] = S[5];
+  v[8] = S[6];
+#pragma unroll
+  for (int q = 9; q < 16; ++q) v[q] = 0.0f;
+}
+
+// One warp's prefetch buffer: a short tile's per-pixel state, ids and records.
+struct BwdBuf {
+  float4 rec[kShortMax][3];
+  float grad[kTilePixels * 3];  // row-major 16x16 pixels x rgb
+  float T[kTilePixels];
+  int last[kTilePixels];
+  int ids[kShortMax];
+};
+
+struct TileOff {
+  int start, n;
+};
+
+__device__ __forceinline__ TileOff load_off(const int32_t* __restrict__ toff, int tile, int total_tiles) {
+  TileOff o{0, 0};
+  if (tile < total_tiles) {
+    o.start = __ldg(&toff[tile]);
+    o.n = __ldg(&toff[tile + 1]) - o.start;
+  }
+  return o;
+}
+
+// Issues (does not wait for) the cp.async copies of one short tile into buf.
+__device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileOff off, BwdBuf* buf, int lane,
+                                                  const float* __restrict__ grad, const float* __restrict__ final_T,
+                                                  const int32_t* __restrict__ last_idx,
+                                                  const float4* __restrict__ pair_rec,
+                                                  const int32_t* __restrict__ ids) {
+  if (tile >= m.total_tiles || off.n == 0 || off.n > kShortMax) return;
+  const TileCoord tc = tile_coord(m, tile);
+  const int x0 = tc.tx * kTile, y0 = tc.ty * kTile;
+  const bool full = (x0 + kTile <= m.W) && (y0 + kTile <= m.H) && ((m.W & 3) == 0);
+  if (full) {
+    // 16-byte chunks: per row 12 of grad, 4 of T, 4 of last_idx.
+    for (int q = lane; q < kTile * 20; q += 32) {
+      const int r = q / 20, k = q - r * 20;
+      const size_t row_pix = ((size_t)tc.b * m.H + y0 + r) * m.W + x0;
+      if (k < 12) {
+        cp_async16(&buf->grad[r * 48 + 4 * k], grad + 3 * row_pix + 4 * k);
+      } else if (k < 16) {
+        cp_async16(&buf->T[r * 16 + 4 * (k - 12)], final_T + row_pix + 4 * (k - 12));
+      } else {
+        cp_async16(&buf->last[r * 16 + 4 * (k - 16)], last_idx + row_pix + 4 * (k - 16));
+      }
+    }
+  } else {
+    for (int p = lane; p < kTilePixels; p += 32) {
+      const int r = p >> 4, c = p & 15;
+      if (x0 + c < m.W && y0 + r < m.H) {
+        const size_t pix = ((size_t)tc.b * m.H + y0 + r) * m.W + x0 + c;
+        cp_async4(&buf->grad[3 * p + 0], grad + 3 * pix + 0);
+        cp_async4(&buf->grad[3 * p + 1], grad + 3 * pix + 1);
+        cp_async4(&buf->grad[3 * p + 2], grad + 3 * pix + 2);
+        cp_async4(&buf->T[p], final_T + pix);
+        cp_async4(&buf->last[p], last_idx + pix);
+      } else {
+        buf->grad[3 * p + 0] = buf->grad[3 * p + 1] = buf->grad[3 * p + 2] = 0.0f;
+        buf->T[p] = 1.0f;
+        buf->last[p] = 0;
+      }
+    }
+  }
+  for (int q = lane; q < 3 * off.n; q += 32) cp_async16(&buf->rec[0][0] + q, pair_rec + 3 * (size_t)off.start + q);
+  for (int q = lane; q < off.n; q += 32) cp_async4(&buf->ids[q], ids + off.start + q);
+}
+
+__global__ void __launch_bounds__(kBwdWarps * 32, 3)
+    k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                       const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
                       float* __restrict__ grad_rec, int32_t* __restrict__ long_tiles,
                       uint32_t* __restrict__ long_count, uint32_t* __restrict__ status) {
-  __shared__ float4 s_rec[kWarps][kWarpBatch][3];
+  extern __shared__ float4 s_dyn[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float4(*my)[3] = s_rec[warp];
-  const int stride = gridDim.x * kWarps;
-  for (int tile = blockIdx.x * kWarps + warp; tile < m.total_tiles; tile += stride) {
-    const int start = __ldg(&toff[tile]);
-    const int n = __ldg(&toff[tile + 1]) - start;
+  BwdBuf* bufs = reinterpret_cast<BwdBuf*>(s_dyn) + 2 * warp;
+  const int stride = gridDim.x * kBwdWarps;
+  int tile = blockIdx.x * kBwdWarps + warp;
+  TileOff cur = load_off(toff, tile, m.total_tiles);
+  TileOff nxt = load_off(toff, tile + stride, m.total_tiles);
+  prefetch_bwd_tile(m, tile, cur, &bufs[0], lane, grad, final_T, last_idx, pair_rec, ids);
+  cp_async_commit();
+  for (int k = 0; tile < m.total_tiles; ++k, tile += stride) {
+    const TileOff nn = load_off(toff, tile + 2 * stride, m.total_tiles);
+    prefetch_bwd_tile(m, tile + stride, nxt, &bufs[(k + 1) & 1], lane, grad, final_T, last_idx, pair_rec, ids);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const BwdBuf& B = bufs[k & 1];
+    const int n = cur.n;
     if (n > kShortMax) {
       if (lane == 0) long_tiles[atomicAdd(long_count, 1u)] = tile;
-      continue;
-    }
-    if (n == 0) continue;
-    const TileCoord tc = tile_coord(m, tile);
-    const int px = tc.tx * kTile + (lane & 15);
-    const int py0 = tc.ty * kTile + (lane >> 4);
-    const float fx = (float)px + 0.5f;
-    const float fy0 = (float)py0 + 0.5f;
-    float gr[kLanePx], gg[kLanePx], gb[kLanePx], Tc[kLanePx], gT[kLanePx];
-    int last[kLanePx];
-    int lmax = 0;
+    } else if (n > 0) {
+      const TileCoord tc = tile_coord(m, tile);
+      const int px = tc.tx * kTile + (lane & 15);
+      const int py0 = tc.ty * kTile + (lane >> 4);
+      const float fx = (float)px + 0.5f;
+      const float fy0 = (float)py0 + 0.5f;
+      float gr[kLanePx], gg[kLanePx], gb[kLanePx], Tc[kLanePx], gT[kLanePx];
+      int last[kLanePx];
+      int lmax = 0;
 #pragma unroll
-    for (int i = 0; i < kLanePx; ++i) {
-      const int py = py0 + 2 * i;
-      gr[i] = gg[i] = gb[i] = 0.0f;
-      Tc[i] = 1.0f;
-      last[i] = 0;
-      if (px < m.W && py < m.H) {
-        const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
-        gr[i] = grad[3 * pix + 0];
-        gg[i] = grad[3 * pix + 1];
-        gb[i] = grad[3 * pix + 2];
-        Tc[i] = final_T[pix];
-        last[i] = min(last_idx[pix], n);
+      for (int i = 0; i < kLanePx; ++i) {
+        const int p = ((lane >> 4) + 2 * i) * kTile + (lane & 15);
+        gr[i] = B.grad[3 * p + 0];
+        gg[i] = B.grad[3 * p + 1];
+        gb[i] = B.grad[3 * p + 2];
+        Tc[i] = B.T[p];
+        last[i] = min(B.last[p], n);
+        gT[i] = gr[i] * m.bg_r + gg[i] * m.bg_g + gb[i] * m.bg_b;
+        lmax = max(lmax, last[i]);
       }
-      gT[i] = gr[i] * m.bg_r + gg[i] * m.bg_g + gb[i] * m.bg_b;
-      lmax = max(lmax, last[i]);
-    }
-    const int tile_last = __reduce_max_sync(kFullMask, lmax);
-    for (int bend = tile_last; bend > 0; bend -= kWarpBatch) {
-      const int bstart = max(0, bend - kWarpBatch);
-      const int cnt = bend - bstart;
-      __syncwarp();
-      int my_gi = -1;
-      if (lane < cnt) {
-        my_gi = load_gi(ids, start + bstart + lane, m.BG, status, kSiteRenderBwd);
-        load_rec(rec, my_gi, my[lane]);
-      }
-      __syncwarp();
-      for (int jj = cnt - 1; jj >= 0; --jj) {
-        const int j = bstart + jj;
-        const float4 p0 = my[jj][0];
-        const float4 p1 = my[jj][1];
-        const float4 p2 = my[jj][2];
+      const int tile_last = __reduce_max_sync(kFullMask, lmax);
+      for (int j = tile_last - 1; j >= 0; --j) {
+        const float4 p0 = B.rec[j][0];
+        const float4 p1 = B.rec[j][1];
+        const float4 p2 = B.rec[j][2];
         const float dx = __fsub_rn(fx, p0.x);
-        const float ta = __fmul_rn(__fmul_rn(p0.z, dx), dx);
-        const float tb = __fmul_rn(__fmul_rn(2.0f, p0.w), dx);
-        float v[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = 0.0f;
+        const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
+        float S[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         bool any = false;
 #pragma unroll
         for (int i = 0; i < kLanePx; ++i) {
-          if (j < last[i]) {
-            const float dy = __fsub_rn(fy0 + (float)(2 * i), p0.y);
-            const float power = power_rn(ta, tb, p1.x, dy);
-            if (power <= 0.0f && power >= p2.z) {
-              pixel_vjp(m, dx, dy, power, p0, p1, p2, gr[i], gg[i], gb[i], Tc[i], gT[i], v);
-              any = true;
-            }
+          const float dy = __fsub_rn(fy0 + (float)(2 * i), p0.y);
+          const float power = power_at(pc, dy);
+          if (j < last[i] && power <= 0.0f && power >= p2.z) {
+            pixel_vjp(m, dy, power, p1, p2, gr[i], gg[i], gb[i], Tc[i], gT[i], S);
+            any = true;
           }
         }
         if (__any_sync(kFullMask, any)) {
+          float v[16];
+          vjp_expand(S, dx, p0.z, p0.w, p1.x, v);
           const float total = warp_reduce_scatter16(v, lane);
-          const int gi = __shfl_sync(kFullMask, my_gi, jj);
+          int gi = B.ids[j];
+          if ((unsigned)gi >= (unsigned)m.BG) {
+            raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
+            gi = -1;
+          }
           const int comp = lane >> 1;
           if (!(lane & 1) && comp < kGradComps && gi >= 0)
             atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + comp, total);
         }
       }
     }
+    __syncwarp();  // bufs[k & 1] is refilled by the next iteration's prefetch
+    cur = nxt;
+    nxt = nn;
   }
+  cp_async_wait<0>();
 }
 
 __global__ void __launch_bounds__(kTilePixels)
@@ -409,21 +518,24 @@ __global__ void __launch_bounds__(kTilePixels)
       for (int jj = cnt - 1; jj >= 0; --jj) {
         const int j = bstart + jj;
         float v[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) v[q] = 0.0f;
         bool any = false;
         if (j < last) {
           const float4 p0 = s_rec[jj][0];
           const float4 p1 = s_rec[jj][1];
           const float dx = __fsub_rn(fx, p0.x);
           const float dy = __fsub_rn(fy, p0.y);
-          const float power = power_rn(__fmul_rn(__fmul_rn(p0.z, dx), dx), __fmul_rn(__fmul_rn(2.0f, p0.w), dx),
-                                       p1.x, dy);
+          const float power = power_at(power_col(p0.z, p0.w, p1.x, dx), dy);
           const float4 p2 = s_rec[jj][2];
           if (power <= 0.0f && power >= p2.z) {
-            pixel_vjp(m, dx, dy, power, p0, p1, p2, gr, gg, gb, T_cur, gT, v);
+            float S[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            pixel_vjp(m, dy, power, p1, p2, gr, gg, gb, T_cur, gT, S);
+            vjp_expand(S, dx, p0.z, p0.w, p1.x, v);
             any = true;
           }
+        }
+        if (!any) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] = 0.0f;
         }
         if (__any_sync(kFullMask, any)) {
           const float total = warp_reduce_scatter16(v, lane);
@@ -483,6 +595,8 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+constexpr size_t kBwdWarpSmem = sizeof(BwdBuf) * 2 * kBwdWarps;
+
 // Persistent grid sizes (CTAs resident per SM x SMs), cached per device.
 struct GridCache {
   int sms = 0;
@@ -497,17 +611,19 @@ const GridCache& grids() {
   if (g.sms == 0) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    auto occ = [&](const void* fn, int threads) {
+    cudaFuncSetAttribute((const void*)k_render_bwd_warp, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kBwdWarpSmem);
+    auto occ = [&](const void* fn, int threads, size_t smem) {
       int b = 1;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, threads, 0) != cudaSuccess || b < 1) b = 1;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, threads, smem) != cudaSuccess || b < 1) b = 1;
       return b * sms;
     };
-    g.fwd_warp[0] = occ((const void*)k_render_fwd_warp<false>, kWarps * 32);
-    g.fwd_warp[1] = occ((const void*)k_render_fwd_warp<true>, kWarps * 32);
-    g.fwd_cta[0] = occ((const void*)k_render_fwd_cta<false>, kTilePixels);
-    g.fwd_cta[1] = occ((const void*)k_render_fwd_cta<true>, kTilePixels);
-    g.bwd_warp = occ((const void*)k_render_bwd_warp, kWarps * 32);
-    g.bwd_cta = occ((const void*)k_render_bwd_cta, kTilePixels);
+    g.fwd_warp[0] = occ((const void*)k_render_fwd_warp<false>, kWarps * 32, 0);
+    g.fwd_warp[1] = occ((const void*)k_render_fwd_warp<true>, kWarps * 32, 0);
+    g.fwd_cta[0] = occ((const void*)k_render_fwd_cta<false>, kTilePixels, 0);
+    g.fwd_cta[1] = occ((const void*)k_render_fwd_cta<true>, kTilePixels, 0);
+    g.bwd_warp = occ((const void*)k_render_bwd_warp, kBwdWarps * 32, kBwdWarpSmem);
+    g.bwd_cta = occ((const void*)k_render_bwd_cta, kTilePixels, 0);
     g.sms = sms;
   }
   return g;
@@ -539,12 +655,14 @@ extern "C" size_t gsb_render_workspace_size(const gsb_raster_meta* meta) {
 
 extern "C" int gsb_render_forward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                                   const int32_t* binned_ids, float* out_rgb, float* final_T, int32_t* last_idx,
-                                  uint32_t* status, void* workspace, size_t workspace_bytes, void* stream_) {
+                                  float* pair_rec, uint32_t* status, void* workspace, size_t workspace_bytes,
+                                  void* stream_) {
   Meta m;
   int rc = make_meta(meta, &m);
   if (rc != GSB_OK) return rc;
   if (!tile_offsets || !out_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
-  if ((final_T == nullptr) != (last_idx == nullptr)) return GSB_ERR_INVALID_ARGUMENT;
+  if ((final_T == nullptr) != (last_idx == nullptr) || (final_T == nullptr) != (pair_rec == nullptr))
+    return GSB_ERR_INVALID_ARGUMENT;
   if (m.BG > 0 && !rec) return GSB_ERR_INVALID_ARGUMENT;
   if (!workspace || workspace_bytes < gsb_render_workspace_size(meta)) return GSB_ERR_WORKSPACE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
@@ -554,18 +672,19 @@ extern "C" int gsb_render_forward(const gsb_raster_meta* meta, const float* rec,
   if (cudaMemsetAsync(w.long_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GSB_ERR_CUDA;
   const GridCache& g = grids();
   const float4* r4 = reinterpret_cast<const float4*>(rec);
+  float4* pr4 = reinterpret_cast<float4*>(pair_rec);
   const int warp_grid = max(1, min(g.fwd_warp[final_T ? 1 : 0], (m.total_tiles + kWarps - 1) / kWarps));
   const int cta_grid = max(1, min(g.fwd_cta[final_T ? 1 : 0], m.total_tiles));
   if (final_T) {
     k_render_fwd_warp<true><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
-                                                                   final_T, last_idx, w.long_tiles, w.long_count,
-                                                                   status);
+                                                                   final_T, last_idx, pr4, w.long_tiles,
+                                                                   w.long_count, status);
     k_render_fwd_cta<true><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, final_T,
                                                                  last_idx, w.long_tiles, w.long_count, status);
   } else {
     k_render_fwd_warp<false><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
-                                                                    nullptr, nullptr, w.long_tiles, w.long_count,
-                                                                    status);
+                                                                    nullptr, nullptr, nullptr, w.long_tiles,
+                                                                    w.long_count, status);
     k_render_fwd_cta<false><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, nullptr,
                                                                   nullptr, w.long_tiles, w.long_count, status);
   }
@@ -575,13 +694,13 @@ extern "C" int gsb_render_forward(const gsb_raster_meta* meta, const float* rec,
 
 extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                                    const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
-                                   const float* grad_rgb, float* grad_rec, uint32_t* status, void* workspace,
-                                   size_t workspace_bytes, void* stream_) {
+                                   const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
+                                   void* workspace, size_t workspace_bytes, void* stream_) {
   Meta m;
   int rc = make_meta(meta, &m);
   if (rc != GSB_OK) return rc;
   if (!tile_offsets || !final_T || !last_idx || !grad_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
-  if (m.BG > 0 && (!rec || !grad_rec)) return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG > 0 && (!rec || !grad_rec || !pair_rec)) return GSB_ERR_INVALID_ARGUMENT;
   if (!workspace || workspace_bytes < gsb_render_workspace_size(meta)) return GSB_ERR_WORKSPACE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (m.BG > 0) {
@@ -594,10 +713,11 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   if (cudaMemsetAsync(w.long_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GSB_ERR_CUDA;
   const GridCache& g = grids();
   const float4* r4 = reinterpret_cast<const float4*>(rec);
-  const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kWarps - 1) / kWarps));
+  const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
   const int cta_grid = max(1, min(g.bwd_cta, m.total_tiles));
-  k_render_bwd_warp<<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, final_T, last_idx,
-                                                           grad_rgb, grad_rec, w.long_tiles, w.long_count, status);
+  k_render_bwd_warp<<<warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream>>>(
+      m, reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx, grad_rgb, grad_rec,
+      w.long_tiles, w.long_count, status);
   k_render_bwd_cta<<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, final_T, last_idx,
                                                          grad_rgb, grad_rec, w.long_tiles, w.long_count, status);
   note_launches(2);

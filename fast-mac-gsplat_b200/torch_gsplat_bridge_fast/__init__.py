@@ -3,6 +3,7 @@ torch API of nbardy/fast-mac-gsplat (torch_gsplat_bridge_fast/__init__.py:1-2 an
 variants/v8_project3d/torch_gsplat_bridge_v8_project3d/__init__.py:1-21)."""
 from .rasterize import (
     ProjectedGaussianRasterizer,
+    check_device_errors,
     RasterConfig,
     RuntimeShaderConfig,
     get_runtime_shader_config,

@@ -20,6 +20,7 @@ GSB_STATUS_TOTAL_PAIRS = 0
 GSB_STATUS_ERROR = 1
 GSB_STATUS_MAX_TILE_COUNT = 2
 GSB_STATUS_ERROR_SITE = 3
+GSB_STATUS_PAIR_TOTAL64 = 4
 GSB_STATUS_WORDS = 8
 GSB_REC_FLOATS = 12
 
@@ -34,6 +35,8 @@ EXPORTED = (
     "gsb_kernel_launches",
     "gsb_bin_prepare_workspace_size",
     "gsb_bin_prepare",
+    "gsb_bin_count",
+    "gsb_bin_sort_scan",
     "gsb_bin_emit_workspace_size",
     "gsb_bin_emit",
     "gsb_tile_stats",
@@ -90,12 +93,14 @@ def load() -> C.CDLL:
         "gsb_kernel_launches": (C.c_uint64, []),
         "gsb_bin_prepare_workspace_size": (sz, [M]),
         "gsb_bin_prepare": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
+        "gsb_bin_count": (C.c_int, [M, p, p, p, p, p, p, sz, p]),
+        "gsb_bin_sort_scan": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_bin_emit_workspace_size": (sz, [M, i64]),
         "gsb_bin_emit": (C.c_int, [M, p, p, i64, p, p, p, p, p, sz, p]),
         "gsb_tile_stats": (C.c_int, [M, p, p, p]),
         "gsb_render_workspace_size": (sz, [M]),
-        "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, sz, p]),
-        "gsb_render_backward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),
+        "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),
+        "gsb_render_backward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_unsort_grads": (C.c_int, [M, p, p, p, p, p, p, p]),
         "gsb_project_forward": (C.c_int, [i32, i32, p, p, p, p, p, p, f32, p, p, p, p, p]),
         "gsb_project_backward": (C.c_int, [i32, i32] + [p] * 10 + [f32] + [p] * 7),

@@ -230,22 +230,52 @@ def _debug_checks() -> bool:
     return os.environ.get("GSPLAT_B200_CHECK", "0") not in ("", "0")
 
 
-def _pinned_status() -> Tensor:
-    buf = getattr(_tls, "status_host", None)
-    if buf is None:
-        buf = torch.empty(N.GSB_STATUS_WORDS, dtype=torch.int32, pin_memory=True)
-        _tls.status_host = buf
+def _pinned(name: str, n: int, dtype) -> Tensor:
+    buf = getattr(_tls, name, None)
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(n, dtype=dtype, pin_memory=True)
+        setattr(_tls, name, buf)
     return buf
 
 
 def _read_status(status: Tensor) -> list:
-    host = _pinned_status()
+    """Synchronous read of a status block (used by the optional debug checks
+    and the overflow check); raises on a device error flag."""
+    host = _pinned("status_host", N.GSB_STATUS_WORDS, torch.int32)
     host.copy_(status, non_blocking=True)
     torch.cuda.current_stream(status.device).synchronize()
     vals = [int(v) & 0xFFFFFFFF for v in host.tolist()]
     if vals[N.GSB_STATUS_ERROR]:
         raise RuntimeError(N.decode_device_error(vals[N.GSB_STATUS_ERROR], vals[N.GSB_STATUS_ERROR_SITE]))
     return vals
+
+
+def _defer_error_check(status: Tensor) -> None:
+    """Copies a call's device error words to pinned memory without waiting; the
+    next forward's host sync (or check_device_errors()) reads and raises them."""
+    host = torch.empty(4, dtype=torch.int32, pin_memory=True)
+    host.copy_(status[:4], non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(status.device))
+    pending = getattr(_tls, "pending_errors", None)
+    if pending is None:
+        pending = _tls.pending_errors = []
+    pending.append((ev, host))
+    if len(pending) > 64:
+        check_device_errors()
+
+
+def check_device_errors() -> None:
+    """Raises RuntimeError if any earlier call's kernels reported a device-side
+    error (bounded-wait timeout, pair overflow, index out of bounds)."""
+    pending = getattr(_tls, "pending_errors", None) or []
+    _tls.pending_errors = []
+    for ev, host in pending:
+        ev.synchronize()
+        flags = int(host[N.GSB_STATUS_ERROR]) & 0xFFFFFFFF
+        site = int(host[N.GSB_STATUS_ERROR_SITE]) & 0xFFFFFFFF
+        if flags:
+            raise RuntimeError(N.decode_device_error(flags, site))
 
 
 def _aligned(t: Tensor, align: int = 16) -> Tensor:
@@ -285,14 +315,28 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     # Locals keep every (possibly copied) input alive until the launch returns.
     m2 = _aligned(means2d_b, 8)
     q2, c2, o2, d2 = (t.contiguous() for t in (conics_b, colors_b, opacities_b, depths_b))
-    N.check(
-        _timed("bin_prepare", lambda: L.gsb_bin_prepare(
-            meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm), N.ptr(st.rec),
-            N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes, stream)),
-        "gsb_bin_prepare",
-    )
-    vals = _read_status(st.status)
-    P = vals[N.GSB_STATUS_TOTAL_PAIRS]
+    timer = _kernel_timer
+    if timer is not None:
+        timer.begin("bin_prepare")
+    N.check(L.gsb_bin_count(meta, N.ptr(m2), N.ptr(q2), N.ptr(o2), N.ptr(d2), N.ptr(st.status), N.ptr(ws),
+                            ws_bytes, stream), "gsb_bin_count")
+    # The pair total is read as soon as the count kernel is done, while the depth
+    # sort and scan run: the host wait overlaps GPU work.
+    total_host = _pinned("total_host", 1, torch.int64)
+    total_host.copy_(st.status[N.GSB_STATUS_PAIR_TOTAL64:N.GSB_STATUS_PAIR_TOTAL64 + 2].view(torch.int64),
+                     non_blocking=True)
+    counted = torch.cuda.Event()
+    counted.record(torch.cuda.current_stream(dev))
+    N.check(L.gsb_bin_sort_scan(meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm),
+                                N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes,
+                                stream), "gsb_bin_sort_scan")
+    if timer is not None:
+        timer.end("bin_prepare")
+    counted.synchronize()
+    check_device_errors()
+    P = int(total_host[0])
+    if P >= 2**31 - 1:
+        raise RuntimeError(f"gsplat_b200: {P} tile-splat pairs exceed the supported 2^31 - 1")
     st.P = P
     T = B * ((config.height + 15) // 16) * ((config.width + 15) // 16)
     st.keys = torch.empty(max(P, 1), dtype=torch.int64, device=dev)[:P]
@@ -331,21 +375,24 @@ def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: boo
     L = N.load()
     dev = st.status.device
     out = torch.empty((B, config.height, config.width, 3), dtype=torch.float32, device=dev)
-    final_T = last_idx = None
+    final_T = last_idx = pair_rec = None
     if save_state:
         final_T = torch.empty((B, config.height, config.width), dtype=torch.float32, device=dev)
         last_idx = torch.empty((B, config.height, config.width), dtype=torch.int32, device=dev)
+        pair_rec = torch.empty((max(st.P, 1), N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
     ws_bytes = L.gsb_render_workspace_size(st.meta)
     ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
     N.check(
         _timed("render_fwd", lambda: L.gsb_render_forward(
             st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out), N.ptr(final_T),
-            N.ptr(last_idx), N.ptr(st.status), N.ptr(ws), ws_bytes, N.stream_ptr(dev))),
+            N.ptr(last_idx), N.ptr(pair_rec), N.ptr(st.status), N.ptr(ws), ws_bytes, N.stream_ptr(dev))),
         "gsb_render_forward",
     )
     if _debug_checks():
         _read_status(st.status)
-    return out, final_T, last_idx
+    else:
+        _defer_error_check(st.status)
+    return out, final_T, last_idx, pair_rec
 
 
 class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
@@ -358,8 +405,9 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         B, G = means2d_b.shape[:2]
         st = _bin(config, means2d_b, conics_b, colors_b, opacities_b, depths_b)
         _check_overflow(st, config)
-        out, final_T, last_idx = _render_forward(st, config, B, save_state=True)
-        ctx.save_for_backward(st.perm, st.rec, st.tile_offsets, st.binned_ids, final_T, last_idx, st.status)
+        out, final_T, last_idx, pair_rec = _render_forward(st, config, B, save_state=True)
+        ctx.save_for_backward(st.perm, st.rec, st.tile_offsets, st.binned_ids, final_T, last_idx, pair_rec,
+                              st.status)
         ctx.meta = st.meta
         ctx.shape = (B, G)
         ctx.depths_shape = depths_b.shape
@@ -367,7 +415,7 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out: Tensor):
-        perm, rec, tile_offsets, binned_ids, final_T, last_idx, status = ctx.saved_tensors
+        perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status = ctx.saved_tensors
         L = N.load()
         B, G = ctx.shape
         dev = rec.device
@@ -379,7 +427,7 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         N.check(
             _timed("render_bwd", lambda: L.gsb_render_backward(
                 ctx.meta, N.ptr(rec), N.ptr(tile_offsets), N.ptr(binned_ids), N.ptr(final_T), N.ptr(last_idx),
-                N.ptr(g), N.ptr(grad_rec), N.ptr(status), N.ptr(ws), ws_bytes, stream)),
+                N.ptr(pair_rec), N.ptr(g), N.ptr(grad_rec), N.ptr(status), N.ptr(ws), ws_bytes, stream)),
             "gsb_render_backward",
         )
         need = ctx.needs_input_grad
@@ -395,6 +443,8 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         )
         if _debug_checks():
             _read_status(status)
+        else:
+            _defer_error_check(status)
         g_depths = torch.zeros(ctx.depths_shape, dtype=torch.float32, device=dev) if need[4] else None
         return g_means, g_conics, g_colors, g_opac, g_depths, None
 
@@ -404,7 +454,7 @@ def _rasterize_chunk_eval(means2d_b, conics_b, colors_b, opacities_b, depths_b, 
     B = means2d_b.shape[0]
     st = _bin(config, means2d_b, conics_b, colors_b, opacities_b, depths_b)
     _check_overflow(st, config)
-    out, _, _ = _render_forward(st, config, B, save_state=False)
+    out, _, _, _ = _render_forward(st, config, B, save_state=False)
     return out
 
 
@@ -637,7 +687,7 @@ def profile_projected_gaussians(means2d: Tensor, conics: Tensor, colors: Tensor,
         counts = (st.tile_offsets[1:] - st.tile_offsets[:-1])
         all_counts.append(counts.cpu().to(torch.float32))
         if run_forward or return_image:
-            out, final_T, last_idx = _render_forward(st, config, b1 - b0, save_state=True)
+            out, final_T, last_idx, _ = _render_forward(st, config, b1 - b0, save_state=True)
             if return_image:
                 images.append(out)
             all_stops.append(_tile_stop_counts(final_T, last_idx, counts, config).cpu().to(torch.float32))

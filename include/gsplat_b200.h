@@ -46,6 +46,7 @@ extern "C" {
 #define GSB_STATUS_ERROR 1          /* OR of GSB_DEVERR_* flags */
 #define GSB_STATUS_MAX_TILE_COUNT 2 /* written by gsb_tile_stats */
 #define GSB_STATUS_ERROR_SITE 3     /* first kernel site that raised an error */
+#define GSB_STATUS_PAIR_TOTAL64 4   /* words 4-5: 64-bit pair total, written by gsb_bin_count */
 #define GSB_STATUS_WORDS 8
 
 #define GSB_DEVERR_LOOKBACK_TIMEOUT 1u /* decoupled look-back spin limit hit */
@@ -102,6 +103,19 @@ int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const flo
                     int32_t* perm, float* rec, int32_t* pair_offsets, uint32_t* status,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* gsb_bin_prepare in two calls on the same workspace, so the caller can read the
+ * pair total early: gsb_bin_count zeroes the status block and counts each splat's
+ * tiles (status words GSB_STATUS_PAIR_TOTAL64.. = 64-bit total P); a device-to-host
+ * copy of that word enqueued right after it completes while gsb_bin_sort_scan
+ * (depth sort, gather, scan) still runs. */
+int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                  const float* opacities, const float* depths, uint32_t* status, void* workspace,
+                  size_t workspace_bytes, void* stream);
+int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const float* conics,
+                      const float* colors, const float* opacities, const float* depths, int32_t* perm,
+                      float* rec, int32_t* pair_offsets, uint32_t* status, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* ---- binning, phase 2 ---------------------------------------------------
  * Replaces: `emit_binned_ids` (…/gsplat_v8_project3d_kernels.metal:743-780), the per-tile
  * `bitonic_sort_ids` (…:594-617) and the tile offsets of metal_bin (…/gsplat_metal.mm:358-361).
@@ -124,18 +138,20 @@ size_t gsb_render_workspace_size(const gsb_raster_meta* meta);
 
 /* Replaces `tile_fast_forward_eval` / `tile_fast_forward_state`
  * (…/gsplat_v8_project3d_kernels.metal:783-929; root csrc/metal/gsplat_fast_kernels.metal:221-294).
- * final_T and last_idx may both be NULL (eval: no saved state). */
+ * Training state: final_T, last_idx and pair_rec [P*12] (the records of each
+ * short tile in list order, read back by the backward) are all given, or all
+ * NULL (eval). */
 int gsb_render_forward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                        const int32_t* binned_ids, float* out_rgb, float* final_T,
-                       int32_t* last_idx, uint32_t* status, void* workspace,
+                       int32_t* last_idx, float* pair_rec, uint32_t* status, void* workspace,
                        size_t workspace_bytes, void* stream);
 
 /* Replaces `tile_fast_backward_saved` (…/gsplat_v8_project3d_kernels.metal:931-1063; root
  * csrc/metal/gsplat_fast_kernels.metal:296-395). Zeroes and accumulates grad_rec [B*G*12]. */
 int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                         const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
-                        const float* grad_rgb, float* grad_rec, uint32_t* status, void* workspace,
-                        size_t workspace_bytes, void* stream);
+                        const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* Replaces the un-sort scatter of the autograd backward
  * (torch_gsplat_bridge_fast/rasterize.py:96-105; …/v8_project3d/…/rasterize.py:583-591, 847-851).

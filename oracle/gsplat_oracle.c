@@ -128,6 +128,17 @@ float orc_sat_log_threshold(float op, float max_alpha) {
   return (float)orc_det_log(ratio);
 }
 
+/* Gaussian exponent at pixel offset (dx, dy): -0.5 (a dx^2 + 2 b dx dy + c dy^2)
+ * (…kernels.metal:587), evaluated as fma(-c/2 dy, dy, fma(-b dx, dy, (-a/2 dx) dx)).
+ * Every step is one correctly rounded IEEE op (fmaf is a single rounding), so the
+ * value is reproducible bit for bit by any IEEE evaluator of the same sequence. */
+float orc_power(float a, float b, float c, float dx, float dy) {
+  const float ta = ((-0.5f * a) * dx) * dx;
+  const float tb = (-b) * dx;
+  const float cd = (-0.5f * c) * dy;
+  return fmaf(cd, dy, fmaf(tb, dy, ta));
+}
+
 static int clamp_f2i(float x) {
   x = fminf(fmaxf(x, -1073741824.0f), 1073741824.0f);
   return (int)x;
@@ -309,8 +320,9 @@ void orc_bin_emit(const orc_meta* m, const float* rec, const int32_t* pair_offse
 }
 
 /* Forward compositing per pixel, in the reference's order and gates. Also
- * reports the saved state: final T and last_idx = 1 + index of the last
- * visible splat consumed (0 when none). */
+ * reports the saved state: final T and last_idx = the number of list entries
+ * the pixel consumed (the reference's per-pixel stop: saturation index + 1, or
+ * the tile count when the pixel never saturates). */
 void orc_render_forward(const orc_meta* m, const float* rec, const int32_t* tile_offsets, const int32_t* ids,
                         float* out_rgb, float* final_T, int32_t* last_idx) {
   const dims_t d = dims_of(m);
@@ -323,12 +335,13 @@ void orc_render_forward(const orc_meta* m, const float* rec, const int32_t* tile
       for (int px = tx * TILE; px < imin(tx * TILE + TILE, d.W); ++px) {
         const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
         float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-        int last = 0;
+        int last = 0; /* entries consumed: n, or the saturation index + 1 */
         if (T > m->transmittance_threshold) {
+          last = n;
           for (int j = 0; j < n; ++j) {
             const float* R = rec + (int64_t)ids[start + j] * REC;
             const float dx = fx - R[0], dy = fy - R[1];
-            const float power = -0.5f * (R[2] * dx * dx + 2.0f * R[3] * dx * dy + R[4] * dy * dy);
+            const float power = orc_power(R[2], R[3], R[4], dx, dy);
             if (!(power <= 0.0f && power >= R[10])) continue; /* eval_alpha gate, see orc_vis_log_threshold */
             const float alpha = fminf(m->max_alpha, R[5] * expf(power));
             const float w = T * alpha;
@@ -336,8 +349,10 @@ void orc_render_forward(const orc_meta* m, const float* rec, const int32_t* tile
             cg += w * R[7];
             cb += w * R[8];
             T *= (1.0f - alpha);
-            last = j + 1;
-            if (T <= m->transmittance_threshold) break;
+            if (T <= m->transmittance_threshold) {
+              last = j + 1;
+              break;
+            }
           }
         }
         const int64_t pix = ((int64_t)b * d.H + py) * d.W + px;
@@ -378,7 +393,7 @@ void orc_render_backward(const orc_meta* m, const float* rec, const int32_t* til
             for (int j = 0; j < n; ++j) {
               const float* R = rec + (int64_t)ids[start + j] * REC;
               const float dx = fx - R[0], dy = fy - R[1];
-              const float power = -0.5f * (R[2] * dx * dx + 2.0f * R[3] * dx * dy + R[4] * dy * dy);
+              const float power = orc_power(R[2], R[3], R[4], dx, dy);
               if (!(power <= 0.0f && power >= R[10])) continue;
               const float alpha = fminf(m->max_alpha, R[5] * expf(power));
               T_final *= (1.0f - alpha);
@@ -397,7 +412,7 @@ void orc_render_backward(const orc_meta* m, const float* rec, const int32_t* til
             const float* R = rec + (int64_t)gi * REC;
             const float dx = fx - R[0], dy = fy - R[1];
             const float a = R[2], bq = R[3], c = R[4], op = R[5];
-            const float power = -0.5f * (a * dx * dx + 2.0f * bq * dx * dy + c * dy * dy);
+            const float power = orc_power(a, bq, c, dx, dy);
             if (!(power <= 0.0f && power >= R[10])) continue;
             const float raw = op * expf(power);
             const float alpha = fminf(m->max_alpha, raw);

@@ -65,7 +65,7 @@ def test_argument_validation_without_gpu():
     m = _meta()
     rc = L.gsb_bin_prepare(C.byref(m), *([None] * 9), None, 0, None)
     assert rc == 1  # null pointers
-    rc = L.gsb_render_forward(C.byref(_meta(height=0)), None, None, None, None, None, None, None, None, 0, None)
+    rc = L.gsb_render_forward(C.byref(_meta(height=0)), None, None, None, None, None, None, None, None, None, 0, None)
     assert rc == 1
     rc = L.gsb_radix_sort_pairs(None, None, None, None, -1, 0, 8, None, None, 0, None)
     assert rc == 1

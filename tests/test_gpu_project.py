@@ -47,10 +47,18 @@ def test_projection_unbatched_and_defaults():
 
 
 def test_projection_c4_scale_matches_torch_restatement():
-    """One view of the config-4 scene (2^20 Gaussians, camera on the radius-25 sphere)."""
+    """One view of the config-4 scene (2^20 Gaussians, camera on the radius-25
+    sphere). Gaussians within 0.2 of the camera plane are left out: there the EWA
+    Jacobian overflows fp32 (det -> inf) and the chain rule produces 0 * inf,
+    which any two evaluation orders turn into different non-finite sums."""
     sc = config_3d(seed=0).to(DEV)
-    ins = [t.clone().requires_grad_(True) for t in (sc.means3d, sc.scales, sc.quats, sc.opacities)]
-    c2w = sc.camera_to_world[:1].clone().requires_grad_(True)
+    c2w0 = sc.camera_to_world[:1]
+    with torch.no_grad():
+        z = TR.project_pinhole(sc.means3d[None], sc.scales[None], sc.quats[None], sc.opacities[None], c2w0,
+                               sc.camera_params[:1], 1e-4)[3][0]
+    keep = z.abs() > 0.2
+    ins = [t[keep].clone().requires_grad_(True) for t in (sc.means3d, sc.scales, sc.quats, sc.opacities)]
+    c2w = c2w0.clone().requires_grad_(True)
     cam = sc.camera_params[:1].clone().requires_grad_(True)
     outs = tgb.project_pinhole_gaussians(*(t[None] for t in ins), cam[:, 0], cam[:, 1], cam[:, 2], cam[:, 3],
                                          camera_to_world=c2w)
@@ -58,9 +66,6 @@ def test_projection_c4_scale_matches_torch_restatement():
     rc2w = c2w.detach().clone().requires_grad_(True)
     rcam = cam.detach().clone().requires_grad_(True)
     refs = TR.project_pinhole(*(t[None] for t in ref_ins), rc2w, rcam, 1e-4)
-    # 2^20 random Gaussians include splats just past the near plane, where the
-    # cov00*cov11 - cov01^2 cancellation makes the conic ill-conditioned in fp32;
-    # the relative gate is the gradient gate (the reference fixture above is 1e-5).
     for o, r, name in zip(outs, refs, ("means2d", "conics", "opac", "depth")):
         assert rel_err_finite(np_(o), np_(r)) <= GRAD_RTOL, name
     gen = torch.Generator(device=DEV).manual_seed(3)

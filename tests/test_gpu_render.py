@@ -54,7 +54,7 @@ def test_saved_state_matches_c_oracle():
     s = config_2d("c1", seed=2)
     cfg = tgb.RasterConfig(s.height, s.width)
     st = _bin(cfg, *(t.to(DEV) for t in s.tensors()))
-    out, T, last = _render_forward(st, cfg, s.B, save_state=True)
+    out, T, last, _ = _render_forward(st, cfg, s.B, save_state=True)
     meta = O.Meta(s.height, s.width, s.B, s.G)
     ref = cpu_oracle(s, torch.zeros(s.B, s.height, s.width, 3))
     assert max_abs(np_(T), ref["final_T"]) <= 1e-5
