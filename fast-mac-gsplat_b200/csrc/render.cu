@@ -30,6 +30,8 @@
 // then prefetches a tile's records, ids and per-pixel state with cp.async one
 // tile ahead (double-buffered shared memory), so its per-tile load latency
 // overlaps the previous tile's arithmetic.
+#include <mutex>
+
 #include "gsb_common.cuh"
 #include "gsb_host.cuh"
 
@@ -736,5 +738,87 @@ extern "C" int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm
   k_unsort<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, perm, reinterpret_cast<const float4*>(grad_rec), g_means2d,
                                                   g_conics, g_colors, g_opacities);
   note_launches(1);
+  return cuda_status(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free forward. The forward's only scratch is the list of long tiles
+// and its counter; here they live in a fixed device array compiled into the
+// library, so the caller provides nothing but inputs and outputs. Meant for
+// hosts that own all device memory and give a plugin no way to allocate (a
+// renderer embedded in an engine with a fixed arena, a plugin ABI without an
+// allocator callback). Every GPU that loads the library keeps this array
+// (4 B x (1 + GSB_NOALLOC_MAX_TILES) = 1 MiB) until the process exits.
+// ---------------------------------------------------------------------------
+namespace gsb {
+namespace {
+
+// [0] = long-tile count, [1 .. GSB_NOALLOC_MAX_TILES] = long-tile ids.
+static __device__ __align__(256) uint32_t g_noalloc_render_scratch[1 + GSB_NOALLOC_MAX_TILES];
+
+// The device address of the array on the current device. In host code the
+// symbol is only a host-side handle; each device's copy is looked up once with
+// that device current and cached.
+uint32_t* noalloc_scratch(int* rc) {
+  static std::mutex mu;
+  static uint32_t* ptr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *rc = GSB_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_render_scratch) != cudaSuccess || p == nullptr) {
+      *rc = GSB_ERR_CUDA;
+      return nullptr;
+    }
+    ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *rc = GSB_OK;
+  return ptr[dev];
+}
+
+}  // namespace
+}  // namespace gsb
+
+extern "C" int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
+                                          const int32_t* binned_ids, float* out_rgb, float* final_T,
+                                          int32_t* last_idx, float* pair_rec, uint32_t* status, void* stream_) {
+  Meta m;
+  int rc = make_meta(meta, &m);
+  if (rc != GSB_OK) return rc;
+  if (m.total_tiles > GSB_NOALLOC_MAX_TILES) return GSB_ERR_CAPACITY;
+  if (!tile_offsets || !out_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
+  if ((final_T == nullptr) != (last_idx == nullptr) || (final_T == nullptr) != (pair_rec == nullptr))
+    return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG > 0 && !rec) return GSB_ERR_INVALID_ARGUMENT;
+  uint32_t* scratch = noalloc_scratch(&rc);
+  if (rc != GSB_OK) return rc;
+  uint32_t* long_count = scratch;
+  int32_t* long_tiles = reinterpret_cast<int32_t*>(scratch + 1);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  // The array keeps the previous call's contents: the counter must restart at 0.
+  if (cudaMemsetAsync(long_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GSB_ERR_CUDA;
+  const GridCache& g = grids();
+  const float4* r4 = reinterpret_cast<const float4*>(rec);
+  float4* pr4 = reinterpret_cast<float4*>(pair_rec);
+  const int warp_grid = max(1, min(g.fwd_warp[final_T ? 1 : 0], (m.total_tiles + kWarps - 1) / kWarps));
+  const int cta_grid = max(1, min(g.fwd_cta[final_T ? 1 : 0], m.total_tiles));
+  if (final_T) {
+    k_render_fwd_warp<true><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
+                                                                   final_T, last_idx, pr4, long_tiles, long_count,
+                                                                   status);
+    k_render_fwd_cta<true><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, final_T,
+                                                                 last_idx, long_tiles, long_count, status);
+  } else {
+    k_render_fwd_warp<false><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
+                                                                    nullptr, nullptr, nullptr, long_tiles,
+                                                                    long_count, status);
+    k_render_fwd_cta<false><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, nullptr,
+                                                                  nullptr, long_tiles, long_count, status);
+  }
+  note_launches(2);
   return cuda_status(cudaGetLastError());
 }

@@ -153,6 +153,24 @@ int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int
                         const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of gsb_render_forward, with no counterpart in the
+ * reference. For callers that cannot allocate device memory themselves (a host
+ * that owns all device memory and gives this library only its inputs and
+ * outputs), it takes no workspace: its scratch (the list of tiles with long
+ * pair lists) is a fixed device array inside the library, holding up to
+ * GSB_NOALLOC_MAX_TILES tiles (B * ceil(H/16) * ceil(W/16)); larger configs
+ * return GSB_ERR_CAPACITY. It allocates nothing and calls no allocating routine.
+ * The first call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress, with the device current), so make it before any stream
+ * capture. All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads, same device) race and must be serialised by the caller.
+ * Same arguments and results as gsb_render_forward otherwise. */
+#define GSB_NOALLOC_MAX_TILES 262144
+int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec,
+                               const int32_t* tile_offsets, const int32_t* binned_ids,
+                               float* out_rgb, float* final_T, int32_t* last_idx, float* pair_rec,
+                               uint32_t* status, void* stream);
+
 /* Replaces the un-sort scatter of the autograd backward
  * (torch_gsplat_bridge_fast/rasterize.py:96-105; …/v8_project3d/…/rasterize.py:583-591, 847-851).
  * Any output pointer may be NULL (that gradient is skipped). */
