@@ -124,12 +124,12 @@ def check(rc: int, what: str) -> None:
 
 
 def ptr(t: torch.Tensor | None):
-    """Device pointer of a tensor (None -> NULL)."""
-    return None if t is None else C.c_void_p(t.data_ptr())
+    """Device pointer of a tensor as an int (None -> NULL)."""
+    return None if t is None else t.data_ptr()
 
 
 def stream_ptr(device: torch.device):
-    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def make_meta(height: int, width: int, batch_size: int, gaussians_per_batch: int, alpha_threshold: float,

@@ -250,32 +250,70 @@ def _read_status(status: Tensor) -> list:
     return vals
 
 
+class _ErrorSlots:
+    """A small ring of pinned buffers and events for deferred device-error reads."""
+
+    def __init__(self, n: int = 16):
+        self.host = torch.empty((n, 4), dtype=torch.int32, pin_memory=True)
+        self.events = [torch.cuda.Event() for _ in range(n)]
+        self.used = [False] * n
+        self.next = 0
+
+    def check(self, i: int) -> None:
+        if self.used[i]:
+            self.used[i] = False
+            self.events[i].synchronize()
+            flags = int(self.host[i, N.GSB_STATUS_ERROR]) & 0xFFFFFFFF
+            if flags:
+                site = int(self.host[i, N.GSB_STATUS_ERROR_SITE]) & 0xFFFFFFFF
+                raise RuntimeError(N.decode_device_error(flags, site))
+
+
+def _error_slots() -> _ErrorSlots:
+    slots = getattr(_tls, "error_slots", None)
+    if slots is None:
+        slots = _tls.error_slots = _ErrorSlots()
+    return slots
+
+
 def _defer_error_check(status: Tensor) -> None:
     """Copies a call's device error words to pinned memory without waiting; the
     next forward's host sync (or check_device_errors()) reads and raises them."""
-    host = torch.empty(4, dtype=torch.int32, pin_memory=True)
-    host.copy_(status[:4], non_blocking=True)
-    ev = torch.cuda.Event()
-    ev.record(torch.cuda.current_stream(status.device))
-    pending = getattr(_tls, "pending_errors", None)
-    if pending is None:
-        pending = _tls.pending_errors = []
-    pending.append((ev, host))
-    if len(pending) > 64:
-        check_device_errors()
+    slots = _error_slots()
+    i = slots.next
+    slots.check(i)  # the slot's previous copy is long done by now
+    slots.next = (i + 1) % len(slots.used)
+    slots.host[i].copy_(status[:4], non_blocking=True)
+    slots.events[i].record(torch.cuda.current_stream(status.device))
+    slots.used[i] = True
 
 
 def check_device_errors() -> None:
     """Raises RuntimeError if any earlier call's kernels reported a device-side
     error (bounded-wait timeout, pair overflow, index out of bounds)."""
-    pending = getattr(_tls, "pending_errors", None) or []
-    _tls.pending_errors = []
-    for ev, host in pending:
-        ev.synchronize()
-        flags = int(host[N.GSB_STATUS_ERROR]) & 0xFFFFFFFF
-        site = int(host[N.GSB_STATUS_ERROR_SITE]) & 0xFFFFFFFF
-        if flags:
-            raise RuntimeError(N.decode_device_error(flags, site))
+    slots = getattr(_tls, "error_slots", None)
+    if slots is None:
+        return
+    for k in range(len(slots.used)):
+        slots.check((slots.next + k) % len(slots.used))
+
+
+def _arena(device: torch.device, specs):
+    """Carves tensors of the given (shape, dtype) from one device allocation
+    (256-byte aligned views)."""
+    offs, off = [], 0
+    for shape, dtype in specs:
+        n = 1
+        for d in shape:
+            n *= int(d)
+        off = (off + 255) & ~255
+        offs.append((off, n, shape, dtype))
+        off += max(n * dtype.itemsize, 1)
+    buf = torch.empty(max(off, 1), dtype=torch.uint8, device=device)
+    out = []
+    for o, n, shape, dtype in offs:
+        out.append(buf[o:o + n * dtype.itemsize].view(dtype).view(shape))
+    return out
 
 
 def _aligned(t: Tensor, align: int = 16) -> Tensor:
@@ -305,13 +343,14 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     BG = B * G
     st = _BinState()
     st.meta = meta
-    st.status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
-    st.perm = torch.empty((B, G), dtype=torch.int32, device=dev)
-    st.rec = torch.empty((BG, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
-    st.pair_offsets = torch.empty(BG + 1, dtype=torch.int32, device=dev)
+    ws_bytes = int(L.gsb_bin_prepare_workspace_size(meta))
+    # What backward keeps comes from one allocation, the scratch from another, so
+    # the scratch is released when binning returns.
+    st.status, st.perm, st.rec, st.pair_offsets = _arena(dev, [
+        ((N.GSB_STATUS_WORDS,), torch.int32), ((B, G), torch.int32), ((BG, N.GSB_REC_FLOATS), torch.float32),
+        ((BG + 1,), torch.int32)])
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     stream = N.stream_ptr(dev)
-    ws_bytes = L.gsb_bin_prepare_workspace_size(meta)
-    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
     # Locals keep every (possibly copied) input alive until the launch returns.
     m2 = _aligned(means2d_b, 8)
     q2, c2, o2, d2 = (t.contiguous() for t in (conics_b, colors_b, opacities_b, depths_b))
@@ -325,7 +364,9 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     total_host = _pinned("total_host", 1, torch.int64)
     total_host.copy_(st.status[N.GSB_STATUS_PAIR_TOTAL64:N.GSB_STATUS_PAIR_TOTAL64 + 2].view(torch.int64),
                      non_blocking=True)
-    counted = torch.cuda.Event()
+    counted = getattr(_tls, "counted_event", None)
+    if counted is None:
+        counted = _tls.counted_event = torch.cuda.Event()
     counted.record(torch.cuda.current_stream(dev))
     N.check(L.gsb_bin_sort_scan(meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm),
                                 N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes,
@@ -339,11 +380,9 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
         raise RuntimeError(f"gsplat_b200: {P} tile-splat pairs exceed the supported 2^31 - 1")
     st.P = P
     T = B * ((config.height + 15) // 16) * ((config.width + 15) // 16)
-    st.keys = torch.empty(max(P, 1), dtype=torch.int64, device=dev)[:P]
-    st.binned_ids = torch.empty(max(P, 1), dtype=torch.int32, device=dev)[:P]
-    st.tile_offsets = torch.empty(T + 1, dtype=torch.int32, device=dev)
-    ws2_bytes = L.gsb_bin_emit_workspace_size(meta, P)
-    ws2 = torch.empty(max(int(ws2_bytes), 1), dtype=torch.uint8, device=dev)
+    ws2_bytes = int(L.gsb_bin_emit_workspace_size(meta, P))
+    st.binned_ids, st.tile_offsets = _arena(dev, [((P,), torch.int32), ((T + 1,), torch.int32)])
+    st.keys, ws2 = _arena(dev, [((P,), torch.int64), ((ws2_bytes,), torch.uint8)])
     N.check(
         _timed("bin_emit", lambda: L.gsb_bin_emit(
             meta, N.ptr(st.rec), N.ptr(st.pair_offsets), P, N.ptr(st.keys), N.ptr(st.binned_ids),
@@ -374,14 +413,16 @@ def _check_overflow(st: _BinState, config: RasterConfig) -> None:
 def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: bool):
     L = N.load()
     dev = st.status.device
-    out = torch.empty((B, config.height, config.width, 3), dtype=torch.float32, device=dev)
+    H, W = config.height, config.width
+    out = torch.empty((B, H, W, 3), dtype=torch.float32, device=dev)
     final_T = last_idx = pair_rec = None
+    ws_bytes = int(L.gsb_render_workspace_size(st.meta))
     if save_state:
-        final_T = torch.empty((B, config.height, config.width), dtype=torch.float32, device=dev)
-        last_idx = torch.empty((B, config.height, config.width), dtype=torch.int32, device=dev)
-        pair_rec = torch.empty((max(st.P, 1), N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
-    ws_bytes = L.gsb_render_workspace_size(st.meta)
-    ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
+        final_T, last_idx, pair_rec, ws = _arena(dev, [
+            ((B, H, W), torch.float32), ((B, H, W), torch.int32), ((max(st.P, 1), N.GSB_REC_FLOATS), torch.float32),
+            ((ws_bytes,), torch.uint8)])
+    else:
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     N.check(
         _timed("render_fwd", lambda: L.gsb_render_forward(
             st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out), N.ptr(final_T),
@@ -421,9 +462,8 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         dev = rec.device
         stream = N.stream_ptr(dev)
         g = _aligned(grad_out.to(torch.float32))
-        grad_rec = torch.empty((B * G, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
-        ws_bytes = L.gsb_render_workspace_size(ctx.meta)
-        ws = torch.empty(max(int(ws_bytes), 1), dtype=torch.uint8, device=dev)
+        ws_bytes = int(L.gsb_render_workspace_size(ctx.meta))
+        grad_rec, ws = _arena(dev, [((B * G, N.GSB_REC_FLOATS), torch.float32), ((ws_bytes,), torch.uint8)])
         N.check(
             _timed("render_bwd", lambda: L.gsb_render_backward(
                 ctx.meta, N.ptr(rec), N.ptr(tile_offsets), N.ptr(binned_ids), N.ptr(final_T), N.ptr(last_idx),
