@@ -39,39 +39,23 @@ __global__ void __launch_bounds__(kSortThreads)
   }
 }
 
-// Exclusive scan of each pass's 256-bin histogram (one block per pass).
-__global__ void __launch_bounds__(kRadix) rs_digit_base(const uint32_t* __restrict__ hist,
-                                                        uint32_t* __restrict__ base) {
-  __shared__ uint32_t s_warp[kRadix / 32];
-  const int p = blockIdx.x;
-  const int t = threadIdx.x;
-  const int lane = t & 31, warp = t >> 5;
-  const uint32_t v = hist[p * kRadix + t];
-  uint32_t x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(kFullMask, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) s_warp[warp] = x;
-  __syncthreads();
-  uint32_t wsum = 0;
-  for (int w = 0; w < warp; ++w) wsum += s_warp[w];
-  base[p * kRadix + t] = wsum + x - v;
-}
-
 // One digit pass. Keys are held warp-striped: warp w owns the contiguous
 // segment [tile + w*32*ITEMS, +32*ITEMS) and lane l holds its items i*32+l, so
-// (item, lane) order is input order and the match_any ranking is stable.
+// (item, lane) order is input order and the match_any ranking is stable. Each
+// CTA also turns the pass's global digit histogram into exclusive digit bases
+// itself (a 256-entry scan), so no separate launch precedes the pass.
+template <int ITEMS>
 __global__ void __launch_bounds__(kSortThreads)
     rs_onesweep(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                 uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
-                int shift, int bits, const uint32_t* __restrict__ digit_base,
+                int shift, int bits, const uint32_t* __restrict__ hist,
                 uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter,
                 uint32_t* __restrict__ status) {
+  constexpr int kTile = kSortThreads * ITEMS;
   __shared__ uint32_t s_part;
   __shared__ uint32_t s_warp_hist[kSortWarps][kRadix];
   __shared__ uint32_t s_prefix[kRadix];
+  __shared__ uint32_t s_scan[kSortWarps];
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -81,18 +65,39 @@ __global__ void __launch_bounds__(kSortThreads)
   const uint32_t part = s_part;
   const uint32_t dmask = (1u << bits) - 1u;
 
-  const int64_t seg = (int64_t)part * kSortTile + (int64_t)warp * (32 * kSortItems);
-  uint64_t k[kSortItems];
-  uint32_t v[kSortItems];
-  uint32_t rank[kSortItems];
+  const int64_t seg = (int64_t)part * kTile + (int64_t)warp * (32 * ITEMS);
+  uint64_t k[ITEMS];
+  uint32_t v[ITEMS];
+  uint32_t rank[ITEMS];
   const uint32_t lt_mask = (1u << lane) - 1u;
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    const int64_t idx = seg + i * 32 + lane;
+    k[i] = idx < n ? keys_in[idx] : 0ull;
+    v[i] = idx < n ? vals_in[idx] : 0u;
+  }
+  // Exclusive digit bases of this pass (the histogram load overlaps the key loads).
+  uint32_t digit_base;
+  {
+    const uint32_t h = hist[tid];
+    uint32_t x = h;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFullMask, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_scan[warp] = x;
+    __syncthreads();
+    uint32_t wsum = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) wsum += (w < warp) ? s_scan[w] : 0u;
+    digit_base = wsum + x - h;
+  }
 
 #pragma unroll
-  for (int i = 0; i < kSortItems; ++i) {
+  for (int i = 0; i < ITEMS; ++i) {
     const int64_t idx = seg + i * 32 + lane;
     const bool valid = idx < n;
-    k[i] = valid ? keys_in[idx] : 0ull;
-    v[i] = valid ? vals_in[idx] : 0u;
     const uint32_t d = valid ? ((uint32_t)(k[i] >> shift) & dmask) : kRadix;  // sentinel group
     const uint32_t peers = __match_any_sync(kFullMask, d);
     uint32_t cnt_before = 0;
@@ -153,12 +158,12 @@ __global__ void __launch_bounds__(kSortThreads)
       if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteSortLookback);
       st_volatile_u32(my, kFlagInc | ((exclusive + sum) & kValueMask));
     }
-    s_prefix[t] = digit_base[t] + exclusive;
+    s_prefix[t] = digit_base + exclusive;
   }
   __syncthreads();
 
 #pragma unroll
-  for (int i = 0; i < kSortItems; ++i) {
+  for (int i = 0; i < ITEMS; ++i) {
     const int64_t idx = seg + i * 32 + lane;
     if (idx < n) {
       const uint32_t d = (uint32_t)(k[i] >> shift) & dmask;
@@ -187,18 +192,30 @@ int grid_for(int64_t n, int threads, int max_blocks) {
 
 }  // namespace
 
+static int sort_items(int64_t n) {
+  // Enough partitions to put about two CTAs on every SM: a pass over few keys
+  // is latency-bound, and a smaller partition shortens each CTA's serial work.
+  if (n >= (int64_t)kSortThreads * 16 * 296) return 16;
+  if (n >= (int64_t)kSortThreads * 8 * 296) return 8;
+  return 4;
+}
+
 cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in,
                              uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
                              int end_bit, uint32_t* status, cudaStream_t stream) {
   const int passes = sort_passes(begin_bit, end_bit);
-  const int64_t parts = sort_partitions(n);
-  // Scratch layout (identical in measuring and running mode).
+  const int items = sort_items(n);
+  const int64_t tile = (int64_t)kSortThreads * items;
+  const int64_t parts = (n + tile - 1) / tile;
+  // Scratch layout (identical in measuring and running mode). Histograms,
+  // partition counters and look-back words are contiguous: one memset clears them.
   uint64_t* k_tmp = ws.take<uint64_t>(passes > 1 ? (size_t)n : 0);
   uint32_t* v_tmp = ws.take<uint32_t>(passes > 1 ? (size_t)n : 0);
-  uint32_t* hist = ws.take<uint32_t>((size_t)kMaxPasses * kRadix);
-  uint32_t* base = ws.take<uint32_t>((size_t)kMaxPasses * kRadix);
-  uint32_t* counters = ws.take<uint32_t>(kMaxPasses);
-  uint32_t* lookback = ws.take<uint32_t>((size_t)passes * (size_t)parts * kRadix);
+  const size_t zero_words = (size_t)kMaxPasses * kRadix + kMaxPasses + (size_t)passes * (size_t)parts * kRadix;
+  uint32_t* zeroed = ws.take<uint32_t>(zero_words);
+  uint32_t* hist = zeroed;
+  uint32_t* counters = hist + (size_t)kMaxPasses * kRadix;
+  uint32_t* lookback = counters + kMaxPasses;
   if (ws.base == nullptr) return cudaSuccess;
   if (n <= 0) return cudaSuccess;
   if (passes == 0) {
@@ -207,16 +224,10 @@ cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t
     return cudaGetLastError();
   }
   const int last_bits = (end_bit - begin_bit) - (passes - 1) * kRadixBits;
-  cudaError_t e = cudaMemsetAsync(hist, 0, sizeof(uint32_t) * kMaxPasses * kRadix, stream);
-  if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(counters, 0, sizeof(uint32_t) * kMaxPasses, stream);
-  if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(lookback, 0, sizeof(uint32_t) * (size_t)passes * (size_t)parts * kRadix, stream);
+  cudaError_t e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
   if (e != cudaSuccess) return e;
   rs_histogram<<<grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream>>>(keys_in, n, begin_bit,
                                                                                 passes, last_bits, hist);
-  note_launches(1);
-  rs_digit_base<<<passes, kRadix, 0, stream>>>(hist, base);
   note_launches(1);
   // Ping-pong so the last pass writes keys_out: pass p writes out when
   // (passes-1-p) is even, else tmp.
@@ -227,8 +238,9 @@ cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t
     uint64_t* ko = to_out ? keys_out : k_tmp;
     uint32_t* vo = to_out ? vals_out : v_tmp;
     const int bits = (p == passes - 1) ? last_bits : kRadixBits;
-    rs_onesweep<<<(unsigned)parts, kSortThreads, 0, stream>>>(
-        ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, base + p * kRadix,
+    auto kernel = items == 16 ? rs_onesweep<16> : items == 8 ? rs_onesweep<8> : rs_onesweep<4>;
+    kernel<<<(unsigned)parts, kSortThreads, 0, stream>>>(
+        ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, hist + p * kRadix,
         lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status);
     note_launches(1);
     ki = ko;

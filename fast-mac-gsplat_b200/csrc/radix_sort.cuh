@@ -1,7 +1,8 @@
 // Stable LSD radix sort of (uint64 key, uint32 value) pairs, onesweep style:
 // one kernel builds the histograms of every digit pass at once, then each
-// 8-bit digit pass ranks a 4096-key partition in shared memory, resolves its
-// global per-digit offsets with decoupled look-back, and scatters.
+// 8-bit digit pass ranks a partition of 1024-4096 keys (fewer keys per
+// partition for short inputs) in shared memory, resolves its global per-digit
+// offsets with decoupled look-back, and scatters.
 #pragma once
 
 #include <stddef.h>
@@ -15,8 +16,6 @@ namespace gsb {
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 16;
-constexpr int kSortTile = kSortThreads * kSortItems;  // 4096 keys per partition
 constexpr int kRadix = 256;
 constexpr int kRadixBits = 8;
 constexpr int64_t kSortMaxN = (int64_t(1) << 30) - 1;  // 30-bit look-back payload
@@ -24,7 +23,6 @@ constexpr int64_t kSortMaxN = (int64_t(1) << 30) - 1;  // 30-bit look-back paylo
 inline int sort_passes(int begin_bit, int end_bit) {
   return end_bit > begin_bit ? (end_bit - begin_bit + kRadixBits - 1) / kRadixBits : 0;
 }
-inline int64_t sort_partitions(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
 
 // Carves the sort's scratch: temp key/value buffers, histograms, partition
 // counters and per-pass look-back tiles. Returns the status of the launches

@@ -12,6 +12,7 @@ C ABI on the current CUDA stream; there is no CPU fallback.
 """
 from __future__ import annotations
 
+import functools
 import os
 import threading
 from dataclasses import dataclass
@@ -251,69 +252,62 @@ def _read_status(status: Tensor) -> list:
 
 
 class _ErrorSlots:
-    """A small ring of pinned buffers and events for deferred device-error reads."""
+    """A small ring of pinned status copies and events for deferred device-error
+    reads (one per forward or backward call). It is shared by all threads, so an
+    error raised by a backward that autograd ran on its own device thread is
+    reported to the thread that calls the next forward."""
 
     def __init__(self, n: int = 16):
-        self.host = torch.empty((n, 4), dtype=torch.int32, pin_memory=True)
+        self.host = torch.empty((n, N.GSB_STATUS_WORDS), dtype=torch.int32, pin_memory=True)
+        self.rows = [self.host[i] for i in range(n)]
+        self.view = self.host.numpy()
         self.events = [torch.cuda.Event() for _ in range(n)]
-        self.used = [False] * n
+        self.streams = [None] * n
         self.next = 0
 
-    def check(self, i: int) -> None:
-        if self.used[i]:
-            self.used[i] = False
+    def check(self, i: int, synced_stream=None) -> None:
+        stream = self.streams[i]
+        if stream is None:
+            return
+        self.streams[i] = None
+        if stream != synced_stream:
             self.events[i].synchronize()
-            flags = int(self.host[i, N.GSB_STATUS_ERROR]) & 0xFFFFFFFF
-            if flags:
-                site = int(self.host[i, N.GSB_STATUS_ERROR_SITE]) & 0xFFFFFFFF
-                raise RuntimeError(N.decode_device_error(flags, site))
+        flags = int(self.view[i, N.GSB_STATUS_ERROR]) & 0xFFFFFFFF
+        if flags:
+            site = int(self.view[i, N.GSB_STATUS_ERROR_SITE]) & 0xFFFFFFFF
+            raise RuntimeError(N.decode_device_error(flags, site))
 
 
-def _error_slots() -> _ErrorSlots:
-    slots = getattr(_tls, "error_slots", None)
-    if slots is None:
-        slots = _tls.error_slots = _ErrorSlots()
-    return slots
+_error_lock = threading.Lock()
+_error_ring: Optional[_ErrorSlots] = None
 
 
-def _defer_error_check(status: Tensor) -> None:
-    """Copies a call's device error words to pinned memory without waiting; the
-    next forward's host sync (or check_device_errors()) reads and raises them."""
-    slots = _error_slots()
-    i = slots.next
-    slots.check(i)  # the slot's previous copy is long done by now
-    slots.next = (i + 1) % len(slots.used)
-    slots.host[i].copy_(status[:4], non_blocking=True)
-    slots.events[i].record(torch.cuda.current_stream(status.device))
-    slots.used[i] = True
+def _defer_error_check(status: Tensor, stream) -> None:
+    """Copies a call's status block to pinned memory without waiting; the next
+    forward's host sync (or check_device_errors()) reads and raises its errors."""
+    global _error_ring
+    with _error_lock:
+        if _error_ring is None:
+            _error_ring = _ErrorSlots()
+        slots = _error_ring
+        i = slots.next
+        slots.next = (i + 1) % len(slots.rows)
+        slots.check(i)  # the slot's previous copy is long done by now
+        slots.rows[i].copy_(status, non_blocking=True)
+        slots.events[i].record(stream)
+        slots.streams[i] = stream.cuda_stream
 
 
-def check_device_errors() -> None:
+def check_device_errors(_synced_stream=None) -> None:
     """Raises RuntimeError if any earlier call's kernels reported a device-side
     error (bounded-wait timeout, pair overflow, index out of bounds)."""
-    slots = getattr(_tls, "error_slots", None)
-    if slots is None:
-        return
-    for k in range(len(slots.used)):
-        slots.check((slots.next + k) % len(slots.used))
-
-
-def _arena(device: torch.device, specs):
-    """Carves tensors of the given (shape, dtype) from one device allocation
-    (256-byte aligned views)."""
-    offs, off = [], 0
-    for shape, dtype in specs:
-        n = 1
-        for d in shape:
-            n *= int(d)
-        off = (off + 255) & ~255
-        offs.append((off, n, shape, dtype))
-        off += max(n * dtype.itemsize, 1)
-    buf = torch.empty(max(off, 1), dtype=torch.uint8, device=device)
-    out = []
-    for o, n, shape, dtype in offs:
-        out.append(buf[o:o + n * dtype.itemsize].view(dtype).view(shape))
-    return out
+    with _error_lock:
+        slots = _error_ring
+        if slots is None:
+            return
+        n = len(slots.rows)
+        for k in range(n):
+            slots.check((slots.next + k) % n, _synced_stream)
 
 
 def _aligned(t: Tensor, align: int = 16) -> Tensor:
@@ -323,9 +317,21 @@ def _aligned(t: Tensor, align: int = 16) -> Tensor:
     return t
 
 
-def _meta_for(config: RasterConfig, B: int, G: int) -> N.GsbRasterMeta:
+def _make_meta(config: RasterConfig, B: int, G: int) -> N.GsbRasterMeta:
     return N.make_meta(config.height, config.width, B, G, config.alpha_threshold, config.transmittance_threshold,
                        config.background)
+
+
+_meta_cached = functools.lru_cache(maxsize=64)(_make_meta)
+
+
+def _meta_for(config: RasterConfig, B: int, G: int) -> N.GsbRasterMeta:
+    """Packed C meta; the library only reads it, so one instance per (config, B, G)
+    is shared across calls."""
+    try:
+        return _meta_cached(config, B, G)
+    except TypeError:  # a config holding an unhashable value (e.g. a list background)
+        return _make_meta(config, B, G)
 
 
 class _BinState:
@@ -344,13 +350,13 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     st = _BinState()
     st.meta = meta
     ws_bytes = int(L.gsb_bin_prepare_workspace_size(meta))
-    # What backward keeps comes from one allocation, the scratch from another, so
-    # the scratch is released when binning returns.
-    st.status, st.perm, st.rec, st.pair_offsets = _arena(dev, [
-        ((N.GSB_STATUS_WORDS,), torch.int32), ((B, G), torch.int32), ((BG, N.GSB_REC_FLOATS), torch.float32),
-        ((BG + 1,), torch.int32)])
+    st.status = torch.empty(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)  # cleared by gsb_bin_count
+    st.perm = torch.empty((B, G), dtype=torch.int32, device=dev)
+    st.rec = torch.empty((BG, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
+    st.pair_offsets = torch.empty(BG + 1, dtype=torch.int32, device=dev)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-    stream = N.stream_ptr(dev)
+    cur = torch.cuda.current_stream(dev)
+    stream = cur.cuda_stream
     # Locals keep every (possibly copied) input alive until the launch returns.
     m2 = _aligned(means2d_b, 8)
     q2, c2, o2, d2 = (t.contiguous() for t in (conics_b, colors_b, opacities_b, depths_b))
@@ -367,22 +373,24 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     counted = getattr(_tls, "counted_event", None)
     if counted is None:
         counted = _tls.counted_event = torch.cuda.Event()
-    counted.record(torch.cuda.current_stream(dev))
+    counted.record(cur)
     N.check(L.gsb_bin_sort_scan(meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm),
                                 N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes,
                                 stream), "gsb_bin_sort_scan")
     if timer is not None:
         timer.end("bin_prepare")
     counted.synchronize()
-    check_device_errors()
+    check_device_errors(stream)  # earlier calls' copies on this stream are complete now
     P = int(total_host[0])
     if P >= 2**31 - 1:
         raise RuntimeError(f"gsplat_b200: {P} tile-splat pairs exceed the supported 2^31 - 1")
     st.P = P
     T = B * ((config.height + 15) // 16) * ((config.width + 15) // 16)
     ws2_bytes = int(L.gsb_bin_emit_workspace_size(meta, P))
-    st.binned_ids, st.tile_offsets = _arena(dev, [((P,), torch.int32), ((T + 1,), torch.int32)])
-    st.keys, ws2 = _arena(dev, [((P,), torch.int64), ((ws2_bytes,), torch.uint8)])
+    st.binned_ids = torch.empty(P, dtype=torch.int32, device=dev)
+    st.tile_offsets = torch.empty(T + 1, dtype=torch.int32, device=dev)
+    st.keys = torch.empty(P, dtype=torch.int64, device=dev)
+    ws2 = torch.empty(max(ws2_bytes, 1), dtype=torch.uint8, device=dev)
     N.check(
         _timed("bin_emit", lambda: L.gsb_bin_emit(
             meta, N.ptr(st.rec), N.ptr(st.pair_offsets), P, N.ptr(st.keys), N.ptr(st.binned_ids),
@@ -418,21 +426,21 @@ def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: boo
     final_T = last_idx = pair_rec = None
     ws_bytes = int(L.gsb_render_workspace_size(st.meta))
     if save_state:
-        final_T, last_idx, pair_rec, ws = _arena(dev, [
-            ((B, H, W), torch.float32), ((B, H, W), torch.int32), ((max(st.P, 1), N.GSB_REC_FLOATS), torch.float32),
-            ((ws_bytes,), torch.uint8)])
-    else:
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+        final_T = torch.empty((B, H, W), dtype=torch.float32, device=dev)
+        last_idx = torch.empty((B, H, W), dtype=torch.int32, device=dev)
+        pair_rec = torch.empty((max(st.P, 1), N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    cur = torch.cuda.current_stream(dev)
     N.check(
         _timed("render_fwd", lambda: L.gsb_render_forward(
             st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out), N.ptr(final_T),
-            N.ptr(last_idx), N.ptr(pair_rec), N.ptr(st.status), N.ptr(ws), ws_bytes, N.stream_ptr(dev))),
+            N.ptr(last_idx), N.ptr(pair_rec), N.ptr(st.status), N.ptr(ws), ws_bytes, cur.cuda_stream)),
         "gsb_render_forward",
     )
     if _debug_checks():
         _read_status(st.status)
     else:
-        _defer_error_check(st.status)
+        _defer_error_check(st.status, cur)
     return out, final_T, last_idx, pair_rec
 
 
@@ -460,10 +468,12 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         L = N.load()
         B, G = ctx.shape
         dev = rec.device
-        stream = N.stream_ptr(dev)
+        cur = torch.cuda.current_stream(dev)
+        stream = cur.cuda_stream
         g = _aligned(grad_out.to(torch.float32))
         ws_bytes = int(L.gsb_render_workspace_size(ctx.meta))
-        grad_rec, ws = _arena(dev, [((B * G, N.GSB_REC_FLOATS), torch.float32), ((ws_bytes,), torch.uint8)])
+        grad_rec = torch.empty((B * G, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
         N.check(
             _timed("render_bwd", lambda: L.gsb_render_backward(
                 ctx.meta, N.ptr(rec), N.ptr(tile_offsets), N.ptr(binned_ids), N.ptr(final_T), N.ptr(last_idx),
@@ -484,7 +494,7 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
         if _debug_checks():
             _read_status(status)
         else:
-            _defer_error_check(status)
+            _defer_error_check(status, cur)
         g_depths = torch.zeros(ctx.depths_shape, dtype=torch.float32, device=dev) if need[4] else None
         return g_means, g_conics, g_colors, g_opac, g_depths, None
 
@@ -526,7 +536,10 @@ def _rasterize_batched(means2d_b, conics_b, colors_b, opacities_b, depths_b, con
     outs = []
     for b0 in range(0, B, chunk_b):
         b1 = min(B, b0 + chunk_b)
-        args = [t[b0:b1].contiguous() for t in (means2d_b, conics_b, colors_b, opacities_b, depths_b)]
+        full = (means2d_b, conics_b, colors_b, opacities_b, depths_b)
+        # A single chunk passes the inputs themselves: a slice would make autograd
+        # allocate and copy a full-size gradient per input.
+        args = [t if chunk_b >= B else t[b0:b1] for t in full]
         if train_mode:
             outs.append(_RasterizeProjectedGaussiansB200.apply(*args, config))
         else:
@@ -544,7 +557,7 @@ def rasterize_projected_gaussians(means2d: Tensor, conics: Tensor, colors: Tenso
         means2d, conics, colors, opacities, depths)
     _runtime_validate(config)
     out = _rasterize_batched(means2d_b, conics_b, colors_b, opacities_b, depths_b, config)
-    return out if was_batched else out[0]
+    return out if was_batched else out.squeeze(0)
 
 
 # ---------------------------------------------------------------------------
@@ -688,7 +701,7 @@ def rasterize_pinhole_gaussians(means3d: Tensor, scales: Tensor, quats: Tensor, 
     _runtime_validate(config)
     out = _rasterize_batched(means2d.contiguous(), conics.contiguous(), colors_b.contiguous(), proj_op.contiguous(),
                              depths.contiguous(), config)
-    return out if was_batched else out[0]
+    return out if was_batched else out.squeeze(0)
 
 
 # ---------------------------------------------------------------------------

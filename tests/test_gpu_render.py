@@ -228,3 +228,24 @@ def test_profile_stats():
     assert 0 < st["mean_stop_ratio"] <= 1.0
     r = tgb.profile_projected_gaussians(*ins, cfg, return_image=True)
     assert r["image"].shape == (4, 512, 1024, 3)
+
+
+def test_deferred_device_error_is_reported(monkeypatch):
+    """A bounds error found by a render kernel (an out-of-range splat id in a tile
+    list; the kernel checks the id and skips the access) is not read back by the
+    call itself. It surfaces at check_device_errors(), through the pinned copy
+    that the call queued."""
+    from torch_gsplat_bridge_fast import rasterize as R
+
+    monkeypatch.setenv("GSPLAT_B200_CHECK", "0")
+    tgb.check_device_errors()  # nothing pending from earlier tests
+    s = config_2d("c0", seed=0)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = R._bin(cfg, *(t.to(DEV) for t in s.tensors()))
+    assert st.P > 0
+    st.binned_ids[0] = s.B * s.G + 5
+    R._render_forward(st, cfg, s.B, save_state=True)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="index out of bounds"):
+        tgb.check_device_errors()
+    tgb.check_device_errors()  # reported once
