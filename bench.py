@@ -138,25 +138,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-class KernelTimer:
-    """CUDA events around each C-ABI call, on the current (launching) stream."""
-
-    def __init__(self):
-        self.events = {}
-
-    def begin(self, name):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        self.events.setdefault(name, []).append([e, None])
-
-    def end(self, name):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record()
-        self.events[name][-1][1] = e
-
-    def summary(self):
-        torch.cuda.synchronize()
-        return {k: [a.elapsed_time(b) for a, b in v] for k, v in self.events.items()}
+# Algorithmic FP32 operations per Gsplat-px evaluation (an FMA counts 2): the
+# forward's exponent, alpha, transmittance and colour update; the backward's
+# recompute, transmittance inverse, colour/opacity/conic/mean VJPs and its share
+# of the per-splat reduction (reference kernels …metal:574-592, 834-840, 1013-1039).
+FLOPS_PER_EVAL = {"render_fwd": 23, "render_bwd": 60}
 
 
 def algorithmic_bytes(kernel: str, B: int, H: int, W: int, G: int, P: int) -> int:
@@ -182,7 +168,7 @@ def run_b200(args):
 
     import torch_gsplat_bridge_fast as tgb
     from torch_gsplat_bridge_fast import _native
-    from torch_gsplat_bridge_fast.rasterize import _bin, set_kernel_timer
+    from torch_gsplat_bridge_fast.rasterize import _bin, kernel_times, set_kernel_timer
     from workloads import config_2d, grad_image
 
     rank, world, local = dist_env()
@@ -213,7 +199,6 @@ def run_b200(args):
     torch.cuda.synchronize()
 
     L = _native.load()
-    timer = KernelTimer()
     step_ms = []
     with ClockSampler(local) as clocks:
         if world > 1:
@@ -221,7 +206,7 @@ def run_b200(args):
         torch.cuda.synchronize()
         launches0 = L.gsb_kernel_launches()
         t_bracket = time.perf_counter()
-        set_kernel_timer(timer)
+        set_kernel_timer(True)
         for _ in range(args.steps):
             flush.zero_()  # L2 flush between timed steps (outside the step events)
             e0 = torch.cuda.Event(enable_timing=True)
@@ -231,7 +216,8 @@ def run_b200(args):
             e1.record()
             e1.synchronize()
             step_ms.append(e0.elapsed_time(e1))
-        set_kernel_timer(None)
+        kt = kernel_times()
+        set_kernel_timer(False)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -240,7 +226,6 @@ def run_b200(args):
     clock = clocks.summary()
     ms = statistics.mean(step_ms)
     ms_med = statistics.median(step_ms)
-    kt = timer.summary()
 
     ms_max = ms
     if world > 1:
@@ -259,6 +244,17 @@ def run_b200(args):
     traffic = load_traffic("k_" + dom, args.config)
     kernels = {k: {"launches_per_step": len(v) / args.steps, "avg_ms": statistics.mean(v),
                    "share": totals[k] / max(sum(totals.values()), 1e-9)} for k, v in kt.items()}
+    # The compositing kernels are FP32-issue bound, not HBM bound: their second
+    # roofline is the FP32 pipe (algorithmic FLOPs per Gsplat-px eval x E).
+    fp32_peak = 148 * 128 * 2 * float(clock.get("sm_max_mhz") or 1965.0) * 1e6 / 1e12
+    roof_fp32 = {}
+    for k, fpe in FLOPS_PER_EVAL.items():
+        if k in kt:
+            tf = fpe * E / (statistics.mean(kt[k]) * 1e-3) / 1e12
+            roof_fp32[k] = {"bound": "fp32", "achieved": round(tf, 2), "peak": round(fp32_peak, 1),
+                            "peak_kind": "nominal: 148 SMs x 128 FP32 lanes x 2 x max SM clock", "unit": "TFLOP/s",
+                            "frac": round(tf / fp32_peak, 4), "flops_per_eval": fpe,
+                            "avg_launch_ms": round(statistics.mean(kt[k]), 4)}
 
     e2e = None
     if not args.no_e2e:
@@ -293,6 +289,7 @@ def run_b200(args):
                          "peak_kind": f"{peak_kind} copy bandwidth", "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "algorithmic_bytes_per_launch": alg,
                          "traffic": traffic, "avg_launch_ms": round(dom_ms, 4)},
+            "roofline_fp32": roof_fp32,
             "clocks": clock,
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -65,5 +65,45 @@ def build(verbose: bool = False) -> Path:
     return LIB_PATH
 
 
+HOST_SRC = CSRC / "host_ops.cpp"
+
+
+def _host_ext_path() -> Path:
+    import sysconfig
+
+    return PKG_ROOT / "torch_gsplat_bridge_fast" / ("_gsb_host" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_host(verbose: bool = False) -> Path:
+    """Builds the native host runtime (_gsb_host, a torch C++ extension module)
+    in-tree with g++, linked to libgsplat_b200.so through an $ORIGIN rpath."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    lib = build(verbose)
+    out = _host_ext_path()
+    deps = [HOST_SRC, lib, REPO_ROOT / "include" / "gsplat_b200.h"]
+    if out.exists() and all(out.stat().st_mtime >= d.stat().st_mtime for d in deps):
+        return out
+    torch_inc = ce.include_paths()
+    torch_lib = str(Path(torch.__file__).resolve().parent / "lib")
+    cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    abi = int(torch.compiled_with_cxx11_abi())
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-w", str(HOST_SRC), "-o", str(out),
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_gsb_host", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           "-I", str(REPO_ROOT / "include"), "-I", sysconfig.get_paths()["include"], "-I", str(cuda_home / "include")]
+    for inc in torch_inc:
+        cmd += ["-I", inc]
+    cmd += ["-L", torch_lib, "-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python", "-lc10_cuda", "-ltorch_cuda",
+            "-L", str(lib.parent), "-lgsplat_b200", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed for {HOST_SRC.name}:\n{res.stderr[-4000:]}")
+    return out
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
+    print(build_host(verbose="-v" in sys.argv))

@@ -263,4 +263,96 @@ __device__ __forceinline__ void for_each_tile(float mx, float my, float a, float
   }
 }
 
+// Packed fp32 pairs for the sm_100 f32x2 instructions: one instruction applies
+// the same correctly rounded IEEE operation to both halves (no flush to zero,
+// like the scalar __fadd_rn/__fmul_rn/__fmaf_rn), so a packed result equals
+// the two scalar results bit for bit while taking one issue slot.
+struct F2 {
+  unsigned long long v;
+};
+__device__ __forceinline__ F2 f2(float lo, float hi) {
+  F2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ F2 f2(float x) { return f2(x, x); }
+__device__ __forceinline__ void split(F2 a, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a.v));
+}
+__device__ __forceinline__ F2 add2(F2 a, F2 b) {
+  F2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) {
+  F2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ F2 mul2(F2 a, F2 b) {
+  F2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
+  F2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+// power_at for two rows of one column (same PowerCol, dy = (lo, hi)).
+__device__ __forceinline__ F2 power_at2(F2 ta, F2 tb, F2 ch, F2 dy) {
+  return fma2(mul2(ch, dy), dy, fma2(tb, dy, ta));
+}
+
+// exp(x) = 2^(x log2 e) on the PTX ex2.approx.ftz.f32 instruction (relative
+// error about 2^-22 for the arguments met here: x in [ln(alpha_thr/op), 0] for
+// a visible splat, so no subnormal results), and 1/x on rcp.approx.ftz.f32.
+// Written as bare PTX so the compositing loops stay free of branches.
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Branch-free visibility select for the compositing loops, written as one PTX
+// block so the compiler cannot turn it into a branch around the exponential
+// (the value is computed unconditionally by the caller):
+//   live = T > t_thr;  vis = live && power <= 0 && power >= vis_thr
+//   returns vis ? value : 0, and sets last = live ? consumed : last.
+__device__ __forceinline__ float vis_select_fwd(float T, float t_thr, float power, float vis_thr, float value,
+                                                int consumed, int& last) {
+  float r;
+  asm("{\n\t.reg .pred pl, pv;\n\t"
+      "setp.gt.f32 pl, %2, %3;\n\t"
+      "setp.le.and.f32 pv, %4, 0f00000000, pl;\n\t"
+      "setp.ge.and.f32 pv, %4, %5, pv;\n\t"
+      "selp.f32 %0, %6, 0f00000000, pv;\n\t"
+      "selp.b32 %1, %7, %1, pl;\n\t}"
+      : "=f"(r), "+r"(last)
+      : "f"(T), "f"(t_thr), "f"(power), "f"(vis_thr), "f"(value), "r"(consumed));
+  return r;
+}
+// Backward form: vis = j < last && power <= 0 && power >= vis_thr; returns
+// vis ? value : 0 and pass = (vis && power < sat_thr) as 0/1.
+__device__ __forceinline__ float vis_select_bwd(int j, int last, float power, float vis_thr, float sat_thr,
+                                                float value, int& pass) {
+  float r;
+  asm("{\n\t.reg .pred pv, ps;\n\t"
+      "setp.lt.s32 pv, %2, %3;\n\t"
+      "setp.le.and.f32 pv, %4, 0f00000000, pv;\n\t"
+      "setp.ge.and.f32 pv, %4, %5, pv;\n\t"
+      "setp.lt.and.f32 ps, %4, %6, pv;\n\t"
+      "selp.f32 %0, %7, 0f00000000, pv;\n\t"
+      "selp.b32 %1, 1, 0, ps;\n\t}"
+      : "=f"(r), "=r"(pass)
+      : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  return r;
+}
+
 }  // namespace gsb

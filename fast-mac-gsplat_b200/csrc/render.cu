@@ -106,8 +106,14 @@ __device__ __forceinline__ float warp_reduce_scatter16(float (&v)[16], int lane)
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
+// A lane's 8 pixels are 4 packed pairs: pair q holds rows py0 + 4q and
+// py0 + 4q + 2 of the lane's column. The loop over a tile's records is free of
+// per-pixel branches: an invisible or finished pixel gets alpha = 0, which
+// leaves its colour and transmittance bit-for-bit unchanged (w = T*0 = 0,
+// T*(1-0) = T), so the 8 pixels' chains interleave. The results equal those of
+// a per-pixel `if (visible)` loop exactly.
 template <bool kSave>
-__global__ void __launch_bounds__(kWarps * 32, 3)
+__global__ void __launch_bounds__(kWarps * 32, 2)
     k_render_fwd_warp(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, float* __restrict__ out, float* __restrict__ final_T,
                       int32_t* __restrict__ last_idx, float4* __restrict__ pair_rec,
@@ -117,6 +123,7 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float4(*my)[3] = s_rec[warp];
   const int stride = gridDim.x * kWarps;
+  const F2 one = f2(1.0f), log2e = f2(kLog2e);
   for (int tile = blockIdx.x * kWarps + warp; tile < m.total_tiles; tile += stride) {
     const int start = __ldg(&toff[tile]);
     const int n = __ldg(&toff[tile + 1]) - start;
@@ -129,21 +136,28 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
     const int py0 = tc.ty * kTile + (lane >> 4);
     const float fx = (float)px + 0.5f;
     const float fy0 = (float)py0 + 0.5f;  // row i is at fy0 + 2i (exact)
-    // T[i] > T_thr marks a live pixel; pixels outside the image start dead (T = 0).
-    // last_idx (the number of list entries the pixel consumed, as the reference's
-    // per-pixel stop) is the saturation index + 1, or n for a pixel that never
-    // saturates; byte i&3 of last4[i>>2] records the saturation (n <= kShortMax < 256).
-    float T[kLanePx], cr[kLanePx], cg[kLanePx], cb[kLanePx];
-    uint32_t last4[2] = {0u, 0u};
+    // T > T_thr marks a live pixel; pixels outside the image start dead (T = 0).
+    // last[i] = entries the pixel consumed (the reference's per-pixel stop): the
+    // index + 1 of the last entry it met while still live.
+    F2 fy[kLanePx / 2], T[kLanePx / 2], cr[kLanePx / 2], cg[kLanePx / 2], cb[kLanePx / 2];
+    int last[kLanePx];
 #pragma unroll
-    for (int i = 0; i < kLanePx; ++i) {
-      T[i] = (px < m.W && py0 + 2 * i < m.H) ? 1.0f : 0.0f;
-      cr[i] = cg[i] = cb[i] = 0.0f;
+    for (int q = 0; q < kLanePx / 2; ++q) {
+      fy[q] = f2(fy0 + (float)(4 * q), fy0 + (float)(4 * q + 2));
+      const bool in_lo = px < m.W && py0 + 4 * q < m.H;
+      const bool in_hi = px < m.W && py0 + 4 * q + 2 < m.H;
+      T[q] = f2(in_lo ? 1.0f : 0.0f, in_hi ? 1.0f : 0.0f);
+      cr[q] = cg[q] = cb[q] = f2(0.0f);
+      last[2 * q] = last[2 * q + 1] = 0;
     }
     for (int base = 0; base < n; base += kWarpBatch) {
       bool live = false;
 #pragma unroll
-      for (int i = 0; i < kLanePx; ++i) live |= T[i] > m.T_thr;
+      for (int q = 0; q < kLanePx / 2; ++q) {
+        float tl, th;
+        split(T[q], tl, th);
+        live |= (tl > m.T_thr) | (th > m.T_thr);
+      }
       if (!__any_sync(kFullMask, live)) break;
       const int cnt = min(kWarpBatch, n - base);
       __syncwarp();
@@ -161,42 +175,56 @@ __global__ void __launch_bounds__(kWarps * 32, 3)
         }
       }
       __syncwarp();
-      if (live) {
-        for (int j = 0; j < cnt; ++j) {
-          const float4 p0 = my[j][0];
-          const float4 p1 = my[j][1];
-          const float4 p2 = my[j][2];
-          const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
+      if (!live) continue;
+      #pragma unroll 1
+      for (int j = 0; j < cnt; ++j) {
+        const float4 p0 = my[j][0];
+        const float4 p1 = my[j][1];
+        const float4 p2 = my[j][2];
+        const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
+        const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
+        const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x);
+        const int consumed = base + j + 1;
 #pragma unroll
-          for (int i = 0; i < kLanePx; ++i) {
-            const float power = power_at(pc, __fsub_rn(fy0 + (float)(2 * i), p0.y));
-            if (T[i] > m.T_thr && power <= 0.0f && power >= p2.z) {
-              const float alpha = fminf(m.max_alpha, p1.y * __expf(power));
-              const float w = T[i] * alpha;
-              cr[i] = fmaf(w, p1.z, cr[i]);
-              cg[i] = fmaf(w, p1.w, cg[i]);
-              cb[i] = fmaf(w, p2.x, cb[i]);
-              T[i] *= 1.0f - alpha;
-              if (T[i] <= m.T_thr)  // saturated: the pixel consumed entries [0, base + j]
-                last4[i >> 2] |= (uint32_t)(base + j + 1) << (8 * (i & 3));
-            }
-          }
+        for (int q = 0; q < kLanePx / 2; ++q) {
+          const F2 power = power_at2(ta, tb, ch, sub2(fy[q], mu_y));
+          float pl, ph, tl, th, xl, xh;
+          split(power, pl, ph);
+          split(T[q], tl, th);
+          split(mul2(power, log2e), xl, xh);
+          const float al = vis_select_fwd(tl, m.T_thr, pl, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xl)), consumed,
+                                          last[2 * q]);
+          const float ah = vis_select_fwd(th, m.T_thr, ph, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xh)), consumed,
+                                          last[2 * q + 1]);
+          const F2 alpha = f2(al, ah);
+          const F2 w = mul2(T[q], alpha);
+          cr[q] = fma2(w, col_r, cr[q]);
+          cg[q] = fma2(w, col_g, cg[q]);
+          cb[q] = fma2(w, col_b, cb[q]);
+          T[q] = mul2(T[q], sub2(one, alpha));
         }
       }
     }
     if (px < m.W) {
 #pragma unroll
-      for (int i = 0; i < kLanePx; ++i) {
-        const int py = py0 + 2 * i;
-        if (py < m.H) {
-          const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
-          out[3 * pix + 0] = fmaf(T[i], m.bg_r, cr[i]);
-          out[3 * pix + 1] = fmaf(T[i], m.bg_g, cg[i]);
-          out[3 * pix + 2] = fmaf(T[i], m.bg_b, cb[i]);
-          if (kSave) {
-            const int sat = (int)((last4[i >> 2] >> (8 * (i & 3))) & 0xffu);
-            final_T[pix] = T[i];
-            last_idx[pix] = sat ? sat : (1.0f > m.T_thr ? n : 0);
+      for (int q = 0; q < kLanePx / 2; ++q) {
+        float tv[2], rv[2], gv[2], bv[2];
+        split(T[q], tv[0], tv[1]);
+        split(cr[q], rv[0], rv[1]);
+        split(cg[q], gv[0], gv[1]);
+        split(cb[q], bv[0], bv[1]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int py = py0 + 4 * q + 2 * h;
+          if (py < m.H) {
+            const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
+            out[3 * pix + 0] = fmaf(tv[h], m.bg_r, rv[h]);
+            out[3 * pix + 1] = fmaf(tv[h], m.bg_g, gv[h]);
+            out[3 * pix + 2] = fmaf(tv[h], m.bg_b, bv[h]);
+            if (kSave) {
+              final_T[pix] = tv[h];
+              last_idx[pix] = last[2 * q + h];
+            }
           }
         }
       }
@@ -299,6 +327,47 @@ __device__ __forceinline__ void pixel_vjp(const Meta& m, float dy, float power, 
   S[5] = fmaf(gg, wc, S[5]);
   S[6] = fmaf(gb, wc, S[6]);
   gT = alpha * dot_gc + (1.0f - alpha) * gT;
+  T_cur = T_prev;
+}
+
+// pixel_vjp for two pixels of one column at once (packed pair arithmetic),
+// free of branches: a pixel that does not see the splat (vis false) gets
+// alpha = 0 and zero gradient terms, which leaves its (T_cur, gT) unchanged
+// (T_cur * rcp(1 - 0) = T_cur; gT + 0 * d = gT) and adds nothing to S.
+// gT advances as gT + alpha (dot_gc - gT), the same value as
+// alpha dot_gc + (1 - alpha) gT up to rounding. S[t] holds per-half partial sums.
+__device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int last_h, F2 dy, float pl, float ph,
+                                           float op, float vis_thr, float sat_thr, F2 col_r, F2 col_g, F2 col_b,
+                                           F2 gr, F2 gg, F2 gb, F2& T_cur, F2& gT, F2 (&S)[7]) {
+  float xl, xh;
+  split(mul2(f2(pl, ph), f2(kLog2e)), xl, xh);
+  const float el = ex2_approx(xl), eh = ex2_approx(xh);
+  const float rl = op * el, rh = op * eh;
+  int pass_l, pass_h;
+  const float al = vis_select_bwd(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l);
+  const float ah = vis_select_bwd(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h);
+  const F2 alpha = f2(al, ah);
+  float oml, omh;
+  split(sub2(f2(1.0f), alpha), oml, omh);
+  const F2 T_prev = mul2(T_cur, f2(rcp_approx(fmaxf(oml, m.eps)), rcp_approx(fmaxf(omh, m.eps))));
+  const F2 dot_gc = fma2(gb, col_b, fma2(gg, col_g, mul2(gr, col_r)));
+  const F2 d = sub2(dot_gc, gT);
+  const F2 g_alpha = mul2(T_prev, d);
+  const F2 wc = mul2(T_prev, alpha);
+  float gal, gah;
+  split(g_alpha, gal, gah);
+  // raw < max_alpha (power below the saturation log-threshold) passes g_alpha to raw.
+  const F2 gp = f2(pass_l ? gal * rl : 0.0f, pass_h ? gah * rh : 0.0f);
+  const F2 ge = f2(pass_l ? gal * el : 0.0f, pass_h ? gah * eh : 0.0f);
+  S[0] = add2(S[0], gp);
+  const F2 gpdy = mul2(gp, dy);
+  S[1] = add2(S[1], gpdy);
+  S[2] = fma2(gpdy, dy, S[2]);
+  S[3] = add2(S[3], ge);
+  S[4] = fma2(gr, wc, S[4]);
+  S[5] = fma2(gg, wc, S[5]);
+  S[6] = fma2(gb, wc, S[6]);
+  gT = fma2(alpha, d, gT);
   T_cur = T_prev;
 }
 
@@ -414,41 +483,58 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
       const int py0 = tc.ty * kTile + (lane >> 4);
       const float fx = (float)px + 0.5f;
       const float fy0 = (float)py0 + 0.5f;
-      float gr[kLanePx], gg[kLanePx], gb[kLanePx], Tc[kLanePx], gT[kLanePx];
+      // Pair q holds rows py0 + 4q and py0 + 4q + 2 (see the forward kernel).
+      F2 fy[kLanePx / 2], gr[kLanePx / 2], gg[kLanePx / 2], gb[kLanePx / 2], Tc[kLanePx / 2], gT[kLanePx / 2];
       int last[kLanePx];
       int lmax = 0;
 #pragma unroll
-      for (int i = 0; i < kLanePx; ++i) {
-        const int p = ((lane >> 4) + 2 * i) * kTile + (lane & 15);
-        gr[i] = B.grad[3 * p + 0];
-        gg[i] = B.grad[3 * p + 1];
-        gb[i] = B.grad[3 * p + 2];
-        Tc[i] = B.T[p];
-        last[i] = min(B.last[p], n);
-        gT[i] = gr[i] * m.bg_r + gg[i] * m.bg_g + gb[i] * m.bg_b;
-        lmax = max(lmax, last[i]);
+      for (int q = 0; q < kLanePx / 2; ++q) {
+        fy[q] = f2(fy0 + (float)(4 * q), fy0 + (float)(4 * q + 2));
+        const int pl = ((lane >> 4) + 4 * q) * kTile + (lane & 15);
+        const int ph = pl + 2 * kTile;
+        gr[q] = f2(B.grad[3 * pl + 0], B.grad[3 * ph + 0]);
+        gg[q] = f2(B.grad[3 * pl + 1], B.grad[3 * ph + 1]);
+        gb[q] = f2(B.grad[3 * pl + 2], B.grad[3 * ph + 2]);
+        Tc[q] = f2(B.T[pl], B.T[ph]);
+        gT[q] = fma2(gb[q], f2(m.bg_b), fma2(gg[q], f2(m.bg_g), mul2(gr[q], f2(m.bg_r))));
+        last[2 * q] = min(B.last[pl], n);
+        last[2 * q + 1] = min(B.last[ph], n);
+        lmax = max(lmax, max(last[2 * q], last[2 * q + 1]));
       }
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
+      #pragma unroll 1
       for (int j = tile_last - 1; j >= 0; --j) {
         const float4 p0 = B.rec[j][0];
         const float4 p1 = B.rec[j][1];
         const float4 p2 = B.rec[j][2];
         const float dx = __fsub_rn(fx, p0.x);
         const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
-        float S[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        bool any = false;
+        const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
+        const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x);
+        F2 S[7];
 #pragma unroll
-        for (int i = 0; i < kLanePx; ++i) {
-          const float dy = __fsub_rn(fy0 + (float)(2 * i), p0.y);
-          const float power = power_at(pc, dy);
-          if (j < last[i] && power <= 0.0f && power >= p2.z) {
-            pixel_vjp(m, dy, power, p1, p2, gr[i], gg[i], gb[i], Tc[i], gT[i], S);
-            any = true;
-          }
+        for (int t = 0; t < 7; ++t) S[t] = f2(0.0f);
+#pragma unroll
+        for (int q = 0; q < kLanePx / 2; ++q) {
+          const F2 dy = sub2(fy[q], mu_y);
+          const F2 power = power_at2(ta, tb, ch, dy);
+          float pl, ph;
+          split(power, pl, ph);
+          pixel_vjp2(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, p1.y, p2.z, p2.w, col_r, col_g, col_b, gr[q],
+                     gg[q], gb[q], Tc[q], gT[q], S);
         }
-        if (__any_sync(kFullMask, any)) {
+        // Every binned splat reaches some pixel of its tile, so the reduction runs
+        // unconditionally; a zero total issues no atomic.
+        {
+          float Sv[7];
+#pragma unroll
+          for (int t = 0; t < 7; ++t) {
+            float lo, hi;
+            split(S[t], lo, hi);
+            Sv[t] = lo + hi;
+          }
           float v[16];
-          vjp_expand(S, dx, p0.z, p0.w, p1.x, v);
+          vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
           const float total = warp_reduce_scatter16(v, lane);
           int gi = B.ids[j];
           if ((unsigned)gi >= (unsigned)m.BG) {
@@ -456,7 +542,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
             gi = -1;
           }
           const int comp = lane >> 1;
-          if (!(lane & 1) && comp < kGradComps && gi >= 0)
+          if (!(lane & 1) && comp < kGradComps && gi >= 0 && total != 0.0f)
             atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + comp, total);
         }
       }

@@ -206,25 +206,35 @@ def _check_3d_inputs(means3d: Tensor, scales: Tensor, quats: Tensor, opacities: 
 # Native pipeline helpers
 # ---------------------------------------------------------------------------
 _tls = threading.local()
-_kernel_timer = None
+_host_mod = None
 
 
-def set_kernel_timer(timer) -> None:
-    """Installs an object with begin(name)/end(name) methods that bench code uses
-    to bracket each C-ABI call with CUDA events on the launching stream
-    (names: bin_prepare, bin_emit, render_fwd, render_bwd, unsort). None removes it."""
-    global _kernel_timer
-    _kernel_timer = timer
+def _host():
+    """The native host runtime (_gsb_host, built in-tree next to libgsplat_b200.so)."""
+    global _host_mod
+    if _host_mod is None:
+        try:
+            from . import _gsb_host as mod
+        except ImportError as e:
+            raise RuntimeError(
+                "gsplat_b200 native host module _gsb_host is missing or does not load. Build it first "
+                "(python fast-mac-gsplat_b200/build_native.py or __graft_entry__.build())."
+            ) from e
+        _host_mod = mod
+    return _host_mod
 
 
-def _timed(name: str, fn):
-    t = _kernel_timer
-    if t is None:
-        return fn()
-    t.begin(name)
-    rc = fn()
-    t.end(name)
-    return rc
+def set_kernel_timer(enabled: bool) -> None:
+    """Turns per-phase CUDA-event timing of the autograd path on or off (phases:
+    bin_prepare, bin_emit, render_fwd, render_bwd, unsort; events on the
+    launching stream). Read the times with kernel_times()."""
+    _host().set_phase_timing(bool(enabled))
+
+
+def kernel_times() -> Dict[str, list]:
+    """Milliseconds of each timed phase since set_kernel_timer(True), in call
+    order per phase name (synchronizes); clears the record."""
+    return dict(_host().take_phase_times())
 
 
 def _debug_checks() -> bool:
@@ -301,6 +311,8 @@ def _defer_error_check(status: Tensor, stream) -> None:
 def check_device_errors(_synced_stream=None) -> None:
     """Raises RuntimeError if any earlier call's kernels reported a device-side
     error (bounded-wait timeout, pair overflow, index out of bounds)."""
+    if _synced_stream is None and _host_mod is not None:
+        _host_mod.check_device_errors()
     with _error_lock:
         slots = _error_ring
         if slots is None:
@@ -360,9 +372,6 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     # Locals keep every (possibly copied) input alive until the launch returns.
     m2 = _aligned(means2d_b, 8)
     q2, c2, o2, d2 = (t.contiguous() for t in (conics_b, colors_b, opacities_b, depths_b))
-    timer = _kernel_timer
-    if timer is not None:
-        timer.begin("bin_prepare")
     N.check(L.gsb_bin_count(meta, N.ptr(m2), N.ptr(q2), N.ptr(o2), N.ptr(d2), N.ptr(st.status), N.ptr(ws),
                             ws_bytes, stream), "gsb_bin_count")
     # The pair total is read as soon as the count kernel is done, while the depth
@@ -377,8 +386,6 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     N.check(L.gsb_bin_sort_scan(meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm),
                                 N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes,
                                 stream), "gsb_bin_sort_scan")
-    if timer is not None:
-        timer.end("bin_prepare")
     counted.synchronize()
     check_device_errors(stream)  # earlier calls' copies on this stream are complete now
     P = int(total_host[0])
@@ -391,31 +398,11 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     st.tile_offsets = torch.empty(T + 1, dtype=torch.int32, device=dev)
     st.keys = torch.empty(P, dtype=torch.int64, device=dev)
     ws2 = torch.empty(max(ws2_bytes, 1), dtype=torch.uint8, device=dev)
-    N.check(
-        _timed("bin_emit", lambda: L.gsb_bin_emit(
-            meta, N.ptr(st.rec), N.ptr(st.pair_offsets), P, N.ptr(st.keys), N.ptr(st.binned_ids),
-            N.ptr(st.tile_offsets), N.ptr(st.status), N.ptr(ws2), ws2_bytes, stream)),
-        "gsb_bin_emit",
-    )
+    N.check(L.gsb_bin_emit(meta, N.ptr(st.rec), N.ptr(st.pair_offsets), P, N.ptr(st.keys), N.ptr(st.binned_ids),
+                           N.ptr(st.tile_offsets), N.ptr(st.status), N.ptr(ws2), ws2_bytes, stream), "gsb_bin_emit")
     if _debug_checks():
         _read_status(st.status)
     return st
-
-
-def _check_overflow(st: _BinState, config: RasterConfig) -> None:
-    """Reference overflow error when the fallback is disabled
-    (…/v8_project3d/…/rasterize.py:756-760, 902-906)."""
-    if config.enable_overflow_fallback:
-        return
-    L = N.load()
-    dev = st.status.device
-    N.check(L.gsb_tile_stats(st.meta, N.ptr(st.tile_offsets), N.ptr(st.status), N.stream_ptr(dev)), "gsb_tile_stats")
-    vals = _read_status(st.status)
-    if vals[N.GSB_STATUS_MAX_TILE_COUNT] > config.pair_cap:
-        raise RuntimeError(
-            f"Tile overflow detected with max_fast_pairs={config.pair_cap}. "
-            "Enable overflow fallback or increase the runtime cap."
-        )
 
 
 def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: bool):
@@ -431,12 +418,9 @@ def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: boo
         pair_rec = torch.empty((max(st.P, 1), N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     cur = torch.cuda.current_stream(dev)
-    N.check(
-        _timed("render_fwd", lambda: L.gsb_render_forward(
-            st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out), N.ptr(final_T),
-            N.ptr(last_idx), N.ptr(pair_rec), N.ptr(st.status), N.ptr(ws), ws_bytes, cur.cuda_stream)),
-        "gsb_render_forward",
-    )
+    N.check(L.gsb_render_forward(st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(out),
+                                 N.ptr(final_T), N.ptr(last_idx), N.ptr(pair_rec), N.ptr(st.status), N.ptr(ws),
+                                 ws_bytes, cur.cuda_stream), "gsb_render_forward")
     if _debug_checks():
         _read_status(st.status)
     else:
@@ -444,68 +428,48 @@ def _render_forward(st: _BinState, config: RasterConfig, B: int, save_state: boo
     return out, final_T, last_idx, pair_rec
 
 
+# eps and max_alpha are fixed in the reference's meta (root rasterize.py:135-136).
+_EPS = 1e-8
+_MAX_ALPHA = 0.99
+
+
+def _host_args(config: RasterConfig):
+    bg = [float(c) for c in config.background]
+    return (config.height, config.width, float(config.alpha_threshold), float(config.transmittance_threshold), bg,
+            _EPS, _MAX_ALPHA)
+
+
 class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
     """Training path (…/v8_project3d/…/rasterize.py:691-852; root rasterize.py:26-106).
     Saves the per-pixel final transmittance and last-contributor index instead of
-    per-tile stop counts; backward un-sorts into input order; depth grad is zero."""
+    per-tile stop counts; backward un-sorts into input order; depth grad is zero.
+    Each direction is one call into the native host runtime (_gsb_host)."""
 
     @staticmethod
     def forward(ctx, means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig):
-        B, G = means2d_b.shape[:2]
-        st = _bin(config, means2d_b, conics_b, colors_b, opacities_b, depths_b)
-        _check_overflow(st, config)
-        out, final_T, last_idx, pair_rec = _render_forward(st, config, B, save_state=True)
-        ctx.save_for_backward(st.perm, st.rec, st.tile_offsets, st.binned_ids, final_T, last_idx, pair_rec,
-                              st.status)
-        ctx.meta = st.meta
-        ctx.shape = (B, G)
+        cap = -1 if config.enable_overflow_fallback else config.pair_cap
+        args = _host_args(config)
+        res = _host().forward(means2d_b, conics_b, colors_b, opacities_b, depths_b, *args, True, cap)
+        out, perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status = res[:9]
+        ctx.save_for_backward(perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status)
+        ctx.host_args = args
         ctx.depths_shape = depths_b.shape
         return out
 
     @staticmethod
     def backward(ctx, grad_out: Tensor):
-        perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status = ctx.saved_tensors
-        L = N.load()
-        B, G = ctx.shape
-        dev = rec.device
-        cur = torch.cuda.current_stream(dev)
-        stream = cur.cuda_stream
-        g = _aligned(grad_out.to(torch.float32))
-        ws_bytes = int(L.gsb_render_workspace_size(ctx.meta))
-        grad_rec = torch.empty((B * G, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-        N.check(
-            _timed("render_bwd", lambda: L.gsb_render_backward(
-                ctx.meta, N.ptr(rec), N.ptr(tile_offsets), N.ptr(binned_ids), N.ptr(final_T), N.ptr(last_idx),
-                N.ptr(pair_rec), N.ptr(g), N.ptr(grad_rec), N.ptr(status), N.ptr(ws), ws_bytes, stream)),
-            "gsb_render_backward",
-        )
         need = ctx.needs_input_grad
-        g_means = torch.empty((B, G, 2), dtype=torch.float32, device=dev) if need[0] else None
-        g_conics = torch.empty((B, G, 3), dtype=torch.float32, device=dev) if need[1] else None
-        g_colors = torch.empty((B, G, 3), dtype=torch.float32, device=dev) if need[2] else None
-        g_opac = torch.empty((B, G), dtype=torch.float32, device=dev) if need[3] else None
-        N.check(
-            _timed("unsort", lambda: L.gsb_unsort_grads(
-                ctx.meta, N.ptr(perm), N.ptr(grad_rec), N.ptr(g_means), N.ptr(g_conics), N.ptr(g_colors),
-                N.ptr(g_opac), stream)),
-            "gsb_unsort_grads",
-        )
-        if _debug_checks():
-            _read_status(status)
-        else:
-            _defer_error_check(status, cur)
+        g_means, g_conics, g_colors, g_opac = _host().backward(*ctx.saved_tensors, grad_out, *ctx.host_args,
+                                                              [bool(x) for x in need[:4]])
+        dev = grad_out.device
         g_depths = torch.zeros(ctx.depths_shape, dtype=torch.float32, device=dev) if need[4] else None
         return g_means, g_conics, g_colors, g_opac, g_depths, None
 
 
 def _rasterize_chunk_eval(means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig) -> Tensor:
     """No-grad path (…/v8_project3d/…/rasterize.py:855-907): no saved state."""
-    B = means2d_b.shape[0]
-    st = _bin(config, means2d_b, conics_b, colors_b, opacities_b, depths_b)
-    _check_overflow(st, config)
-    out, _, _, _ = _render_forward(st, config, B, save_state=False)
-    return out
+    cap = -1 if config.enable_overflow_fallback else config.pair_cap
+    return _host().forward(means2d_b, conics_b, colors_b, opacities_b, depths_b, *_host_args(config), False, cap)[0]
 
 
 def _should_use_training_path(means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor) -> bool:

@@ -249,3 +249,27 @@ def test_deferred_device_error_is_reported(monkeypatch):
     with pytest.raises(RuntimeError, match="index out of bounds"):
         tgb.check_device_errors()
     tgb.check_device_errors()  # reported once
+
+
+def test_host_runtime_reports_deferred_backward_error(monkeypatch):
+    """The native host runtime queues its device-error copy the same way: an
+    out-of-range splat id met by the backward kernel (which checks it and skips
+    the access) is raised by check_device_errors(), once."""
+    from torch_gsplat_bridge_fast import rasterize as R
+
+    monkeypatch.setenv("GSPLAT_B200_CHECK", "0")
+    tgb.check_device_errors()
+    s = config_2d("c0", seed=0)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    host = R._host()
+    res = host.forward(*(t.to(DEV) for t in s.tensors()), *R._host_args(cfg), True, -1)
+    out, perm, rec, tile_offsets, ids, final_T, last_idx, pair_rec, status = res[:9]
+    torch.cuda.synchronize()
+    tgb.check_device_errors()  # the forward itself was clean
+    ids[0] = s.B * s.G + 5
+    host.backward(perm, rec, tile_offsets, ids, final_T, last_idx, pair_rec, status, torch.ones_like(out),
+                  *R._host_args(cfg), [True] * 4)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="index out of bounds"):
+        tgb.check_device_errors()
+    tgb.check_device_errors()
