@@ -9,6 +9,10 @@ tiled_scan_work). Multi-GPU: one process per GPU (torchrun), each rank renders i
 own view (seed = rank), no data-path collective: weak scaling.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+--config c4 runs the shared-3D-scene step instead (G=2^20 Gaussians, one 1080p
+camera per rank): projection, binning, compositing fwd+bwd, projection VJP, then
+the per-Gaussian gradients summed across ranks with NCCL all-reduce.
 """
 from __future__ import annotations
 
@@ -41,7 +45,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3"))
+    ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3", "c4"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -411,6 +415,122 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_shared3d(args):
+    import torch.distributed as dist
+
+    import torch_gsplat_bridge_fast as tgb
+    from torch_gsplat_bridge_fast import _native
+    from torch_gsplat_bridge_fast.distributed import SharedGradAllReduce
+    from torch_gsplat_bridge_fast.rasterize import _bin
+    from workloads import config_3d, grad_image
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    sc = config_3d(seed=0)  # the same scene on every rank
+    view = rank % sc.camera_to_world.shape[0]
+    H, W, G = sc.height, sc.width, sc.means3d.shape[0]
+    cfg = tgb.RasterConfig(H, W)
+    fx, fy, cx, cy = (float(v) for v in sc.camera_params[view])
+    c2w = sc.camera_to_world[view].to(dev)
+    params = [t.to(dev).requires_grad_(True) for t in (sc.means3d, sc.scales, sc.quats, sc.opacities, sc.colors)]
+    gimg = grad_image(1, H, W, seed=2000 + rank)[0].to(dev)
+    with torch.no_grad():
+        m2, q2, o2, d2 = tgb.project_pinhole_gaussians(*params[:4], fx, fy, cx, cy, camera_to_world=c2w)
+        st = _bin(cfg, m2[None].contiguous(), q2[None].contiguous(), params[4][None].contiguous(),
+                  o2[None].contiguous(), d2[None].contiguous())
+        E = tiled_work(st.tile_offsets, 1, H, W)
+        P = st.P
+        del st
+    reducer = SharedGradAllReduce(params) if world > 1 else None
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step(timing=None):
+        for p in params:
+            p.grad = None
+        img = tgb.rasterize_pinhole_gaussians(*params, fx, fy, cx, cy, camera_to_world=c2w, config=cfg)
+        img.backward(gimg)
+        if reducer is not None:
+            if timing is not None:
+                timing[0].record()
+            reducer()
+            if timing is not None:
+                timing[1].record()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    L = _native.load()
+    step_ms, ar_ms = [], []
+    with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = L.gsb_kernel_launches()
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step((a0, a1))
+            e1.record()
+            e1.synchronize()
+            step_ms.append(e0.elapsed_time(e1))
+            if reducer is not None:
+                ar_ms.append(a0.elapsed_time(a1))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        launches = L.gsb_kernel_launches() - launches0
+    clock = clocks.summary()
+    ms = statistics.mean(step_ms)
+    stats = torch.tensor([ms, float(E)], device=dev, dtype=torch.float64)
+    if world > 1:
+        mx = stats[:1].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = stats[1:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_max, E_total = float(mx.item()), float(tot.item())
+    else:
+        ms_max, E_total = ms, float(E)
+    allreduce = None
+    if reducer is not None:
+        t = statistics.mean(ar_ms) * 1e-3
+        nbytes = reducer.bytes
+        allreduce = {"bytes": nbytes, "avg_ms": round(t * 1e3, 4), "algbw_GBs": round(nbytes / t / 1e9, 1),
+                     "busbw_GBs": round(2 * (world - 1) / world * nbytes / t / 1e9, 1),
+                     "buckets": len(reducer.buckets)}
+    if rank == 0:
+        line = {
+            "metric": "Gsplat-px evals/s, c4 shared-3D fwd+bwd + gradient all-reduce",
+            "value": round(E_total / (ms_max * 1e-3) / 1e9, 3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms_max, 4),
+            "ms_per_step_median": round(statistics.median(step_ms), 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp32",
+            "data": "synthetic (seeded; BASELINE c4 distributions)",
+            "config": {"workload": f"c4: G={G} shared 3D Gaussians, one {W}x{H} camera per rank (view = rank mod 8)",
+                       "pairs_rank0_view": P, "evals_rank0_view": E, "evals_all_ranks": E_total,
+                       "l2": "flushed (256 MB write) between steps",
+                       "parallelism": f"{world} rank(s); per-Gaussian grads (14 floats) summed with NCCL all-reduce"},
+            "gpu_launches": int(launches),
+            "allreduce": allreduce,
+            "clocks": clock,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -419,6 +539,9 @@ def main():
     if not torch.cuda.is_available():
         print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
         sys.exit(1)
+    if args.config == "c4":
+        run_shared3d(args)
+        return
     run_b200(args)
 
 
