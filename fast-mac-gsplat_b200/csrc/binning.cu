@@ -25,27 +25,178 @@ constexpr unsigned long long kScanInc = 2ull << 62;
 constexpr unsigned long long kScanMask = (1ull << 62) - 1ull;
 constexpr int kLookWin = 8;  // predecessors read per look-back step
 
+// One splat's candidate tiles (its snugbox in tiles, row-major) and the
+// constants of the exact ellipse-rectangle test. The two divisions of
+// ellipse_rect do not depend on the tile and are taken once here; the test
+// then evaluates the same correctly rounded operation sequence per tile.
+struct SplatTiles {
+  float mx, my, a, b, c, tau, kc, ka;
+  int tx0, ty0, w, n;  // candidates [tx0, tx0 + w) x [ty0, ty0 + n / w); n = 0: none
+};
+
+__device__ __forceinline__ SplatTiles splat_tiles(float mx, float my, float a, float b, float c, float op,
+                                                  const Meta& m) {
+  SplatTiles s;
+  s.mx = mx, s.my = my, s.a = a, s.b = b, s.c = c;
+  s.tau = 0.0f, s.kc = 0.0f, s.ka = 0.0f;
+  s.tx0 = 0, s.ty0 = 0, s.w = 1, s.n = 0;
+  float tau;
+  if (!support_tau(op, m.alpha_thr, m.eps, &tau)) return s;
+  const PixBox bb = snugbox(mx, my, a, b, c, tau, m.W, m.H, m.eps);
+  if (bb.x0 > bb.x1 || bb.y0 > bb.y1) return s;
+  s.tau = tau;
+  s.tx0 = bb.x0 / kTile;
+  s.ty0 = bb.y0 / kTile;
+  s.w = bb.x1 / kTile - s.tx0 + 1;
+  s.n = s.w * (bb.y1 / kTile - s.ty0 + 1);
+  if (c > 1e-8f) s.kc = -__fdiv_rn(b, c);
+  if (a > 1e-8f) s.ka = -__fdiv_rn(b, a);
+  return s;
+}
+
+// ellipse_rect of tile (tx, ty) with the hoisted constants (same decisions).
+__device__ __forceinline__ bool tile_hit(const SplatTiles& s, int tx, int ty, const Meta& m) {
+  const float rx0 = tile_rx0(tx), rx1 = tile_rx1(tx, m.W);
+  const float ry0 = tile_rx0(ty), ry1 = tile_rx1(ty, m.H);
+  if (s.mx >= rx0 && s.mx <= rx1 && s.my >= ry0 && s.my <= ry1) return true;
+  const float dx0 = __fsub_rn(rx0, s.mx);
+  const float dx1 = __fsub_rn(rx1, s.mx);
+  const float dy0 = __fsub_rn(ry0, s.my);
+  const float dy1 = __fsub_rn(ry1, s.my);
+  float qmin = __int_as_float(0x7f800000);
+  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx0, dy0));
+  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx0, dy1));
+  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx1, dy0));
+  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx1, dy1));
+  if (s.c > 1e-8f) {
+    float dy = fminf(fmaxf(__fmul_rn(s.kc, dx0), dy0), dy1);
+    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx0, dy));
+    dy = fminf(fmaxf(__fmul_rn(s.kc, dx1), dy0), dy1);
+    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx1, dy));
+  }
+  if (s.a > 1e-8f) {
+    float dx = fminf(fmaxf(__fmul_rn(s.ka, dy0), dx0), dx1);
+    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx, dy0));
+    dx = fminf(fmaxf(__fmul_rn(s.ka, dy1), dx0), dx1);
+    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx, dy1));
+  }
+  return qmin <= s.tau;
+}
+
+// Row of candidate `local` (0 <= local < n) of a splat whose box is w tiles wide.
+__device__ __forceinline__ int cand_row(int local, int w) {
+  int r = (int)(((float)local + 0.5f) * __frcp_rn((float)w));
+  while (r > 0 && r * w > local) --r;
+  while ((r + 1) * w <= local) ++r;
+  return r;
+}
+
+// Per-warp shared state of warp_tiles.
+struct WarpTilesSmem {
+  SplatTiles t[32];
+  int incl[32];  // inclusive scan of the candidate counts
+  int hits[32];  // running hit count per owner
+};
+
+// Visits every candidate tile of the warp's 32 splats (lane j owns splat j),
+// spread evenly over the lanes: round r tests candidates 32r .. 32r+31 of the
+// warp's concatenated row-major candidate lists, so a warp costs its total
+// candidate count / 32 rounds however unevenly the splats are sized. Hits are
+// numbered per owner in row-major tile order (the reference's loop order):
+// visit(owner, tx, ty, slot) runs for each hit with slot = its index in the
+// owner's list. On return sm.hits[j] is splat j's hit count.
+template <typename Visit>
+__device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m, WarpTilesSmem& sm,
+                                           Visit&& visit) {
+  const int lane = threadIdx.x & 31;
+  long long incl = mine.n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long y = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const long long total = __shfl_sync(kFullMask, incl, 31);
+  sm.hits[lane] = 0;
+  if (total > 0x7fffffffll) {
+    // Beyond int range for the warp: each lane walks its own candidates.
+    int cnt = 0;
+    for (int local = 0; local < mine.n; ++local) {
+      const int row = cand_row(local, mine.w);
+      const int tx = mine.tx0 + (local - row * mine.w), ty = mine.ty0 + row;
+      if (tile_hit(mine, tx, ty, m)) visit(lane, tx, ty, cnt++);
+    }
+    sm.hits[lane] = cnt;
+    __syncwarp();
+    return;
+  }
+  sm.t[lane] = mine;
+  sm.incl[lane] = (int)incl;
+  __syncwarp();
+  for (int base = 0; base < (int)total; base += 32) {
+    const int k = base + lane;
+    int owner = -1, tx = 0, ty = 0;
+    bool hit = false;
+    if (k < (int)total) {
+      int lo = 0, hi = 31;  // first owner whose inclusive end exceeds k
+#pragma unroll
+      for (int step = 0; step < 5; ++step) {
+        const int mid = (lo + hi) >> 1;
+        if (sm.incl[mid] > k) hi = mid;
+        else lo = mid + 1;
+      }
+      owner = lo;
+      const SplatTiles& s = sm.t[owner];
+      const int local = k - (owner ? sm.incl[owner - 1] : 0);
+      const int row = cand_row(local, s.w);
+      tx = s.tx0 + (local - row * s.w);
+      ty = s.ty0 + row;
+      hit = tile_hit(s, tx, ty, m);
+    }
+    // Owners are non-decreasing across lanes: segments of equal owner.
+    const int prev = __shfl_up_sync(kFullMask, owner, 1);
+    const unsigned starts = __ballot_sync(kFullMask, lane == 0 || owner != prev);
+    const unsigned hits = __ballot_sync(kFullMask, hit);
+    const unsigned le = (lane == 31) ? 0xffffffffu : ((2u << lane) - 1u);
+    const int seg0 = 31 - __clz(starts & le);
+    const unsigned above = starts & ~le;
+    const unsigned seg = (above ? ((1u << (__ffs(above) - 1)) - 1u) : 0xffffffffu) & ~((1u << seg0) - 1u);
+    const int before = __popc(hits & seg & ((1u << lane) - 1u));
+    const int base_slot = owner >= 0 ? sm.hits[owner] : 0;
+    __syncwarp();
+    if (lane == seg0 && owner >= 0) sm.hits[owner] = base_slot + __popc(hits & seg);
+    if (hit) visit(owner, tx, ty, base_slot + before);
+    __syncwarp();
+  }
+}
+
 // Per splat in input order: depth-sort key (view in the high word) and the
-// exact number of tiles its support ellipse touches.
+// exact number of tiles its support ellipse touches; the pair total is added
+// into status words 4-5 (64-bit) for the host's early read.
 __global__ void __launch_bounds__(256)
     k_prepare(Meta m, const float2* __restrict__ means2d, const float* __restrict__ conics,
               const float* __restrict__ opacities, const float* __restrict__ depths,
               uint64_t* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
               uint32_t* __restrict__ counts, uint32_t* __restrict__ status) {
+  __shared__ WarpTilesSmem s_warp[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= m.BG) return;
-  const int b = i / m.G;
-  sort_keys[i] = ((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]);
-  sort_vals[i] = (uint32_t)i;
-  const float2 mu = means2d[i];
-  const float a = conics[3 * i + 0], bq = conics[3 * i + 1], c = conics[3 * i + 2];
-  uint32_t n = 0;
-  for_each_tile(mu.x, mu.y, a, bq, c, opacities[i], m, [&](int, int) { ++n; });
-  counts[i] = n;
-  // Pair total (64-bit, order-independent integer sum) for the host's early read.
-  const unsigned long long wsum = __reduce_add_sync(__activemask(), n);
-  if ((threadIdx.x & 31) == __ffs(__activemask()) - 1 && wsum)
-    atomicAdd(reinterpret_cast<unsigned long long*>(status + GSB_STATUS_PAIR_TOTAL64), wsum);
+  const bool valid = i < m.BG;
+  SplatTiles t = splat_tiles(0.f, 0.f, 0.f, 0.f, 0.f, 0.f, m);
+  if (valid) {
+    const int b = i / m.G;
+    sort_keys[i] = ((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]);
+    sort_vals[i] = (uint32_t)i;
+    const float2 mu = means2d[i];
+    t = splat_tiles(mu.x, mu.y, conics[3 * i + 0], conics[3 * i + 1], conics[3 * i + 2], opacities[i], m);
+  }
+  WarpTilesSmem& sm = s_warp[warp];
+  warp_tiles(t, m, sm, [](int, int, int, int) {});
+  const uint32_t n = valid ? (uint32_t)sm.hits[lane] : 0u;
+  if (valid) counts[i] = n;
+  unsigned long long wsum = n;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(kFullMask, wsum, o);
+  if (lane == 0 && wsum) atomicAdd(reinterpret_cast<unsigned long long*>(status + GSB_STATUS_PAIR_TOTAL64), wsum);
 }
 
 // Gathers splats into depth-rank order (packed 48-byte records), and turns the
@@ -170,31 +321,41 @@ __global__ void __launch_bounds__(kScanThreads)
   }
 }
 
-// Re-runs the tile loop per splat in depth-rank order and writes its pairs at
-// its scan slot: key = (global_tile << 32) | depth_key, value = rank index.
+// Re-runs the tile test per splat in depth-rank order (warp-cooperatively, as
+// k_prepare) and writes its pairs at its scan slot, in row-major tile order:
+// key = (global_tile << 32) | depth_key, value = rank index.
 __global__ void __launch_bounds__(256)
     k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
            uint64_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status) {
+  __shared__ WarpTilesSmem s_warp[8];
+  __shared__ int s_start[8][32], s_cnt[8][32];
+  __shared__ uint32_t s_dk[8][32], s_tbase[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= m.BG) return;
-  const int start = pair_offsets[r];
-  const int n = pair_offsets[r + 1] - start;
-  if (n <= 0) return;
-  const float4 p0 = rec[3 * r + 0];
-  const float4 p1 = rec[3 * r + 1];
-  const float4 p2 = rec[3 * r + 2];
-  const uint32_t dk = __float_as_uint(p2.y);
-  const uint32_t tile_base = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
-  int k = 0;
-  for_each_tile(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m, [&](int tx, int ty) {
-    if (k < n) {
-      const uint32_t tile = tile_base + (uint32_t)(ty * m.tiles_x + tx);
-      keys[start + k] = ((uint64_t)tile << 32) | dk;
-      vals[start + k] = (uint32_t)r;
+  const bool valid = r < m.BG;
+  SplatTiles t = splat_tiles(0.f, 0.f, 0.f, 0.f, 0.f, 0.f, m);
+  int start = 0, cnt = 0;
+  if (valid) {
+    start = pair_offsets[r];
+    cnt = pair_offsets[r + 1] - start;
+    const float4 p0 = rec[3 * r + 0];
+    const float4 p1 = rec[3 * r + 1];
+    s_dk[warp][lane] = __float_as_uint(rec[3 * r + 2].y);
+    s_tbase[warp][lane] = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
+    if (cnt > 0) t = splat_tiles(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m);
+  }
+  s_start[warp][lane] = start;
+  s_cnt[warp][lane] = cnt;
+  WarpTilesSmem& sm = s_warp[warp];
+  const int r0 = r - lane;
+  warp_tiles(t, m, sm, [&](int owner, int tx, int ty, int slot) {
+    if (slot < s_cnt[warp][owner]) {
+      const int64_t idx = (int64_t)s_start[warp][owner] + slot;
+      keys[idx] = ((uint64_t)(s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx)) << 32) | s_dk[warp][owner];
+      vals[idx] = (uint32_t)(r0 + owner);
     }
-    ++k;
   });
-  if (k != n) raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteEmit);
+  if (valid && sm.hits[lane] != cnt) raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteEmit);
 }
 
 // tile_offsets[t] = index of the first sorted pair of tile t (= exclusive

@@ -39,11 +39,27 @@ __global__ void __launch_bounds__(kSortThreads)
   }
 }
 
+// Shared memory of one pass: the partition's keys and values staged in digit
+// order (so the global scatter is coalesced), and the digit bookkeeping.
+template <int ITEMS>
+struct OnesweepSmem {
+  uint64_t keys[kSortThreads * ITEMS];
+  uint32_t vals[kSortThreads * ITEMS];
+  uint32_t warp_hist[kSortWarps][kRadix];  // per-warp digit counts, then exclusive over warps
+  uint32_t local_base[kRadix];             // exclusive scan of the partition's digit counts
+  uint32_t global_base[kRadix];            // digit base + look-back exclusive prefix
+  uint32_t scan[kSortWarps];
+  uint32_t part;
+};
+
 // One digit pass. Keys are held warp-striped: warp w owns the contiguous
 // segment [tile + w*32*ITEMS, +32*ITEMS) and lane l holds its items i*32+l, so
 // (item, lane) order is input order and the match_any ranking is stable. Each
 // CTA also turns the pass's global digit histogram into exclusive digit bases
-// itself (a 256-entry scan), so no separate launch precedes the pass.
+// itself (a 256-entry scan), so no separate launch precedes the pass. The
+// ranked keys are first placed in digit order in shared memory (while the
+// look-back resolves), then written out by consecutive threads, so each
+// digit's run leaves the CTA as contiguous stores.
 template <int ITEMS>
 __global__ void __launch_bounds__(kSortThreads)
     rs_onesweep(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
@@ -52,20 +68,18 @@ __global__ void __launch_bounds__(kSortThreads)
                 uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter,
                 uint32_t* __restrict__ status) {
   constexpr int kTile = kSortThreads * ITEMS;
-  __shared__ uint32_t s_part;
-  __shared__ uint32_t s_warp_hist[kSortWarps][kRadix];
-  __shared__ uint32_t s_prefix[kRadix];
-  __shared__ uint32_t s_scan[kSortWarps];
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  OnesweepSmem<ITEMS>& sm = *reinterpret_cast<OnesweepSmem<ITEMS>*>(s_raw);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_part = atomicAdd(part_counter, 1u);
-  for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&s_warp_hist[0][0])[i] = 0u;
+  if (tid == 0) sm.part = atomicAdd(part_counter, 1u);
+  for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&sm.warp_hist[0][0])[i] = 0u;
   __syncthreads();
-  const uint32_t part = s_part;
+  const uint32_t part = sm.part;
   const uint32_t dmask = (1u << bits) - 1u;
-
-  const int64_t seg = (int64_t)part * kTile + (int64_t)warp * (32 * ITEMS);
+  const int64_t tile0 = (int64_t)part * kTile;
+  const int64_t seg = tile0 + (int64_t)warp * (32 * ITEMS);
   uint64_t k[ITEMS];
   uint32_t v[ITEMS];
   uint32_t rank[ITEMS];
@@ -86,11 +100,11 @@ __global__ void __launch_bounds__(kSortThreads)
       const uint32_t y = __shfl_up_sync(kFullMask, x, o);
       if (lane >= o) x += y;
     }
-    if (lane == 31) s_scan[warp] = x;
+    if (lane == 31) sm.scan[warp] = x;
     __syncthreads();
     uint32_t wsum = 0;
 #pragma unroll
-    for (int w = 0; w < kSortWarps; ++w) wsum += (w < warp) ? s_scan[w] : 0u;
+    for (int w = 0; w < kSortWarps; ++w) wsum += (w < warp) ? sm.scan[w] : 0u;
     digit_base = wsum + x - h;
   }
 
@@ -101,75 +115,103 @@ __global__ void __launch_bounds__(kSortThreads)
     const uint32_t d = valid ? ((uint32_t)(k[i] >> shift) & dmask) : kRadix;  // sentinel group
     const uint32_t peers = __match_any_sync(kFullMask, d);
     uint32_t cnt_before = 0;
-    if (valid) cnt_before = s_warp_hist[warp][d];
+    if (valid) cnt_before = sm.warp_hist[warp][d];
     __syncwarp();
     rank[i] = cnt_before + __popc(peers & lt_mask);
     const int leader = 31 - __clz(peers);
-    if (valid && lane == leader) s_warp_hist[warp][d] = cnt_before + __popc(peers);
+    if (valid && lane == leader) sm.warp_hist[warp][d] = cnt_before + __popc(peers);
     __syncwarp();
   }
   __syncthreads();
 
-  // Digit t: exclusive scan over warps, partition total, decoupled look-back.
+  // Digit t: exclusive scan over warps, partition total, its local base (a
+  // block scan over digits), then publish the aggregate for the look-back.
+  const int t = tid;
+  uint32_t sum = 0;
+#pragma unroll
+  for (int w = 0; w < kSortWarps; ++w) {
+    const uint32_t c = sm.warp_hist[w][t];
+    sm.warp_hist[w][t] = sum;
+    sum += c;
+  }
+  uint32_t* my = lookback + (size_t)part * kRadix + t;
+  st_volatile_u32(my, (part == 0 ? kFlagInc : kFlagAgg) | sum);
   {
-    const int t = tid;
-    uint32_t sum = 0;
+    uint32_t x = sum;
 #pragma unroll
-    for (int w = 0; w < kSortWarps; ++w) {
-      const uint32_t c = s_warp_hist[w][t];
-      s_warp_hist[w][t] = sum;
-      sum += c;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFullMask, x, o);
+      if (lane >= o) x += y;
     }
-    uint32_t* my = lookback + (size_t)part * kRadix + t;
-    uint32_t exclusive = 0;
-    if (part == 0) {
-      st_volatile_u32(my, kFlagInc | sum);
-    } else {
-      st_volatile_u32(my, kFlagAgg | sum);
-      // Windowed look-back: read kLookWin predecessors at once, consume them
-      // nearest-first until an inclusive prefix is found (one L2 round trip per
-      // window instead of one per predecessor).
-      int64_t j = (int64_t)part - 1;
-      int spins = 0;
-      bool failed = false, done = false;
-      while (!done && !failed) {
-        uint32_t w[kLookWin];
+    __syncthreads();  // sm.scan is reused
+    if (lane == 31) sm.scan[warp] = x;
+    __syncthreads();
+    uint32_t wsum = 0;
 #pragma unroll
-        for (int q = 0; q < kLookWin; ++q)
-          w[q] = (j - q >= 0) ? ld_volatile_u32(lookback + (size_t)(j - q) * kRadix + t) : kFlagInc;
-#pragma unroll
-        for (int q = 0; q < kLookWin; ++q) {
-          if (done || failed) break;
-          uint32_t x = w[q];
-          while (!(x & (kFlagAgg | kFlagInc))) {
-            if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
-              failed = true;
-              break;
-            }
-            __nanosleep(32);
-            x = ld_volatile_u32(lookback + (size_t)(j - q) * kRadix + t);
-          }
-          if (failed) break;
-          exclusive += x & kValueMask;
-          if (x & kFlagInc) done = true;
-        }
-        j -= kLookWin;
-      }
-      if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteSortLookback);
-      st_volatile_u32(my, kFlagInc | ((exclusive + sum) & kValueMask));
-    }
-    s_prefix[t] = digit_base + exclusive;
+    for (int w = 0; w < kSortWarps; ++w) wsum += (w < warp) ? sm.scan[w] : 0u;
+    sm.local_base[t] = wsum + x - sum;
   }
   __syncthreads();
-
+  // Stage the partition in digit order.
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const int64_t idx = seg + i * 32 + lane;
     if (idx < n) {
       const uint32_t d = (uint32_t)(k[i] >> shift) & dmask;
-      const uint32_t pos = s_prefix[d] + s_warp_hist[warp][d] + rank[i];
-      keys_out[pos] = k[i];
-      vals_out[pos] = v[i];
+      const uint32_t lp = sm.local_base[d] + sm.warp_hist[warp][d] + rank[i];
+      sm.keys[lp] = k[i];
+      sm.vals[lp] = v[i];
+    }
+  }
+  // Decoupled look-back for digit t.
+  uint32_t exclusive = 0;
+  if (part != 0) {
+    // Windowed look-back: read kLookWin predecessors at once, consume them
+    // nearest-first until an inclusive prefix is found (one L2 round trip per
+    // window instead of one per predecessor).
+    int64_t j = (int64_t)part - 1;
+    int spins = 0;
+    bool failed = false, done = false;
+    while (!done && !failed) {
+      uint32_t w[kLookWin];
+#pragma unroll
+      for (int q = 0; q < kLookWin; ++q)
+        w[q] = (j - q >= 0) ? ld_volatile_u32(lookback + (size_t)(j - q) * kRadix + t) : kFlagInc;
+#pragma unroll
+      for (int q = 0; q < kLookWin; ++q) {
+        if (done || failed) break;
+        uint32_t x = w[q];
+        while (!(x & (kFlagAgg | kFlagInc))) {
+          if (++spins > kSpinLimit || ((spins & 1023) == 0 && ld_volatile_u32(&status[GSB_STATUS_ERROR]))) {
+            failed = true;
+            break;
+          }
+          __nanosleep(32);
+          x = ld_volatile_u32(lookback + (size_t)(j - q) * kRadix + t);
+        }
+        if (failed) break;
+        exclusive += x & kValueMask;
+        if (x & kFlagInc) done = true;
+      }
+      j -= kLookWin;
+    }
+    if (failed) raise_error(status, GSB_DEVERR_LOOKBACK_TIMEOUT, kSiteSortLookback);
+    st_volatile_u32(my, kFlagInc | ((exclusive + sum) & kValueMask));
+  }
+  sm.global_base[t] = digit_base + exclusive;
+  __syncthreads();
+
+  // Coalesced scatter: staged entry e goes to global_base[d] + (e - local_base[d]).
+  const int valid_n = (int)min((int64_t)kTile, n - tile0);
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    const int e = i * kSortThreads + tid;
+    if (e < valid_n) {
+      const uint64_t key = sm.keys[e];
+      const uint32_t d = (uint32_t)(key >> shift) & dmask;
+      const uint32_t pos = sm.global_base[d] + ((uint32_t)e - sm.local_base[d]);
+      keys_out[pos] = key;
+      vals_out[pos] = sm.vals[e];
     }
   }
 }
@@ -191,6 +233,22 @@ int grid_for(int64_t n, int threads, int max_blocks) {
 }
 
 }  // namespace
+
+// Opts the 16-item pass into more than 48 KB of dynamic shared memory (once
+// per device).
+static cudaError_t onesweep_smem_optin() {
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (done[dev & 63]) return cudaSuccess;
+  e = cudaFuncSetAttribute(rs_onesweep<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)sizeof(OnesweepSmem<16>));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(rs_onesweep<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)sizeof(OnesweepSmem<8>));
+  if (e == cudaSuccess) done[dev & 63] = true;
+  return e;
+}
 
 static int sort_items(int64_t n) {
   // Enough partitions to put about two CTAs on every SM: a pass over few keys
@@ -224,7 +282,9 @@ cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t
     return cudaGetLastError();
   }
   const int last_bits = (end_bit - begin_bit) - (passes - 1) * kRadixBits;
-  cudaError_t e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
+  cudaError_t e = onesweep_smem_optin();
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
   if (e != cudaSuccess) return e;
   rs_histogram<<<grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream>>>(keys_in, n, begin_bit,
                                                                                 passes, last_bits, hist);
@@ -239,7 +299,9 @@ cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t
     uint32_t* vo = to_out ? vals_out : v_tmp;
     const int bits = (p == passes - 1) ? last_bits : kRadixBits;
     auto kernel = items == 16 ? rs_onesweep<16> : items == 8 ? rs_onesweep<8> : rs_onesweep<4>;
-    kernel<<<(unsigned)parts, kSortThreads, 0, stream>>>(
+    const size_t smem = items == 16 ? sizeof(OnesweepSmem<16>)
+                                    : items == 8 ? sizeof(OnesweepSmem<8>) : sizeof(OnesweepSmem<4>);
+    kernel<<<(unsigned)parts, kSortThreads, smem, stream>>>(
         ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, hist + p * kRadix,
         lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status);
     note_launches(1);
