@@ -18,7 +18,7 @@ namespace gsb {
 namespace {
 
 constexpr int kScanThreads = 256;
-constexpr int kScanItems = 8;
+constexpr int kScanItems = 4;
 constexpr int kScanTile = kScanThreads * kScanItems;
 constexpr unsigned long long kScanAgg = 1ull << 62;
 constexpr unsigned long long kScanInc = 2ull << 62;
@@ -219,29 +219,42 @@ __global__ void __launch_bounds__(kScanThreads)
   const int64_t part = s_part;
   const int64_t r0 = part * kScanTile + (int64_t)tid * kScanItems;
 
-  uint32_t c[kScanItems];
+  // Loads first (all independent: the ranks' source indices, then every
+  // gathered field), so a thread has all its memory requests in flight at once.
+  uint32_t orig[kScanItems];
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) orig[i] = (r0 + i < m.BG) ? sorted_vals[r0 + i] : 0u;
+  uint32_t c[kScanItems], dk[kScanItems];
+  float2 mu[kScanItems];
+  float ca[kScanItems], cb[kScanItems], cc[kScanItems], op[kScanItems], cr[kScanItems], cg[kScanItems],
+      cbl[kScanItems];
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    const bool ok = r0 + i < m.BG;
+    const uint32_t o = orig[i];
+    c[i] = ok ? counts[o] : 0u;
+    dk[i] = ok ? (uint32_t)sorted_keys[r0 + i] : 0u;
+    mu[i] = ok ? means2d[o] : make_float2(0.f, 0.f);
+    ca[i] = ok ? conics[3 * o + 0] : 0.f;
+    cb[i] = ok ? conics[3 * o + 1] : 0.f;
+    cc[i] = ok ? conics[3 * o + 2] : 0.f;
+    op[i] = ok ? opacities[o] : 0.f;
+    cr[i] = ok ? colors[3 * o + 0] : 0.f;
+    cg[i] = ok ? colors[3 * o + 1] : 0.f;
+    cbl[i] = ok ? colors[3 * o + 2] : 0.f;
+  }
   unsigned long long tsum = 0;
 #pragma unroll
   for (int i = 0; i < kScanItems; ++i) {
     const int64_t r = r0 + i;
-    c[i] = 0;
+    tsum += c[i];
     if (r < m.BG) {
-      const uint32_t orig = sorted_vals[r];
       const int b = (int)(r / m.G);
-      c[i] = counts[orig];
-      tsum += c[i];
-      const float2 mu = means2d[orig];
-      const float4 p0 = make_float4(mu.x, mu.y, conics[3 * orig + 0], conics[3 * orig + 1]);
-      const float4 p1 = make_float4(conics[3 * orig + 2], opacities[orig], colors[3 * orig + 0],
-                                    colors[3 * orig + 1]);
-      const float op = opacities[orig];
-      const float4 p2 = make_float4(colors[3 * orig + 2], __uint_as_float((uint32_t)sorted_keys[r]),
-                                    vis_log_threshold(op, m.alpha_thr, m.max_alpha),
-                                    sat_log_threshold(op, m.max_alpha));
-      rec[3 * r + 0] = p0;
-      rec[3 * r + 1] = p1;
-      rec[3 * r + 2] = p2;
-      perm[r] = (int32_t)(orig - (uint32_t)b * (uint32_t)m.G);
+      rec[3 * r + 0] = make_float4(mu[i].x, mu[i].y, ca[i], cb[i]);
+      rec[3 * r + 1] = make_float4(cc[i], op[i], cr[i], cg[i]);
+      rec[3 * r + 2] = make_float4(cbl[i], __uint_as_float(dk[i]), vis_log_threshold(op[i], m.alpha_thr, m.max_alpha),
+                                   sat_log_threshold(op[i], m.max_alpha));
+      perm[r] = (int32_t)(orig[i] - (uint32_t)b * (uint32_t)m.G);
     }
   }
   // Block-wide exclusive scan of the thread sums.

@@ -336,29 +336,38 @@ __device__ __forceinline__ void pixel_vjp(const Meta& m, float dy, float power, 
 // (T_cur * rcp(1 - 0) = T_cur; gT + 0 * d = gT) and adds nothing to S.
 // gT advances as gT + alpha (dot_gc - gT), the same value as
 // alpha dot_gc + (1 - alpha) gT up to rounding. S[t] holds per-half partial sums.
+// kClampOm: clamp 1 - alpha at eps (only needed when max_alpha > 1 - eps;
+// otherwise 1 - alpha >= 1 - max_alpha >= eps already).
+template <bool kClampOm>
 __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int last_h, F2 dy, float pl, float ph,
-                                           float op, float vis_thr, float sat_thr, F2 col_r, F2 col_g, F2 col_b,
+                                           F2 op, float vis_thr, float sat_thr, F2 col_r, F2 col_g, F2 col_b,
                                            F2 gr, F2 gg, F2 gb, F2& T_cur, F2& gT, F2 (&S)[7]) {
   float xl, xh;
   split(mul2(f2(pl, ph), f2(kLog2e)), xl, xh);
-  const float el = ex2_approx(xl), eh = ex2_approx(xh);
-  const float rl = op * el, rh = op * eh;
+  const F2 e = f2(ex2_approx(xl), ex2_approx(xh));
+  float rl, rh;
+  split(mul2(op, e), rl, rh);
   int pass_l, pass_h;
   const float al = vis_select_bwd(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l);
   const float ah = vis_select_bwd(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h);
   const F2 alpha = f2(al, ah);
   float oml, omh;
   split(sub2(f2(1.0f), alpha), oml, omh);
-  const F2 T_prev = mul2(T_cur, f2(rcp_approx(fmaxf(oml, m.eps)), rcp_approx(fmaxf(omh, m.eps))));
+  if (kClampOm) {
+    oml = fmaxf(oml, m.eps);
+    omh = fmaxf(omh, m.eps);
+  }
+  const F2 T_prev = mul2(T_cur, f2(rcp_approx(oml), rcp_approx(omh)));
   const F2 dot_gc = fma2(gb, col_b, fma2(gg, col_g, mul2(gr, col_r)));
   const F2 d = sub2(dot_gc, gT);
   const F2 g_alpha = mul2(T_prev, d);
   const F2 wc = mul2(T_prev, alpha);
-  float gal, gah;
-  split(g_alpha, gal, gah);
-  // raw < max_alpha (power below the saturation log-threshold) passes g_alpha to raw.
-  const F2 gp = f2(pass_l ? gal * rl : 0.0f, pass_h ? gah * rh : 0.0f);
-  const F2 ge = f2(pass_l ? gal * el : 0.0f, pass_h ? gah * eh : 0.0f);
+  // raw < max_alpha (power below the saturation log-threshold) passes g_alpha
+  // to raw: d op = g_alpha e, d power = g_alpha raw = (g_alpha e) op.
+  float gel, geh;
+  split(mul2(g_alpha, e), gel, geh);
+  const F2 ge = f2(pass_l ? gel : 0.0f, pass_h ? geh : 0.0f);
+  const F2 gp = mul2(ge, op);
   S[0] = add2(S[0], gp);
   const F2 gpdy = mul2(gp, dy);
   S[1] = add2(S[1], gpdy);
@@ -452,6 +461,7 @@ __device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileO
   for (int q = lane; q < off.n; q += 32) cp_async4(&buf->ids[q], ids + off.start + q);
 }
 
+template <bool kClampOm>
 __global__ void __launch_bounds__(kBwdWarps * 32, 3)
     k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, const float* __restrict__ final_T,
@@ -502,7 +512,16 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         lmax = max(lmax, max(last[2 * q], last[2 * q + 1]));
       }
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
-      #pragma unroll 1
+      // Software pipeline: the warp reduction (a chain of dependent shuffle
+      // levels) and atomics of splat j+1 are issued in the same iteration, in
+      // the same basic block, as the independent pixel terms of splat j, so
+      // the two interleave. pv/pgi hold the pending splat (zeros and -1 before
+      // the first); the last one is committed after the loop.
+      float pv[kGradComps];
+#pragma unroll
+      for (int t = 0; t < kGradComps; ++t) pv[t] = 0.0f;
+      int pgi = -1;
+#pragma unroll 1
       for (int j = tile_last - 1; j >= 0; --j) {
         const float4 p0 = B.rec[j][0];
         const float4 p1 = B.rec[j][1];
@@ -510,7 +529,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         const float dx = __fsub_rn(fx, p0.x);
         const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
         const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
-        const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x);
+        const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x), op = f2(p1.y);
         F2 S[7];
 #pragma unroll
         for (int t = 0; t < 7; ++t) S[t] = f2(0.0f);
@@ -520,31 +539,46 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
           const F2 power = power_at2(ta, tb, ch, dy);
           float pl, ph;
           split(power, pl, ph);
-          pixel_vjp2(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, p1.y, p2.z, p2.w, col_r, col_g, col_b, gr[q],
-                     gg[q], gb[q], Tc[q], gT[q], S);
+          pixel_vjp2<kClampOm>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z, p2.w, col_r, col_g, col_b,
+                               gr[q], gg[q], gb[q], Tc[q], gT[q], S);
         }
-        // Every binned splat reaches some pixel of its tile, so the reduction runs
-        // unconditionally; a zero total issues no atomic.
+        float total;
         {
-          float Sv[7];
-#pragma unroll
-          for (int t = 0; t < 7; ++t) {
-            float lo, hi;
-            split(S[t], lo, hi);
-            Sv[t] = lo + hi;
-          }
           float v[16];
-          vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
-          const float total = warp_reduce_scatter16(v, lane);
-          int gi = B.ids[j];
-          if ((unsigned)gi >= (unsigned)m.BG) {
-            raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
-            gi = -1;
-          }
-          const int comp = lane >> 1;
-          if (!(lane & 1) && comp < kGradComps && gi >= 0 && total != 0.0f)
-            atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + comp, total);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) v[t] = t < kGradComps ? pv[t] : 0.0f;
+          total = warp_reduce_scatter16(v, lane);
         }
+        float Sv[7];
+#pragma unroll
+        for (int t = 0; t < 7; ++t) {
+          float lo, hi;
+          split(S[t], lo, hi);
+          Sv[t] = lo + hi;
+        }
+        float v[16];
+        vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
+#pragma unroll
+        for (int t = 0; t < kGradComps; ++t) pv[t] = v[t];
+        // Commit the previous splat (a zero total issues no atomic), then take
+        // this splat's id.
+        const int comp = lane >> 1;
+        if (!(lane & 1) && comp < kGradComps && pgi >= 0 && total != 0.0f)
+          atomicAdd(grad_rec + (size_t)pgi * GSB_REC_FLOATS + comp, total);
+        pgi = B.ids[j];
+        if ((unsigned)pgi >= (unsigned)m.BG) {
+          raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
+          pgi = -1;
+        }
+      }
+      {
+        float v[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = t < kGradComps ? pv[t] : 0.0f;
+        const float total = warp_reduce_scatter16(v, lane);
+        const int comp = lane >> 1;
+        if (!(lane & 1) && comp < kGradComps && pgi >= 0 && total != 0.0f)
+          atomicAdd(grad_rec + (size_t)pgi * GSB_REC_FLOATS + comp, total);
       }
     }
     __syncwarp();  // bufs[k & 1] is refilled by the next iteration's prefetch
@@ -699,7 +733,9 @@ const GridCache& grids() {
   if (g.sms == 0) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute((const void*)k_render_bwd_warp, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute((const void*)k_render_bwd_warp<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kBwdWarpSmem);
+    cudaFuncSetAttribute((const void*)k_render_bwd_warp<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kBwdWarpSmem);
     auto occ = [&](const void* fn, int threads, size_t smem) {
       int b = 1;
@@ -710,7 +746,7 @@ const GridCache& grids() {
     g.fwd_warp[1] = occ((const void*)k_render_fwd_warp<true>, kWarps * 32, 0);
     g.fwd_cta[0] = occ((const void*)k_render_fwd_cta<false>, kTilePixels, 0);
     g.fwd_cta[1] = occ((const void*)k_render_fwd_cta<true>, kTilePixels, 0);
-    g.bwd_warp = occ((const void*)k_render_bwd_warp, kBwdWarps * 32, kBwdWarpSmem);
+    g.bwd_warp = occ((const void*)k_render_bwd_warp<false>, kBwdWarps * 32, kBwdWarpSmem);
     g.bwd_cta = occ((const void*)k_render_bwd_cta, kTilePixels, 0);
     g.sms = sms;
   }
@@ -803,7 +839,9 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   const float4* r4 = reinterpret_cast<const float4*>(rec);
   const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
   const int cta_grid = max(1, min(g.bwd_cta, m.total_tiles));
-  k_render_bwd_warp<<<warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream>>>(
+  // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
+  auto bwd_warp = (1.0f - m.max_alpha >= m.eps) ? k_render_bwd_warp<false> : k_render_bwd_warp<true>;
+  bwd_warp<<<warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream>>>(
       m, reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx, grad_rgb, grad_rec,
       w.long_tiles, w.long_count, status);
   k_render_bwd_cta<<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, final_T, last_idx,
