@@ -172,10 +172,11 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
 // Per splat in input order: depth-sort key (view in the high word) and the
 // exact number of tiles its support ellipse touches; the pair total is added
 // into status words 4-5 (64-bit) for the host's early read.
+template <typename K>
 __global__ void __launch_bounds__(256)
     k_prepare(Meta m, const float2* __restrict__ means2d, const float* __restrict__ conics,
               const float* __restrict__ opacities, const float* __restrict__ depths,
-              uint64_t* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
+              K* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
               uint32_t* __restrict__ counts, uint32_t* __restrict__ status) {
   __shared__ WarpTilesSmem s_warp[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -184,7 +185,8 @@ __global__ void __launch_bounds__(256)
   SplatTiles t = splat_tiles(0.f, 0.f, 0.f, 0.f, 0.f, 0.f, m);
   if (valid) {
     const int b = i / m.G;
-    sort_keys[i] = ((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]);
+    // One view: the 32-bit depth key alone; several: the view in the high word.
+    sort_keys[i] = (K)(((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]));
     sort_vals[i] = (uint32_t)i;
     const float2 mu = means2d[i];
     t = splat_tiles(mu.x, mu.y, conics[3 * i + 0], conics[3 * i + 1], conics[3 * i + 2], opacities[i], m);
@@ -202,8 +204,9 @@ __global__ void __launch_bounds__(256)
 // Gathers splats into depth-rank order (packed 48-byte records), and turns the
 // per-splat tile counts into exclusive pair offsets with a single-pass chained
 // scan (dynamic partition ids + decoupled look-back).
+template <typename K>
 __global__ void __launch_bounds__(kScanThreads)
-    k_gather_scan(Meta m, const uint64_t* __restrict__ sorted_keys,
+    k_gather_scan(Meta m, const K* __restrict__ sorted_keys,
                   const uint32_t* __restrict__ sorted_vals, const float2* __restrict__ means2d,
                   const float* __restrict__ conics, const float* __restrict__ colors,
                   const float* __restrict__ opacities, const uint32_t* __restrict__ counts,
@@ -243,6 +246,7 @@ __global__ void __launch_bounds__(kScanThreads)
     cg[i] = ok ? colors[3 * o + 1] : 0.f;
     cbl[i] = ok ? colors[3 * o + 2] : 0.f;
   }
+  asm volatile("" ::: "memory");  // all gathers in flight before the first use
   unsigned long long tsum = 0;
 #pragma unroll
   for (int i = 0; i < kScanItems; ++i) {
@@ -336,13 +340,14 @@ __global__ void __launch_bounds__(kScanThreads)
 
 // Re-runs the tile test per splat in depth-rank order (warp-cooperatively, as
 // k_prepare) and writes its pairs at its scan slot, in row-major tile order:
-// key = (global_tile << 32) | depth_key, value = rank index.
+// key = global tile index (32 bits), value = rank index. The stable sort on
+// the tile key then leaves each tile's list in rank (= depth) order.
 __global__ void __launch_bounds__(256)
     k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
-           uint64_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status) {
+           uint32_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status) {
   __shared__ WarpTilesSmem s_warp[8];
   __shared__ int s_start[8][32], s_cnt[8][32];
-  __shared__ uint32_t s_dk[8][32], s_tbase[8][32];
+  __shared__ uint32_t s_tbase[8][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = r < m.BG;
@@ -353,7 +358,6 @@ __global__ void __launch_bounds__(256)
     cnt = pair_offsets[r + 1] - start;
     const float4 p0 = rec[3 * r + 0];
     const float4 p1 = rec[3 * r + 1];
-    s_dk[warp][lane] = __float_as_uint(rec[3 * r + 2].y);
     s_tbase[warp][lane] = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
     if (cnt > 0) t = splat_tiles(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m);
   }
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(256)
   warp_tiles(t, m, sm, [&](int owner, int tx, int ty, int slot) {
     if (slot < s_cnt[warp][owner]) {
       const int64_t idx = (int64_t)s_start[warp][owner] + slot;
-      keys[idx] = ((uint64_t)(s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx)) << 32) | s_dk[warp][owner];
+      keys[idx] = s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx);
       vals[idx] = (uint32_t)(r0 + owner);
     }
   });
@@ -373,16 +377,18 @@ __global__ void __launch_bounds__(256)
 
 // tile_offsets[t] = index of the first sorted pair of tile t (= exclusive
 // prefix of per-tile counts); every entry is written by exactly one thread.
+// keys64 (optional) receives (tile << 32) | depth_key of each sorted pair.
 __global__ void __launch_bounds__(256)
-    k_ranges(const uint64_t* __restrict__ keys, int64_t n_pairs, int total_tiles,
-             int32_t* __restrict__ tile_offsets) {
+    k_ranges(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, const float4* __restrict__ rec,
+             int64_t n_pairs, int total_tiles, int32_t* __restrict__ tile_offsets, uint64_t* __restrict__ keys64) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_pairs) return;
-  const int64_t t = (int64_t)(keys[i] >> 32);
-  const int64_t tp = (i == 0) ? -1 : (int64_t)(keys[i - 1] >> 32);
+  const int64_t t = keys[i];
+  const int64_t tp = (i == 0) ? -1 : (int64_t)keys[i - 1];
   for (int64_t s = tp + 1; s <= t; ++s) tile_offsets[s] = (int32_t)i;
   if (i == n_pairs - 1)
     for (int64_t s = t + 1; s <= total_tiles; ++s) tile_offsets[s] = (int32_t)n_pairs;
+  if (keys64) keys64[i] = ((uint64_t)t << 32) | __float_as_uint(rec[3 * (size_t)vals[i] + 2].y);
 }
 
 __global__ void k_fill_i32(int32_t* __restrict__ p, int64_t n, int32_t v) {
@@ -401,7 +407,7 @@ __global__ void __launch_bounds__(256)
 
 // Workspace carve of gsb_bin_prepare (shared by size query and run).
 struct PrepareWs {
-  uint64_t* keys_in;
+  uint64_t* keys_in;  // 64-bit keys (B > 1), or 32-bit keys in the same space (B == 1)
   uint32_t* vals_in;
   uint64_t* keys_sorted;
   uint32_t* vals_sorted;
@@ -422,6 +428,7 @@ void carve_prepare(Carver& c, const Meta& m, PrepareWs* w) {
 }
 
 int depth_sort_end_bit(const Meta& m) { return 32 + (m.B > 1 ? bits_for(m.B - 1) : 0); }
+bool depth_keys32(const Meta& m) { return m.B == 1; }
 
 }  // namespace
 }  // namespace gsb
@@ -434,7 +441,8 @@ extern "C" size_t gsb_bin_prepare_workspace_size(const gsb_raster_meta* meta) {
   Carver c(nullptr);
   PrepareWs w;
   carve_prepare(c, m, &w);
-  radix_sort_pairs(c, nullptr, nullptr, nullptr, nullptr, m.BG, 0, depth_sort_end_bit(m), nullptr, 0);
+  radix_sort_pairs(c, (const uint64_t*)nullptr, nullptr, nullptr, nullptr, m.BG, 0, depth_sort_end_bit(m), nullptr,
+                   0);
   return c.off + 256;
 }
 
@@ -455,8 +463,14 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   Carver c(workspace);
   PrepareWs w;
   carve_prepare(c, m, &w);
-  k_prepare<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics, opacities,
-                                                   depths, w.keys_in, w.vals_in, w.counts, status);
+  if (depth_keys32(m))
+    k_prepare<uint32_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
+                                                               opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in),
+                                                               w.vals_in, w.counts, status);
+  else
+    k_prepare<uint64_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
+                                                               opacities, depths, w.keys_in, w.vals_in, w.counts,
+                                                               status);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
@@ -484,12 +498,24 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
   if (e != cudaSuccess) return GSB_ERR_CUDA;
   e = cudaMemsetAsync(w.counter, 0, sizeof(uint32_t), stream);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-  e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
-                       status, stream);
-  if (e != cudaSuccess) return GSB_ERR_CUDA;
-  k_gather_scan<<<parts, kScanThreads, 0, stream>>>(
-      m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
-      w.counts, reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
+  if (depth_keys32(m)) {
+    uint32_t* k32_in = reinterpret_cast<uint32_t*>(w.keys_in);
+    uint32_t* k32_sorted = reinterpret_cast<uint32_t*>(w.keys_sorted);
+    // 32-bit keys in the 64-bit key buffers; the sort's scratch (carved after
+    // them) is smaller than the 64-bit sort's that the workspace is sized for.
+    e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream);
+    if (e != cudaSuccess) return GSB_ERR_CUDA;
+    k_gather_scan<uint32_t><<<parts, kScanThreads, 0, stream>>>(
+        m, k32_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities, w.counts,
+        reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
+  } else {
+    e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
+                         status, stream);
+    if (e != cudaSuccess) return GSB_ERR_CUDA;
+    k_gather_scan<uint64_t><<<parts, kScanThreads, 0, stream>>>(
+        m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
+        w.counts, reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
+  }
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
@@ -506,14 +532,16 @@ extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d
 
 namespace {
 struct EmitWs {
-  uint64_t* keys;
+  uint32_t* keys;         // emitted tile keys, rank order
   uint32_t* vals;
+  uint32_t* keys_sorted;  // tile keys after the sort
 };
 void carve_emit(Carver& c, int64_t P, EmitWs* w) {
-  w->keys = c.take<uint64_t>((size_t)P);
+  w->keys = c.take<uint32_t>((size_t)P);
   w->vals = c.take<uint32_t>((size_t)P);
+  w->keys_sorted = c.take<uint32_t>((size_t)P);
 }
-int tile_end_bit(const Meta& m) { return 32 + (m.total_tiles > 1 ? bits_for(m.total_tiles - 1) : 0); }
+int tile_end_bit(const Meta& m) { return m.total_tiles > 1 ? bits_for(m.total_tiles - 1) : 0; }
 }  // namespace
 
 extern "C" size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64_t total_pairs) {
@@ -522,7 +550,8 @@ extern "C" size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64
   Carver c(nullptr);
   EmitWs w;
   carve_emit(c, total_pairs, &w);
-  radix_sort_pairs(c, nullptr, nullptr, nullptr, nullptr, total_pairs, 32, tile_end_bit(m), nullptr, 0);
+  radix_sort_pairs(c, (const uint32_t*)nullptr, nullptr, nullptr, nullptr, total_pairs, 0, tile_end_bit(m), nullptr,
+                   0);
   return c.off + 256;
 }
 
@@ -535,7 +564,7 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   if (rc != GSB_OK) return rc;
   if (total_pairs < 0 || !tile_offsets || !status) return GSB_ERR_INVALID_ARGUMENT;
   if (total_pairs >= kSortMaxN) return GSB_ERR_CAPACITY;
-  if (total_pairs > 0 && (!rec || !pair_offsets || !keys || !binned_ids)) return GSB_ERR_INVALID_ARGUMENT;
+  if (total_pairs > 0 && (!rec || !pair_offsets || !binned_ids)) return GSB_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < gsb_bin_emit_workspace_size(meta, total_pairs) || (total_pairs > 0 && !workspace))
     return GSB_ERR_WORKSPACE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
@@ -551,10 +580,12 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   k_emit<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float4*>(rec), pair_offsets,
                                                 w.keys, w.vals, status);
   note_launches(1);
-  cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, keys, reinterpret_cast<uint32_t*>(binned_ids),
-                                   total_pairs, 32, tile_end_bit(m), status, stream);
+  cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
+                                   total_pairs, 0, tile_end_bit(m), status, stream);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-  k_ranges<<<grid1d(total_pairs, 256), 256, 0, stream>>>(keys, total_pairs, m.total_tiles, tile_offsets);
+  k_ranges<<<grid1d(total_pairs, 256), 256, 0, stream>>>(w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
+                                                         reinterpret_cast<const float4*>(rec), total_pairs,
+                                                         m.total_tiles, tile_offsets, keys);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }

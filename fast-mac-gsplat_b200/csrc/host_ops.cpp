@@ -198,7 +198,7 @@ PairRead& pair_read() {
 // pair_cap >= 0 raises the reference's overflow error when a tile holds more
 // pairs than pair_cap (the overflow fallback disabled); -1 skips the check.
 // Returns [out] (eval) or [out, perm, rec, tile_offsets, binned_ids, final_T,
-// last_idx, pair_rec, status, render_ws, keys] (training state; keys for tests).
+// last_idx, pair_rec, status, render_ws] (training state).
 std::vector<Tensor> forward(Tensor means2d, Tensor conics, Tensor colors, Tensor opacities, Tensor depths,
                             int64_t H, int64_t W, double alpha_thr, double T_thr, std::vector<double> bg,
                             double eps, double max_alpha, bool save_state, int64_t pair_cap) {
@@ -243,11 +243,10 @@ std::vector<Tensor> forward(Tensor means2d, Tensor conics, Tensor colors, Tensor
   const size_t ws2_bytes = gsb_bin_emit_workspace_size(&meta, P);
   Tensor binned_ids = empty({P}, at::kInt, dev);
   Tensor tile_offsets = empty({T + 1}, at::kInt, dev);
-  Tensor keys = empty({P}, at::kLong, dev);
   Tensor ws2 = empty({static_cast<int64_t>(std::max<size_t>(ws2_bytes, 1))}, at::kByte, dev);
   {
     Phase ph("bin_emit", means2d);
-    check(gsb_bin_emit(&meta, ptr<float>(rec), ptr<int32_t>(pair_offsets), P, ptr<uint64_t>(keys),
+    check(gsb_bin_emit(&meta, ptr<float>(rec), ptr<int32_t>(pair_offsets), P, /*keys=*/nullptr,
                        ptr<int32_t>(binned_ids), ptr<int32_t>(tile_offsets), ptr<uint32_t>(status), ws2.data_ptr(),
                        ws2_bytes, stream),
           "gsb_bin_emit");
@@ -283,7 +282,7 @@ std::vector<Tensor> forward(Tensor means2d, Tensor conics, Tensor colors, Tensor
   else
     errors().defer(status);
   if (!save_state) return {out};
-  return {out, perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status, rws, keys};
+  return {out, perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status, rws};
 }
 
 // backward(perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec,

@@ -30,5 +30,9 @@ inline int sort_passes(int begin_bit, int end_bit) {
 cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in,
                              uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
                              int end_bit, uint32_t* status, cudaStream_t stream);
+// 32-bit keys (end_bit <= 32): 8 bytes per pair moved per pass instead of 12.
+cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in,
+                             uint32_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
+                             int end_bit, uint32_t* status, cudaStream_t stream);
 
 }  // namespace gsb

@@ -99,7 +99,30 @@ class RasterConfig:
         return int(self.max_tile_pairs if self.max_tile_pairs is not None else self.max_fast_pairs)
 
 
+_validated: Dict[Any, RuntimeShaderConfig] = {}
+
+
 def _runtime_validate(config: RasterConfig) -> RuntimeShaderConfig:
+    """Checks the config against the runtime shader config (read from the
+    environment on every call, as the reference does); a (config, environment)
+    pair that passed once is remembered."""
+    env = (os.environ.get("GSP_TILE_SIZE"), os.environ.get("GSP_CHUNK"), os.environ.get("GSP_FAST_CAP"))
+    try:
+        hit = _validated.get((config, env))
+    except TypeError:  # unhashable config field
+        hit = None
+    if hit is not None:
+        return hit
+    rt = _runtime_validate_uncached(config)
+    try:
+        if len(_validated) < 256:
+            _validated[(config, env)] = rt
+    except TypeError:
+        pass
+    return rt
+
+
+def _runtime_validate_uncached(config: RasterConfig) -> RuntimeShaderConfig:
     rt = get_runtime_shader_config()
     if config.tile_size != rt.tile_size:
         raise ValueError(

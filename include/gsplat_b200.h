@@ -119,8 +119,10 @@ int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const f
 /* ---- binning, phase 2 ---------------------------------------------------
  * Replaces: `emit_binned_ids` (…/gsplat_v8_project3d_kernels.metal:743-780), the per-tile
  * `bitonic_sort_ids` (…:594-617) and the tile offsets of metal_bin (…/gsplat_metal.mm:358-361).
- * Emits (tile<<32 | depth_key, rank) pairs at the scan offsets, stable radix-sorts them
- * by tile, and writes tile ranges. `total_pairs` is status[GSB_STATUS_TOTAL_PAIRS]. */
+ * Emits (tile, rank) pairs at the scan offsets, stable radix-sorts them by tile (32-bit
+ * keys), and writes tile ranges. `total_pairs` is status[GSB_STATUS_TOTAL_PAIRS].
+ * `keys` is optional (NULL skips it): it receives (tile<<32 | depth_key) of each sorted
+ * pair, the full 64-bit order key. */
 size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64_t total_pairs);
 int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
                  int64_t total_pairs, uint64_t* keys, int32_t* binned_ids, int32_t* tile_offsets,
