@@ -169,6 +169,21 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
   }
 }
 
+// Scratch that later kernels of the same phase need cleared, zeroed by the
+// phase's first kernel instead of separate memset launches.
+struct ZeroList {
+  uint32_t* ptr[3];
+  size_t words[3];
+};
+
+__device__ __forceinline__ void zero_words(const ZeroList& z) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t t0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+    for (size_t i = t0; i < z.words[r]; i += stride) z.ptr[r][i] = 0u;
+}
+
 // Per splat in input order: depth-sort key (view in the high word) and the
 // exact number of tiles its support ellipse touches; the pair total is added
 // into status words 4-5 (64-bit) for the host's early read.
@@ -177,8 +192,9 @@ __global__ void __launch_bounds__(256)
     k_prepare(Meta m, const float2* __restrict__ means2d, const float* __restrict__ conics,
               const float* __restrict__ opacities, const float* __restrict__ depths,
               K* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
-              uint32_t* __restrict__ counts, uint32_t* __restrict__ status) {
+              uint32_t* __restrict__ counts, uint32_t* __restrict__ status, ZeroList zero) {
   __shared__ WarpTilesSmem s_warp[8];
+  zero_words(zero);  // the depth sort's and the scan's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = i < m.BG;
@@ -344,8 +360,10 @@ __global__ void __launch_bounds__(kScanThreads)
 // the tile key then leaves each tile's list in rank (= depth) order.
 __global__ void __launch_bounds__(256)
     k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
-           uint32_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status) {
+           uint32_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status,
+           ZeroList zero) {
   __shared__ WarpTilesSmem s_warp[8];
+  zero_words(zero);  // the tile sort's scratch
   __shared__ int s_start[8][32], s_cnt[8][32];
   __shared__ uint32_t s_tbase[8][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -442,7 +460,7 @@ extern "C" size_t gsb_bin_prepare_workspace_size(const gsb_raster_meta* meta) {
   PrepareWs w;
   carve_prepare(c, m, &w);
   radix_sort_pairs(c, (const uint64_t*)nullptr, nullptr, nullptr, nullptr, m.BG, 0, depth_sort_end_bit(m), nullptr,
-                   0);
+                   0, false);
   return c.off + 256;
 }
 
@@ -463,14 +481,24 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   Carver c(workspace);
   PrepareWs w;
   carve_prepare(c, m, &w);
+  const int parts = (m.BG + kScanTile - 1) / kScanTile;
+  const ZeroRegion sz = radix_sort_zero_region(c, m.BG, 0, depth_keys32(m) ? 32 : depth_sort_end_bit(m),
+                                               depth_keys32(m));
+  ZeroList zero;
+  zero.ptr[0] = reinterpret_cast<uint32_t*>(w.lookback);
+  zero.words[0] = 2 * (size_t)(parts + 1);
+  zero.ptr[1] = w.counter;
+  zero.words[1] = 1;
+  zero.ptr[2] = sz.ptr;
+  zero.words[2] = sz.words;
   if (depth_keys32(m))
     k_prepare<uint32_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
                                                                opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in),
-                                                               w.vals_in, w.counts, status);
+                                                               w.vals_in, w.counts, status, zero);
   else
     k_prepare<uint64_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
                                                                opacities, depths, w.keys_in, w.vals_in, w.counts,
-                                                               status);
+                                                               status, zero);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
@@ -493,24 +521,23 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
   Carver c(workspace);
   PrepareWs w;
   carve_prepare(c, m, &w);
+  // k_prepare (gsb_bin_count) cleared the scan's look-back words and counter
+  // and the depth sort's scratch.
   const int parts = (m.BG + kScanTile - 1) / kScanTile;
-  cudaError_t e = cudaMemsetAsync(w.lookback, 0, sizeof(unsigned long long) * (parts + 1), stream);
-  if (e != cudaSuccess) return GSB_ERR_CUDA;
-  e = cudaMemsetAsync(w.counter, 0, sizeof(uint32_t), stream);
-  if (e != cudaSuccess) return GSB_ERR_CUDA;
+  cudaError_t e;
   if (depth_keys32(m)) {
     uint32_t* k32_in = reinterpret_cast<uint32_t*>(w.keys_in);
     uint32_t* k32_sorted = reinterpret_cast<uint32_t*>(w.keys_sorted);
     // 32-bit keys in the 64-bit key buffers; the sort's scratch (carved after
     // them) is smaller than the 64-bit sort's that the workspace is sized for.
-    e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream);
+    e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream, true);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
     k_gather_scan<uint32_t><<<parts, kScanThreads, 0, stream>>>(
         m, k32_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities, w.counts,
         reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
   } else {
     e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
-                         status, stream);
+                         status, stream, true);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
     k_gather_scan<uint64_t><<<parts, kScanThreads, 0, stream>>>(
         m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
@@ -551,7 +578,7 @@ extern "C" size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64
   EmitWs w;
   carve_emit(c, total_pairs, &w);
   radix_sort_pairs(c, (const uint32_t*)nullptr, nullptr, nullptr, nullptr, total_pairs, 0, tile_end_bit(m), nullptr,
-                   0);
+                   0, false);
   return c.off + 256;
 }
 
@@ -577,11 +604,17 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   Carver c(workspace);
   EmitWs w;
   carve_emit(c, total_pairs, &w);
+  const ZeroRegion sz = radix_sort_zero_region(c, total_pairs, 0, tile_end_bit(m), true);
+  ZeroList zero;
+  zero.ptr[0] = sz.ptr;
+  zero.words[0] = sz.words;
+  zero.ptr[1] = zero.ptr[2] = nullptr;
+  zero.words[1] = zero.words[2] = 0;
   k_emit<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float4*>(rec), pair_offsets,
-                                                w.keys, w.vals, status);
+                                                w.keys, w.vals, status, zero);
   note_launches(1);
   cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
-                                   total_pairs, 0, tile_end_bit(m), status, stream);
+                                   total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
   k_ranges<<<grid1d(total_pairs, 256), 256, 0, stream>>>(w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
                                                          reinterpret_cast<const float4*>(rec), total_pairs,

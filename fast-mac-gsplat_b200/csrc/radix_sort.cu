@@ -282,7 +282,7 @@ static int sort_items(int64_t n) {
 template <typename K>
 static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32_t* vals_in, K* keys_out,
                                       uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                                      cudaStream_t stream) {
+                                      cudaStream_t stream, bool scratch_zeroed) {
   const int passes = sort_passes(begin_bit, end_bit);
   const int items = sort_items(n);
   const int64_t tile = (int64_t)kSortThreads * items;
@@ -306,8 +306,10 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
   const int last_bits = (end_bit - begin_bit) - (passes - 1) * kRadixBits;
   cudaError_t e = onesweep_smem_optin<K>();
   if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
-  if (e != cudaSuccess) return e;
+  if (!scratch_zeroed) {
+    e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
+    if (e != cudaSuccess) return e;
+  }
   rs_histogram<K><<<grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream>>>(keys_in, n, begin_bit, passes,
                                                                                    last_bits, hist);
   note_launches(1);
@@ -335,21 +337,43 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
 
 cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
                              uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                             cudaStream_t stream) {
-  return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream);
+                             cudaStream_t stream, bool scratch_zeroed) {
+  return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream,
+                            scratch_zeroed);
 }
 
 cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                              uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                             cudaStream_t stream) {
-  return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream);
+                             cudaStream_t stream, bool scratch_zeroed) {
+  return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream,
+                            scratch_zeroed);
+}
+
+template <typename K>
+static ZeroRegion radix_sort_zero_region_t(Carver ws, int64_t n, int begin_bit, int end_bit) {
+  const int passes = sort_passes(begin_bit, end_bit);
+  const int64_t tile = (int64_t)kSortThreads * sort_items(n);
+  const int64_t parts = (n + tile - 1) / tile;
+  ws.take<K>(passes > 1 ? (size_t)n : 0);
+  ws.take<uint32_t>(passes > 1 ? (size_t)n : 0);
+  const size_t zero_words = (size_t)kMaxPasses * kRadix + kMaxPasses + (size_t)passes * (size_t)parts * kRadix;
+  ZeroRegion z;
+  z.words = zero_words;
+  z.ptr = ws.take<uint32_t>(zero_words);
+  return z;
+}
+
+ZeroRegion radix_sort_zero_region(Carver ws, int64_t n, int begin_bit, int end_bit, bool keys32) {
+  return keys32 ? radix_sort_zero_region_t<uint32_t>(ws, n, begin_bit, end_bit)
+                : radix_sort_zero_region_t<uint64_t>(ws, n, begin_bit, end_bit);
 }
 
 }  // namespace gsb
 
 extern "C" size_t gsb_radix_sort_pairs_workspace_size(int64_t n, int begin_bit, int end_bit) {
   gsb::Carver c(nullptr);
-  gsb::radix_sort_pairs(c, (const uint64_t*)nullptr, nullptr, nullptr, nullptr, n, begin_bit, end_bit, nullptr, 0);
+  gsb::radix_sort_pairs(c, (const uint64_t*)nullptr, nullptr, nullptr, nullptr, n, begin_bit, end_bit, nullptr, 0,
+                        false);
   return c.off + 256;
 }
 
@@ -364,7 +388,7 @@ extern "C" int gsb_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* val
   if (workspace_bytes < gsb_radix_sort_pairs_workspace_size(n, begin_bit, end_bit)) return GSB_ERR_WORKSPACE;
   if (n > 0 && workspace == nullptr) return GSB_ERR_WORKSPACE;
   gsb::Carver c(workspace);
-  const cudaError_t e = gsb::radix_sort_pairs(c, keys_in, vals_in, keys_out, vals_out, n, begin_bit,
-                                              end_bit, status, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = gsb::radix_sort_pairs(c, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit,
+                                              status, static_cast<cudaStream_t>(stream), false);
   return e == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }

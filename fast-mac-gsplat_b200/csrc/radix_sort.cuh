@@ -27,12 +27,22 @@ inline int sort_passes(int begin_bit, int end_bit) {
 // Carves the sort's scratch: temp key/value buffers, histograms, partition
 // counters and per-pass look-back tiles. Returns the status of the launches
 // when running (base != nullptr); measuring mode launches nothing.
+// scratch_zeroed: the caller has already cleared the sort's zero-initialised
+// scratch (radix_sort_zero_region) in an earlier kernel, saving a memset launch.
 cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in,
                              uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
-                             int end_bit, uint32_t* status, cudaStream_t stream);
+                             int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed);
 // 32-bit keys (end_bit <= 32): 8 bytes per pair moved per pass instead of 12.
 cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in,
                              uint32_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
-                             int end_bit, uint32_t* status, cudaStream_t stream);
+                             int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed);
+
+// The words a radix_sort_pairs call carved from `ws` (at its current offset)
+// needs cleared before it runs (histograms, partition counters, look-back).
+struct ZeroRegion {
+  uint32_t* ptr = nullptr;
+  size_t words = 0;
+};
+ZeroRegion radix_sort_zero_region(Carver ws, int64_t n, int begin_bit, int end_bit, bool keys32);
 
 }  // namespace gsb
