@@ -8,6 +8,8 @@
 // camera axes in its columns (x_cam = R^T (m - t)), +z is forward, EWA adds 0.3
 // to the 2D covariance diagonal and clamps the determinant at 1e-6, splats with
 // z <= near_plane get opacity 0.
+#include <algorithm>
+
 #include "gsb_common.cuh"
 #include "gsb_host.cuh"
 
@@ -159,17 +161,14 @@ __device__ __forceinline__ void sym_bilinear_bwd(float g, const float3& u, const
 
 __device__ __forceinline__ float3 add3(float3 a, float3 b) { return make_float3(a.x + b.x, a.y + b.y, a.z + b.z); }
 
-__global__ void __launch_bounds__(256)
-    k_project_bwd(int B, int G, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
-                  const float* __restrict__ g_opac_in, const float* __restrict__ g_depth,
-                  const float* __restrict__ means3d, const float* __restrict__ scales,
-                  const float4* __restrict__ quats, const float* __restrict__ c2w, const float* __restrict__ cam,
-                  float near_plane, float* __restrict__ g_means3d, float* __restrict__ g_scales,
-                  float4* __restrict__ g_quats, float* __restrict__ g_opac, float* __restrict__ g_c2w,
-                  float* __restrict__ g_cam) {
-  const int64_t n = (int64_t)B * G;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const bool active = i < n;
+// VJP of one Gaussian: writes its per-Gaussian gradients and returns its view;
+// cg receives its 16 camera-gradient terms (zeros when !active).
+__device__ __forceinline__ int project_bwd_one(
+    int G, int64_t n, int64_t i, bool active, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
+    const float* __restrict__ g_opac_in, const float* __restrict__ g_depth, const float* __restrict__ means3d,
+    const float* __restrict__ scales, const float4* __restrict__ quats, const float* __restrict__ c2w,
+    const float* __restrict__ cam, float near_plane, float* __restrict__ g_means3d, float* __restrict__ g_scales,
+    float4* __restrict__ g_quats, float* __restrict__ g_opac, float (&cg)[16]) {
   const int64_t ii = active ? i : n - 1;  // inactive lanes recompute a valid item, contribute zeros
   const int b = (int)(ii / G);
   const Cam k = load_cam(c2w, cam, b);
@@ -315,9 +314,6 @@ __global__ void __launch_bounds__(256)
     g_opac[i] = p.front ? ((g_opac_in) ? g_opac_in[i] : 0.f) : 0.f;
   }
 
-  // Camera gradients: 16 per-view sums. Warp-reduce when the whole warp sees
-  // one view (the common case), then one atomic per value per warp.
-  float cg[16];
   cg[0] = g_col0.x; cg[1] = g_col1.x; cg[2] = g_col2.x; cg[3] = -g_dx;
   cg[4] = g_col0.y; cg[5] = g_col1.y; cg[6] = g_col2.y; cg[7] = -g_dy;
   cg[8] = g_col0.z; cg[9] = g_col1.z; cg[10] = g_col2.z; cg[11] = -g_dz;
@@ -326,28 +322,78 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int t = 0; t < 16; ++t) cg[t] = 0.f;
   }
-  const int lane = threadIdx.x & 31;
-  const int b0 = __shfl_sync(kFullMask, b, 0);
-  const bool uniform = __all_sync(kFullMask, b == b0);
-  if (uniform) {
+  return b;
+}
+
+__device__ __forceinline__ void cam_grad_atomics(float* g_c2w, float* g_cam, int b, const float (&v)[16]) {
+#pragma unroll
+  for (int t = 0; t < 12; ++t) atomicAdd(&g_c2w[16 * b + t], v[t]);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) atomicAdd(&g_cam[4 * b + t], v[12 + t]);
+}
+
+// Persistent grid (a few CTAs per SM), one Gaussian per thread per iteration.
+// The 16 per-view camera-gradient sums are accumulated per thread, then
+// reduced across the CTA in shared memory: one atomic per value per CTA
+// instead of per warp (all of a view's atomics hit one cache line, so their
+// number sets the cost: 16 per warp at c4 serialised to ~0.46 ms).
+__global__ void __launch_bounds__(256)
+    k_project_bwd(int B, int G, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
+                  const float* __restrict__ g_opac_in, const float* __restrict__ g_depth,
+                  const float* __restrict__ means3d, const float* __restrict__ scales,
+                  const float4* __restrict__ quats, const float* __restrict__ c2w, const float* __restrict__ cam,
+                  float near_plane, float* __restrict__ g_means3d, float* __restrict__ g_scales,
+                  float4* __restrict__ g_quats, float* __restrict__ g_opac, float* __restrict__ g_c2w,
+                  float* __restrict__ g_cam) {
+  __shared__ float s_red[8][16];
+  __shared__ int s_view;
+  const int64_t n = (int64_t)B * G;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+  int cur = -1;  // view of acc
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < n; base += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    const bool active = i < n;
+    float cg[16];
+    const int b = project_bwd_one(G, n, i, active, g_m2d, g_con, g_opac_in, g_depth, means3d, scales, quats, c2w,
+                                  cam, near_plane, g_means3d, g_scales, g_quats, g_opac, cg);
+    if (active) {
+      if (b != cur) {  // a thread crosses into the next view: flush the previous one
+        if (cur >= 0) cam_grad_atomics(g_c2w, g_cam, cur, acc);
+#pragma unroll
+        for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+        cur = b;
+      }
+#pragma unroll
+      for (int t = 0; t < 16; ++t) acc[t] += cg[t];
+    }
+  }
+  if (threadIdx.x == 0) s_view = -1;
+  __syncthreads();
+  if (cur >= 0) atomicMax(&s_view, cur);
+  __syncthreads();
+  const int ref = s_view;
+  if (__syncthreads_and(cur < 0 || cur == ref)) {
+    if (ref < 0) return;  // the CTA had no Gaussian
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
-      float v = cg[t];
+      float v = acc[t];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
-      cg[t] = v;
+      if (lane == 0) s_red[warp][t] = v;
     }
-    if (lane == 0) {
+    __syncthreads();
+    if (threadIdx.x < 16) {
+      float v = 0.f;
 #pragma unroll
-      for (int t = 0; t < 12; ++t) atomicAdd(&g_c2w[16 * b0 + t], cg[t]);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) atomicAdd(&g_cam[4 * b0 + t], cg[12 + t]);
+      for (int w = 0; w < 8; ++w) v += s_red[w][threadIdx.x];
+      if (threadIdx.x < 12) atomicAdd(&g_c2w[16 * ref + threadIdx.x], v);
+      else atomicAdd(&g_cam[4 * ref + threadIdx.x - 12], v);
     }
-  } else if (active) {
-#pragma unroll
-    for (int t = 0; t < 12; ++t) atomicAdd(&g_c2w[16 * b + t], cg[t]);
-#pragma unroll
-    for (int t = 0; t < 4; ++t) atomicAdd(&g_cam[4 * b + t], cg[12 + t]);
+  } else if (cur >= 0) {
+    cam_grad_atomics(g_c2w, g_cam, cur, acc);
   }
 }
 
@@ -399,7 +445,11 @@ extern "C" int gsb_project_backward(int32_t batch_size, int32_t gaussians_per_ba
   if (!means3d || !scales || !quats || !camera_to_world || !camera_params || !g_means3d || !g_scales ||
       !g_quats || !g_opacities)
     return GSB_ERR_INVALID_ARGUMENT;
-  k_project_bwd<<<grid1d(n, 256), 256, 0, stream>>>(
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n + 255) / 256;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, 2 * (int64_t)sms));
+  k_project_bwd<<<grid, 256, 0, stream>>>(
       batch_size, gaussians_per_batch, reinterpret_cast<const float2*>(grad_means2d), grad_conics, grad_opacities,
       grad_depths, means3d, scales, reinterpret_cast<const float4*>(quats), camera_to_world, camera_params,
       near_plane, g_means3d, g_scales, reinterpret_cast<float4*>(g_quats), g_opacities, g_camera_to_world,
