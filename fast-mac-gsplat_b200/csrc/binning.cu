@@ -91,11 +91,14 @@ __device__ __forceinline__ int cand_row(int local, int w) {
   return r;
 }
 
+constexpr int kMaskCands = 64;  // splats with at most this many candidate tiles keep a hit mask
+
 // Per-warp shared state of warp_tiles.
 struct WarpTilesSmem {
   SplatTiles t[32];
-  int incl[32];  // inclusive scan of the candidate counts
-  int hits[32];  // running hit count per owner
+  int incl[32];                  // inclusive scan of the candidate counts
+  int hits[32];                  // running hit count per owner
+  unsigned long long mask[32];   // hit mask per owner with <= kMaskCands candidates (kMasks)
 };
 
 // Visits every candidate tile of the warp's 32 splats (lane j owns splat j),
@@ -104,8 +107,9 @@ struct WarpTilesSmem {
 // candidate count / 32 rounds however unevenly the splats are sized. Hits are
 // numbered per owner in row-major tile order (the reference's loop order):
 // visit(owner, tx, ty, slot) runs for each hit with slot = its index in the
-// owner's list. On return sm.hits[j] is splat j's hit count.
-template <typename Visit>
+// owner's list and local = its candidate index in the owner's row-major box.
+// On return sm.hits[j] is splat j's hit count.
+template <bool kMasks = false, typename Visit>
 __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m, WarpTilesSmem& sm,
                                            Visit&& visit) {
   const int lane = threadIdx.x & 31;
@@ -117,24 +121,28 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
   }
   const long long total = __shfl_sync(kFullMask, incl, 31);
   sm.hits[lane] = 0;
+  sm.t[lane] = mine;
+  if (kMasks) sm.mask[lane] = 0ull;
   if (total > 0x7fffffffll) {
     // Beyond int range for the warp: each lane walks its own candidates.
     int cnt = 0;
     for (int local = 0; local < mine.n; ++local) {
       const int row = cand_row(local, mine.w);
       const int tx = mine.tx0 + (local - row * mine.w), ty = mine.ty0 + row;
-      if (tile_hit(mine, tx, ty, m)) visit(lane, tx, ty, cnt++);
+      if (tile_hit(mine, tx, ty, m)) {
+        if (kMasks && mine.n <= kMaskCands) sm.mask[lane] |= 1ull << local;
+        visit(lane, tx, ty, cnt++, local);
+      }
     }
     sm.hits[lane] = cnt;
     __syncwarp();
     return;
   }
-  sm.t[lane] = mine;
   sm.incl[lane] = (int)incl;
   __syncwarp();
   for (int base = 0; base < (int)total; base += 32) {
     const int k = base + lane;
-    int owner = -1, tx = 0, ty = 0;
+    int owner = -1, tx = 0, ty = 0, local = 0;
     bool hit = false;
     if (k < (int)total) {
       int lo = 0, hi = 31;  // first owner whose inclusive end exceeds k
@@ -146,7 +154,7 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
       }
       owner = lo;
       const SplatTiles& s = sm.t[owner];
-      const int local = k - (owner ? sm.incl[owner - 1] : 0);
+      local = k - (owner ? sm.incl[owner - 1] : 0);
       const int row = cand_row(local, s.w);
       tx = s.tx0 + (local - row * s.w);
       ty = s.ty0 + row;
@@ -163,8 +171,13 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
     const int before = __popc(hits & seg & ((1u << lane) - 1u));
     const int base_slot = owner >= 0 ? sm.hits[owner] : 0;
     __syncwarp();
-    if (lane == seg0 && owner >= 0) sm.hits[owner] = base_slot + __popc(hits & seg);
-    if (hit) visit(owner, tx, ty, base_slot + before);
+    if (lane == seg0 && owner >= 0) {
+      sm.hits[owner] = base_slot + __popc(hits & seg);
+      // The segment's lanes hold consecutive candidates local, local+1, ...
+      if (kMasks && sm.t[owner].n <= kMaskCands)
+        sm.mask[owner] |= (unsigned long long)((hits & seg) >> seg0) << local;
+    }
+    if (hit) visit(owner, tx, ty, base_slot + before, local);
     __syncwarp();
   }
 }
@@ -192,7 +205,8 @@ __global__ void __launch_bounds__(256)
     k_prepare(Meta m, const float2* __restrict__ means2d, const float* __restrict__ conics,
               const float* __restrict__ opacities, const float* __restrict__ depths,
               K* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
-              uint32_t* __restrict__ counts, uint32_t* __restrict__ status, ZeroList zero) {
+              uint32_t* __restrict__ counts, unsigned long long* __restrict__ masks, uint32_t* __restrict__ status,
+              ZeroList zero) {
   __shared__ WarpTilesSmem s_warp[8];
   zero_words(zero);  // the depth sort's and the scan's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -208,9 +222,15 @@ __global__ void __launch_bounds__(256)
     t = splat_tiles(mu.x, mu.y, conics[3 * i + 0], conics[3 * i + 1], conics[3 * i + 2], opacities[i], m);
   }
   WarpTilesSmem& sm = s_warp[warp];
-  warp_tiles(t, m, sm, [](int, int, int, int) {});
+  // Splats with at most kMaskCands candidates also record which ones hit, so
+  // k_emit writes their pairs without testing the tiles again.
+  warp_tiles<true>(t, m, sm, [](int, int, int, int, int) {});
+  __syncwarp();
   const uint32_t n = valid ? (uint32_t)sm.hits[lane] : 0u;
-  if (valid) counts[i] = n;
+  if (valid) {
+    counts[i] = n;
+    masks[i] = sm.mask[lane];
+  }
   unsigned long long wsum = n;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(kFullMask, wsum, o);
@@ -226,6 +246,7 @@ __global__ void __launch_bounds__(kScanThreads)
                   const uint32_t* __restrict__ sorted_vals, const float2* __restrict__ means2d,
                   const float* __restrict__ conics, const float* __restrict__ colors,
                   const float* __restrict__ opacities, const uint32_t* __restrict__ counts,
+                  const unsigned long long* __restrict__ masks_in, unsigned long long* __restrict__ masks_out,
                   float4* __restrict__ rec, int32_t* __restrict__ perm,
                   int32_t* __restrict__ pair_offsets, unsigned long long* __restrict__ lookback,
                   uint32_t* __restrict__ part_counter, uint32_t* __restrict__ status) {
@@ -275,6 +296,7 @@ __global__ void __launch_bounds__(kScanThreads)
       rec[3 * r + 2] = make_float4(cbl[i], __uint_as_float(dk[i]), vis_log_threshold(op[i], m.alpha_thr, m.max_alpha),
                                    sat_log_threshold(op[i], m.max_alpha));
       perm[r] = (int32_t)(orig[i] - (uint32_t)b * (uint32_t)m.G);
+      if (masks_out) masks_out[r] = masks_in[orig[i]];
     }
   }
   // Block-wide exclusive scan of the thread sums.
@@ -360,53 +382,90 @@ __global__ void __launch_bounds__(kScanThreads)
 // the tile key then leaves each tile's list in rank (= depth) order.
 __global__ void __launch_bounds__(256)
     k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
-           uint32_t* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t* __restrict__ status,
-           ZeroList zero) {
+           const unsigned long long* __restrict__ masks, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+           uint32_t* __restrict__ status, ZeroList zero) {
   __shared__ WarpTilesSmem s_warp[8];
-  zero_words(zero);  // the tile sort's scratch
   __shared__ int s_start[8][32], s_cnt[8][32];
   __shared__ uint32_t s_tbase[8][32];
+  zero_words(zero);  // the tile sort's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = r < m.BG;
   SplatTiles t = splat_tiles(0.f, 0.f, 0.f, 0.f, 0.f, 0.f, m);
   int start = 0, cnt = 0;
+  uint32_t tbase = 0;
   if (valid) {
     start = pair_offsets[r];
     cnt = pair_offsets[r + 1] - start;
     const float4 p0 = rec[3 * r + 0];
     const float4 p1 = rec[3 * r + 1];
-    s_tbase[warp][lane] = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
+    tbase = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
     if (cnt > 0) t = splat_tiles(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m);
+  }
+  // A splat with a recorded hit mask writes its pairs straight from it (the
+  // set bits in row-major candidate order); the others are tested again.
+  int own_hits = -1;
+  if (masks && t.n > 0 && t.n <= kMaskCands) {
+    unsigned long long bits = masks[r];
+    own_hits = __popcll(bits);
+    int slot = 0;
+    while (bits && slot < cnt) {
+      const int local = __ffsll(bits) - 1;
+      bits &= bits - 1;
+      const int row = cand_row(local, t.w);
+      const int tx = t.tx0 + (local - row * t.w), ty = t.ty0 + row;
+      keys[(int64_t)start + slot] = tbase + (uint32_t)(ty * m.tiles_x + tx);
+      vals[(int64_t)start + slot] = (uint32_t)r;
+      ++slot;
+    }
+    t.n = 0;
   }
   s_start[warp][lane] = start;
   s_cnt[warp][lane] = cnt;
+  s_tbase[warp][lane] = tbase;
   WarpTilesSmem& sm = s_warp[warp];
   const int r0 = r - lane;
-  warp_tiles(t, m, sm, [&](int owner, int tx, int ty, int slot) {
+  warp_tiles(t, m, sm, [&](int owner, int tx, int ty, int slot, int) {
     if (slot < s_cnt[warp][owner]) {
       const int64_t idx = (int64_t)s_start[warp][owner] + slot;
       keys[idx] = s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx);
       vals[idx] = (uint32_t)(r0 + owner);
     }
   });
-  if (valid && sm.hits[lane] != cnt) raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteEmit);
+  const int hits = own_hits >= 0 ? own_hits : sm.hits[lane];
+  if (valid && hits != cnt) raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteEmit);
 }
 
 // tile_offsets[t] = index of the first sorted pair of tile t (= exclusive
 // prefix of per-tile counts); every entry is written by exactly one thread.
+// A thread takes 4 consecutive sorted pairs (one 16-byte load of keys).
 // keys64 (optional) receives (tile << 32) | depth_key of each sorted pair.
 __global__ void __launch_bounds__(256)
     k_ranges(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, const float4* __restrict__ rec,
              int64_t n_pairs, int total_tiles, int32_t* __restrict__ tile_offsets, uint64_t* __restrict__ keys64) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_pairs) return;
-  const int64_t t = keys[i];
-  const int64_t tp = (i == 0) ? -1 : (int64_t)keys[i - 1];
-  for (int64_t s = tp + 1; s <= t; ++s) tile_offsets[s] = (int32_t)i;
-  if (i == n_pairs - 1)
-    for (int64_t s = t + 1; s <= total_tiles; ++s) tile_offsets[s] = (int32_t)n_pairs;
-  if (keys64) keys64[i] = ((uint64_t)t << 32) | __float_as_uint(rec[3 * (size_t)vals[i] + 2].y);
+  const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i0 >= n_pairs) return;
+  uint32_t k[4];
+  if (i0 + 4 <= n_pairs) {
+    const uint4 q = *reinterpret_cast<const uint4*>(keys + i0);  // keys is 256-byte aligned
+    k[0] = q.x, k[1] = q.y, k[2] = q.z, k[3] = q.w;
+  } else {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) k[u] = (i0 + u < n_pairs) ? keys[i0 + u] : 0u;
+  }
+  int64_t prev = (i0 == 0) ? -1 : (int64_t)keys[i0 - 1];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t i = i0 + u;
+    if (i < n_pairs) {
+      const int64_t t = k[u];
+      for (int64_t s = prev + 1; s <= t; ++s) tile_offsets[s] = (int32_t)i;
+      if (i == n_pairs - 1)
+        for (int64_t s = t + 1; s <= total_tiles; ++s) tile_offsets[s] = (int32_t)n_pairs;
+      if (keys64) keys64[i] = ((uint64_t)t << 32) | __float_as_uint(rec[3 * (size_t)vals[i] + 2].y);
+      prev = t;
+    }
+  }
 }
 
 __global__ void k_fill_i32(int32_t* __restrict__ p, int64_t n, int32_t v) {
@@ -430,6 +489,7 @@ struct PrepareWs {
   uint64_t* keys_sorted;
   uint32_t* vals_sorted;
   uint32_t* counts;
+  unsigned long long* masks;  // hit masks of splats with <= kMaskCands candidates, input order
   unsigned long long* lookback;
   uint32_t* counter;
 };
@@ -441,6 +501,7 @@ void carve_prepare(Carver& c, const Meta& m, PrepareWs* w) {
   w->keys_sorted = c.take<uint64_t>(n);
   w->vals_sorted = c.take<uint32_t>(n);
   w->counts = c.take<uint32_t>(n);
+  w->masks = c.take<unsigned long long>(n);
   w->lookback = c.take<unsigned long long>((n + kScanTile - 1) / kScanTile + 1);
   w->counter = c.take<uint32_t>(1);
 }
@@ -494,19 +555,19 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   if (depth_keys32(m))
     k_prepare<uint32_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
                                                                opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in),
-                                                               w.vals_in, w.counts, status, zero);
+                                                               w.vals_in, w.counts, w.masks, status, zero);
   else
     k_prepare<uint64_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
                                                                opacities, depths, w.keys_in, w.vals_in, w.counts,
-                                                               status, zero);
+                                                               w.masks, status, zero);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
 
 extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const float* conics,
                                  const float* colors, const float* opacities, const float* depths, int32_t* perm,
-                                 float* rec, int32_t* pair_offsets, uint32_t* status, void* workspace,
-                                 size_t workspace_bytes, void* stream_) {
+                                 float* rec, int32_t* pair_offsets, uint64_t* tile_masks, uint32_t* status,
+                                 void* workspace, size_t workspace_bytes, void* stream_) {
   Meta m;
   int rc = make_meta(meta, &m);
   if (rc != GSB_OK) return rc;
@@ -534,14 +595,16 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
     if (e != cudaSuccess) return GSB_ERR_CUDA;
     k_gather_scan<uint32_t><<<parts, kScanThreads, 0, stream>>>(
         m, k32_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities, w.counts,
-        reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
+        w.masks, reinterpret_cast<unsigned long long*>(tile_masks), reinterpret_cast<float4*>(rec), perm,
+        pair_offsets, w.lookback, w.counter, status);
   } else {
     e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
                          status, stream, true);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
     k_gather_scan<uint64_t><<<parts, kScanThreads, 0, stream>>>(
         m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
-        w.counts, reinterpret_cast<float4*>(rec), perm, pair_offsets, w.lookback, w.counter, status);
+        w.counts, w.masks, reinterpret_cast<unsigned long long*>(tile_masks), reinterpret_cast<float4*>(rec), perm,
+        pair_offsets, w.lookback, w.counter, status);
   }
   note_launches(1);
   return cuda_status(cudaGetLastError());
@@ -553,8 +616,8 @@ extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d
                                size_t workspace_bytes, void* stream) {
   int rc = gsb_bin_count(meta, means2d, conics, opacities, depths, status, workspace, workspace_bytes, stream);
   if (rc != GSB_OK) return rc;
-  return gsb_bin_sort_scan(meta, means2d, conics, colors, opacities, depths, perm, rec, pair_offsets, status,
-                           workspace, workspace_bytes, stream);
+  return gsb_bin_sort_scan(meta, means2d, conics, colors, opacities, depths, perm, rec, pair_offsets,
+                           /*tile_masks=*/nullptr, status, workspace, workspace_bytes, stream);
 }
 
 namespace {
@@ -583,7 +646,7 @@ extern "C" size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64
 }
 
 extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
-                            int64_t total_pairs, uint64_t* keys, int32_t* binned_ids,
+                            const uint64_t* tile_masks, int64_t total_pairs, uint64_t* keys, int32_t* binned_ids,
                             int32_t* tile_offsets, uint32_t* status, void* workspace,
                             size_t workspace_bytes, void* stream_) {
   Meta m;
@@ -611,12 +674,13 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   zero.ptr[1] = zero.ptr[2] = nullptr;
   zero.words[1] = zero.words[2] = 0;
   k_emit<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float4*>(rec), pair_offsets,
-                                                w.keys, w.vals, status, zero);
+                                                reinterpret_cast<const unsigned long long*>(tile_masks), w.keys,
+                                                w.vals, status, zero);
   note_launches(1);
   cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
                                    total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-  k_ranges<<<grid1d(total_pairs, 256), 256, 0, stream>>>(w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
+  k_ranges<<<grid1d((total_pairs + 3) / 4, 256), 256, 0, stream>>>(w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
                                                          reinterpret_cast<const float4*>(rec), total_pairs,
                                                          m.total_tiles, tile_offsets, keys);
   note_launches(1);

@@ -216,6 +216,7 @@ std::vector<Tensor> forward(Tensor means2d, Tensor conics, Tensor colors, Tensor
   Tensor perm = empty({B, G}, at::kInt, dev);
   Tensor rec = empty({BG, GSB_REC_FLOATS}, at::kFloat, dev);
   Tensor pair_offsets = empty({BG + 1}, at::kInt, dev);
+  Tensor tile_masks = empty({BG}, at::kLong, dev);
   Tensor ws = empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 1))}, at::kByte, dev);
   auto cur = at::cuda::getCurrentCUDAStream(dev.index());
   PairRead& pr = pair_read();
@@ -230,7 +231,8 @@ std::vector<Tensor> forward(Tensor means2d, Tensor conics, Tensor colors, Tensor
     pr.host.copy_(status.narrow(0, GSB_STATUS_PAIR_TOTAL64, 2).view(at::kLong), /*non_blocking=*/true);
     pr.done.record(cur);
     check(gsb_bin_sort_scan(&meta, ptr<float>(m2), ptr<float>(q2), ptr<float>(c2), ptr<float>(o2), ptr<float>(d2),
-                            ptr<int32_t>(perm), ptr<float>(rec), ptr<int32_t>(pair_offsets), ptr<uint32_t>(status),
+                            ptr<int32_t>(perm), ptr<float>(rec), ptr<int32_t>(pair_offsets), ptr<uint64_t>(tile_masks),
+                            ptr<uint32_t>(status),
                             ws.data_ptr(), ws_bytes, stream),
           "gsb_bin_sort_scan");
   }
@@ -246,7 +248,8 @@ std::vector<Tensor> forward(Tensor means2d, Tensor conics, Tensor colors, Tensor
   Tensor ws2 = empty({static_cast<int64_t>(std::max<size_t>(ws2_bytes, 1))}, at::kByte, dev);
   {
     Phase ph("bin_emit", means2d);
-    check(gsb_bin_emit(&meta, ptr<float>(rec), ptr<int32_t>(pair_offsets), P, /*keys=*/nullptr,
+    check(gsb_bin_emit(&meta, ptr<float>(rec), ptr<int32_t>(pair_offsets), ptr<uint64_t>(tile_masks), P,
+                       /*keys=*/nullptr,
                        ptr<int32_t>(binned_ids), ptr<int32_t>(tile_offsets), ptr<uint32_t>(status), ws2.data_ptr(),
                        ws2_bytes, stream),
           "gsb_bin_emit");

@@ -95,9 +95,9 @@ def load() -> C.CDLL:
         "gsb_bin_prepare_workspace_size": (sz, [M]),
         "gsb_bin_prepare": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_bin_count": (C.c_int, [M, p, p, p, p, p, p, sz, p]),
-        "gsb_bin_sort_scan": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
+        "gsb_bin_sort_scan": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_bin_emit_workspace_size": (sz, [M, i64]),
-        "gsb_bin_emit": (C.c_int, [M, p, p, i64, p, p, p, p, p, sz, p]),
+        "gsb_bin_emit": (C.c_int, [M, p, p, p, i64, p, p, p, p, p, sz, p]),
         "gsb_tile_stats": (C.c_int, [M, p, p, p]),
         "gsb_render_workspace_size": (sz, [M]),
         "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),

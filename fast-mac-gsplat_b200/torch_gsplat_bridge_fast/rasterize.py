@@ -389,6 +389,7 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     st.perm = torch.empty((B, G), dtype=torch.int32, device=dev)
     st.rec = torch.empty((BG, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
     st.pair_offsets = torch.empty(BG + 1, dtype=torch.int32, device=dev)
+    tile_masks = torch.empty(BG, dtype=torch.int64, device=dev)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     cur = torch.cuda.current_stream(dev)
     stream = cur.cuda_stream
@@ -407,8 +408,8 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
         counted = _tls.counted_event = torch.cuda.Event()
     counted.record(cur)
     N.check(L.gsb_bin_sort_scan(meta, N.ptr(m2), N.ptr(q2), N.ptr(c2), N.ptr(o2), N.ptr(d2), N.ptr(st.perm),
-                                N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(st.status), N.ptr(ws), ws_bytes,
-                                stream), "gsb_bin_sort_scan")
+                                N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(tile_masks), N.ptr(st.status),
+                                N.ptr(ws), ws_bytes, stream), "gsb_bin_sort_scan")
     counted.synchronize()
     check_device_errors(stream)  # earlier calls' copies on this stream are complete now
     P = int(total_host[0])
@@ -421,7 +422,8 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     st.tile_offsets = torch.empty(T + 1, dtype=torch.int32, device=dev)
     st.keys = torch.empty(P, dtype=torch.int64, device=dev)
     ws2 = torch.empty(max(ws2_bytes, 1), dtype=torch.uint8, device=dev)
-    N.check(L.gsb_bin_emit(meta, N.ptr(st.rec), N.ptr(st.pair_offsets), P, N.ptr(st.keys), N.ptr(st.binned_ids),
+    N.check(L.gsb_bin_emit(meta, N.ptr(st.rec), N.ptr(st.pair_offsets), N.ptr(tile_masks), P, N.ptr(st.keys),
+                           N.ptr(st.binned_ids),
                            N.ptr(st.tile_offsets), N.ptr(st.status), N.ptr(ws2), ws2_bytes, stream), "gsb_bin_emit")
     if _debug_checks():
         _read_status(st.status)

@@ -111,10 +111,13 @@ int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const flo
 int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, const float* conics,
                   const float* opacities, const float* depths, uint32_t* status, void* workspace,
                   size_t workspace_bytes, void* stream);
+/* tile_masks (optional, [B*G] in rank order): for a splat whose snugbox holds at most 64
+ * candidate tiles, bit k marks candidate k (row-major in its box) as hit; gsb_bin_emit
+ * then writes its pairs from the mask instead of testing the tiles again. */
 int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const float* conics,
                       const float* colors, const float* opacities, const float* depths, int32_t* perm,
-                      float* rec, int32_t* pair_offsets, uint32_t* status, void* workspace,
-                      size_t workspace_bytes, void* stream);
+                      float* rec, int32_t* pair_offsets, uint64_t* tile_masks, uint32_t* status,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- binning, phase 2 ---------------------------------------------------
  * Replaces: `emit_binned_ids` (…/gsplat_v8_project3d_kernels.metal:743-780), the per-tile
@@ -122,11 +125,13 @@ int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const f
  * Emits (tile, rank) pairs at the scan offsets, stable radix-sorts them by tile (32-bit
  * keys), and writes tile ranges. `total_pairs` is status[GSB_STATUS_TOTAL_PAIRS].
  * `keys` is optional (NULL skips it): it receives (tile<<32 | depth_key) of each sorted
- * pair, the full 64-bit order key. */
+ * pair, the full 64-bit order key. `tile_masks` is optional: the masks written by
+ * gsb_bin_sort_scan for these records. */
 size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64_t total_pairs);
 int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
-                 int64_t total_pairs, uint64_t* keys, int32_t* binned_ids, int32_t* tile_offsets,
-                 uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+                 const uint64_t* tile_masks, int64_t total_pairs, uint64_t* keys, int32_t* binned_ids,
+                 int32_t* tile_offsets, uint32_t* status, void* workspace, size_t workspace_bytes,
+                 void* stream);
 
 /* Max pairs over tiles -> status[GSB_STATUS_MAX_TILE_COUNT] (overflow check of
  * variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:756-760). */
