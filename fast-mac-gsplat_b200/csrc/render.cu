@@ -395,13 +395,27 @@ __device__ __forceinline__ void vjp_expand(const float* S, float dx, float a, fl
   for (int q = 9; q < 16; ++q) v[q] = 0.0f;
 }
 
-// One warp's prefetch buffer: a short tile's per-pixel state, ids and records.
-struct BwdBuf {
-  float4 rec[kShortMax][3];
+// One warp's shared memory in the backward warp kernel: the per-pixel state of
+// its next tile (single buffer: it is copied to registers when the tile
+// starts, after which the next tile's prefetch may overwrite it), the records
+// and ids of the current and next tile (double buffer), and the rows of the
+// chunked gradient reduction.
+struct BwdState {
   float grad[kTilePixels * 3];  // row-major 16x16 pixels x rgb
   float T[kTilePixels];
   int last[kTilePixels];
+};
+struct BwdRecs {
+  float4 rec[kShortMax][3];
   int ids[kShortMax];
+};
+constexpr int kRedChunk = 3;    // records whose gradients are reduced together
+constexpr int kRedStride = 36;  // padded row (32 lanes + 4): conflict-free 16-byte row reads
+struct BwdWarpSmem {
+  BwdState st;
+  BwdRecs rec[2];
+  float red[kRedChunk * kGradComps][kRedStride];
+  int red_gi[kRedChunk];
 };
 
 struct TileOff {
@@ -417,9 +431,11 @@ __device__ __forceinline__ TileOff load_off(const int32_t* __restrict__ toff, in
   return o;
 }
 
-// Issues (does not wait for) the cp.async copies of one short tile into buf.
-__device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileOff off, BwdBuf* buf, int lane,
-                                                  const float* __restrict__ grad, const float* __restrict__ final_T,
+// Issues (does not wait for) the cp.async copies of one short tile's per-pixel
+// state, records and ids.
+__device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileOff off, BwdState* st,
+                                                  BwdRecs* rb, int lane, const float* __restrict__ grad,
+                                                  const float* __restrict__ final_T,
                                                   const int32_t* __restrict__ last_idx,
                                                   const float4* __restrict__ pair_rec,
                                                   const int32_t* __restrict__ ids) {
@@ -433,11 +449,11 @@ __device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileO
       const int r = q / 20, k = q - r * 20;
       const size_t row_pix = ((size_t)tc.b * m.H + y0 + r) * m.W + x0;
       if (k < 12) {
-        cp_async16(&buf->grad[r * 48 + 4 * k], grad + 3 * row_pix + 4 * k);
+        cp_async16(&st->grad[r * 48 + 4 * k], grad + 3 * row_pix + 4 * k);
       } else if (k < 16) {
-        cp_async16(&buf->T[r * 16 + 4 * (k - 12)], final_T + row_pix + 4 * (k - 12));
+        cp_async16(&st->T[r * 16 + 4 * (k - 12)], final_T + row_pix + 4 * (k - 12));
       } else {
-        cp_async16(&buf->last[r * 16 + 4 * (k - 16)], last_idx + row_pix + 4 * (k - 16));
+        cp_async16(&st->last[r * 16 + 4 * (k - 16)], last_idx + row_pix + 4 * (k - 16));
       }
     }
   } else {
@@ -445,20 +461,45 @@ __device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileO
       const int r = p >> 4, c = p & 15;
       if (x0 + c < m.W && y0 + r < m.H) {
         const size_t pix = ((size_t)tc.b * m.H + y0 + r) * m.W + x0 + c;
-        cp_async4(&buf->grad[3 * p + 0], grad + 3 * pix + 0);
-        cp_async4(&buf->grad[3 * p + 1], grad + 3 * pix + 1);
-        cp_async4(&buf->grad[3 * p + 2], grad + 3 * pix + 2);
-        cp_async4(&buf->T[p], final_T + pix);
-        cp_async4(&buf->last[p], last_idx + pix);
+        cp_async4(&st->grad[3 * p + 0], grad + 3 * pix + 0);
+        cp_async4(&st->grad[3 * p + 1], grad + 3 * pix + 1);
+        cp_async4(&st->grad[3 * p + 2], grad + 3 * pix + 2);
+        cp_async4(&st->T[p], final_T + pix);
+        cp_async4(&st->last[p], last_idx + pix);
       } else {
-        buf->grad[3 * p + 0] = buf->grad[3 * p + 1] = buf->grad[3 * p + 2] = 0.0f;
-        buf->T[p] = 1.0f;
-        buf->last[p] = 0;
+        st->grad[3 * p + 0] = st->grad[3 * p + 1] = st->grad[3 * p + 2] = 0.0f;
+        st->T[p] = 1.0f;
+        st->last[p] = 0;
       }
     }
   }
-  for (int q = lane; q < 3 * off.n; q += 32) cp_async16(&buf->rec[0][0] + q, pair_rec + 3 * (size_t)off.start + q);
-  for (int q = lane; q < off.n; q += 32) cp_async4(&buf->ids[q], ids + off.start + q);
+  for (int q = lane; q < 3 * off.n; q += 32) cp_async16(&rb->rec[0][0] + q, pair_rec + 3 * (size_t)off.start + q);
+  for (int q = lane; q < off.n; q += 32) cp_async4(&rb->ids[q], ids + off.start + q);
+}
+
+// Sums the staged gradient rows of `count` records (row = record slot x
+// component, one value per lane) and adds each nonzero total to grad_rec: lane
+// L takes row L, reads it with 16-byte loads and sums it as packed pairs.
+__device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, float* __restrict__ grad_rec) {
+  __syncwarp();
+  if (lane < count * kGradComps) {
+    const float4* row = reinterpret_cast<const float4*>(&W.red[lane][0]);
+    F2 acc0 = f2(0.0f), acc1 = f2(0.0f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = row[i];
+      acc0 = add2(acc0, f2(v.x, v.y));
+      acc1 = add2(acc1, f2(v.z, v.w));
+    }
+    float a0, a1, a2, a3;
+    split(acc0, a0, a1);
+    split(acc1, a2, a3);
+    const float total = (a0 + a1) + (a2 + a3);
+    const int slot = lane / kGradComps, comp = lane - slot * kGradComps;
+    const int gi = W.red_gi[slot];
+    if (gi >= 0 && total != 0.0f) atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + comp, total);
+  }
+  __syncwarp();
 }
 
 template <bool kClampOm>
@@ -470,62 +511,59 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
                       uint32_t* __restrict__ long_count, uint32_t* __restrict__ status) {
   extern __shared__ float4 s_dyn[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  BwdBuf* bufs = reinterpret_cast<BwdBuf*>(s_dyn) + 2 * warp;
+  BwdWarpSmem& W = reinterpret_cast<BwdWarpSmem*>(s_dyn)[warp];
   const int stride = gridDim.x * kBwdWarps;
   int tile = blockIdx.x * kBwdWarps + warp;
   TileOff cur = load_off(toff, tile, m.total_tiles);
   TileOff nxt = load_off(toff, tile + stride, m.total_tiles);
-  prefetch_bwd_tile(m, tile, cur, &bufs[0], lane, grad, final_T, last_idx, pair_rec, ids);
+  prefetch_bwd_tile(m, tile, cur, &W.st, &W.rec[0], lane, grad, final_T, last_idx, pair_rec, ids);
   cp_async_commit();
   for (int k = 0; tile < m.total_tiles; ++k, tile += stride) {
     const TileOff nn = load_off(toff, tile + 2 * stride, m.total_tiles);
-    prefetch_bwd_tile(m, tile + stride, nxt, &bufs[(k + 1) & 1], lane, grad, final_T, last_idx, pair_rec, ids);
-    cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<0>();
     __syncwarp();
-    const BwdBuf& B = bufs[k & 1];
+    const BwdRecs& R = W.rec[k & 1];
     const int n = cur.n;
-    if (n > kShortMax) {
-      if (lane == 0) long_tiles[atomicAdd(long_count, 1u)] = tile;
-    } else if (n > 0) {
-      const TileCoord tc = tile_coord(m, tile);
-      const int px = tc.tx * kTile + (lane & 15);
-      const int py0 = tc.ty * kTile + (lane >> 4);
-      const float fx = (float)px + 0.5f;
-      const float fy0 = (float)py0 + 0.5f;
-      // Pair q holds rows py0 + 4q and py0 + 4q + 2 (see the forward kernel).
-      F2 fy[kLanePx / 2], gr[kLanePx / 2], gg[kLanePx / 2], gb[kLanePx / 2], Tc[kLanePx / 2], gT[kLanePx / 2];
-      int last[kLanePx];
-      int lmax = 0;
+    const bool work = n > 0 && n <= kShortMax;
+    const TileCoord tc = tile_coord(m, tile);
+    const int px = tc.tx * kTile + (lane & 15);
+    const int py0 = tc.ty * kTile + (lane >> 4);
+    const float fx = (float)px + 0.5f;
+    const float fy0 = (float)py0 + 0.5f;
+    // Pair q holds rows py0 + 4q and py0 + 4q + 2 (see the forward kernel).
+    F2 fy[kLanePx / 2], gr[kLanePx / 2], gg[kLanePx / 2], gb[kLanePx / 2], Tc[kLanePx / 2], gT[kLanePx / 2];
+    int last[kLanePx];
+    int lmax = 0;
+    if (work) {
 #pragma unroll
       for (int q = 0; q < kLanePx / 2; ++q) {
         fy[q] = f2(fy0 + (float)(4 * q), fy0 + (float)(4 * q + 2));
         const int pl = ((lane >> 4) + 4 * q) * kTile + (lane & 15);
         const int ph = pl + 2 * kTile;
-        gr[q] = f2(B.grad[3 * pl + 0], B.grad[3 * ph + 0]);
-        gg[q] = f2(B.grad[3 * pl + 1], B.grad[3 * ph + 1]);
-        gb[q] = f2(B.grad[3 * pl + 2], B.grad[3 * ph + 2]);
-        Tc[q] = f2(B.T[pl], B.T[ph]);
+        gr[q] = f2(W.st.grad[3 * pl + 0], W.st.grad[3 * ph + 0]);
+        gg[q] = f2(W.st.grad[3 * pl + 1], W.st.grad[3 * ph + 1]);
+        gb[q] = f2(W.st.grad[3 * pl + 2], W.st.grad[3 * ph + 2]);
+        Tc[q] = f2(W.st.T[pl], W.st.T[ph]);
         gT[q] = fma2(gb[q], f2(m.bg_b), fma2(gg[q], f2(m.bg_g), mul2(gr[q], f2(m.bg_r))));
-        last[2 * q] = min(B.last[pl], n);
-        last[2 * q + 1] = min(B.last[ph], n);
+        last[2 * q] = min(W.st.last[pl], n);
+        last[2 * q + 1] = min(W.st.last[ph], n);
         lmax = max(lmax, max(last[2 * q], last[2 * q + 1]));
       }
+    }
+    __syncwarp();  // W.st is read: the next tile's prefetch may overwrite it
+    prefetch_bwd_tile(m, tile + stride, nxt, &W.st, &W.rec[(k + 1) & 1], lane, grad, final_T, last_idx, pair_rec,
+                      ids);
+    cp_async_commit();
+    if (n > kShortMax) {
+      if (lane == 0) long_tiles[atomicAdd(long_count, 1u)] = tile;
+    } else if (work) {
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
-      // Software pipeline: the warp reduction (a chain of dependent shuffle
-      // levels) and atomics of splat j+1 are issued in the same iteration, in
-      // the same basic block, as the independent pixel terms of splat j, so
-      // the two interleave. pv/pgi hold the pending splat (zeros and -1 before
-      // the first); the last one is committed after the loop.
-      float pv[kGradComps];
-#pragma unroll
-      for (int t = 0; t < kGradComps; ++t) pv[t] = 0.0f;
-      int pgi = -1;
+      int slot = 0;
 #pragma unroll 1
       for (int j = tile_last - 1; j >= 0; --j) {
-        const float4 p0 = B.rec[j][0];
-        const float4 p1 = B.rec[j][1];
-        const float4 p2 = B.rec[j][2];
+        const float4 p0 = R.rec[j][0];
+        const float4 p1 = R.rec[j][1];
+        const float4 p2 = R.rec[j][2];
         const float dx = __fsub_rn(fx, p0.x);
         const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
         const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
@@ -542,13 +580,6 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
           pixel_vjp2<kClampOm>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z, p2.w, col_r, col_g, col_b,
                                gr[q], gg[q], gb[q], Tc[q], gT[q], S);
         }
-        float total;
-        {
-          float v[16];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) v[t] = t < kGradComps ? pv[t] : 0.0f;
-          total = warp_reduce_scatter16(v, lane);
-        }
         float Sv[7];
 #pragma unroll
         for (int t = 0; t < 7; ++t) {
@@ -558,30 +589,25 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
         }
         float v[16];
         vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
+        // Stage this splat's 9 lane values; every kRedChunk splats the warp
+        // sums the staged rows (one row per lane) and adds them to grad_rec.
 #pragma unroll
-        for (int t = 0; t < kGradComps; ++t) pv[t] = v[t];
-        // Commit the previous splat (a zero total issues no atomic), then take
-        // this splat's id.
-        const int comp = lane >> 1;
-        if (!(lane & 1) && comp < kGradComps && pgi >= 0 && total != 0.0f)
-          atomicAdd(grad_rec + (size_t)pgi * GSB_REC_FLOATS + comp, total);
-        pgi = B.ids[j];
-        if ((unsigned)pgi >= (unsigned)m.BG) {
-          raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
-          pgi = -1;
+        for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
+        if (lane == 0) {
+          int gi = R.ids[j];
+          if ((unsigned)gi >= (unsigned)m.BG) {
+            raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
+            gi = -1;
+          }
+          W.red_gi[slot] = gi;
+        }
+        if (++slot == kRedChunk) {
+          flush_red(W, slot, lane, grad_rec);
+          slot = 0;
         }
       }
-      {
-        float v[16];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) v[t] = t < kGradComps ? pv[t] : 0.0f;
-        const float total = warp_reduce_scatter16(v, lane);
-        const int comp = lane >> 1;
-        if (!(lane & 1) && comp < kGradComps && pgi >= 0 && total != 0.0f)
-          atomicAdd(grad_rec + (size_t)pgi * GSB_REC_FLOATS + comp, total);
-      }
+      if (slot > 0) flush_red(W, slot, lane, grad_rec);
     }
-    __syncwarp();  // bufs[k & 1] is refilled by the next iteration's prefetch
     cur = nxt;
     nxt = nn;
   }
@@ -717,7 +743,7 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-constexpr size_t kBwdWarpSmem = sizeof(BwdBuf) * 2 * kBwdWarps;
+constexpr size_t kBwdWarpSmem = sizeof(BwdWarpSmem) * kBwdWarps;
 
 // Persistent grid sizes (CTAs resident per SM x SMs), cached per device.
 struct GridCache {

@@ -143,3 +143,28 @@ def test_radix_sort_is_stable_and_exact(n, begin, end):
     order = np.argsort(digit, kind="stable")
     assert np.array_equal(v, vals[order])
     assert np.array_equal(k, keys[order])
+
+
+@pytest.mark.parametrize("name", ["c1", "c2"])
+def test_emit_without_masks_matches(name):
+    """gsb_bin_emit re-tests every candidate tile when no hit masks are given
+    (tile_masks = NULL, the C-ABI example's path); its pairs must equal those
+    written from the masks, and the oracle's."""
+    s = config_2d(name, seed=3)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV).contiguous() for t in s.tensors()))
+    L = N.load()
+    T = st.tile_offsets.numel() - 1
+    keys = torch.empty(st.P, dtype=torch.int64, device=DEV)
+    ids = torch.empty(st.P, dtype=torch.int32, device=DEV)
+    toff = torch.empty(T + 1, dtype=torch.int32, device=DEV)
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    wsb = int(L.gsb_bin_emit_workspace_size(st.meta, st.P))
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=DEV)
+    N.check(L.gsb_bin_emit(st.meta, N.ptr(st.rec), N.ptr(st.pair_offsets), None, st.P, N.ptr(keys), N.ptr(ids),
+                           N.ptr(toff), N.ptr(status), N.ptr(ws), wsb, N.stream_ptr(DEV)), "gsb_bin_emit")
+    torch.cuda.synchronize()
+    assert int(status[N.GSB_STATUS_ERROR]) == 0
+    assert torch.equal(keys, st.keys) and torch.equal(ids, st.binned_ids) and torch.equal(toff, st.tile_offsets)
+    c = cpu_bin(s)
+    assert np.array_equal(keys.cpu().numpy().view(np.uint64), c["keys"])
