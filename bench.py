@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3", "c4"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sh-degree", type=int, default=-1,
+                    help="c4 only: colours from spherical harmonics of this degree (0-3) instead of RGB")
     return ap.parse_args()
 
 
@@ -460,21 +462,33 @@ def run_shared3d(args):
     fx, fy, cx, cy = (float(v) for v in sc.camera_params[view])
     c2w = sc.camera_to_world[view].to(dev)
     params = [t.to(dev).requires_grad_(True) for t in (sc.means3d, sc.scales, sc.quats, sc.opacities, sc.colors)]
+    deg = args.sh_degree
+    if deg >= 0:  # colour from SH: 48 (degree 3) coefficients per Gaussian replace the RGB
+        K = (deg + 1) ** 2
+        gsh = torch.Generator().manual_seed(11)
+        sh = torch.randn(G, K, 3, generator=gsh) * 0.2
+        sh[:, 0] = (sc.colors - 0.5) / 0.28209479177387814  # degree-0 term reproduces the RGB
+        params[4] = sh.to(dev).requires_grad_(True)
+
+    def colors_of(p):
+        return tgb.spherical_harmonics_colors(p[4], p[0], c2w, degree=deg) if deg >= 0 else p[4]
     gimg = grad_image(1, H, W, seed=2000 + rank)[0].to(dev)
     with torch.no_grad():
         m2, q2, o2, d2 = tgb.project_pinhole_gaussians(*params[:4], fx, fy, cx, cy, camera_to_world=c2w)
-        st = _bin(cfg, m2[None].contiguous(), q2[None].contiguous(), params[4][None].contiguous(),
+        st = _bin(cfg, m2[None].contiguous(), q2[None].contiguous(), colors_of(params)[None].contiguous(),
                   o2[None].contiguous(), d2[None].contiguous())
         E = tiled_work(st.tile_offsets, 1, H, W)
         P = st.P
         del st
     reducer = SharedGradAllReduce(params) if world > 1 else None
+    reducer_floats = sum(p[0].numel() for p in params)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def step(timing=None):
         for p in params:
             p.grad = None
-        img = tgb.rasterize_pinhole_gaussians(*params, fx, fy, cx, cy, camera_to_world=c2w, config=cfg)
+        img = tgb.rasterize_pinhole_gaussians(*params[:4], colors_of(params), fx, fy, cx, cy, camera_to_world=c2w,
+                                              config=cfg)
         img.backward(gimg)
         if reducer is not None:
             if timing is not None:
@@ -544,7 +558,8 @@ def run_shared3d(args):
             "config": {"workload": f"c4: G={G} shared 3D Gaussians, one {W}x{H} camera per rank (view = rank mod 8)",
                        "pairs_rank0_view": P, "evals_rank0_view": E, "evals_all_ranks": E_total,
                        "l2": "flushed (256 MB write) between steps",
-                       "parallelism": f"{world} rank(s); per-Gaussian grads (14 floats) summed with NCCL all-reduce"},
+                       "parallelism": f"{world} rank(s); per-Gaussian grads ({reducer_floats} floats) summed with NCCL all-reduce",
+            "colors": f"spherical harmonics degree {deg}" if deg >= 0 else "RGB"},
             "gpu_launches": int(launches),
             "allreduce": allreduce,
             "clocks": clock,

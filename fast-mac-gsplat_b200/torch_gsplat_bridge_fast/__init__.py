@@ -12,6 +12,7 @@ from .rasterize import (
     rasterize_pinhole_gaussians,
     rasterize_projected_gaussians,
 )
+from .sh import spherical_harmonics_colors
 
 __all__ = [
     "RasterConfig",
@@ -22,4 +23,5 @@ __all__ = [
     "rasterize_pinhole_gaussians",
     "rasterize_projected_gaussians",
     "profile_projected_gaussians",
+    "spherical_harmonics_colors",
 ]

@@ -49,6 +49,8 @@ EXPORTED = (
     "gsb_project_backward",
     "gsb_radix_sort_pairs_workspace_size",
     "gsb_radix_sort_pairs",
+    "gsb_sh_forward",
+    "gsb_sh_backward",
 )
 
 
@@ -108,6 +110,8 @@ def load() -> C.CDLL:
         "gsb_project_backward": (C.c_int, [i32, i32] + [p] * 10 + [f32] + [p] * 7),
         "gsb_radix_sort_pairs_workspace_size": (sz, [i64, C.c_int, C.c_int]),
         "gsb_radix_sort_pairs": (C.c_int, [p, p, p, p, i64, C.c_int, C.c_int, p, p, sz, p]),
+        "gsb_sh_forward": (C.c_int, [i32, i32, i32, p, p, p, p, p]),
+        "gsb_sh_backward": (C.c_int, [i32, i32, i32, p, p, p, p, p, p, p, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -206,6 +206,23 @@ int gsb_project_backward(int32_t batch_size, int32_t gaussians_per_batch,
                          float* g_scales, float* g_quats, float* g_opacities,
                          float* g_camera_to_world, float* g_camera_params, void* stream);
 
+/* ---- spherical-harmonic colours -------------------------------------------
+ * No reference counterpart: the reference takes raw RGB colours
+ * (variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:958-1003). These
+ * turn per-Gaussian real-SH coefficients sh_coeffs [G, (degree+1)^2, 3] (degree 0-3,
+ * shared by all views) into colours [B, G, 3] for each camera:
+ *   colour = max(0, 0.5 + sum_k coeff_k Y_k(normalize(mean - camera centre))),
+ * the camera centre being column 3 of the row-major camera_to_world [B,4,4].
+ * The backward takes the forward's colours (for the clamp) and writes
+ * g_sh_coeffs [G,K,3], g_means3d [G,3] (optional, the SH term only) and
+ * g_camera_to_world [B,16] (optional; only the centre column is nonzero). */
+int gsb_sh_forward(int32_t batch_size, int32_t gaussians, int32_t degree, const float* sh_coeffs,
+                   const float* means3d, const float* camera_to_world, float* colors, void* stream);
+int gsb_sh_backward(int32_t batch_size, int32_t gaussians, int32_t degree, const float* sh_coeffs,
+                    const float* means3d, const float* camera_to_world, const float* colors,
+                    const float* grad_colors, float* g_sh_coeffs, float* g_means3d,
+                    float* g_camera_to_world, void* stream);
+
 /* ---- building blocks, exported for parity tests -------------------------
  * Stable LSD radix sort of (uint64 key, uint32 value) pairs on key bits
  * [begin_bit, end_bit) (onesweep: one histogram pass + one pass per 8-bit digit).

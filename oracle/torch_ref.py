@@ -174,3 +174,41 @@ def saturating_reference_pixels(means2d, conics, colors, opacities, depths, px, 
         out = out + (t_before * a_eff) @ c[s:e]
         T = T * torch.prod(1.0 - a_eff, dim=1, keepdim=True)
     return out + T * torch.tensor(bg, dtype=dt, device=dev)
+
+
+# ---------------------------------------------------------------------------
+# Spherical-harmonic colours (no reference counterpart: the reference takes
+# RGB). Real SH basis, degree <= 3, in the (y, z, x) ordering of the common
+# 3D Gaussian splatting convention; each constant is
+# sqrt((2l+1)/(4 pi) (l-|m|)!/(l+|m|)!) (times sqrt 2 for m != 0) with the
+# Cartesian polynomial of Y_lm. Used as the fp32 reference of the CUDA kernel.
+# ---------------------------------------------------------------------------
+def sh_basis(dirs: Tensor, degree: int) -> Tensor:
+    """dirs [..., 3] unit vectors -> basis [..., (degree+1)^2]."""
+    x, y, z = dirs.unbind(-1)
+    out = [torch.full_like(x, 0.28209479177387814)]
+    if degree >= 1:
+        c1 = 0.4886025119029199
+        out += [-c1 * y, c1 * z, -c1 * x]
+    if degree >= 2:
+        xx, yy, zz = x * x, y * y, z * z
+        out += [1.0925484305920792 * x * y, -1.0925484305920792 * y * z,
+                0.31539156525252005 * (2 * zz - xx - yy), -1.0925484305920792 * x * z,
+                0.5462742152960396 * (xx - yy)]
+    if degree >= 3:
+        out += [-0.5900435899266435 * y * (3 * xx - yy), 2.890611442640554 * x * y * z,
+                -0.4570457994644658 * y * (4 * zz - xx - yy), 0.3731763325901154 * z * (2 * zz - 3 * xx - 3 * yy),
+                -0.4570457994644658 * x * (4 * zz - xx - yy), 1.445305721320277 * z * (xx - yy),
+                -0.5900435899266435 * x * (xx - 3 * yy)]
+    return torch.stack(out, dim=-1)
+
+
+def sh_colors_reference(sh: Tensor, means3d: Tensor, camera_to_world: Tensor, degree: int) -> Tensor:
+    """sh [G,K,3], means3d [G,3], camera_to_world [B,4,4] -> colours [B,G,3]:
+    max(0, 0.5 + sum_k sh_k Y_k(normalize(mean - centre)))."""
+    centre = camera_to_world[:, :3, 3]
+    d = means3d[None] - centre[:, None]
+    d = d / torch.sqrt((d * d).sum(-1, keepdim=True).clamp_min(1e-24))
+    Y = sh_basis(d, degree)
+    K = Y.shape[-1]
+    return torch.clamp_min((Y[..., None] * sh[None, :, :K]).sum(-2) + 0.5, 0.0)
