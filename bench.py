@@ -48,6 +48,11 @@ def parse_args():
     ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3", "c4"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--trace", default="",
+                    help="replay a recorded batch (torch.save'd dict of means2d/conics/colors/opacities/depths) "
+                         "instead of the synthetic config; with --height/--width")
+    ap.add_argument("--height", type=int, default=4096)
+    ap.add_argument("--width", type=int, default=4096)
     ap.add_argument("--sh-degree", type=int, default=-1,
                     help="c4 only: colours from spherical harmonics of this degree (0-3) instead of RGB")
     return ap.parse_args()
@@ -183,7 +188,12 @@ def run_b200(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    s = config_2d(args.config, seed=rank)
+    if args.trace:
+        from workloads import load_trace
+
+        s = load_trace(args.trace, args.height, args.width)
+    else:
+        s = config_2d(args.config, seed=rank)
     B, G, H, W = s.B, s.G, s.height, s.width
     cfg = tgb.RasterConfig(H, W)
     base = [t.to(dev) for t in s.tensors()]
@@ -267,7 +277,7 @@ def run_b200(args):
         e2e = measure_e2e(tgb, s, gimg.cpu(), cfg, dev, E, steps=min(args.steps, 10))
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.trace:
         cpu = cpu_baseline(args.config, seed=0)
 
     if rank == 0:
@@ -286,7 +296,8 @@ def run_b200(args):
             "vs_baseline": None,
             "dtype": "fp32",
             "data": "synthetic (seeded; BASELINE config distributions)",
-            "config": {"workload": f"{args.config}: B={B}, {W}x{H}, G={G} 2D splats per GPU, fwd+bwd",
+            "config": {"workload": (f"trace {os.path.basename(args.trace)}" if args.trace else args.config)
+                       + f": B={B}, {W}x{H}, G={G} 2D splats per GPU, fwd+bwd",
                        "pairs_per_view": P, "evals_per_view_E": E, "l2": "flushed (256 MB write) between steps",
                        "parallelism": f"views sharded, {world} rank(s), no collective"},
             "gpu_launches": int(launches),

@@ -123,3 +123,21 @@ def test_batch_chunk_policy_matches_reference():
     assert _choose_batch_chunk_size(tgb.RasterConfig(512, 1024), 4, 2048, 2048) == 4
     assert _choose_batch_chunk_size(tgb.RasterConfig(512, 1024, batch_strategy="serial"), 4, 2048, 2048) == 1
     assert _choose_batch_chunk_size(cfg, 8, 65536, 65536) == 4
+
+
+def test_trace_replay_loader(tmp_path):
+    """The trace format of the reference benchmark's real_trace case: a dict of the
+    five splat tensors, [G,...] or [B,G,...], truncated to the requested sizes."""
+    from workloads import load_trace, make_2d
+
+    s = make_2d(2, 300, 64, 80, seed=4)
+    path = tmp_path / "trace.pt"
+    torch.save({k: t for k, t in zip(("means2d", "conics", "colors", "opacities", "depths"), s.tensors())}, path)
+    t = load_trace(str(path), 64, 80, batch=1, gaussians=200)
+    assert (t.B, t.G, t.height, t.width) == (1, 200, 64, 80)
+    assert torch.equal(t.means2d, s.means2d[:1, :200])
+    torch.save({k: v[0] for k, v in zip(("means2d", "conics", "colors", "opacities", "depths"), s.tensors())}, path)
+    assert load_trace(str(path), 64, 80).means2d.shape == (1, 300, 2)
+    torch.save({"means2d": s.means2d}, path)
+    with pytest.raises(ValueError, match="missing"):
+        load_trace(str(path), 64, 80)

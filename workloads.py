@@ -149,3 +149,26 @@ def config_3d(G: int = 1 << 20, views: int = 8, seed: int = 0, H: int = 1080, W:
     cam = torch.tensor([[f, f, W / 2, H / 2]] * views, dtype=torch.float32)
     return Splats3D(means.contiguous(), scales.contiguous(), quats.contiguous(), opac.contiguous(), rgb.contiguous(),
                     c2w.contiguous(), cam, H, W)
+
+
+TRACE_KEYS = ("means2d", "conics", "colors", "opacities", "depths")
+
+
+def load_trace(path: str, height: int, width: int, batch: int = 0, gaussians: int = 0) -> Splats2D:
+    """A recorded frame batch instead of synthetic splats: a torch.save'd dict
+    with the five projected-splat tensors ([G,...] or [B,G,...]), truncated to
+    the requested batch/gaussian counts when they are positive. Same contract
+    as the reference benchmark's real_trace case
+    (variants/v8/benchmarks/benchmark_mps.py:26-46)."""
+    data = torch.load(path, map_location="cpu")
+    missing = [k for k in TRACE_KEYS if k not in data]
+    if missing:
+        raise ValueError(f"trace file is missing {missing[0]!r}")
+    ts = [data[k].to(dtype=torch.float32) for k in TRACE_KEYS]
+    if ts[0].ndim == 2:
+        ts = [t.unsqueeze(0) for t in ts]
+    B0, G0 = ts[0].shape[:2]
+    B = min(B0, batch) if batch > 0 else B0
+    G = min(G0, gaussians) if gaussians > 0 else G0
+    ts = [t[:B, :G].contiguous() for t in ts]
+    return Splats2D(*ts, height, width)
