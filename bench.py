@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--trace", default="",
                     help="replay a recorded batch (torch.save'd dict of means2d/conics/colors/opacities/depths) "
                          "instead of the synthetic config; with --height/--width")
+    ap.add_argument("--matrix", action="store_true",
+                    help="one JSON line per BASELINE config c0-c4: forward-only and forward+backward ms")
     ap.add_argument("--height", type=int, default=4096)
     ap.add_argument("--width", type=int, default=4096)
     ap.add_argument("--sh-degree", type=int, default=-1,
@@ -281,8 +283,9 @@ def run_b200(args):
         cpu = cpu_baseline(args.config, seed=0)
 
     if rank == 0:
+        default_workload = args.config == CONFIG_NAME and not args.trace
         line = {
-            "metric": METRIC,
+            "metric": METRIC if default_workload else f"Gsplat-px evals/s, fwd+bwd at {W}x{H} x {G:,} splats x {B} views",
             "value": round(value, 3),
             "unit": UNIT,
             "n_gpus": world,
@@ -295,7 +298,8 @@ def run_b200(args):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "fp32",
-            "data": "synthetic (seeded; BASELINE config distributions)",
+            "data": f"recorded trace {os.path.basename(args.trace)}" if args.trace
+            else "synthetic (seeded; BASELINE config distributions)",
             "config": {"workload": (f"trace {os.path.basename(args.trace)}" if args.trace else args.config)
                        + f": B={B}, {W}x{H}, G={G} 2D splats per GPU, fwd+bwd",
                        "pairs_per_view": P, "evals_per_view_E": E, "l2": "flushed (256 MB write) between steps",
@@ -581,6 +585,72 @@ def run_shared3d(args):
         dist.destroy_process_group()
 
 
+def _median_ms(fn, reps: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def run_matrix(args):
+    """Forward-only (no-grad path) and forward+backward medians on c0-c3 (2D
+    splats) and c4 (3D scene, one camera), one JSON line each: the table of the
+    reference's benchmark_full_matrix.py for this renderer."""
+    import torch_gsplat_bridge_fast as tgb
+    from torch_gsplat_bridge_fast.rasterize import _bin
+    from workloads import config_2d, config_3d, grad_image
+
+    dev = torch.device("cuda", 0)
+    reps = max(args.steps, 5)
+    for name in ("c0", "c1", "c2", "c3"):
+        s = config_2d(name, seed=0)
+        cfg = tgb.RasterConfig(s.height, s.width)
+        base = [t.to(dev) for t in s.tensors()]
+        g = grad_image(s.B, s.height, s.width, seed=1000).to(dev)
+        st = _bin(cfg, *base)
+        E, P = tiled_work(st.tile_offsets, s.B, s.height, s.width), st.P
+        del st
+
+        def fwd():
+            with torch.no_grad():
+                tgb.rasterize_projected_gaussians(*base, cfg)
+
+        def fwd_bwd():
+            ins = [t.detach().requires_grad_(i < 4) for i, t in enumerate(base)]
+            tgb.rasterize_projected_gaussians(*ins, cfg).backward(g)
+
+        f_ms, fb_ms = _median_ms(fwd, reps), _median_ms(fwd_bwd, reps)
+        print(json.dumps({"matrix": name, "B": s.B, "G": s.G, "H": s.height, "W": s.width, "pairs": P, "evals": E,
+                          "fwd_ms": round(f_ms, 4), "fwd_bwd_ms": round(fb_ms, 4),
+                          "fwd_bwd_gsplat_px_per_s": round(E / (fb_ms * 1e-3) / 1e9, 3)}), flush=True)
+    sc = config_3d(seed=0)
+    cfg = tgb.RasterConfig(sc.height, sc.width)
+    fx, fy, cx, cy = (float(v) for v in sc.camera_params[0])
+    c2w = sc.camera_to_world[0].to(dev)
+    params = [t.to(dev) for t in (sc.means3d, sc.scales, sc.quats, sc.opacities, sc.colors)]
+    gimg = grad_image(1, sc.height, sc.width, seed=2000)[0].to(dev)
+
+    def fwd3():
+        with torch.no_grad():
+            tgb.rasterize_pinhole_gaussians(*params, fx, fy, cx, cy, camera_to_world=c2w, config=cfg)
+
+    def fwd_bwd3():
+        ps = [p.detach().requires_grad_(True) for p in params]
+        tgb.rasterize_pinhole_gaussians(*ps, fx, fy, cx, cy, camera_to_world=c2w, config=cfg).backward(gimg)
+
+    f_ms, fb_ms = _median_ms(fwd3, reps), _median_ms(fwd_bwd3, reps)
+    print(json.dumps({"matrix": "c4", "G": sc.means3d.shape[0], "H": sc.height, "W": sc.width, "views": 1,
+                      "fwd_ms": round(f_ms, 4), "fwd_bwd_ms": round(fb_ms, 4)}), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -589,6 +659,9 @@ def main():
     if not torch.cuda.is_available():
         print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
         sys.exit(1)
+    if args.matrix:
+        run_matrix(args)
+        return
     if args.config == "c4":
         run_shared3d(args)
         return
