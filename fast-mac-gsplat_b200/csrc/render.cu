@@ -38,7 +38,8 @@
 namespace gsb {
 namespace {
 
-constexpr int kShortMax = 64;   // pairs per tile handled by one warp
+constexpr int kShortMax = 64;   // pairs per tile handled by one warp (forward)
+constexpr int kBwdShortMax = 48;  // same in the backward: smaller record buffers let 4 CTAs share an SM
 constexpr int kWarpBatch = 32;  // records staged per warp round (forward)
 constexpr int kLanePx = 8;      // pixels per lane in the warp kernels: rows py0 + 2i
 constexpr int kWarps = 8;       // warps per CTA (forward warp kernel, CTA kernels)
@@ -406,8 +407,8 @@ struct BwdState {
   int last[kTilePixels];
 };
 struct BwdRecs {
-  float4 rec[kShortMax][3];
-  int ids[kShortMax];
+  float4 rec[kBwdShortMax][3];
+  int ids[kBwdShortMax];
 };
 constexpr int kRedChunk = 3;    // records whose gradients are reduced together
 constexpr int kRedStride = 36;  // padded row (32 lanes + 4): conflict-free 16-byte row reads
@@ -439,7 +440,7 @@ __device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileO
                                                   const int32_t* __restrict__ last_idx,
                                                   const float4* __restrict__ pair_rec,
                                                   const int32_t* __restrict__ ids) {
-  if (tile >= m.total_tiles || off.n == 0 || off.n > kShortMax) return;
+  if (tile >= m.total_tiles || off.n == 0 || off.n > kBwdShortMax) return;
   const TileCoord tc = tile_coord(m, tile);
   const int x0 = tc.tx * kTile, y0 = tc.ty * kTile;
   const bool full = (x0 + kTile <= m.W) && (y0 + kTile <= m.H) && ((m.W & 3) == 0);
@@ -503,7 +504,7 @@ __device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, f
 }
 
 template <bool kClampOm>
-__global__ void __launch_bounds__(kBwdWarps * 32, 3)
+__global__ void __launch_bounds__(kBwdWarps * 32, 4)
     k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                       const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
     __syncwarp();
     const BwdRecs& R = W.rec[k & 1];
     const int n = cur.n;
-    const bool work = n > 0 && n <= kShortMax;
+    const bool work = n > 0 && n <= kBwdShortMax;
     const TileCoord tc = tile_coord(m, tile);
     const int px = tc.tx * kTile + (lane & 15);
     const int py0 = tc.ty * kTile + (lane >> 4);
@@ -554,7 +555,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3)
     prefetch_bwd_tile(m, tile + stride, nxt, &W.st, &W.rec[(k + 1) & 1], lane, grad, final_T, last_idx, pair_rec,
                       ids);
     cp_async_commit();
-    if (n > kShortMax) {
+    if (n > kBwdShortMax) {
       if (lane == 0) long_tiles[atomicAdd(long_count, 1u)] = tile;
     } else if (work) {
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
