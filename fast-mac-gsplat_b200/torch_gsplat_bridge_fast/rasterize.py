@@ -233,7 +233,8 @@ _host_mod = None
 
 
 def _host():
-    """The native host runtime (_gsb_host, built in-tree next to libgsplat_b200.so)."""
+    """The native host runtime (_gsb_host, built in-tree next to libgsplat_b200.so).
+    Loading it registers the torch.ops.gsplat_b200 op namespace."""
     global _host_mod
     if _host_mod is None:
         try:
@@ -245,6 +246,20 @@ def _host():
             ) from e
         _host_mod = mod
     return _host_mod
+
+
+_ops_ns = None
+
+
+def _ops():
+    """torch.ops.gsplat_b200: rasterize_fwd, bin, render_fwd_eval,
+    render_fwd_train, render_bwd, project_fwd, project_bwd, sh_fwd, sh_bwd
+    (CUDA dispatch key only)."""
+    global _ops_ns
+    if _ops_ns is None:
+        _host()
+        _ops_ns = torch.ops.gsplat_b200
+    return _ops_ns
 
 
 def set_kernel_timer(enabled: bool) -> None:
@@ -459,8 +474,11 @@ _MAX_ALPHA = 0.99
 
 
 def _host_args(config: RasterConfig):
+    """The scalar raster arguments of the torch.ops.gsplat_b200 schemas:
+    height, width, alpha_threshold, transmittance_threshold, bg_r, bg_g, bg_b,
+    eps, max_alpha."""
     bg = [float(c) for c in config.background]
-    return (config.height, config.width, float(config.alpha_threshold), float(config.transmittance_threshold), bg,
+    return (config.height, config.width, float(config.alpha_threshold), float(config.transmittance_threshold), *bg,
             _EPS, _MAX_ALPHA)
 
 
@@ -468,14 +486,14 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
     """Training path (…/v8_project3d/…/rasterize.py:691-852; root rasterize.py:26-106).
     Saves the per-pixel final transmittance and last-contributor index instead of
     per-tile stop counts; backward un-sorts into input order; depth grad is zero.
-    Each direction is one call into the native host runtime (_gsb_host)."""
+    Each direction is one torch op (gsplat_b200::rasterize_fwd / render_bwd)."""
 
     @staticmethod
     def forward(ctx, means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig):
         cap = -1 if config.enable_overflow_fallback else config.pair_cap
         args = _host_args(config)
-        res = _host().forward(means2d_b, conics_b, colors_b, opacities_b, depths_b, *args, True, cap)
-        out, perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status = res[:9]
+        res = _ops().rasterize_fwd(means2d_b, conics_b, colors_b, opacities_b, depths_b, *args, True, cap)
+        out, perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status = res
         ctx.save_for_backward(perm, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, status)
         ctx.host_args = args
         ctx.depths_shape = depths_b.shape
@@ -484,8 +502,8 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out: Tensor):
         need = ctx.needs_input_grad
-        g_means, g_conics, g_colors, g_opac = _host().backward(*ctx.saved_tensors, grad_out, *ctx.host_args,
-                                                              [bool(x) for x in need[:4]])
+        g_means, g_conics, g_colors, g_opac = _ops().render_bwd(*ctx.saved_tensors, grad_out, *ctx.host_args,
+                                                                [bool(x) for x in need[:4]])
         dev = grad_out.device
         g_depths = torch.zeros(ctx.depths_shape, dtype=torch.float32, device=dev) if need[4] else None
         return g_means, g_conics, g_colors, g_opac, g_depths, None
@@ -494,7 +512,8 @@ class _RasterizeProjectedGaussiansB200(torch.autograd.Function):
 def _rasterize_chunk_eval(means2d_b, conics_b, colors_b, opacities_b, depths_b, config: RasterConfig) -> Tensor:
     """No-grad path (…/v8_project3d/…/rasterize.py:855-907): no saved state."""
     cap = -1 if config.enable_overflow_fallback else config.pair_cap
-    return _host().forward(means2d_b, conics_b, colors_b, opacities_b, depths_b, *_host_args(config), False, cap)[0]
+    return _ops().rasterize_fwd(means2d_b, conics_b, colors_b, opacities_b, depths_b, *_host_args(config), False,
+                                cap)[0]
 
 
 def _should_use_training_path(means2d: Tensor, conics: Tensor, colors: Tensor, opacities: Tensor) -> bool:
@@ -581,22 +600,8 @@ def _projection_backward_requested(*values) -> bool:
 
 
 def _project_forward_native(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params, near_plane):
-    L = N.load()
-    B, G = means3d_b.shape[:2]
-    dev = means3d_b.device
-    out_m = torch.empty((B, G, 2), dtype=torch.float32, device=dev)
-    out_c = torch.empty((B, G, 3), dtype=torch.float32, device=dev)
-    out_o = torch.empty((B, G), dtype=torch.float32, device=dev)
-    out_d = torch.empty((B, G), dtype=torch.float32, device=dev)
-    m3, s3, o3 = means3d_b.contiguous(), scales_b.contiguous(), opacities_b.contiguous()
-    q4, k16, k4 = _aligned(quats_b), _aligned(c2w_b), _aligned(camera_params)
-    N.check(
-        L.gsb_project_forward(B, G, N.ptr(m3), N.ptr(s3), N.ptr(q4), N.ptr(o3), N.ptr(k16), N.ptr(k4),
-                              float(near_plane), N.ptr(out_m), N.ptr(out_c), N.ptr(out_o), N.ptr(out_d),
-                              N.stream_ptr(dev)),
-        "gsb_project_forward",
-    )
-    return out_m, out_c, out_o, out_d
+    return tuple(_ops().project_fwd(means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params,
+                                    float(near_plane)))
 
 
 class _ProjectPinholeGaussiansB200(torch.autograd.Function):
@@ -614,30 +619,8 @@ class _ProjectPinholeGaussiansB200(torch.autograd.Function):
         means3d_b, scales_b, quats_b, opacities_b, c2w_b, camera_params = ctx.saved_tensors
         if not any(ctx.needs_input_grad[:6]):
             return (None,) * 7
-        L = N.load()
-        B, G = means3d_b.shape[:2]
-        dev = means3d_b.device
-
-        def opt(g):
-            return None if g is None else _aligned(g.to(torch.float32))
-
-        g_m2d, g_con, g_op, g_depth = opt(g_m2d), opt(g_con), opt(g_op), opt(g_depth)
-        gm3 = torch.empty_like(means3d_b)
-        gs = torch.empty_like(scales_b)
-        gq = torch.empty((B, G, 4), dtype=torch.float32, device=dev)
-        go = torch.empty_like(opacities_b)
-        gc2w = torch.empty((B, 4, 4), dtype=torch.float32, device=dev)
-        gcam = torch.empty((B, 4), dtype=torch.float32, device=dev)
-        m3, s3, o3 = means3d_b.contiguous(), scales_b.contiguous(), opacities_b.contiguous()
-        q4, k16, k4 = _aligned(quats_b), _aligned(c2w_b), _aligned(camera_params)
-        N.check(
-            L.gsb_project_backward(B, G, N.ptr(g_m2d), N.ptr(g_con), N.ptr(g_op), N.ptr(g_depth), N.ptr(m3),
-                                   N.ptr(s3), N.ptr(q4), N.ptr(o3), N.ptr(k16), N.ptr(k4), ctx.near_plane,
-                                   N.ptr(gm3), N.ptr(gs), N.ptr(gq), N.ptr(go), N.ptr(gc2w), N.ptr(gcam),
-                                   N.stream_ptr(dev)),
-            "gsb_project_backward",
-        )
-        grads = [gm3, gs, gq, go, gc2w, gcam]
+        grads = list(_ops().project_bwd(g_m2d, g_con, g_op, g_depth, means3d_b, scales_b, quats_b, opacities_b,
+                                        c2w_b, camera_params, ctx.near_plane))
         for i, need in enumerate(ctx.needs_input_grad[:6]):
             if not need:
                 grads[i] = None

@@ -17,19 +17,17 @@ from typing import Optional
 import torch
 from torch import Tensor
 
-from . import _native as N
+from .rasterize import _ops
 
 _K_OF_DEGREE = {0: 1, 1: 4, 2: 9, 3: 16}
 
 
 class _ShColors(torch.autograd.Function):
+    """gsplat_b200::sh_fwd / sh_bwd."""
+
     @staticmethod
     def forward(ctx, sh: Tensor, means3d: Tensor, c2w: Tensor, degree: int):
-        L = N.load()
-        B, G = c2w.shape[0], means3d.shape[0]
-        colors = torch.empty((B, G, 3), dtype=torch.float32, device=means3d.device)
-        N.check(L.gsb_sh_forward(B, G, degree, N.ptr(sh), N.ptr(means3d), N.ptr(c2w), N.ptr(colors),
-                                 N.stream_ptr(means3d.device)), "gsb_sh_forward")
+        colors = _ops().sh_fwd(sh, means3d, c2w, degree)
         ctx.save_for_backward(sh, means3d, c2w, colors)
         ctx.degree = degree
         return colors
@@ -37,16 +35,9 @@ class _ShColors(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_colors: Tensor):
         sh, means3d, c2w, colors = ctx.saved_tensors
-        L = N.load()
-        B, G = c2w.shape[0], means3d.shape[0]
         need = ctx.needs_input_grad
-        g_sh = torch.empty_like(sh)
-        g_means = torch.empty_like(means3d) if need[1] else None
-        g_c2w = torch.empty((B, 4, 4), dtype=torch.float32, device=sh.device) if need[2] else None
-        g = g_colors.to(torch.float32).contiguous()
-        N.check(L.gsb_sh_backward(B, G, ctx.degree, N.ptr(sh), N.ptr(means3d), N.ptr(c2w), N.ptr(colors), N.ptr(g),
-                                  N.ptr(g_sh), N.ptr(g_means), N.ptr(g_c2w), N.stream_ptr(sh.device)),
-                "gsb_sh_backward")
+        g_sh, g_means, g_c2w = _ops().sh_bwd(sh, means3d, c2w, colors, g_colors, ctx.degree, bool(need[1]),
+                                             bool(need[2]))
         return (g_sh if need[0] else None), g_means, g_c2w, None
 
 

@@ -141,3 +141,32 @@ def test_trace_replay_loader(tmp_path):
     torch.save({"means2d": s.means2d}, path)
     with pytest.raises(ValueError, match="missing"):
         load_trace(str(path), 64, 80)
+
+
+_OPS = ("rasterize_fwd", "bin", "render_fwd_eval", "render_fwd_train", "render_bwd", "project_fwd", "project_bwd",
+        "sh_fwd", "sh_bwd")
+
+
+def test_torch_op_namespace_registered_for_cuda_only():
+    """torch.ops.gsplat_b200 mirrors the reference's op namespace
+    (variants/v8_project3d/csrc/bindings.cpp:173-193) with scalar meta
+    arguments; only the CUDA dispatch key has kernels, so CPU tensors raise
+    instead of reaching a fallback."""
+    from torch_gsplat_bridge_fast.rasterize import _host_args, _ops
+
+    ops = _ops()
+    for name in _OPS:
+        schema = str(getattr(ops, name).default._schema)
+        assert schema.startswith(f"gsplat_b200::{name}("), schema
+    raster = "int height, int width, float alpha_threshold, float transmittance_threshold, float bg_r, float bg_g, " \
+             "float bg_b, float eps, float max_alpha"
+    for name in ("rasterize_fwd", "bin", "render_fwd_eval", "render_fwd_train", "render_bwd"):
+        assert raster in str(getattr(ops, name).default._schema), name
+    assert "Tensor(a!) status" in str(ops.render_bwd.default._schema)
+    args = _host_args(tgb.RasterConfig(16, 16))
+    assert len(args) == 9
+    cpu = (torch.zeros(1, 4, 2), torch.zeros(1, 4, 3), torch.zeros(1, 4, 3), torch.zeros(1, 4), torch.zeros(1, 4))
+    with pytest.raises(NotImplementedError, match="CPU"):
+        ops.rasterize_fwd(*cpu, *args, False, -1)
+    with pytest.raises(NotImplementedError, match="CPU"):
+        ops.sh_fwd(torch.zeros(4, 1, 3), torch.zeros(4, 3), torch.eye(4)[None], 0)

@@ -4,6 +4,8 @@ reference's early-stop oracle, plus the reference's own fixtures through the
 public API. Gates: image max-abs <= 1e-4; gradients <= 1e-3 relative."""
 from __future__ import annotations
 
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -261,15 +263,87 @@ def test_host_runtime_reports_deferred_backward_error(monkeypatch):
     tgb.check_device_errors()
     s = config_2d("c0", seed=0)
     cfg = tgb.RasterConfig(s.height, s.width)
-    host = R._host()
-    res = host.forward(*(t.to(DEV) for t in s.tensors()), *R._host_args(cfg), True, -1)
-    out, perm, rec, tile_offsets, ids, final_T, last_idx, pair_rec, status = res[:9]
+    ops = R._ops()
+    res = ops.rasterize_fwd(*(t.to(DEV) for t in s.tensors()), *R._host_args(cfg), True, -1)
+    out, perm, rec, tile_offsets, ids, final_T, last_idx, pair_rec, status = res
     torch.cuda.synchronize()
     tgb.check_device_errors()  # the forward itself was clean
     ids[0] = s.B * s.G + 5
-    host.backward(perm, rec, tile_offsets, ids, final_T, last_idx, pair_rec, status, torch.ones_like(out),
-                  *R._host_args(cfg), [True] * 4)
+    ops.render_bwd(perm, rec, tile_offsets, ids, final_T, last_idx, pair_rec, status, torch.ones_like(out),
+                   *R._host_args(cfg), [True] * 4)
     torch.cuda.synchronize()
     with pytest.raises(RuntimeError, match="index out of bounds"):
         tgb.check_device_errors()
     tgb.check_device_errors()
+
+
+def test_split_ops_match_one_call_op():
+    """bin -> render_fwd_train -> render_bwd (and render_fwd_eval) give the same
+    bits as the one-call rasterize_fwd + render_bwd; gradients, which sum
+    per-tile partials with float atomics in any order, agree to 1e-6 relative."""
+    from torch_gsplat_bridge_fast import rasterize as R
+
+    s = config_2d("c2", seed=3)
+    cfg = tgb.RasterConfig(s.height, s.width, background=(0.1, 0.2, 0.3))
+    args = R._host_args(cfg)
+    ops = R._ops()
+    ins = [t.to(DEV) for t in s.tensors()]
+    fused = ops.rasterize_fwd(*ins, *args, True, -1)
+    perm, rec, toff, ids, status = ops.bin(*ins, *args, -1)
+    img, final_T, last_idx, pair_rec = ops.render_fwd_train(rec, toff, ids, status, s.B, *args)
+    img_eval = ops.render_fwd_eval(rec, toff, ids, status, s.B, *args)
+    for a, b in zip((img, perm, rec, toff, ids, final_T, last_idx), fused[:7]):
+        assert torch.equal(a, b)
+    assert torch.equal(img_eval, img)
+    g = grad_image(s.B, s.height, s.width, seed=4).to(DEV)
+    got = ops.render_bwd(perm, rec, toff, ids, final_T, last_idx, pair_rec, status, g, *args, [True, False, True, True])
+    want = ops.render_bwd(*fused[1:], g, *args, [True] * 4)
+    assert got[1] is None
+    for i in (0, 2, 3):
+        assert rel_err(np_(got[i]), np_(want[i])) <= 1e-6, i
+    tgb.check_device_errors()
+
+
+def _edge_geometry_splats(B=2, G=3000, H=136, W=200, seed=11):
+    """Hard geometry for the compositing kernels: needle ellipses (axis ratio
+    1..60), sub-pixel and huge sigmas, centres up to 80 px off screen,
+    opacities near 0 and 1."""
+    from workloads import Splats2D, conic_from_sigma
+
+    g = torch.Generator().manual_seed(seed)
+    means = torch.rand(B, G, 2, generator=g) * torch.tensor([W + 160.0, H + 160.0]) - 80.0
+    major = torch.exp(torch.rand(B, G, generator=g) * math.log(200.0)) * 0.4  # 0.4 .. 80 px
+    ratio = torch.exp(torch.rand(B, G, generator=g) * math.log(60.0))
+    sig = torch.stack([major, major / ratio], -1)
+    theta = torch.rand(B, G, generator=g) * math.pi
+    opac = torch.where(torch.rand(B, G, generator=g) < 0.2, torch.full((B, G), 0.999),
+                       torch.rand(B, G, generator=g) * 0.9 + 0.001)
+    rgb = torch.rand(B, G, 3, generator=g)
+    depth = torch.rand(B, G, generator=g) * 50.0 + 0.1
+    return Splats2D(means.contiguous(), conic_from_sigma(sig, theta), rgb, opac.contiguous(), depth.contiguous(), H, W)
+
+
+@pytest.mark.parametrize("alpha_threshold", [1.0 / 255.0, 1e-4])
+def test_edge_geometry_matches_c_oracle(alpha_threshold):
+    """Needle, sub-pixel, huge and off-screen splats (_edge_geometry_splats)
+    with the default and a 40x smaller alpha threshold (larger support): the
+    image, saved state and gradients match the C oracle."""
+    from torch_gsplat_bridge_fast.rasterize import _bin, _render_forward
+
+    s = _edge_geometry_splats()
+    cfg = tgb.RasterConfig(s.height, s.width, alpha_threshold=alpha_threshold)
+    gimg = grad_image(s.B, s.height, s.width, seed=12)
+    meta = O.Meta(s.height, s.width, s.B, s.G, alpha_threshold=alpha_threshold)
+    ref = O.full_forward_backward(meta, *(t.numpy() for t in s.tensors()), gimg.numpy())
+    st = _bin(cfg, *(t.to(DEV) for t in s.tensors()))
+    out, T, last, _ = _render_forward(st, cfg, s.B, save_state=True)
+    assert max_abs(np_(out), ref["image"]) <= IMAGE_ATOL
+    assert max_abs(np_(T), ref["final_T"]) <= 1e-5
+    assert np.mean(np_(last) == ref["last_idx"]) >= 0.9999
+    ins = [t.to(DEV).clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+    img = tgb.rasterize_projected_gaussians(*ins, cfg)
+    img.backward(gimg.to(DEV))
+    assert max_abs(np_(img), ref["image"]) <= IMAGE_ATOL
+    for t, want, key in zip(ins[:4], ref["grads"], GRAD_KEYS):
+        got = np_(t.grad).reshape(want.shape)
+        assert rel_err(got, want) <= GRAD_RTOL, key
