@@ -207,6 +207,8 @@ __global__ void __launch_bounds__(256)
               K* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
               uint32_t* __restrict__ counts, unsigned long long* __restrict__ masks, uint32_t* __restrict__ status,
               ZeroList zero) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ WarpTilesSmem s_warp[8];
   zero_words(zero);  // the depth sort's and the scan's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -250,6 +252,8 @@ __global__ void __launch_bounds__(kScanThreads)
                   float4* __restrict__ rec, int32_t* __restrict__ perm,
                   int32_t* __restrict__ pair_offsets, unsigned long long* __restrict__ lookback,
                   uint32_t* __restrict__ part_counter, uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t s_part;
   __shared__ unsigned long long s_warp[kScanThreads / 32];
   __shared__ unsigned long long s_exclusive;
@@ -384,6 +388,8 @@ __global__ void __launch_bounds__(256)
     k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
            const unsigned long long* __restrict__ masks, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
            uint32_t* __restrict__ status, ZeroList zero) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ WarpTilesSmem s_warp[8];
   __shared__ int s_start[8][32], s_cnt[8][32];
   __shared__ uint32_t s_tbase[8][32];
@@ -443,6 +449,8 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     k_ranges(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, const float4* __restrict__ rec,
              int64_t n_pairs, int total_tiles, int32_t* __restrict__ tile_offsets, uint64_t* __restrict__ keys64) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
   if (i0 >= n_pairs) return;
   uint32_t k[4];
@@ -469,12 +477,16 @@ __global__ void __launch_bounds__(256)
 }
 
 __global__ void k_fill_i32(int32_t* __restrict__ p, int64_t n, int32_t v) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = v;
 }
 
 __global__ void __launch_bounds__(256)
     k_tile_max(const int32_t* __restrict__ tile_offsets, int total_tiles, uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   uint32_t c = 0;
   if (t < total_tiles) c = (uint32_t)(tile_offsets[t + 1] - tile_offsets[t]);
@@ -553,11 +565,11 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   zero.ptr[2] = sz.ptr;
   zero.words[2] = sz.words;
   if (depth_keys32(m))
-    k_prepare<uint32_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
+    launch_pdl(k_prepare<uint32_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d), conics,
                                                                opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in),
                                                                w.vals_in, w.counts, w.masks, status, zero);
   else
-    k_prepare<uint64_t><<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float2*>(means2d), conics,
+    launch_pdl(k_prepare<uint64_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d), conics,
                                                                opacities, depths, w.keys_in, w.vals_in, w.counts,
                                                                w.masks, status, zero);
   note_launches(1);
@@ -593,7 +605,7 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
     // them) is smaller than the 64-bit sort's that the workspace is sized for.
     e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream, true);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
-    k_gather_scan<uint32_t><<<parts, kScanThreads, 0, stream>>>(
+    launch_pdl(k_gather_scan<uint32_t>, parts, kScanThreads, 0, stream, 
         m, k32_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities, w.counts,
         w.masks, reinterpret_cast<unsigned long long*>(tile_masks), reinterpret_cast<float4*>(rec), perm,
         pair_offsets, w.lookback, w.counter, status);
@@ -601,7 +613,7 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
     e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
                          status, stream, true);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
-    k_gather_scan<uint64_t><<<parts, kScanThreads, 0, stream>>>(
+    launch_pdl(k_gather_scan<uint64_t>, parts, kScanThreads, 0, stream, 
         m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
         w.counts, w.masks, reinterpret_cast<unsigned long long*>(tile_masks), reinterpret_cast<float4*>(rec), perm,
         pair_offsets, w.lookback, w.counter, status);
@@ -660,7 +672,7 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int64_t T1 = (int64_t)m.total_tiles + 1;
   if (total_pairs == 0) {
-    k_fill_i32<<<grid1d(T1, 256), 256, 0, stream>>>(tile_offsets, T1, 0);
+    launch_pdl(k_fill_i32, grid1d(T1, 256), 256, 0, stream, tile_offsets, T1, 0);
     note_launches(1);
     return cuda_status(cudaGetLastError());
   }
@@ -673,14 +685,14 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   zero.words[0] = sz.words;
   zero.ptr[1] = zero.ptr[2] = nullptr;
   zero.words[1] = zero.words[2] = 0;
-  k_emit<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, reinterpret_cast<const float4*>(rec), pair_offsets,
+  launch_pdl(k_emit, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float4*>(rec), pair_offsets,
                                                 reinterpret_cast<const unsigned long long*>(tile_masks), w.keys,
                                                 w.vals, status, zero);
   note_launches(1);
   cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
                                    total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-  k_ranges<<<grid1d((total_pairs + 3) / 4, 256), 256, 0, stream>>>(w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
+  launch_pdl(k_ranges, grid1d((total_pairs + 3) / 4, 256), 256, 0, stream, w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
                                                          reinterpret_cast<const float4*>(rec), total_pairs,
                                                          m.total_tiles, tile_offsets, keys);
   note_launches(1);
@@ -696,7 +708,7 @@ extern "C" int gsb_tile_stats(const gsb_raster_meta* meta, const int32_t* tile_o
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   cudaError_t e = cudaMemsetAsync(&status[GSB_STATUS_MAX_TILE_COUNT], 0, sizeof(uint32_t), stream);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-  k_tile_max<<<grid1d(m.total_tiles, 256), 256, 0, stream>>>(tile_offsets, m.total_tiles, status);
+  launch_pdl(k_tile_max, grid1d(m.total_tiles, 256), 256, 0, stream, tile_offsets, m.total_tiles, status);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }

@@ -267,6 +267,16 @@ __device__ __forceinline__ void for_each_tile(float mx, float my, float a, float
 // the same correctly rounded IEEE operation to both halves (no flush to zero,
 // like the scalar __fadd_rn/__fmul_rn/__fmaf_rn), so a packed result equals
 // the two scalar results bit for bit while taking one issue slot.
+// Programmatic dependent launch (sm_90+). Every kernel of this library is
+// launched with programmatic stream serialization (launch_pdl) and begins with
+// pdl_wait(): it blocks, in hardware and without spinning, until the preceding
+// grid of the stream has completed and its writes are visible, so the kernel
+// reads and writes nothing before that. pdl_trigger() then lets the next
+// kernel of the stream be scheduled once every CTA of this grid has started,
+// which hides the launch latency between the dependent kernels of a step.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 struct F2 {
   unsigned long long v;
 };

@@ -74,4 +74,24 @@ inline int grid1d(int64_t n, int threads) {
 
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? GSB_OK : GSB_ERR_CUDA; }
 
+// Launches a kernel of this library with programmatic stream serialization
+// (the kernel starts with pdl_wait / pdl_trigger, see gsb_common.cuh).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  static_assert(sizeof...(KArgs) == sizeof...(Args), "kernel argument count");
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+
 }  // namespace gsb

@@ -127,6 +127,8 @@ __global__ void __launch_bounds__(256)
                   const float* __restrict__ c2w, const float* __restrict__ cam, float near_plane,
                   float2* __restrict__ out_means2d, float* __restrict__ out_conics,
                   float* __restrict__ out_opac, float* __restrict__ out_depth) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * G) return;
   const int b = (int)(i / G);
@@ -345,6 +347,8 @@ __global__ void __launch_bounds__(256)
                   float near_plane, float* __restrict__ g_means3d, float* __restrict__ g_scales,
                   float4* __restrict__ g_quats, float* __restrict__ g_opac, float* __restrict__ g_c2w,
                   float* __restrict__ g_cam) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float s_red[8][16];
   __shared__ int s_view;
   const int64_t n = (int64_t)B * G;
@@ -415,7 +419,7 @@ extern "C" int gsb_project_forward(int32_t batch_size, int32_t gaussians_per_bat
       !out_conics || !out_opacities || !out_depths)
     return GSB_ERR_INVALID_ARGUMENT;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  k_project_fwd<<<grid1d(n, 256), 256, 0, stream>>>(batch_size, gaussians_per_batch, means3d, scales,
+  launch_pdl(k_project_fwd, grid1d(n, 256), 256, 0, stream, batch_size, gaussians_per_batch, means3d, scales,
                                                     reinterpret_cast<const float4*>(quats), opacities,
                                                     camera_to_world, camera_params, near_plane,
                                                     reinterpret_cast<float2*>(out_means2d), out_conics,
@@ -449,7 +453,7 @@ extern "C" int gsb_project_backward(int32_t batch_size, int32_t gaussians_per_ba
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t want = (n + 255) / 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, 2 * (int64_t)sms));
-  k_project_bwd<<<grid, 256, 0, stream>>>(
+  launch_pdl(k_project_bwd, grid, 256, 0, stream, 
       batch_size, gaussians_per_batch, reinterpret_cast<const float2*>(grad_means2d), grad_conics, grad_opacities,
       grad_depths, means3d, scales, reinterpret_cast<const float4*>(quats), camera_to_world, camera_params,
       near_plane, g_means3d, g_scales, reinterpret_cast<float4*>(g_quats), g_opacities, g_camera_to_world,

@@ -21,6 +21,8 @@ template <typename K>
 __global__ void __launch_bounds__(kSortThreads)
     rs_histogram(const K* __restrict__ keys, int64_t n, int begin_bit, int passes,
                  int last_bits, uint32_t* __restrict__ hist) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t s_hist[kMaxPasses][kRadix];
   for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) s_hist[i / kRadix][i % kRadix] = 0;
   __syncthreads();
@@ -69,6 +71,8 @@ __global__ void __launch_bounds__(kSortThreads)
                 int shift, int bits, const uint32_t* __restrict__ hist,
                 uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter,
                 uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kTile = kSortThreads * ITEMS;
   extern __shared__ __align__(16) unsigned char s_raw[];
   OnesweepSmem<K, ITEMS>& sm = *reinterpret_cast<OnesweepSmem<K, ITEMS>*>(s_raw);
@@ -237,6 +241,8 @@ __global__ void __launch_bounds__(kSortThreads)
 template <typename K>
 __global__ void rs_copy(const K* __restrict__ ki, const uint32_t* __restrict__ vi, K* __restrict__ ko,
                         uint32_t* __restrict__ vo, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     ko[i] = ki[i];
@@ -299,7 +305,7 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
   if (ws.base == nullptr) return cudaSuccess;
   if (n <= 0) return cudaSuccess;
   if (passes == 0) {
-    rs_copy<K><<<grid_for(n, 256, 148 * 8), 256, 0, stream>>>(keys_in, vals_in, keys_out, vals_out, n);
+    launch_pdl(rs_copy<K>, grid_for(n, 256, 148 * 8), 256, 0, stream, keys_in, vals_in, keys_out, vals_out, n);
     note_launches(1);
     return cudaGetLastError();
   }
@@ -310,7 +316,7 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
     if (e != cudaSuccess) return e;
   }
-  rs_histogram<K><<<grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream>>>(keys_in, n, begin_bit, passes,
+  launch_pdl(rs_histogram<K>, grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream, keys_in, n, begin_bit, passes,
                                                                                    last_bits, hist);
   note_launches(1);
   // Ping-pong so the last pass writes keys_out: pass p writes out when
@@ -325,7 +331,7 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     auto kernel = items == 16 ? rs_onesweep<K, 16> : items == 8 ? rs_onesweep<K, 8> : rs_onesweep<K, 4>;
     const size_t smem = items == 16 ? sizeof(OnesweepSmem<K, 16>)
                                     : items == 8 ? sizeof(OnesweepSmem<K, 8>) : sizeof(OnesweepSmem<K, 4>);
-    kernel<<<(unsigned)parts, kSortThreads, smem, stream>>>(
+    launch_pdl(kernel, (unsigned)parts, kSortThreads, smem, stream, 
         ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, hist + p * kRadix,
         lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status);
     note_launches(1);

@@ -118,8 +118,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     k_render_fwd_warp(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, float* __restrict__ out, float* __restrict__ final_T,
                       int32_t* __restrict__ last_idx, float4* __restrict__ pair_rec,
-                      int32_t* __restrict__ long_tiles, uint32_t* __restrict__ long_count,
                       uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float4 s_rec[kWarps][kWarpBatch][3];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float4(*my)[3] = s_rec[warp];
@@ -128,10 +129,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   for (int tile = blockIdx.x * kWarps + warp; tile < m.total_tiles; tile += stride) {
     const int start = __ldg(&toff[tile]);
     const int n = __ldg(&toff[tile + 1]) - start;
-    if (n > kShortMax) {
-      if (lane == 0) long_tiles[atomicAdd(long_count, 1u)] = tile;
-      continue;
-    }
+    if (n > kShortMax) continue;  // k_render_fwd_cta finds and renders the long tiles
     const TileCoord tc = tile_coord(m, tile);
     const int px = tc.tx * kTile + (lane & 15);
     const int py0 = tc.ty * kTile + (lane >> 4);
@@ -233,17 +231,49 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   }
 }
 
+// The CTA kernels find their long tiles themselves (no list, counter or
+// memset between the warp and CTA kernels): in chunk k, thread i of CTA b
+// checks tile b + (256k + i) * gridDim.x, so the long tiles of a clustered
+// scene spread over all CTAs. The tiles found are compacted into s_long (one
+// ballot per warp); returns how many. All threads call it; it ends with a
+// barrier.
+__device__ __forceinline__ int collect_long_tiles(const Meta& m, const int32_t* __restrict__ toff, int short_max,
+                                                  long long chunk, int* s_long, int* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long t = (long long)blockIdx.x + (chunk * blockDim.x + threadIdx.x) * (long long)gridDim.x;
+  bool is_long = false;
+  if (t < m.total_tiles) is_long = __ldg(&toff[t + 1]) - __ldg(&toff[t]) > short_max;
+  const unsigned bal = __ballot_sync(kFullMask, is_long);
+  if (lane == 0) s_warp[warp] = __popc(bal);
+  __syncthreads();
+  int off = 0, total = 0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+    off += w < warp ? s_warp[w] : 0;
+    total += s_warp[w];
+  }
+  if (is_long) s_long[off + __popc(bal & ((1u << lane) - 1u))] = (int)t;
+  __syncthreads();
+  return total;
+}
+// True while chunk k of this CTA's strided slice starts inside the tile range.
+__device__ __forceinline__ bool long_chunk_live(const Meta& m, long long chunk) {
+  return (long long)blockIdx.x + chunk * blockDim.x * (long long)gridDim.x < m.total_tiles;
+}
+
 // CTA per long tile, one pixel per thread, 256-record shared-memory batches.
 template <bool kSave>
 __global__ void __launch_bounds__(kTilePixels)
     k_render_fwd_cta(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                      const int32_t* __restrict__ ids, float* __restrict__ out, float* __restrict__ final_T,
-                     int32_t* __restrict__ last_idx, const int32_t* __restrict__ long_tiles,
-                     const uint32_t* __restrict__ long_count, uint32_t* __restrict__ status) {
+                     int32_t* __restrict__ last_idx, uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float4 s_rec[kBatch][3];
-  const uint32_t n_long = *long_count;
-  for (uint32_t k = blockIdx.x; k < n_long; k += gridDim.x) {
-    const int tile = long_tiles[k];
+  __shared__ int s_long[kTilePixels], s_warp[kTilePixels / 32];
+  for (long long chunk = 0; long_chunk_live(m, chunk); ++chunk) {
+  const int n_long = collect_long_tiles(m, toff, kShortMax, chunk, s_long, s_warp);
+  for (int k = 0; k < n_long; ++k) {
+    const int tile = s_long[k];
     const TileCoord tc = tile_coord(m, tile);
     const int px = tc.tx * kTile + (threadIdx.x & 15);
     const int py = tc.ty * kTile + (threadIdx.x >> 4);
@@ -293,6 +323,7 @@ __global__ void __launch_bounds__(kTilePixels)
       }
     }
     __syncthreads();  // s_rec reuse by the next tile
+  }
   }
 }
 
@@ -508,8 +539,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                       const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
-                      float* __restrict__ grad_rec, int32_t* __restrict__ long_tiles,
-                      uint32_t* __restrict__ long_count, uint32_t* __restrict__ status) {
+                      float* __restrict__ grad_rec, uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float4 s_dyn[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   BwdWarpSmem& W = reinterpret_cast<BwdWarpSmem*>(s_dyn)[warp];
@@ -555,9 +587,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     prefetch_bwd_tile(m, tile + stride, nxt, &W.st, &W.rec[(k + 1) & 1], lane, grad, final_T, last_idx, pair_rec,
                       ids);
     cp_async_commit();
-    if (n > kBwdShortMax) {
-      if (lane == 0) long_tiles[atomicAdd(long_count, 1u)] = tile;
-    } else if (work) {
+    if (work) {  // tiles above kBwdShortMax: k_render_bwd_cta finds them
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
       int slot = 0;
 #pragma unroll 1
@@ -619,16 +649,19 @@ __global__ void __launch_bounds__(kTilePixels)
     k_render_bwd_cta(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                      const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                      const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
-                     float* __restrict__ grad_rec, const int32_t* __restrict__ long_tiles,
-                     const uint32_t* __restrict__ long_count, uint32_t* __restrict__ status) {
+                     float* __restrict__ grad_rec, uint32_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float4 s_rec[kBatch][3];
   __shared__ int s_gi[kBatch];
   __shared__ float s_acc[kBatch][kGradComps];
   __shared__ int s_max[kWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t n_long = *long_count;
-  for (uint32_t k = blockIdx.x; k < n_long; k += gridDim.x) {
-    const int tile = long_tiles[k];
+  __shared__ int s_long[kTilePixels], s_warp[kTilePixels / 32];
+  for (long long chunk = 0; long_chunk_live(m, chunk); ++chunk) {
+  const int n_long = collect_long_tiles(m, toff, kBwdShortMax, chunk, s_long, s_warp);
+  for (int k = 0; k < n_long; ++k) {
+    const int tile = s_long[k];
     const TileCoord tc = tile_coord(m, tile);
     const int px = tc.tx * kTile + (threadIdx.x & 15);
     const int py = tc.ty * kTile + (threadIdx.x >> 4);
@@ -713,6 +746,7 @@ __global__ void __launch_bounds__(kTilePixels)
       __syncthreads();
     }
   }
+  }
 }
 
 // grad_rec (depth-rank order, packed) -> user layout in input order.
@@ -720,6 +754,8 @@ __global__ void __launch_bounds__(256)
     k_unsort(Meta m, const int32_t* __restrict__ perm, const float4* __restrict__ grad_rec,
              float* __restrict__ g_means2d, float* __restrict__ g_conics, float* __restrict__ g_colors,
              float* __restrict__ g_opac) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= m.BG) return;
   const int b = r / m.G;
@@ -780,29 +816,51 @@ const GridCache& grids() {
   return g;
 }
 
-struct RenderWs {
-  uint32_t* long_count;
-  int32_t* long_tiles;
-};
-
-void carve_render(Carver& c, const Meta& m, RenderWs* w) {
-  w->long_count = c.take<uint32_t>(1);
-  w->long_tiles = c.take<int32_t>((size_t)m.total_tiles);
-}
-
 }  // namespace
 }  // namespace gsb
 
 using namespace gsb;
 
+// The compositing kernels need no scratch (the CTA kernels find their long
+// tiles themselves); the workspace arguments stay in the ABI, unused.
 extern "C" size_t gsb_render_workspace_size(const gsb_raster_meta* meta) {
   Meta m;
-  if (make_meta(meta, &m) != GSB_OK) return 0;
-  Carver c(nullptr);
-  RenderWs w;
-  carve_render(c, m, &w);
-  return c.off + 256;
+  (void)make_meta(meta, &m);
+  return 0;
 }
+
+namespace gsb {
+namespace {
+
+// The forward's two launches: warp per short tile, then CTA per long tile.
+int launch_forward(const Meta& m, const float* rec, const int32_t* tile_offsets, const int32_t* binned_ids,
+                   float* out_rgb, float* final_T, int32_t* last_idx, float* pair_rec, uint32_t* status,
+                   cudaStream_t stream) {
+  const GridCache& g = grids();
+  const float4* r4 = reinterpret_cast<const float4*>(rec);
+  float4* pr4 = reinterpret_cast<float4*>(pair_rec);
+  const int warp_grid = max(1, min(g.fwd_warp[final_T ? 1 : 0], (m.total_tiles + kWarps - 1) / kWarps));
+  const int cta_grid = max(1, min(g.fwd_cta[final_T ? 1 : 0], m.total_tiles));
+  cudaError_t e;
+  if (final_T) {
+    e = launch_pdl(k_render_fwd_warp<true>, warp_grid, kWarps * 32, 0, stream, m, r4, tile_offsets, binned_ids,
+                   out_rgb, final_T, last_idx, pr4, status);
+    if (e == cudaSuccess)
+      e = launch_pdl(k_render_fwd_cta<true>, cta_grid, kTilePixels, 0, stream, m, r4, tile_offsets, binned_ids,
+                     out_rgb, final_T, last_idx, status);
+  } else {
+    e = launch_pdl(k_render_fwd_warp<false>, warp_grid, kWarps * 32, 0, stream, m, r4, tile_offsets, binned_ids,
+                   out_rgb, nullptr, nullptr, nullptr, status);
+    if (e == cudaSuccess)
+      e = launch_pdl(k_render_fwd_cta<false>, cta_grid, kTilePixels, 0, stream, m, r4, tile_offsets, binned_ids,
+                     out_rgb, nullptr, nullptr, status);
+  }
+  note_launches(2);
+  return cuda_status(e);
+}
+
+}  // namespace
+}  // namespace gsb
 
 extern "C" int gsb_render_forward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                                   const int32_t* binned_ids, float* out_rgb, float* final_T, int32_t* last_idx,
@@ -815,32 +873,10 @@ extern "C" int gsb_render_forward(const gsb_raster_meta* meta, const float* rec,
   if ((final_T == nullptr) != (last_idx == nullptr) || (final_T == nullptr) != (pair_rec == nullptr))
     return GSB_ERR_INVALID_ARGUMENT;
   if (m.BG > 0 && !rec) return GSB_ERR_INVALID_ARGUMENT;
-  if (!workspace || workspace_bytes < gsb_render_workspace_size(meta)) return GSB_ERR_WORKSPACE;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  Carver c(workspace);
-  RenderWs w;
-  carve_render(c, m, &w);
-  if (cudaMemsetAsync(w.long_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GSB_ERR_CUDA;
-  const GridCache& g = grids();
-  const float4* r4 = reinterpret_cast<const float4*>(rec);
-  float4* pr4 = reinterpret_cast<float4*>(pair_rec);
-  const int warp_grid = max(1, min(g.fwd_warp[final_T ? 1 : 0], (m.total_tiles + kWarps - 1) / kWarps));
-  const int cta_grid = max(1, min(g.fwd_cta[final_T ? 1 : 0], m.total_tiles));
-  if (final_T) {
-    k_render_fwd_warp<true><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
-                                                                   final_T, last_idx, pr4, w.long_tiles,
-                                                                   w.long_count, status);
-    k_render_fwd_cta<true><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, final_T,
-                                                                 last_idx, w.long_tiles, w.long_count, status);
-  } else {
-    k_render_fwd_warp<false><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
-                                                                    nullptr, nullptr, nullptr, w.long_tiles,
-                                                                    w.long_count, status);
-    k_render_fwd_cta<false><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, nullptr,
-                                                                  nullptr, w.long_tiles, w.long_count, status);
-  }
-  note_launches(2);
-  return cuda_status(cudaGetLastError());
+  (void)workspace;
+  (void)workspace_bytes;
+  return launch_forward(m, rec, tile_offsets, binned_ids, out_rgb, final_T, last_idx, pair_rec, status,
+                        static_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
@@ -852,29 +888,27 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   if (rc != GSB_OK) return rc;
   if (!tile_offsets || !final_T || !last_idx || !grad_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
   if (m.BG > 0 && (!rec || !grad_rec || !pair_rec)) return GSB_ERR_INVALID_ARGUMENT;
-  if (!workspace || workspace_bytes < gsb_render_workspace_size(meta)) return GSB_ERR_WORKSPACE;
+  (void)workspace;
+  (void)workspace_bytes;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (m.BG > 0) {
     cudaError_t e = cudaMemsetAsync(grad_rec, 0, sizeof(float) * GSB_REC_FLOATS * (size_t)m.BG, stream);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
   }
-  Carver c(workspace);
-  RenderWs w;
-  carve_render(c, m, &w);
-  if (cudaMemsetAsync(w.long_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GSB_ERR_CUDA;
   const GridCache& g = grids();
   const float4* r4 = reinterpret_cast<const float4*>(rec);
   const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
   const int cta_grid = max(1, min(g.bwd_cta, m.total_tiles));
   // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
   auto bwd_warp = (1.0f - m.max_alpha >= m.eps) ? k_render_bwd_warp<false> : k_render_bwd_warp<true>;
-  bwd_warp<<<warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream>>>(
-      m, reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx, grad_rgb, grad_rec,
-      w.long_tiles, w.long_count, status);
-  k_render_bwd_cta<<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, final_T, last_idx,
-                                                         grad_rgb, grad_rec, w.long_tiles, w.long_count, status);
+  cudaError_t e = launch_pdl(bwd_warp, warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream, m,
+                             reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx,
+                             grad_rgb, grad_rec, status);
+  if (e == cudaSuccess)
+    e = launch_pdl(k_render_bwd_cta, cta_grid, kTilePixels, 0, stream, m, r4, tile_offsets, binned_ids, final_T,
+                   last_idx, grad_rgb, grad_rec, status);
   note_launches(2);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 extern "C" int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm, const float* grad_rec,
@@ -886,90 +920,21 @@ extern "C" int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm
   if (m.BG == 0) return GSB_OK;
   if (!perm || !grad_rec) return GSB_ERR_INVALID_ARGUMENT;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  k_unsort<<<grid1d(m.BG, 256), 256, 0, stream>>>(m, perm, reinterpret_cast<const float4*>(grad_rec), g_means2d,
-                                                  g_conics, g_colors, g_opacities);
+  const cudaError_t e = launch_pdl(k_unsort, grid1d(m.BG, 256), 256, 0, stream, m, perm,
+                                   reinterpret_cast<const float4*>(grad_rec), g_means2d, g_conics, g_colors,
+                                   g_opacities);
   note_launches(1);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 // ---------------------------------------------------------------------------
-// Allocation-free forward. The forward's only scratch is the list of long tiles
-// and its counter; here they live in a fixed device array compiled into the
-// library, so the caller provides nothing but inputs and outputs. Meant for
-// hosts that own all device memory and give a plugin no way to allocate (a
-// renderer embedded in an engine with a fixed arena, a plugin ABI without an
-// allocator callback). Every GPU that loads the library keeps this array
-// (4 B x (1 + GSB_NOALLOC_MAX_TILES) = 1 MiB) until the process exits.
+// Allocation-free forward: the compositing forward needs no scratch, so this is
+// gsb_render_forward without the (unused) workspace arguments. Meant for hosts
+// that own all device memory and give a plugin no way to allocate.
 // ---------------------------------------------------------------------------
-namespace gsb {
-namespace {
-
-// [0] = long-tile count, [1 .. GSB_NOALLOC_MAX_TILES] = long-tile ids.
-static __device__ __align__(256) uint32_t g_noalloc_render_scratch[1 + GSB_NOALLOC_MAX_TILES];
-
-// The device address of the array on the current device. In host code the
-// symbol is only a host-side handle; each device's copy is looked up once with
-// that device current and cached.
-uint32_t* noalloc_scratch(int* rc) {
-  static std::mutex mu;
-  static uint32_t* ptr[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    *rc = GSB_ERR_CUDA;
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  if (ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_render_scratch) != cudaSuccess || p == nullptr) {
-      *rc = GSB_ERR_CUDA;
-      return nullptr;
-    }
-    ptr[dev] = static_cast<uint32_t*>(p);
-  }
-  *rc = GSB_OK;
-  return ptr[dev];
-}
-
-}  // namespace
-}  // namespace gsb
-
 extern "C" int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                                           const int32_t* binned_ids, float* out_rgb, float* final_T,
                                           int32_t* last_idx, float* pair_rec, uint32_t* status, void* stream_) {
-  Meta m;
-  int rc = make_meta(meta, &m);
-  if (rc != GSB_OK) return rc;
-  if (m.total_tiles > GSB_NOALLOC_MAX_TILES) return GSB_ERR_CAPACITY;
-  if (!tile_offsets || !out_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
-  if ((final_T == nullptr) != (last_idx == nullptr) || (final_T == nullptr) != (pair_rec == nullptr))
-    return GSB_ERR_INVALID_ARGUMENT;
-  if (m.BG > 0 && !rec) return GSB_ERR_INVALID_ARGUMENT;
-  uint32_t* scratch = noalloc_scratch(&rc);
-  if (rc != GSB_OK) return rc;
-  uint32_t* long_count = scratch;
-  int32_t* long_tiles = reinterpret_cast<int32_t*>(scratch + 1);
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  // The array keeps the previous call's contents: the counter must restart at 0.
-  if (cudaMemsetAsync(long_count, 0, sizeof(uint32_t), stream) != cudaSuccess) return GSB_ERR_CUDA;
-  const GridCache& g = grids();
-  const float4* r4 = reinterpret_cast<const float4*>(rec);
-  float4* pr4 = reinterpret_cast<float4*>(pair_rec);
-  const int warp_grid = max(1, min(g.fwd_warp[final_T ? 1 : 0], (m.total_tiles + kWarps - 1) / kWarps));
-  const int cta_grid = max(1, min(g.fwd_cta[final_T ? 1 : 0], m.total_tiles));
-  if (final_T) {
-    k_render_fwd_warp<true><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
-                                                                   final_T, last_idx, pr4, long_tiles, long_count,
-                                                                   status);
-    k_render_fwd_cta<true><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, final_T,
-                                                                 last_idx, long_tiles, long_count, status);
-  } else {
-    k_render_fwd_warp<false><<<warp_grid, kWarps * 32, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb,
-                                                                    nullptr, nullptr, nullptr, long_tiles,
-                                                                    long_count, status);
-    k_render_fwd_cta<false><<<cta_grid, kTilePixels, 0, stream>>>(m, r4, tile_offsets, binned_ids, out_rgb, nullptr,
-                                                                  nullptr, long_tiles, long_count, status);
-  }
-  note_launches(2);
-  return cuda_status(cudaGetLastError());
+  return gsb_render_forward(meta, rec, tile_offsets, binned_ids, out_rgb, final_T, last_idx, pair_rec, status,
+                            nullptr, 0, stream_);
 }

@@ -101,6 +101,8 @@ __device__ __forceinline__ Dir view_dir(const float* __restrict__ means3d, const
 __global__ void __launch_bounds__(256)
     k_sh_fwd(int B, int G, int K, const float* __restrict__ coeffs, const float* __restrict__ means3d,
              const float* __restrict__ c2w, float* __restrict__ colors) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * G) return;
   const int b = (int)(i / G), g = (int)(i - (int64_t)b * G);
@@ -132,6 +134,8 @@ __global__ void __launch_bounds__(256)
     k_sh_bwd(int B, int G, int K, const float* __restrict__ coeffs, const float* __restrict__ means3d,
              const float* __restrict__ c2w, const float* __restrict__ colors, const float* __restrict__ g_colors,
              float* __restrict__ g_coeffs, float* __restrict__ g_means3d, float* __restrict__ g_c2w) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float s_center[kShSmemViews][3];
   const bool smem_views = B <= kShSmemViews;
   if (g_c2w && smem_views)
@@ -224,7 +228,7 @@ extern "C" int gsb_sh_forward(int32_t batch_size, int32_t gaussians, int32_t deg
   if (n == 0) return GSB_OK;
   if (!sh_coeffs || !means3d || !camera_to_world || !colors) return GSB_ERR_INVALID_ARGUMENT;
   if (n >= (int64_t(1) << 31)) return GSB_ERR_CAPACITY;
-  k_sh_fwd<<<grid1d(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(batch_size, gaussians, sh_k(degree),
+  launch_pdl(k_sh_fwd, grid1d(n, 256), 256, 0, static_cast<cudaStream_t>(stream), batch_size, gaussians, sh_k(degree),
                                                                           sh_coeffs, means3d, camera_to_world,
                                                                           colors);
   note_launches(1);
@@ -244,7 +248,7 @@ extern "C" int gsb_sh_backward(int32_t batch_size, int32_t gaussians, int32_t de
   if (g_camera_to_world &&
       cudaMemsetAsync(g_camera_to_world, 0, sizeof(float) * 16 * (size_t)batch_size, s) != cudaSuccess)
     return GSB_ERR_CUDA;
-  k_sh_bwd<<<grid1d(gaussians, 256), 256, 0, s>>>(batch_size, gaussians, sh_k(degree), sh_coeffs, means3d,
+  launch_pdl(k_sh_bwd, grid1d(gaussians, 256), 256, 0, s, batch_size, gaussians, sh_k(degree), sh_coeffs, means3d,
                                                   camera_to_world, colors, grad_colors, g_sh_coeffs, g_means3d,
                                                   g_camera_to_world);
   note_launches(1);

@@ -139,8 +139,9 @@ int gsb_tile_stats(const gsb_raster_meta* meta, const int32_t* tile_offsets, uin
                    void* stream);
 
 /* ---- compositing ---------------------------------------------------------
- * Workspace of gsb_render_forward / gsb_render_backward (a list of the tiles
- * with long pair lists, which get a CTA each; the others get a warp each). */
+ * Workspace of gsb_render_forward / gsb_render_backward: now 0 bytes (short
+ * tiles get a warp each; the kernel for long tiles finds them itself). The
+ * workspace arguments are kept for ABI stability and may be NULL. */
 size_t gsb_render_workspace_size(const gsb_raster_meta* meta);
 
 /* Replaces `tile_fast_forward_eval` / `tile_fast_forward_state`
@@ -163,16 +164,9 @@ int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int
 /* Allocation-free variant of gsb_render_forward, with no counterpart in the
  * reference. For callers that cannot allocate device memory themselves (a host
  * that owns all device memory and gives this library only its inputs and
- * outputs), it takes no workspace: its scratch (the list of tiles with long
- * pair lists) is a fixed device array inside the library, holding up to
- * GSB_NOALLOC_MAX_TILES tiles (B * ceil(H/16) * ceil(W/16)); larger configs
- * return GSB_ERR_CAPACITY. It allocates nothing and calls no allocating routine.
- * The first call on a device looks up that device's copy of the array
- * (cudaGetSymbolAddress, with the device current), so make it before any stream
- * capture. All calls share the one array: calls that overlap on the GPU (other
- * streams, other threads, same device) race and must be serialised by the caller.
- * Same arguments and results as gsb_render_forward otherwise. */
-#define GSB_NOALLOC_MAX_TILES 262144
+ * outputs): it takes no workspace arguments, since the compositing kernels need
+ * no scratch, and allocates nothing. Calls on different streams do not
+ * interfere. Same arguments and results as gsb_render_forward otherwise. */
 int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec,
                                const int32_t* tile_offsets, const int32_t* binned_ids,
                                float* out_rgb, float* final_T, int32_t* last_idx, float* pair_rec,
