@@ -80,16 +80,29 @@ std::array<uint32_t, GSB_STATUS_WORDS> read_status(const Tensor& status) {
   return v;
 }
 
+// The small device-to-host reads (the pair total, the deferred status copies)
+// run on a side stream per device, ordered after the producing kernels by an
+// event, so the compute stream never queues behind a copy.
+c10::cuda::CUDAStream side_stream(c10::DeviceIndex dev) {
+  static std::mutex mu;
+  static std::map<int, c10::cuda::CUDAStream>* streams = new std::map<int, c10::cuda::CUDAStream>();
+  std::lock_guard<std::mutex> g(mu);
+  auto it = streams->find(dev);
+  if (it == streams->end()) it = streams->emplace(dev, c10::cuda::getStreamFromPool(true, dev)).first;
+  return it->second;
+}
+
 // Deferred device-error reads: each forward/backward queues a copy of its
-// status block into a pinned slot; the next forward (after its pair-count
-// sync, which orders every earlier copy on that stream) or
+// status block into a pinned slot on the side stream; the next forward (after
+// its pair-count read, which follows every earlier copy on the side stream) or
 // check_device_errors() reads them. Shared by all threads, because autograd
 // runs backward on its own device thread.
 struct ErrorRing {
   static constexpr int kSlots = 16;
   std::mutex mu;
   Tensor host;  // [kSlots, GSB_STATUS_WORDS] int32, pinned
-  std::vector<at::cuda::CUDAEvent> events;
+  std::vector<at::cuda::CUDAEvent> events;  // copy done (side stream)
+  std::vector<at::cuda::CUDAEvent> issued;  // status final (compute stream)
   std::array<cudaStream_t, kSlots> streams{};
   std::array<bool, kSlots> used{};
   int next = 0;
@@ -98,6 +111,7 @@ struct ErrorRing {
     if (!host.defined()) {
       host = at::empty({kSlots, GSB_STATUS_WORDS}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
       events.resize(kSlots);
+      issued.resize(kSlots);
     }
   }
   // Caller holds mu.
@@ -115,10 +129,18 @@ struct ErrorRing {
     const int i = next;
     next = (next + 1) % kSlots;
     check_slot(i, nullptr);
-    auto stream = at::cuda::getCurrentCUDAStream(status.device().index());
-    host[i].copy_(status, /*non_blocking=*/true);
-    events[i].record(stream);
-    streams[i] = stream.stream();
+    const auto dev = status.device().index();
+    auto cur = at::cuda::getCurrentCUDAStream(dev);
+    auto side = side_stream(dev);
+    issued[i].record(cur);
+    issued[i].block(side);
+    {
+      const c10::cuda::CUDAStreamGuard sg(side);
+      host[i].copy_(status, /*non_blocking=*/true);
+    }
+    status.record_stream(side);  // the allocator keeps it until the copy is done
+    events[i].record(side);
+    streams[i] = side.stream();
     used[i] = true;
   }
   void check_all(cudaStream_t synced) {
@@ -188,9 +210,11 @@ Tensor aligned(const Tensor& t, int64_t align) {
   return c;
 }
 
-// Pinned scalar for the pair total and the event that marks its copy.
+// Pinned scalar for the pair total and the events that order its copy (on the
+// side stream) after the count kernel.
 struct PairRead {
   Tensor host;
+  at::cuda::CUDAEvent counted;
   at::cuda::CUDAEvent done;
 };
 PairRead& pair_read() {
@@ -251,18 +275,25 @@ Binned bin_impl(const gsb_raster_meta& meta, const Tensor& means2d, const Tensor
     check(gsb_bin_count(&meta, ptr<float>(m2), ptr<float>(q2), ptr<float>(o2), ptr<float>(d2),
                         ptr<uint32_t>(r.status), ws.data_ptr(), ws_bytes, stream),
           "gsb_bin_count");
-    // The pair total is read as soon as the count kernel is done, while the
-    // depth sort and scan run.
+    // The pair total is read on the side stream as soon as the count kernel is
+    // done, while the depth sort and scan run on the compute stream.
     if (!pr.host.defined()) pr.host = at::empty({1}, at::TensorOptions().dtype(at::kLong).pinned_memory(true));
-    pr.host.copy_(r.status.narrow(0, GSB_STATUS_PAIR_TOTAL64, 2).view(at::kLong), /*non_blocking=*/true);
-    pr.done.record(cur);
+    auto side = side_stream(dev.index());
+    pr.counted.record(cur);
+    pr.counted.block(side);
+    {
+      const c10::cuda::CUDAStreamGuard sg(side);
+      pr.host.copy_(r.status.narrow(0, GSB_STATUS_PAIR_TOTAL64, 2).view(at::kLong), /*non_blocking=*/true);
+    }
+    r.status.record_stream(side);
+    pr.done.record(side);
     check(gsb_bin_sort_scan(&meta, ptr<float>(m2), ptr<float>(q2), ptr<float>(c2), ptr<float>(o2), ptr<float>(d2),
                             ptr<int32_t>(r.perm), ptr<float>(r.rec), ptr<int32_t>(pair_offsets),
                             ptr<uint64_t>(tile_masks), ptr<uint32_t>(r.status), ws.data_ptr(), ws_bytes, stream),
           "gsb_bin_sort_scan");
   }
   pr.done.synchronize();
-  errors().check_all(cur.stream());  // every earlier copy on this stream is complete now
+  errors().check_all(side_stream(dev.index()).stream());  // every earlier copy on the side stream is complete now
   const int64_t P = pr.host.data_ptr<int64_t>()[0];
   if (P >= (int64_t(1) << 31) - 1)
     throw std::runtime_error("gsplat_b200: " + std::to_string(P) + " tile-splat pairs exceed the supported 2^31 - 1");
