@@ -476,17 +476,19 @@ __device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileO
   const int x0 = tc.tx * kTile, y0 = tc.ty * kTile;
   const bool full = (x0 + kTile <= m.W) && (y0 + kTile <= m.H) && ((m.W & 3) == 0);
   if (full) {
-    // 16-byte chunks: per row 12 of grad, 4 of T, 4 of last_idx.
-    for (int q = lane; q < kTile * 20; q += 32) {
-      const int r = q / 20, k = q - r * 20;
-      const size_t row_pix = ((size_t)tc.b * m.H + y0 + r) * m.W + x0;
-      if (k < 12) {
-        cp_async16(&st->grad[r * 48 + 4 * k], grad + 3 * row_pix + 4 * k);
-      } else if (k < 16) {
-        cp_async16(&st->T[r * 16 + 4 * (k - 12)], final_T + row_pix + 4 * (k - 12));
-      } else {
-        cp_async16(&st->last[r * 16 + 4 * (k - 16)], last_idx + row_pix + 4 * (k - 16));
-      }
+    // 16-byte chunks, one loop per array so no lane diverges: per row 12 of
+    // grad, 4 of T, 4 of last_idx.
+    const size_t pix0 = ((size_t)tc.b * m.H + y0) * m.W + x0;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {  // 16 rows x 12 chunks = 192 = 6 per lane
+      const int q = lane + 32 * i, r = q / 12, k = q - r * 12;
+      cp_async16(&st->grad[r * 48 + 4 * k], grad + 3 * (pix0 + (size_t)r * m.W) + 4 * k);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {  // 16 rows x 4 chunks = 64 = 2 per lane, for T and for last_idx
+      const int q = lane + 32 * i, r = q >> 2, k = q & 3;
+      cp_async16(&st->T[r * 16 + 4 * k], final_T + pix0 + (size_t)r * m.W + 4 * k);
+      cp_async16(&st->last[r * 16 + 4 * k], last_idx + pix0 + (size_t)r * m.W + 4 * k);
     }
   } else {
     for (int p = lane; p < kTilePixels; p += 32) {
