@@ -24,11 +24,24 @@ enum ErrorSite : uint32_t {
 
 // Raster configuration passed to kernels by value (no device meta tensors, no
 // host re-parse of meta tensors per op as in csrc/shared/common.h:28-37).
+// Division of a non-negative int32 n by a run-time invariant d >= 1 without a
+// divide instruction: q = (umulhi(n, mul) + n) >> shift, with shift =
+// ceil(log2 d) and mul = floor(2^32 (2^shift - d) / d) + 1 (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994,
+// round-up method; for n < 2^31 the sum stays below 2^32). Set on the host.
+struct FastDiv {
+  uint32_t mul, shift;
+};
+__device__ __forceinline__ int fast_div(int n, FastDiv f) {
+  return (int)((__umulhi((uint32_t)n, f.mul) + (uint32_t)n) >> f.shift);
+}
+
 struct Meta {
   int H, W;
   int tiles_x, tiles_y, tiles_per_image;
   int B, G, BG, total_tiles;
   float alpha_thr, T_thr, bg_r, bg_g, bg_b, eps, max_alpha;
+  FastDiv div_tiles_x, div_tiles_per_image;
 };
 
 __device__ __forceinline__ void raise_error(uint32_t* status, uint32_t flag, uint32_t site) {

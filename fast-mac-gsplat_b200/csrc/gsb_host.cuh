@@ -28,6 +28,16 @@ struct Carver {
 // Process-wide count of kernel launches issued by this library.
 void note_launches(uint64_t n);
 
+// Magic numbers of fast_div for a divisor 1 <= d < 2^31.
+inline FastDiv make_fast_div(uint32_t d) {
+  FastDiv f;
+  uint32_t l = 0;
+  while ((uint64_t(1) << l) < d) ++l;
+  f.shift = l;
+  f.mul = (uint32_t)(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+  return f;
+}
+
 // Validates a gsb_raster_meta and expands it into the kernel-side Meta.
 inline int make_meta(const gsb_raster_meta* in, Meta* m) {
   if (in == nullptr || m == nullptr) return GSB_ERR_INVALID_ARGUMENT;
@@ -58,6 +68,8 @@ inline int make_meta(const gsb_raster_meta* in, Meta* m) {
   m->bg_b = in->background[2];
   m->eps = in->eps;
   m->max_alpha = in->max_alpha;
+  m->div_tiles_x = make_fast_div((uint32_t)tiles_x);
+  m->div_tiles_per_image = make_fast_div((uint32_t)tpi);
   return GSB_OK;
 }
 

@@ -53,9 +53,9 @@ struct TileCoord {
 
 __device__ __forceinline__ TileCoord tile_coord(const Meta& m, int tile) {
   TileCoord c;
-  c.b = tile / m.tiles_per_image;
+  c.b = fast_div(tile, m.div_tiles_per_image);
   const int local = tile - c.b * m.tiles_per_image;
-  c.ty = local / m.tiles_x;
+  c.ty = fast_div(local, m.div_tiles_x);
   c.tx = local - c.ty * m.tiles_x;
   return c;
 }
@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       }
     }
     if (px < m.W) {
+      const size_t pix0 = ((size_t)tc.b * m.H + py0) * m.W + px;
 #pragma unroll
       for (int q = 0; q < kLanePx / 2; ++q) {
         float tv[2], rv[2], gv[2], bv[2];
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         for (int h = 0; h < 2; ++h) {
           const int py = py0 + 4 * q + 2 * h;
           if (py < m.H) {
-            const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
+            const size_t pix = pix0 + (size_t)(4 * q + 2 * h) * (size_t)m.W;
             out[3 * pix + 0] = fmaf(tv[h], m.bg_r, rv[h]);
             out[3 * pix + 1] = fmaf(tv[h], m.bg_g, gv[h]);
             out[3 * pix + 2] = fmaf(tv[h], m.bg_b, bv[h]);

@@ -170,3 +170,37 @@ def test_torch_op_namespace_registered_for_cuda_only():
         ops.rasterize_fwd(*cpu, *args, False, -1)
     with pytest.raises(NotImplementedError, match="CPU"):
         ops.sh_fwd(torch.zeros(4, 1, 3), torch.zeros(4, 3), torch.eye(4)[None], 0)
+
+
+def _fast_div_magic(d):
+    """make_fast_div (csrc/gsb_host.cuh): shift = ceil(log2 d),
+    mul = floor(2^32 (2^shift - d) / d) + 1."""
+    shift = 0
+    while (1 << shift) < d:
+        shift += 1
+    return ((1 << 32) * ((1 << shift) - d)) // d + 1, shift
+
+
+def test_fast_division_by_invariant_matches_integer_division():
+    """tile_coord divides tile ids by the tiles per image and per row with
+    fast_div: q = (umulhi(n, mul) + n) >> shift (csrc/gsb_common.cuh). Checked
+    against exact division for every divisor a raster can produce up to 2^16,
+    a spread of larger ones, and numerators at the ends of the int32 range and
+    at every multiple boundary."""
+    import numpy as np
+
+    rng = np.random.default_rng(0)
+    divisors = list(range(1, 1 << 16, 37)) + [2 ** k for k in range(31)] + [2 ** k - 1 for k in range(2, 32)] + \
+        [2 ** k + 1 for k in range(2, 31)] + [int(x) for x in rng.integers(1, 2 ** 31 - 1, 200)]
+    for d in divisors:
+        mul, shift = _fast_div_magic(d)
+        assert 0 <= mul < 2 ** 32 and shift <= 31
+        n = np.concatenate([rng.integers(0, 2 ** 31 - 1, 2000, dtype=np.int64), np.arange(0, 64),
+                            np.array([2 ** 31 - 1, 2 ** 31 - 2]),
+                            np.clip(np.arange(1, 40) * d + np.array([-1, 0, 1])[:, None], 0, 2 ** 31 - 1).ravel()])
+        n = n.astype(np.uint64)
+        hi = (n * np.uint64(mul)) >> np.uint64(32)
+        s = hi + n
+        assert int(s.max()) < 2 ** 32
+        q = s >> np.uint64(shift)
+        assert np.array_equal(q, n // np.uint64(d)), d
