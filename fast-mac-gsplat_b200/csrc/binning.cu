@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(256)
   const bool valid = i < m.BG;
   SplatTiles t = splat_tiles(0.f, 0.f, 0.f, 0.f, 0.f, 0.f, m);
   if (valid) {
-    const int b = i / m.G;
+    const int b = fast_div(i, m.div_G);
     // One view: the 32-bit depth key alone; several: the view in the high word.
     sort_keys[i] = (K)(((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]));
     sort_vals[i] = (uint32_t)i;
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kScanThreads)
     const int64_t r = r0 + i;
     tsum += c[i];
     if (r < m.BG) {
-      const int b = (int)(r / m.G);
+      const int b = fast_div((int)r, m.div_G);
       rec[3 * r + 0] = make_float4(mu[i].x, mu[i].y, ca[i], cb[i]);
       rec[3 * r + 1] = make_float4(cc[i], op[i], cr[i], cg[i]);
       rec[3 * r + 2] = make_float4(cbl[i], __uint_as_float(dk[i]), vis_log_threshold(op[i], m.alpha_thr, m.max_alpha),
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(256)
     cnt = pair_offsets[r + 1] - start;
     const float4 p0 = rec[3 * r + 0];
     const float4 p1 = rec[3 * r + 1];
-    tbase = (uint32_t)(r / m.G) * (uint32_t)m.tiles_per_image;
+    tbase = (uint32_t)fast_div(r, m.div_G) * (uint32_t)m.tiles_per_image;
     if (cnt > 0) t = splat_tiles(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m);
   }
   // A splat with a recorded hit mask writes its pairs straight from it (the

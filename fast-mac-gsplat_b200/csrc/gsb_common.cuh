@@ -41,7 +41,7 @@ struct Meta {
   int tiles_x, tiles_y, tiles_per_image;
   int B, G, BG, total_tiles;
   float alpha_thr, T_thr, bg_r, bg_g, bg_b, eps, max_alpha;
-  FastDiv div_tiles_x, div_tiles_per_image;
+  FastDiv div_tiles_x, div_tiles_per_image, div_G;  // div_G: G, or 1 when G = 0
 };
 
 __device__ __forceinline__ void raise_error(uint32_t* status, uint32_t flag, uint32_t site) {

@@ -28,9 +28,10 @@ struct Carver {
 // Process-wide count of kernel launches issued by this library.
 void note_launches(uint64_t n);
 
-// Magic numbers of fast_div for a divisor 1 <= d < 2^31.
+// Magic numbers of fast_div for a divisor 1 <= d < 2^31 (d = 0 is taken as 1).
 inline FastDiv make_fast_div(uint32_t d) {
   FastDiv f;
+  if (d == 0) d = 1;
   uint32_t l = 0;
   while ((uint64_t(1) << l) < d) ++l;
   f.shift = l;
@@ -70,6 +71,7 @@ inline int make_meta(const gsb_raster_meta* in, Meta* m) {
   m->max_alpha = in->max_alpha;
   m->div_tiles_x = make_fast_div((uint32_t)tiles_x);
   m->div_tiles_per_image = make_fast_div((uint32_t)tpi);
+  m->div_G = make_fast_div(in->gaussians_per_batch > 0 ? (uint32_t)in->gaussians_per_batch : 1u);
   return GSB_OK;
 }
 

@@ -122,7 +122,7 @@ __device__ __forceinline__ Proj project_one(const float3 mu, const float3 s, con
 }
 
 __global__ void __launch_bounds__(256)
-    k_project_fwd(int B, int G, const float* __restrict__ means3d, const float* __restrict__ scales,
+    k_project_fwd(int B, int G, FastDiv gdiv, const float* __restrict__ means3d, const float* __restrict__ scales,
                   const float4* __restrict__ quats, const float* __restrict__ opacities,
                   const float* __restrict__ c2w, const float* __restrict__ cam, float near_plane,
                   float2* __restrict__ out_means2d, float* __restrict__ out_conics,
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256)
   pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * G) return;
-  const int b = (int)(i / G);
+  const int b = fast_div((int)i, gdiv);  // i < 2^31 (checked on the host)
   const Cam k = load_cam(c2w, cam, b);
   const float3 mu = make_float3(means3d[3 * i + 0], means3d[3 * i + 1], means3d[3 * i + 2]);
   const float3 s = make_float3(scales[3 * i + 0], scales[3 * i + 1], scales[3 * i + 2]);
@@ -166,13 +166,13 @@ __device__ __forceinline__ float3 add3(float3 a, float3 b) { return make_float3(
 // VJP of one Gaussian: writes its per-Gaussian gradients and returns its view;
 // cg receives its 16 camera-gradient terms (zeros when !active).
 __device__ __forceinline__ int project_bwd_one(
-    int G, int64_t n, int64_t i, bool active, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
+    FastDiv gdiv, int64_t n, int64_t i, bool active, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
     const float* __restrict__ g_opac_in, const float* __restrict__ g_depth, const float* __restrict__ means3d,
     const float* __restrict__ scales, const float4* __restrict__ quats, const float* __restrict__ c2w,
     const float* __restrict__ cam, float near_plane, float* __restrict__ g_means3d, float* __restrict__ g_scales,
     float4* __restrict__ g_quats, float* __restrict__ g_opac, float (&cg)[16]) {
   const int64_t ii = active ? i : n - 1;  // inactive lanes recompute a valid item, contribute zeros
-  const int b = (int)(ii / G);
+  const int b = fast_div((int)ii, gdiv);  // ii < 2^31 (checked on the host)
   const Cam k = load_cam(c2w, cam, b);
   const float3 mu = make_float3(means3d[3 * ii + 0], means3d[3 * ii + 1], means3d[3 * ii + 2]);
   const float3 s = make_float3(scales[3 * ii + 0], scales[3 * ii + 1], scales[3 * ii + 2]);
@@ -340,7 +340,7 @@ __device__ __forceinline__ void cam_grad_atomics(float* g_c2w, float* g_cam, int
 // instead of per warp (all of a view's atomics hit one cache line, so their
 // number sets the cost: 16 per warp at c4 serialised to ~0.46 ms).
 __global__ void __launch_bounds__(256)
-    k_project_bwd(int B, int G, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
+    k_project_bwd(int B, int G, FastDiv gdiv, const float2* __restrict__ g_m2d, const float* __restrict__ g_con,
                   const float* __restrict__ g_opac_in, const float* __restrict__ g_depth,
                   const float* __restrict__ means3d, const float* __restrict__ scales,
                   const float4* __restrict__ quats, const float* __restrict__ c2w, const float* __restrict__ cam,
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(256)
     const int64_t i = base + threadIdx.x;
     const bool active = i < n;
     float cg[16];
-    const int b = project_bwd_one(G, n, i, active, g_m2d, g_con, g_opac_in, g_depth, means3d, scales, quats, c2w,
+    const int b = project_bwd_one(gdiv, n, i, active, g_m2d, g_con, g_opac_in, g_depth, means3d, scales, quats, c2w,
                                   cam, near_plane, g_means3d, g_scales, g_quats, g_opac, cg);
     if (active) {
       if (b != cur) {  // a thread crosses into the next view: flush the previous one
@@ -419,7 +419,8 @@ extern "C" int gsb_project_forward(int32_t batch_size, int32_t gaussians_per_bat
       !out_conics || !out_opacities || !out_depths)
     return GSB_ERR_INVALID_ARGUMENT;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  launch_pdl(k_project_fwd, grid1d(n, 256), 256, 0, stream, batch_size, gaussians_per_batch, means3d, scales,
+  launch_pdl(k_project_fwd, grid1d(n, 256), 256, 0, stream, batch_size, gaussians_per_batch,
+             make_fast_div((uint32_t)gaussians_per_batch), means3d, scales,
                                                     reinterpret_cast<const float4*>(quats), opacities,
                                                     camera_to_world, camera_params, near_plane,
                                                     reinterpret_cast<float2*>(out_means2d), out_conics,
@@ -454,7 +455,8 @@ extern "C" int gsb_project_backward(int32_t batch_size, int32_t gaussians_per_ba
   const int64_t want = (n + 255) / 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, 2 * (int64_t)sms));
   launch_pdl(k_project_bwd, grid, 256, 0, stream, 
-      batch_size, gaussians_per_batch, reinterpret_cast<const float2*>(grad_means2d), grad_conics, grad_opacities,
+      batch_size, gaussians_per_batch, make_fast_div((uint32_t)gaussians_per_batch),
+      reinterpret_cast<const float2*>(grad_means2d), grad_conics, grad_opacities,
       grad_depths, means3d, scales, reinterpret_cast<const float4*>(quats), camera_to_world, camera_params,
       near_plane, g_means3d, g_scales, reinterpret_cast<float4*>(g_quats), g_opacities, g_camera_to_world,
       g_camera_params);

@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(256)
   pdl_trigger();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= m.BG) return;
-  const int b = r / m.G;
+  const int b = fast_div(r, m.div_G);
   const int o = b * m.G + perm[r];
   const float4 q0 = grad_rec[3 * r + 0];
   const float4 q1 = grad_rec[3 * r + 1];

@@ -99,13 +99,13 @@ __device__ __forceinline__ Dir view_dir(const float* __restrict__ means3d, const
 
 // One thread per (view, Gaussian): colours [B, G, 3].
 __global__ void __launch_bounds__(256)
-    k_sh_fwd(int B, int G, int K, const float* __restrict__ coeffs, const float* __restrict__ means3d,
+    k_sh_fwd(int B, int G, FastDiv gdiv, int K, const float* __restrict__ coeffs, const float* __restrict__ means3d,
              const float* __restrict__ c2w, float* __restrict__ colors) {
   pdl_wait();
   pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)B * G) return;
-  const int b = (int)(i / G), g = (int)(i - (int64_t)b * G);
+  const int b = fast_div((int)i, gdiv), g = (int)(i - (int64_t)b * G);  // i < 2^31 (checked on the host)
   const Dir d = view_dir(means3d, c2w, g, b);
   float Y[kShMaxK];
   sh_basis(K, d.x, d.y, d.z, Y);
@@ -228,7 +228,8 @@ extern "C" int gsb_sh_forward(int32_t batch_size, int32_t gaussians, int32_t deg
   if (n == 0) return GSB_OK;
   if (!sh_coeffs || !means3d || !camera_to_world || !colors) return GSB_ERR_INVALID_ARGUMENT;
   if (n >= (int64_t(1) << 31)) return GSB_ERR_CAPACITY;
-  launch_pdl(k_sh_fwd, grid1d(n, 256), 256, 0, static_cast<cudaStream_t>(stream), batch_size, gaussians, sh_k(degree),
+  launch_pdl(k_sh_fwd, grid1d(n, 256), 256, 0, static_cast<cudaStream_t>(stream), batch_size, gaussians,
+             make_fast_div((uint32_t)gaussians), sh_k(degree),
                                                                           sh_coeffs, means3d, camera_to_world,
                                                                           colors);
   note_launches(1);
