@@ -18,7 +18,7 @@ namespace gsb {
 namespace {
 
 constexpr int kScanThreads = 256;
-constexpr int kScanItems = 4;
+constexpr int kScanItems = 2;
 constexpr int kScanTile = kScanThreads * kScanItems;
 constexpr unsigned long long kScanAgg = 1ull << 62;
 constexpr unsigned long long kScanInc = 2ull << 62;
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(256)
 // per-splat tile counts into exclusive pair offsets with a single-pass chained
 // scan (dynamic partition ids + decoupled look-back).
 template <typename K>
-__global__ void __launch_bounds__(kScanThreads)
+__global__ void __launch_bounds__(kScanThreads, 2)
     k_gather_scan(Meta m, const K* __restrict__ sorted_keys,
                   const uint32_t* __restrict__ sorted_vals, const float2* __restrict__ means2d,
                   const float* __restrict__ conics, const float* __restrict__ colors,
@@ -290,19 +290,7 @@ __global__ void __launch_bounds__(kScanThreads)
   asm volatile("" ::: "memory");  // all gathers in flight before the first use
   unsigned long long tsum = 0;
 #pragma unroll
-  for (int i = 0; i < kScanItems; ++i) {
-    const int64_t r = r0 + i;
-    tsum += c[i];
-    if (r < m.BG) {
-      const int b = fast_div((int)r, m.div_G);
-      rec[3 * r + 0] = make_float4(mu[i].x, mu[i].y, ca[i], cb[i]);
-      rec[3 * r + 1] = make_float4(cc[i], op[i], cr[i], cg[i]);
-      rec[3 * r + 2] = make_float4(cbl[i], __uint_as_float(dk[i]), vis_log_threshold(op[i], m.alpha_thr, m.max_alpha),
-                                   sat_log_threshold(op[i], m.max_alpha));
-      perm[r] = (int32_t)(orig[i] - (uint32_t)b * (uint32_t)m.G);
-      if (masks_out) masks_out[r] = masks_in[orig[i]];
-    }
-  }
+  for (int i = 0; i < kScanItems; ++i) tsum += c[i];
   // Block-wide exclusive scan of the thread sums.
   unsigned long long x = tsum;
 #pragma unroll
@@ -357,6 +345,20 @@ __global__ void __launch_bounds__(kScanThreads)
       st_volatile_u64(&lookback[part], kScanInc | ((excl + block_total) & kScanMask));
     }
     s_exclusive = excl;
+  }
+  // The gathered records are written while thread 0 waits on its predecessors.
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i) {
+    const int64_t r = r0 + i;
+    if (r < m.BG) {
+      const int b = fast_div((int)r, m.div_G);
+      rec[3 * r + 0] = make_float4(mu[i].x, mu[i].y, ca[i], cb[i]);
+      rec[3 * r + 1] = make_float4(cc[i], op[i], cr[i], cg[i]);
+      rec[3 * r + 2] = make_float4(cbl[i], __uint_as_float(dk[i]), vis_log_threshold(op[i], m.alpha_thr, m.max_alpha),
+                                   sat_log_threshold(op[i], m.max_alpha));
+      perm[r] = (int32_t)(orig[i] - (uint32_t)b * (uint32_t)m.G);
+      if (masks_out) masks_out[r] = masks_in[orig[i]];
+    }
   }
   __syncthreads();
   unsigned long long run = s_exclusive + thread_excl;
