@@ -55,6 +55,9 @@ def parse_args():
                     help="one JSON line per BASELINE config c0-c4: forward-only and forward+backward ms")
     ap.add_argument("--height", type=int, default=4096)
     ap.add_argument("--width", type=int, default=4096)
+    ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
+                    help="c4 with several GPUs: gradient sum by the library's NVLink peer-memory kernel "
+                         "(default) or by NCCL all-reduce (the baseline)")
     ap.add_argument("--sh-degree", type=int, default=-1,
                     help="c4 only: colours from spherical harmonics of this degree (0-3) instead of RGB")
     return ap.parse_args()
@@ -461,7 +464,7 @@ def run_shared3d(args):
 
     import torch_gsplat_bridge_fast as tgb
     from torch_gsplat_bridge_fast import _native
-    from torch_gsplat_bridge_fast.distributed import SharedGradAllReduce
+    from torch_gsplat_bridge_fast.distributed import PeerGradAllReduce, SharedGradAllReduce
     from torch_gsplat_bridge_fast.rasterize import _bin
     from workloads import config_3d, grad_image
 
@@ -495,7 +498,9 @@ def run_shared3d(args):
         E = tiled_work(st.tile_offsets, 1, H, W)
         P = st.P
         del st
-    reducer = SharedGradAllReduce(params) if world > 1 else None
+    reducer = None
+    if world > 1:
+        reducer = PeerGradAllReduce(params) if args.allreduce == "peer" else SharedGradAllReduce(params)
     reducer_floats = sum(p[0].numel() for p in params)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
@@ -552,9 +557,13 @@ def run_shared3d(args):
     if reducer is not None:
         t = statistics.mean(ar_ms) * 1e-3
         nbytes = reducer.bytes
-        allreduce = {"bytes": nbytes, "avg_ms": round(t * 1e3, 4), "algbw_GBs": round(nbytes / t / 1e9, 1),
+        allreduce = {"impl": "peer-memory kernel (gsb_peer_allreduce_sum)" if args.allreduce == "peer"
+                     else "NCCL all-reduce", "bytes": nbytes, "avg_ms": round(t * 1e3, 4),
+                     "algbw_GBs": round(nbytes / t / 1e9, 1),
                      "busbw_GBs": round(2 * (world - 1) / world * nbytes / t / 1e9, 1),
-                     "buckets": len(reducer.buckets)}
+                     "includes": "pack into the flat buffer, the sum, unpack"}
+        if args.allreduce == "peer":
+            reducer.check_errors()
     if rank == 0:
         line = {
             "metric": "Gsplat-px evals/s, c4 shared-3D fwd+bwd + gradient all-reduce",
@@ -573,7 +582,8 @@ def run_shared3d(args):
             "config": {"workload": f"c4: G={G} shared 3D Gaussians, one {W}x{H} camera per rank (view = rank mod 8)",
                        "pairs_rank0_view": P, "evals_rank0_view": E, "evals_all_ranks": E_total,
                        "l2": "flushed (256 MB write) between steps",
-                       "parallelism": f"{world} rank(s); per-Gaussian grads ({reducer_floats} floats) summed with NCCL all-reduce",
+                       "parallelism": f"{world} rank(s); per-Gaussian grads ({reducer_floats} floats) summed with "
+                                      + ("the NVLink peer-memory kernel" if args.allreduce == "peer" else "NCCL all-reduce"),
             "colors": f"spherical harmonics degree {deg}" if deg >= 0 else "RGB"},
             "gpu_launches": int(launches),
             "allreduce": allreduce,
@@ -581,6 +591,8 @@ def run_shared3d(args):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if isinstance(reducer, PeerGradAllReduce):
+            reducer.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -20,6 +20,8 @@ enum ErrorSite : uint32_t {
   kSiteRender = 4,
   kSiteRenderBwd = 5,
   kSiteScanTotal = 6,
+  kSitePeerStart = 7,
+  kSitePeerEnd = 8,
 };
 
 // Raster configuration passed to kernels by value (no device meta tensors, no

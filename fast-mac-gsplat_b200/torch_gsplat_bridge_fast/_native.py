@@ -23,6 +23,10 @@ GSB_STATUS_ERROR_SITE = 3
 GSB_STATUS_PAIR_TOTAL64 = 4
 GSB_STATUS_WORDS = 8
 GSB_REC_FLOATS = 12
+GSB_PEER_MAX_RANKS = 8
+GSB_PEER_FLAG_BYTES = 256
+GSB_PEER_HANDLE_BYTES = 64
+GSB_DEVERR_PEER_TIMEOUT = 8
 
 DEVERR_LOOKBACK_TIMEOUT = 1
 DEVERR_PAIR_OVERFLOW = 2
@@ -51,6 +55,12 @@ EXPORTED = (
     "gsb_radix_sort_pairs",
     "gsb_sh_forward",
     "gsb_sh_backward",
+    "gsb_peer_buffer_alloc",
+    "gsb_peer_buffer_free",
+    "gsb_peer_handle",
+    "gsb_peer_open",
+    "gsb_peer_close",
+    "gsb_peer_allreduce_sum",
 )
 
 
@@ -112,6 +122,12 @@ def load() -> C.CDLL:
         "gsb_radix_sort_pairs": (C.c_int, [p, p, p, p, i64, C.c_int, C.c_int, p, p, sz, p]),
         "gsb_sh_forward": (C.c_int, [i32, i32, i32, p, p, p, p, p]),
         "gsb_sh_backward": (C.c_int, [i32, i32, i32, p, p, p, p, p, p, p, p, p]),
+        "gsb_peer_buffer_alloc": (C.c_int, [sz, C.POINTER(p)]),
+        "gsb_peer_buffer_free": (C.c_int, [p]),
+        "gsb_peer_handle": (C.c_int, [p, p]),
+        "gsb_peer_open": (C.c_int, [p, C.POINTER(p)]),
+        "gsb_peer_close": (C.c_int, [p]),
+        "gsb_peer_allreduce_sum": (C.c_int, [i32, i32, C.POINTER(p), i64, C.c_uint32, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

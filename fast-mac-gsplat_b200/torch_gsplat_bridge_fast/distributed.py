@@ -9,14 +9,15 @@ variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:910-938). He
   (weak scaling).
 * Shared 3D Gaussians (every rank renders a different camera of the same
   scene): the per-Gaussian gradients of the shared parameters are summed
-  across ranks with NCCL all-reduce (sum, fp32) over NVLink. The gradients are
-  packed into one flat buffer, cut into buckets and reduced asynchronously;
-  `start()` can be called on a side stream while other work proceeds.
-
-The same code runs on CPU tensors with the gloo backend (tests).
+  across ranks. `PeerGradAllReduce` does it with this library's own kernel
+  over NVLink peer memory (gsb_peer_allreduce_sum: CUDA IPC buffers, a
+  two-shot reduce in one kernel per rank). `SharedGradAllReduce` does it with
+  NCCL all-reduce (sum, fp32) in buckets, asynchronously; it is the baseline,
+  and the one that runs on CPU tensors with the gloo backend (tests).
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import List, Optional, Sequence
 
 import torch
@@ -30,26 +31,17 @@ def shard_views(num_views: int, world_size: int, rank: int) -> List[int]:
     return list(range(rank, num_views, world_size))
 
 
-class SharedGradAllReduce:
-    """Sums the .grad of shared parameters across ranks.
+class _FlatGrads:
+    """The .grad of the shared parameters packed into one flat fp32 buffer."""
 
-    params: the shared leaf tensors (e.g. means3d, scales, quats, opacities, colors).
-    bucket_bytes: size of each all-reduce bucket (fp32 elements * 4).
-    """
-
-    def __init__(self, params: Sequence[torch.Tensor], bucket_bytes: int = 64 << 20,
-                 group: Optional[dist.ProcessGroup] = None):
+    def _init_flat(self, params: Sequence[torch.Tensor], flat: Optional[torch.Tensor] = None) -> None:
         if not params:
             raise ValueError("no parameters")
         self.params = list(params)
-        self.group = group
-        dev = self.params[0].device
         self.numels = [p.numel() for p in self.params]
         self.total = sum(self.numels)
-        self.flat = torch.zeros(self.total, dtype=torch.float32, device=dev)
-        elems = max(1, bucket_bytes // 4)
-        self.buckets = [(s, min(self.total, s + elems)) for s in range(0, self.total, elems)]
-        self._works = []
+        dev = self.params[0].device
+        self.flat = flat if flat is not None else torch.zeros(self.total, dtype=torch.float32, device=dev)
 
     def _pack(self) -> None:
         off = 0
@@ -71,6 +63,26 @@ class SharedGradAllReduce:
                 p.grad.copy_(g)
             off += n
 
+    @property
+    def bytes(self) -> int:
+        return self.total * 4
+
+
+class SharedGradAllReduce(_FlatGrads):
+    """Sums the .grad of shared parameters across ranks with NCCL (or gloo).
+
+    params: the shared leaf tensors (e.g. means3d, scales, quats, opacities, colors).
+    bucket_bytes: size of each all-reduce bucket (fp32 elements * 4).
+    """
+
+    def __init__(self, params: Sequence[torch.Tensor], bucket_bytes: int = 64 << 20,
+                 group: Optional[dist.ProcessGroup] = None):
+        self._init_flat(params)
+        self.group = group
+        elems = max(1, bucket_bytes // 4)
+        self.buckets = [(s, min(self.total, s + elems)) for s in range(0, self.total, elems)]
+        self._works = []
+
     def start(self) -> None:
         """Packs the local gradients and launches the bucketed async all-reduce."""
         self._pack()
@@ -88,6 +100,89 @@ class SharedGradAllReduce:
         self.start()
         self.finish()
 
-    @property
-    def bytes(self) -> int:
-        return self.total * 4
+
+class _DeviceArray:
+    """A raw device allocation seen by torch.as_tensor (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, n_floats: int):
+        self.__cuda_array_interface__ = {"shape": (n_floats,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGradAllReduce(_FlatGrads):
+    """Sums the .grad of shared parameters across the ranks of one node with
+    gsb_peer_allreduce_sum: each rank owns a CUDA IPC buffer that every other
+    rank maps; one kernel per call barriers on flags in those buffers, adds
+    rank r's shard of all buffers over NVLink and writes the sum into all of
+    them. One process per GPU, all ranks on one node, at most 8 ranks; `group`
+    is used only to exchange the IPC handles (any backend).
+    """
+
+    def __init__(self, params: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None):
+        from . import _native as N
+
+        self._N = N
+        self._L = N.load()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > N.GSB_PEER_MAX_RANKS:
+            raise ValueError(f"PeerGradAllReduce supports at most {N.GSB_PEER_MAX_RANKS} ranks")
+        dev = params[0].device
+        if dev.type != "cuda":
+            raise ValueError("PeerGradAllReduce needs CUDA parameters")
+        total = sum(p.numel() for p in params)
+        self.padded = (total + 3) // 4 * 4  # the kernel moves 16-byte vectors
+        with torch.cuda.device(dev):
+            base = C.c_void_p()
+            N.check(self._L.gsb_peer_buffer_alloc(self.padded * 4, C.byref(base)), "gsb_peer_buffer_alloc")
+            self._own = base.value
+            handle = (C.c_char * N.GSB_PEER_HANDLE_BYTES)()
+            N.check(self._L.gsb_peer_handle(C.c_void_p(self._own), handle), "gsb_peer_handle")
+            handles: List[Optional[bytes]] = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._opened = []
+            bases = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                peer = C.c_void_p()
+                N.check(self._L.gsb_peer_open(C.create_string_buffer(h, len(h)), C.byref(peer)), "gsb_peer_open")
+                self._opened.append(peer.value)
+                bases.append(peer.value)
+            self._bases = (C.c_void_p * self.world)(*bases)
+            data = torch.as_tensor(_DeviceArray(self._own + N.GSB_PEER_FLAG_BYTES, self.padded), device=dev)
+            data.zero_()
+        self._init_flat(params, flat=data[:total])
+        self._data = data
+        self.status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
+        self.epoch = 0
+
+    def __call__(self) -> None:
+        self._pack()
+        self.epoch += 1
+        stream = torch.cuda.current_stream(self._data.device).cuda_stream
+        self._N.check(self._L.gsb_peer_allreduce_sum(self.rank, self.world, self._bases, self.padded,
+                                                     self.epoch & 0xFFFFFFFF, self._N.ptr(self.status), stream),
+                      "gsb_peer_allreduce_sum")
+        self._unpack()
+
+    def check_errors(self) -> None:
+        """Raises if a call timed out waiting for a peer (synchronizes)."""
+        flags = int(self.status[self._N.GSB_STATUS_ERROR].item())
+        if flags:
+            raise RuntimeError(f"gsplat_b200 peer all-reduce: a rank did not reach a barrier in time "
+                               f"(device error flags {flags})")
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective: every rank calls it)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self._data.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            self._L.gsb_peer_close(C.c_void_p(p))
+        dist.barrier(group=self.group)
+        self._L.gsb_peer_buffer_free(C.c_void_p(self._own))
+        self._own = None

@@ -52,6 +52,7 @@ extern "C" {
 #define GSB_DEVERR_LOOKBACK_TIMEOUT 1u /* decoupled look-back spin limit hit */
 #define GSB_DEVERR_PAIR_OVERFLOW 2u    /* emit wrote past its scan slot / P >= 2^31 */
 #define GSB_DEVERR_BOUNDS 4u           /* index outside its buffer */
+#define GSB_DEVERR_PEER_TIMEOUT 8u     /* a peer did not reach a gsb_peer_allreduce_sum barrier in time */
 
 /* ---- packed splat record (12 floats, 48 B, 16-B aligned) --------------- */
 #define GSB_REC_FLOATS 12
@@ -216,6 +217,34 @@ int gsb_sh_backward(int32_t batch_size, int32_t gaussians, int32_t degree, const
                     const float* means3d, const float* camera_to_world, const float* colors,
                     const float* grad_colors, float* g_sh_coeffs, float* g_means3d,
                     float* g_camera_to_world, void* stream);
+
+/* ---- multi-GPU: gradient sum over NVLink peer memory -----------------------
+ * No counterpart in the reference, which is single-device. Sums a float buffer
+ * across the ranks of one node in place, replacing the NCCL all-reduce of the
+ * shared-Gaussian gradients. Each rank owns one peer buffer: GSB_PEER_FLAG_BYTES
+ * of barrier flags followed by the data. The buffer is exported with a
+ * GSB_PEER_HANDLE_BYTES CUDA IPC handle and mapped by every other rank, which
+ * passes all ranks' base pointers in rank order. */
+#define GSB_PEER_MAX_RANKS 8
+#define GSB_PEER_FLAG_BYTES 256
+#define GSB_PEER_HANDLE_BYTES 64
+/* cudaMalloc of GSB_PEER_FLAG_BYTES + data_bytes on the current device, flags zeroed. */
+int gsb_peer_buffer_alloc(size_t data_bytes, void** base);
+int gsb_peer_buffer_free(void* base);
+/* IPC handle of a buffer from gsb_peer_buffer_alloc; a peer process maps it with gsb_peer_open. */
+int gsb_peer_handle(const void* base, void* handle);
+int gsb_peer_open(const void* handle, void** base);
+int gsb_peer_close(void* base);
+/* bases[r] = rank r's buffer as mapped in this process (bases[rank] = own).
+ * Sums data[0 .. n_floats) over all ranks and leaves the sum in every rank's
+ * buffer. One kernel: a start barrier (every rank's data is final), rank r
+ * adds shard r of all buffers over NVLink and stores the sum into all of them,
+ * then an end barrier. Every rank calls it with the same n_floats and epoch;
+ * epoch counts the calls from 1 and grows by one per call. Barrier waits are
+ * bounded (about 10 s): a rank that does not arrive raises
+ * GSB_DEVERR_PEER_TIMEOUT in status[GSB_STATUS_ERROR] and the kernel returns. */
+int gsb_peer_allreduce_sum(int32_t rank, int32_t world, void* const* bases, int64_t n_floats, uint32_t epoch,
+                           uint32_t* status, void* stream);
 
 /* ---- building blocks, exported for parity tests -------------------------
  * Stable LSD radix sort of (uint64 key, uint32 value) pairs on key bits

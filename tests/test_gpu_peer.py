@@ -1,0 +1,107 @@
+"""The NVLink peer-memory gradient sum (PeerGradAllReduce over
+gsb_peer_allreduce_sum) against the same sum computed on the CPU.
+
+Each rank fills the .grad of a few shared parameters from seeds every rank
+knows, so every rank can compute the expected sum itself. The sum is taken in
+rank order on both sides, so the comparison is exact. The multi-rank case runs
+one process per GPU and is skipped with fewer than two GPUs; the one-rank case
+(no kernel, the buffer is its own sum) runs anywhere with a GPU.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1000, 3), (1000, 4), (1000,), (1001, 3), (300_001,)]  # odd total: the buffer pads to 4 floats
+
+
+def _grads(step: int, rank: int):
+    return [torch.randn(s, generator=torch.Generator().manual_seed(1000 * step + 10 * rank + i))
+            for i, s in enumerate(SHAPES)]
+
+
+def _expected(step: int, world: int):
+    per_rank = [_grads(step, r) for r in range(world)]
+    out = []
+    for i in range(len(SHAPES)):
+        acc = per_rank[0][i].clone()
+        for r in range(1, world):
+            acc = acc + per_rank[r][i]
+        out.append(acc)
+    return out
+
+
+def _worker(rank: int, world: int, port: int, q) -> None:
+    try:
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [root, os.path.join(root, "fast-mac-gsplat_b200")]
+        from torch_gsplat_bridge_fast.distributed import PeerGradAllReduce
+
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        dev = torch.device("cuda", rank)
+        params = [torch.zeros(s, device=dev, requires_grad=True) for s in SHAPES]
+        red = PeerGradAllReduce(params)
+        worst = 0.0
+        for step in range(3):
+            for p, g in zip(params, _grads(step, rank)):
+                p.grad = g.to(dev)
+            red()
+            for p, want in zip(params, _expected(step, world)):
+                worst = max(worst, float((p.grad.cpu() - want).abs().max()))
+        red.check_errors()
+        red.close()
+        dist.destroy_process_group()
+        q.put((rank, worst, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, repr(e)))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(world: int) -> None:
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    try:
+        for _ in range(world):
+            results.append(q.get(timeout=240))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, worst, err in sorted(results, key=lambda r: r[0]):
+        assert err is None, f"rank {rank}: {err}"
+        assert worst == 0.0, f"rank {rank}: max abs error {worst}"
+
+
+def test_peer_allreduce_one_rank_leaves_the_buffer():
+    _run(1)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_allreduce_two_ranks_matches_cpu_sum():
+    _run(2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+def test_peer_allreduce_four_ranks_matches_cpu_sum():
+    _run(4)
