@@ -561,7 +561,8 @@ def run_shared3d(args):
                      else "NCCL all-reduce", "bytes": nbytes, "avg_ms": round(t * 1e3, 4),
                      "algbw_GBs": round(nbytes / t / 1e9, 1),
                      "busbw_GBs": round(2 * (world - 1) / world * nbytes / t / 1e9, 1),
-                     "includes": "pack into the flat buffer, the sum, unpack"}
+                     "includes": "pack into the flat buffer and the sum; the summed grads are views into the buffer"
+                     if args.allreduce == "peer" else "pack into the flat buffer, the sum, copy back"}
         if args.allreduce == "peer":
             reducer.check_errors()
     if rank == 0:

@@ -63,6 +63,12 @@ class _FlatGrads:
                 p.grad.copy_(g)
             off += n
 
+    def _unpack_views(self) -> None:
+        off = 0
+        for p, n in zip(self.params, self.numels):
+            p.grad = self.flat[off:off + n].view_as(p)
+            off += n
+
     @property
     def bytes(self) -> int:
         return self.total * 4
@@ -116,9 +122,14 @@ class PeerGradAllReduce(_FlatGrads):
     rank r's shard of all buffers over NVLink and writes the sum into all of
     them. One process per GPU, all ranks on one node, at most 8 ranks; `group`
     is used only to exchange the IPC handles (any backend).
+
+    grads_as_views: after a call each parameter's .grad is a view into the
+    summed buffer (no copy back), valid until the next call, as with DDP's
+    gradient_as_bucket_view. False copies the sums into the .grad tensors.
     """
 
-    def __init__(self, params: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None):
+    def __init__(self, params: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None,
+                 grads_as_views: bool = True):
         from . import _native as N
 
         self._N = N
@@ -158,6 +169,7 @@ class PeerGradAllReduce(_FlatGrads):
         self._data = data
         self.status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
         self.epoch = 0
+        self.grads_as_views = grads_as_views
 
     def __call__(self) -> None:
         self._pack()
@@ -166,7 +178,10 @@ class PeerGradAllReduce(_FlatGrads):
         self._N.check(self._L.gsb_peer_allreduce_sum(self.rank, self.world, self._bases, self.padded,
                                                      self.epoch & 0xFFFFFFFF, self._N.ptr(self.status), stream),
                       "gsb_peer_allreduce_sum")
-        self._unpack()
+        if self.grads_as_views:
+            self._unpack_views()
+        else:
+            self._unpack()
 
     def check_errors(self) -> None:
         """Raises if a call timed out waiting for a peer (synchronizes)."""

@@ -38,7 +38,7 @@ def _expected(step: int, world: int):
     return out
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:
+def _worker(rank: int, world: int, port: int, q, views: bool = True) -> None:
     try:
         import sys
 
@@ -50,7 +50,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
         dev = torch.device("cuda", rank)
         params = [torch.zeros(s, device=dev, requires_grad=True) for s in SHAPES]
-        red = PeerGradAllReduce(params)
+        red = PeerGradAllReduce(params, grads_as_views=views)
         worst = 0.0
         for step in range(3):
             for p, g in zip(params, _grads(step, rank)):
@@ -72,11 +72,11 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(world: int) -> None:
+def _run(world: int, views: bool = True) -> None:
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, views)) for r in range(world)]
     for p in procs:
         p.start()
     results = []
@@ -98,8 +98,9 @@ def test_peer_allreduce_one_rank_leaves_the_buffer():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_allreduce_two_ranks_matches_cpu_sum():
-    _run(2)
+@pytest.mark.parametrize("views", [True, False])
+def test_peer_allreduce_two_ranks_matches_cpu_sum(views):
+    _run(2, views)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
