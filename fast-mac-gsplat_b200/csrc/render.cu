@@ -45,6 +45,7 @@ constexpr int kLanePx = 8;      // pixels per lane in the warp kernels: rows py0
 constexpr int kWarps = 8;       // warps per CTA (forward warp kernel, CTA kernels)
 constexpr int kBwdWarps = 4;    // warps per CTA (backward warp kernel)
 constexpr int kBatch = 256;     // records staged per CTA round (long kernels)
+constexpr int kCtaThreads = 128;  // threads per long tile in the CTA kernels (2 pixels each)
 constexpr int kGradComps = 9;
 
 struct TileCoord {
@@ -236,14 +237,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 // memset between the warp and CTA kernels): in chunk k, thread i of CTA b
 // checks tile b + (256k + i) * gridDim.x, so the long tiles of a clustered
 // scene spread over all CTAs. The tiles found are compacted into s_long (one
-// ballot per warp); returns how many. All threads call it; it ends with a
-// barrier.
+// ballot per warp); a tile is long when short_max < pairs <= long_max. Returns
+// how many. All threads call it; it ends with a barrier.
 __device__ __forceinline__ int collect_long_tiles(const Meta& m, const int32_t* __restrict__ toff, int short_max,
-                                                  long long chunk, int* s_long, int* s_warp) {
+                                                  int long_max, long long chunk, int* s_long, int* s_warp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long t = (long long)blockIdx.x + (chunk * blockDim.x + threadIdx.x) * (long long)gridDim.x;
   bool is_long = false;
-  if (t < m.total_tiles) is_long = __ldg(&toff[t + 1]) - __ldg(&toff[t]) > short_max;
+  if (t < m.total_tiles) {
+    const int n = __ldg(&toff[t + 1]) - __ldg(&toff[t]);
+    is_long = n > short_max && n <= long_max;
+  }
   const unsigned bal = __ballot_sync(kFullMask, is_long);
   if (lane == 0) s_warp[warp] = __popc(bal);
   __syncthreads();
@@ -261,70 +265,93 @@ __device__ __forceinline__ bool long_chunk_live(const Meta& m, long long chunk) 
   return (long long)blockIdx.x + chunk * blockDim.x * (long long)gridDim.x < m.total_tiles;
 }
 
-// CTA per long tile, one pixel per thread, 256-record shared-memory batches.
+// CTA of kCtaThreads per long tile. A thread owns 2 pixels of one column (rows
+// r and r + 8), packed as one f32x2 pair, and runs the warp kernel's
+// branch-free record body on them, so the per-record work is amortised over 2
+// pixels and done with packed instructions. Records are staged kBatch at a time
+// in shared memory; the CTA stops early once no pixel is live.
 template <bool kSave>
-__global__ void __launch_bounds__(kTilePixels)
+__global__ void __launch_bounds__(kCtaThreads)
     k_render_fwd_cta(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                      const int32_t* __restrict__ ids, float* __restrict__ out, float* __restrict__ final_T,
                      int32_t* __restrict__ last_idx, uint32_t* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
   __shared__ float4 s_rec[kBatch][3];
-  __shared__ int s_long[kTilePixels], s_warp[kTilePixels / 32];
+  __shared__ int s_long[kCtaThreads], s_warp[kCtaThreads / 32];
+  const int t = threadIdx.x;
+  const F2 one = f2(1.0f), log2e = f2(kLog2e);
   for (long long chunk = 0; long_chunk_live(m, chunk); ++chunk) {
-  const int n_long = collect_long_tiles(m, toff, kShortMax, chunk, s_long, s_warp);
-  for (int k = 0; k < n_long; ++k) {
-    const int tile = s_long[k];
-    const TileCoord tc = tile_coord(m, tile);
-    const int px = tc.tx * kTile + (threadIdx.x & 15);
-    const int py = tc.ty * kTile + (threadIdx.x >> 4);
-    const bool valid = px < m.W && py < m.H;
-    const int start = toff[tile];
-    const int n = toff[tile + 1] - start;
-    const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-    float T = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-    int last = n;  // entries consumed: n unless the pixel saturates
-    bool alive = valid && (T > m.T_thr);
-    if (!alive) last = 0;
-    for (int base = 0; base < n; base += kBatch) {
-      if (__syncthreads_count(alive) == 0) break;
-      const int cnt = min(kBatch, n - base);
-      if ((int)threadIdx.x < cnt)
-        load_rec(rec, load_gi(ids, start + base + threadIdx.x, m.BG, status, kSiteRender), s_rec[threadIdx.x]);
-      __syncthreads();
-      if (alive) {
-        for (int j = 0; j < cnt; ++j) {
-          const float4 p0 = s_rec[j][0];
-          const float4 p1 = s_rec[j][1];
-          const float power = power_at(power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x)), __fsub_rn(fy, p0.y));
-          const float4 p2 = s_rec[j][2];
-          if (!(power <= 0.0f && power >= p2.z)) continue;
-          const float alpha = fminf(m.max_alpha, p1.y * __expf(power));
-          const float w = T * alpha;
-          cr = fmaf(w, p1.z, cr);
-          cg = fmaf(w, p1.w, cg);
-          cb = fmaf(w, p2.x, cb);
-          T *= 1.0f - alpha;
-          if (T <= m.T_thr) {
-            last = base + j + 1;
-            alive = false;
-            break;
+    const int n_long = collect_long_tiles(m, toff, kShortMax, 0x7fffffff, chunk, s_long, s_warp);
+    for (int k = 0; k < n_long; ++k) {
+      const int tile = s_long[k];
+      const TileCoord tc = tile_coord(m, tile);
+      const int px = tc.tx * kTile + (t & 15);
+      const int py0 = tc.ty * kTile + (t >> 4);  // rows py0 and py0 + 8
+      const float fx = (float)px + 0.5f;
+      const F2 fy = f2((float)py0 + 0.5f, (float)py0 + 8.5f);
+      const bool in_lo = px < m.W && py0 < m.H, in_hi = px < m.W && py0 + 8 < m.H;
+      F2 T = f2(in_lo ? 1.0f : 0.0f, in_hi ? 1.0f : 0.0f), cr = f2(0.0f), cg = f2(0.0f), cb = f2(0.0f);
+      int last_l = 0, last_h = 0;
+      const int start = __ldg(&toff[tile]);
+      const int n = __ldg(&toff[tile + 1]) - start;
+      for (int base = 0; base < n; base += kBatch) {
+        float tl, th;
+        split(T, tl, th);
+        const bool live = (tl > m.T_thr) | (th > m.T_thr);
+        if (__syncthreads_count(live) == 0) break;
+        const int cnt = min(kBatch, n - base);
+        for (int i = t; i < cnt; i += kCtaThreads)
+          load_rec(rec, load_gi(ids, start + base + i, m.BG, status, kSiteRender), s_rec[i]);
+        __syncthreads();
+#pragma unroll 1
+          for (int j = 0; j < cnt; ++j) {
+            const float4 p0 = s_rec[j][0];
+            const float4 p1 = s_rec[j][1];
+            const float4 p2 = s_rec[j][2];
+            const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
+            const F2 power = power_at2(f2(pc.ta), f2(pc.tb), f2(pc.ch), sub2(fy, f2(p0.y)));
+            const int consumed = base + j + 1;
+            float pl, ph, xl, xh;
+            split(T, tl, th);
+            // The warp leaves the batch once its 64 pixels are all finished.
+            if (!__any_sync(kFullMask, (tl > m.T_thr) | (th > m.T_thr))) break;
+            split(power, pl, ph);
+            split(mul2(power, log2e), xl, xh);
+            const float al =
+                vis_select_fwd(tl, m.T_thr, pl, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xl)), consumed, last_l);
+            const float ah =
+                vis_select_fwd(th, m.T_thr, ph, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xh)), consumed, last_h);
+            const F2 alpha = f2(al, ah);
+            const F2 w = mul2(T, alpha);
+            cr = fma2(w, f2(p1.z), cr);
+            cg = fma2(w, f2(p1.w), cg);
+            cb = fma2(w, f2(p2.x), cb);
+            T = mul2(T, sub2(one, alpha));
+          }
+        __syncthreads();  // s_rec is refilled by the next batch
+      }
+      float tv[2], rv[2], gv[2], bv[2];
+      split(T, tv[0], tv[1]);
+      split(cr, rv[0], rv[1]);
+      split(cg, gv[0], gv[1]);
+      split(cb, bv[0], bv[1]);
+      const int lastv[2] = {last_l, last_h};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int py = py0 + 8 * h;
+        if (px < m.W && py < m.H) {
+          const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
+          out[3 * pix + 0] = fmaf(tv[h], m.bg_r, rv[h]);
+          out[3 * pix + 1] = fmaf(tv[h], m.bg_g, gv[h]);
+          out[3 * pix + 2] = fmaf(tv[h], m.bg_b, bv[h]);
+          if (kSave) {
+            final_T[pix] = tv[h];
+            last_idx[pix] = lastv[h];
           }
         }
       }
     }
-    if (valid) {
-      const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
-      out[3 * pix + 0] = fmaf(T, m.bg_r, cr);
-      out[3 * pix + 1] = fmaf(T, m.bg_g, cg);
-      out[3 * pix + 2] = fmaf(T, m.bg_b, cb);
-      if (kSave) {
-        final_T[pix] = T;
-        last_idx[pix] = last;
-      }
-    }
-    __syncthreads();  // s_rec reuse by the next tile
-  }
   }
 }
 
@@ -648,7 +675,37 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
   cp_async_wait<0>();
 }
 
-__global__ void __launch_bounds__(kTilePixels)
+// Sums the staged rows of `count` records of one warp (row = record slot x
+// component, one value per lane) into the CTA's per-record accumulators.
+__device__ __forceinline__ void flush_red_cta(float (*red)[kRedStride], const int* red_j, int count, int lane,
+                                              float (*acc)[kGradComps]) {
+  __syncwarp();
+  if (lane < count * kGradComps) {
+    const float4* row = reinterpret_cast<const float4*>(&red[lane][0]);
+    F2 a0 = f2(0.0f), a1 = f2(0.0f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = row[i];
+      a0 = add2(a0, f2(v.x, v.y));
+      a1 = add2(a1, f2(v.z, v.w));
+    }
+    float x0, x1, x2, x3;
+    split(a0, x0, x1);
+    split(a1, x2, x3);
+    const float total = (x0 + x1) + (x2 + x3);
+    const int slot = lane / kGradComps, comp = lane - slot * kGradComps;
+    if (total != 0.0f) atomicAdd(&acc[red_j[slot]][comp], total);
+  }
+  __syncwarp();
+}
+
+// CTA of kCtaThreads per long tile, 2 pixels per thread as in the forward CTA
+// kernel, with the warp kernel's packed per-pixel VJP (pixel_vjp2). Per record a
+// thread sums its pair's moments, expands them once, and the warp reduces the
+// 9 gradient components of its 64 pixels (one reduce-scatter) into shared
+// accumulators; each batch of records ends with one vector atomic per record.
+template <bool kClampOm>
+__global__ void __launch_bounds__(kCtaThreads)
     k_render_bwd_cta(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                      const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                      const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
@@ -658,97 +715,117 @@ __global__ void __launch_bounds__(kTilePixels)
   __shared__ float4 s_rec[kBatch][3];
   __shared__ int s_gi[kBatch];
   __shared__ float s_acc[kBatch][kGradComps];
-  __shared__ int s_max[kWarps];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __shared__ int s_long[kTilePixels], s_warp[kTilePixels / 32];
+  __shared__ __align__(16) float s_red[kCtaThreads / 32][kRedChunk * kGradComps][kRedStride];
+  __shared__ int s_red_j[kCtaThreads / 32][kRedChunk];
+  __shared__ int s_max[kCtaThreads / 32];
+  __shared__ int s_long[kCtaThreads], s_warp[kCtaThreads / 32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   for (long long chunk = 0; long_chunk_live(m, chunk); ++chunk) {
-  const int n_long = collect_long_tiles(m, toff, kBwdShortMax, chunk, s_long, s_warp);
-  for (int k = 0; k < n_long; ++k) {
-    const int tile = s_long[k];
-    const TileCoord tc = tile_coord(m, tile);
-    const int px = tc.tx * kTile + (threadIdx.x & 15);
-    const int py = tc.ty * kTile + (threadIdx.x >> 4);
-    const bool valid = px < m.W && py < m.H;
-    const int start = toff[tile];
-    const int n = toff[tile + 1] - start;
-    float gr = 0.f, gg = 0.f, gb = 0.f, T_cur = 1.0f;
-    int last = 0;
-    if (valid) {
-      const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
-      gr = grad[3 * pix + 0];
-      gg = grad[3 * pix + 1];
-      gb = grad[3 * pix + 2];
-      T_cur = final_T[pix];
-      last = min(last_idx[pix], n);
-    }
-    float gT = gr * m.bg_r + gg * m.bg_g + gb * m.bg_b;
-    const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-    const int wmax = __reduce_max_sync(kFullMask, last);
-    if (lane == 0) s_max[warp] = wmax;
-    __syncthreads();
-    int tile_last = 0;
+    const int n_long = collect_long_tiles(m, toff, kBwdShortMax, 0x7fffffff, chunk, s_long, s_warp);
+    for (int k = 0; k < n_long; ++k) {
+      const int tile = s_long[k];
+      const TileCoord tc = tile_coord(m, tile);
+      const int px = tc.tx * kTile + (t & 15);
+      const int py0 = tc.ty * kTile + (t >> 4);  // rows py0 and py0 + 8
+      const float fx = (float)px + 0.5f;
+      const F2 fy = f2((float)py0 + 0.5f, (float)py0 + 8.5f);
+      const int start = toff[tile];
+      const int n = toff[tile + 1] - start;
+      float g[2][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}}, Tv[2] = {1.0f, 1.0f};
+      int lastv[2] = {0, 0};
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) tile_last = max(tile_last, s_max[w]);
-
-    for (int bend = tile_last; bend > 0; bend -= kBatch) {
-      const int bstart = max(0, bend - kBatch);
-      const int cnt = bend - bstart;
-      if ((int)threadIdx.x < cnt) {
-        const int gi = load_gi(ids, start + bstart + threadIdx.x, m.BG, status, kSiteRenderBwd);
-        s_gi[threadIdx.x] = gi;
-        load_rec(rec, gi, s_rec[threadIdx.x]);
+      for (int h = 0; h < 2; ++h) {
+        const int py = py0 + 8 * h;
+        if (px < m.W && py < m.H) {
+          const size_t pix = ((size_t)tc.b * m.H + py) * m.W + px;
+          g[h][0] = grad[3 * pix + 0];
+          g[h][1] = grad[3 * pix + 1];
+          g[h][2] = grad[3 * pix + 2];
+          Tv[h] = final_T[pix];
+          lastv[h] = min(last_idx[pix], n);
+        }
       }
-      for (int i = threadIdx.x; i < cnt * kGradComps; i += kTilePixels) (&s_acc[0][0])[i] = 0.0f;
+      const F2 gr = f2(g[0][0], g[1][0]), gg = f2(g[0][1], g[1][1]), gb = f2(g[0][2], g[1][2]);
+      F2 Tc = f2(Tv[0], Tv[1]);
+      F2 gT = fma2(gb, f2(m.bg_b), fma2(gg, f2(m.bg_g), mul2(gr, f2(m.bg_r))));
+      const int wmax = __reduce_max_sync(kFullMask, max(lastv[0], lastv[1]));
+      if (lane == 0) s_max[warp] = wmax;
       __syncthreads();
-      for (int jj = cnt - 1; jj >= 0; --jj) {
-        const int j = bstart + jj;
-        float v[16];
-        bool any = false;
-        if (j < last) {
+      int tile_last = 0;
+#pragma unroll
+      for (int w = 0; w < kCtaThreads / 32; ++w) tile_last = max(tile_last, s_max[w]);
+      for (int bend = tile_last; bend > 0; bend -= kBatch) {
+        const int bstart = max(0, bend - kBatch);
+        const int cnt = bend - bstart;
+        for (int i = t; i < cnt; i += kCtaThreads) {
+          const int gi = load_gi(ids, start + bstart + i, m.BG, status, kSiteRenderBwd);
+          s_gi[i] = gi;
+          load_rec(rec, gi, s_rec[i]);
+        }
+        for (int i = t; i < cnt * kGradComps; i += kCtaThreads) (&s_acc[0][0])[i] = 0.0f;
+        __syncthreads();
+        int slot = 0;
+#pragma unroll 1
+        for (int jj = cnt - 1; jj >= 0; --jj) {
+          const int j = bstart + jj;
           const float4 p0 = s_rec[jj][0];
           const float4 p1 = s_rec[jj][1];
-          const float dx = __fsub_rn(fx, p0.x);
-          const float dy = __fsub_rn(fy, p0.y);
-          const float power = power_at(power_col(p0.z, p0.w, p1.x, dx), dy);
           const float4 p2 = s_rec[jj][2];
-          if (power <= 0.0f && power >= p2.z) {
-            float S[7] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            pixel_vjp(m, dy, power, p1, p2, gr, gg, gb, T_cur, gT, S);
-            vjp_expand(S, dx, p0.z, p0.w, p1.x, v);
-            any = true;
+          const float dx = __fsub_rn(fx, p0.x);
+          const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
+          const F2 dy = sub2(fy, f2(p0.y));
+          const F2 power = power_at2(f2(pc.ta), f2(pc.tb), f2(pc.ch), dy);
+          float pl, ph;
+          split(power, pl, ph);
+          // Skip (warp-uniform) a record no pixel of this warp sees before its stop:
+          // its alpha is 0 there, so it changes no state and adds no gradient.
+          const bool vis = ((j < lastv[0]) & (pl <= 0.0f) & (pl >= p2.z)) | ((j < lastv[1]) & (ph <= 0.0f) & (ph >= p2.z));
+          if (!__any_sync(kFullMask, vis)) continue;
+          F2 S[7];
+#pragma unroll
+          for (int q = 0; q < 7; ++q) S[q] = f2(0.0f);
+          pixel_vjp2<kClampOm>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w, f2(p1.z), f2(p1.w),
+                               f2(p2.x), gr, gg, gb, Tc, gT, S);
+          float Sv[7];
+#pragma unroll
+          for (int q = 0; q < 7; ++q) {
+            float lo, hi;
+            split(S[q], lo, hi);
+            Sv[q] = lo + hi;
+          }
+          float v[16];
+          vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
+          // Stage the lane values of this record; every kRedChunk records the
+          // warp sums the staged rows (one row per lane) into s_acc.
+#pragma unroll
+          for (int q = 0; q < kGradComps; ++q) s_red[warp][slot * kGradComps + q][lane] = v[q];
+          if (lane == 0) s_red_j[warp][slot] = jj;
+          if (++slot == kRedChunk) {
+            flush_red_cta(s_red[warp], s_red_j[warp], slot, lane, s_acc);
+            slot = 0;
           }
         }
-        if (!any) {
+        if (slot > 0) flush_red_cta(s_red[warp], s_red_j[warp], slot, lane, s_acc);
+        __syncthreads();
+        for (int i = t; i < cnt; i += kCtaThreads) {
+          const int gi = s_gi[i];
+          float acc[kGradComps];
+          bool nz = false;
 #pragma unroll
-          for (int q = 0; q < 16; ++q) v[q] = 0.0f;
+          for (int q = 0; q < kGradComps; ++q) {
+            acc[q] = s_acc[i][q];
+            nz |= (acc[q] != 0.0f);
+          }
+          if (nz && gi >= 0) {
+            float4* g4 = reinterpret_cast<float4*>(grad_rec + (size_t)gi * GSB_REC_FLOATS);
+            atomicAdd(g4 + 0, make_float4(acc[0], acc[1], acc[2], acc[3]));
+            atomicAdd(g4 + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
+            atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + 8, acc[8]);
+          }
         }
-        if (__any_sync(kFullMask, any)) {
-          const float total = warp_reduce_scatter16(v, lane);
-          const int comp = lane >> 1;
-          if (!(lane & 1) && comp < kGradComps) atomicAdd(&s_acc[jj][comp], total);
-        }
+        __syncthreads();  // s_rec / s_acc are refilled by the next batch
       }
-      __syncthreads();
-      if ((int)threadIdx.x < cnt) {
-        const int s = threadIdx.x;
-        const int gi = s_gi[s];
-        float acc[kGradComps];
-        bool nz = false;
-#pragma unroll
-        for (int q = 0; q < kGradComps; ++q) {
-          acc[q] = s_acc[s][q];
-          nz |= (acc[q] != 0.0f);
-        }
-        if (nz && gi >= 0) {
-          float4* g4 = reinterpret_cast<float4*>(grad_rec + (size_t)gi * GSB_REC_FLOATS);
-          atomicAdd(g4 + 0, make_float4(acc[0], acc[1], acc[2], acc[3]));
-          atomicAdd(g4 + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
-          atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + 8, acc[8]);
-        }
-      }
-      __syncthreads();
     }
-  }
   }
 }
 
@@ -810,10 +887,10 @@ const GridCache& grids() {
     };
     g.fwd_warp[0] = occ((const void*)k_render_fwd_warp<false>, kWarps * 32, 0);
     g.fwd_warp[1] = occ((const void*)k_render_fwd_warp<true>, kWarps * 32, 0);
-    g.fwd_cta[0] = occ((const void*)k_render_fwd_cta<false>, kTilePixels, 0);
-    g.fwd_cta[1] = occ((const void*)k_render_fwd_cta<true>, kTilePixels, 0);
+    g.fwd_cta[0] = occ((const void*)k_render_fwd_cta<false>, kCtaThreads, 0);
+    g.fwd_cta[1] = occ((const void*)k_render_fwd_cta<true>, kCtaThreads, 0);
     g.bwd_warp = occ((const void*)k_render_bwd_warp<false>, kBwdWarps * 32, kBwdWarpSmem);
-    g.bwd_cta = occ((const void*)k_render_bwd_cta, kTilePixels, 0);
+    g.bwd_cta = occ((const void*)k_render_bwd_cta<false>, kCtaThreads, 0);
     g.sms = sms;
   }
   return g;
@@ -849,13 +926,13 @@ int launch_forward(const Meta& m, const float* rec, const int32_t* tile_offsets,
     e = launch_pdl(k_render_fwd_warp<true>, warp_grid, kWarps * 32, 0, stream, m, r4, tile_offsets, binned_ids,
                    out_rgb, final_T, last_idx, pr4, status);
     if (e == cudaSuccess)
-      e = launch_pdl(k_render_fwd_cta<true>, cta_grid, kTilePixels, 0, stream, m, r4, tile_offsets, binned_ids,
+      e = launch_pdl(k_render_fwd_cta<true>, cta_grid, kCtaThreads, 0, stream, m, r4, tile_offsets, binned_ids,
                      out_rgb, final_T, last_idx, status);
   } else {
     e = launch_pdl(k_render_fwd_warp<false>, warp_grid, kWarps * 32, 0, stream, m, r4, tile_offsets, binned_ids,
                    out_rgb, nullptr, nullptr, nullptr, status);
     if (e == cudaSuccess)
-      e = launch_pdl(k_render_fwd_cta<false>, cta_grid, kTilePixels, 0, stream, m, r4, tile_offsets, binned_ids,
+      e = launch_pdl(k_render_fwd_cta<false>, cta_grid, kCtaThreads, 0, stream, m, r4, tile_offsets, binned_ids,
                      out_rgb, nullptr, nullptr, status);
   }
   note_launches(2);
@@ -903,12 +980,14 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
   const int cta_grid = max(1, min(g.bwd_cta, m.total_tiles));
   // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
-  auto bwd_warp = (1.0f - m.max_alpha >= m.eps) ? k_render_bwd_warp<false> : k_render_bwd_warp<true>;
+  const bool clamp_om = !(1.0f - m.max_alpha >= m.eps);
+  auto bwd_warp = clamp_om ? k_render_bwd_warp<true> : k_render_bwd_warp<false>;
+  auto bwd_cta = clamp_om ? k_render_bwd_cta<true> : k_render_bwd_cta<false>;
   cudaError_t e = launch_pdl(bwd_warp, warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream, m,
                              reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx,
                              grad_rgb, grad_rec, status);
   if (e == cudaSuccess)
-    e = launch_pdl(k_render_bwd_cta, cta_grid, kTilePixels, 0, stream, m, r4, tile_offsets, binned_ids, final_T,
+    e = launch_pdl(bwd_cta, cta_grid, kCtaThreads, 0, stream, m, r4, tile_offsets, binned_ids, final_T,
                    last_idx, grad_rgb, grad_rec, status);
   note_launches(2);
   return cuda_status(e);
