@@ -968,6 +968,8 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   if (rc != GSB_OK) return rc;
   if (!tile_offsets || !final_T || !last_idx || !grad_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
   if (m.BG > 0 && (!rec || !grad_rec || !pair_rec)) return GSB_ERR_INVALID_ARGUMENT;
+  // pair_rec is staged with 16-byte asynchronous copies.
+  if (reinterpret_cast<uintptr_t>(pair_rec) & 15u) return GSB_ERR_INVALID_ARGUMENT;
   (void)workspace;
   (void)workspace_bytes;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);

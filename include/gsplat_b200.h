@@ -156,7 +156,8 @@ int gsb_render_forward(const gsb_raster_meta* meta, const float* rec, const int3
                        size_t workspace_bytes, void* stream);
 
 /* Replaces `tile_fast_backward_saved` (…/gsplat_v8_project3d_kernels.metal:931-1063; root
- * csrc/metal/gsplat_fast_kernels.metal:296-395). Zeroes and accumulates grad_rec [B*G*12]. */
+ * csrc/metal/gsplat_fast_kernels.metal:296-395). Zeroes and accumulates grad_rec [B*G*12].
+ * pair_rec must be 16-byte aligned (its tiles are staged with 16-byte asynchronous copies). */
 int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                         const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
                         const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
