@@ -10,6 +10,8 @@
 // The B200 design replaces the per-tile atomic cursors + per-tile bitonic sort
 // with deterministic scan offsets in depth-rank order followed by a stable
 // radix sort on the tile bits, so every output is bit-reproducible.
+#include <algorithm>
+
 #include "gsb_common.cuh"
 #include "gsb_host.cuh"
 #include "radix_sort.cuh"
@@ -92,6 +94,12 @@ __device__ __forceinline__ int cand_row(int local, int w) {
 }
 
 constexpr int kMaskCands = 64;  // splats with at most this many candidate tiles keep a hit mask
+// Larger splats keep their hit bits in the region after the per-splat slots of
+// tile_masks: kBigMaskWords words per splat on average are reserved, handed out
+// in splat-sized pieces by an atomic cursor (status word GSB_STATUS_MASK_WORDS).
+// A splat that finds the region full keeps no bits and is tested again by k_emit.
+constexpr uint32_t kBigMaskWords = 8;
+constexpr unsigned long long kNoBigMask = ~0ull;
 
 // Per-warp shared state of warp_tiles.
 struct WarpTilesSmem {
@@ -99,6 +107,15 @@ struct WarpTilesSmem {
   int incl[32];                  // inclusive scan of the candidate counts
   int hits[32];                  // running hit count per owner
   unsigned long long mask[32];   // hit mask per owner with <= kMaskCands candidates (kMasks)
+  int big[32];                   // word offset of a larger owner's hit bits, or -1
+};
+
+// Hit bits of splats with more than kMaskCands candidates (k_prepare writes,
+// k_emit reads): words[big + (local >> 5)] bit (local & 31) marks candidate local.
+struct BigBits {
+  uint32_t* words = nullptr;  // nullptr: none
+  uint32_t capacity = 0;      // words in the region
+  uint32_t* cursor = nullptr; // words handed out so far (k_prepare)
 };
 
 // Visits every candidate tile of the warp's 32 splats (lane j owns splat j),
@@ -109,10 +126,36 @@ struct WarpTilesSmem {
 // visit(owner, tx, ty, slot) runs for each hit with slot = its index in the
 // owner's list and local = its candidate index in the owner's row-major box.
 // On return sm.hits[j] is splat j's hit count.
+// kMasks (k_prepare): record hit masks, and hit bits of larger splats in
+// `big` when it has room.
 template <bool kMasks = false, typename Visit>
 __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m, WarpTilesSmem& sm,
-                                           Visit&& visit) {
+                                           Visit&& visit, BigBits big = BigBits()) {
   const int lane = threadIdx.x & 31;
+  if (kMasks) {
+    // One cursor atomic per warp: the lanes' word counts are summed, and each
+    // lane takes its piece of the warp's range (if the range fits, else none).
+    int b = -1;
+    if (big.words) {
+      const uint32_t words = mine.n > kMaskCands ? ((uint32_t)mine.n + 31u) >> 5 : 0u;
+      uint32_t excl = words;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFullMask, excl, o);
+        if (lane >= o) excl += y;
+      }
+      const uint32_t warp_words = __shfl_sync(kFullMask, excl, 31);
+      excl -= words;
+      uint32_t at = 0u;
+      if (lane == 0 && warp_words) at = atomicAdd(big.cursor, warp_words);
+      at = __shfl_sync(kFullMask, at, 0);
+      if (words && at <= big.capacity && warp_words <= big.capacity - at) {
+        for (uint32_t w = 0; w < words; ++w) big.words[at + excl + w] = 0u;
+        b = (int)(at + excl);
+      }
+    }
+    sm.big[lane] = b;  // read by other lanes after the __syncwarp below
+  }
   long long incl = mine.n;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -129,8 +172,10 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
     for (int local = 0; local < mine.n; ++local) {
       const int row = cand_row(local, mine.w);
       const int tx = mine.tx0 + (local - row * mine.w), ty = mine.ty0 + row;
+      const int bb = kMasks ? sm.big[lane] : -1;
       if (tile_hit(mine, tx, ty, m)) {
         if (kMasks && mine.n <= kMaskCands) sm.mask[lane] |= 1ull << local;
+        if (kMasks && bb >= 0) atomicOr(&big.words[bb + (local >> 5)], 1u << (local & 31));
         visit(lane, tx, ty, cnt++, local);
       }
     }
@@ -176,6 +221,16 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
       // The segment's lanes hold consecutive candidates local, local+1, ...
       if (kMasks && sm.t[owner].n <= kMaskCands)
         sm.mask[owner] |= (unsigned long long)((hits & seg) >> seg0) << local;
+      const int bb = kMasks ? sm.big[owner] : -1;
+      if (kMasks && bb >= 0) {
+        // The segment's hits are candidates local .. local + len - 1: at most two words.
+        const uint32_t bits = (hits & seg) >> seg0;
+        const int w0 = local >> 5, off = local & 31;
+        if (bits) {
+          atomicOr(&big.words[bb + w0], bits << off);
+          if (off && (bits >> (32 - off))) atomicOr(&big.words[bb + w0 + 1], bits >> (32 - off));
+        }
+      }
     }
     if (hit) visit(owner, tx, ty, base_slot + before, local);
     __syncwarp();
@@ -206,7 +261,7 @@ __global__ void __launch_bounds__(256)
               const float* __restrict__ opacities, const float* __restrict__ depths,
               K* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
               uint32_t* __restrict__ counts, unsigned long long* __restrict__ masks, uint32_t* __restrict__ status,
-              ZeroList zero) {
+              ZeroList zero, BigBits big) {
   pdl_wait();
   pdl_trigger();
   __shared__ WarpTilesSmem s_warp[8];
@@ -226,12 +281,15 @@ __global__ void __launch_bounds__(256)
   WarpTilesSmem& sm = s_warp[warp];
   // Splats with at most kMaskCands candidates also record which ones hit, so
   // k_emit writes their pairs without testing the tiles again.
-  warp_tiles<true>(t, m, sm, [](int, int, int, int, int) {});
+  warp_tiles<true>(t, m, sm, [](int, int, int, int, int) {}, big);
   __syncwarp();
   const uint32_t n = valid ? (uint32_t)sm.hits[lane] : 0u;
   if (valid) {
     counts[i] = n;
-    masks[i] = sm.mask[lane];
+    // The slot: the hit mask, or for a larger splat the word offset of its
+    // hit bits (kNoBigMask when it has none).
+    masks[i] = t.n <= kMaskCands ? sm.mask[lane]
+                                 : (sm.big[lane] >= 0 ? (unsigned long long)sm.big[lane] : kNoBigMask);
   }
   unsigned long long wsum = n;
 #pragma unroll
@@ -386,13 +444,131 @@ __global__ void __launch_bounds__(kScanThreads, 2)
 // k_prepare) and writes its pairs at its scan slot, in row-major tile order:
 // key = global tile index (32 bits), value = rank index. The stable sort on
 // the tile key then leaves each tile's list in rank (= depth) order.
+// Per-warp shared state of warp_emit_bits.
+struct BitsEmitSmem {
+  int incl[32];  // inclusive scan of the owners' bit-word counts
+  int done[32];  // pairs written per owner so far
+  int bo[32], w[32], tx0[32], ty0[32], start[32], cnt[32];
+  uint32_t tbase[32];
+  // The round's 32 words: bits, inclusive popcount prefix, owner, word index, first slot.
+  uint32_t rbits[32];
+  int rpre[32], rowner[32], rwi[32], rslot[32];
+};
+
+// Writes the pairs of the warp's splats that kept hit bits (bo >= 0). Their bit
+// words are taken 32 at a time (round r covers words 32r .. 32r+31 of the
+// concatenated lists); a word's first pair slot is its owner's pairs so far
+// plus the popcounts of the owner's earlier words in the round (a segmented
+// warp scan). The round's pairs are then written by consecutive lanes: pair q
+// finds its word by a binary search over the popcount prefix and its bit as the
+// (q - word start)-th set bit, so consecutive lanes write consecutive slots and
+// each splat's pairs keep row-major candidate order. Costs one round per 32
+// words instead of one per 32 candidates. Returns the number of pairs of this
+// lane's splat.
+__device__ __forceinline__ int warp_emit_bits(int bo, const SplatTiles& t, int start, int cnt, uint32_t tbase,
+                                              int r0, const uint32_t* __restrict__ words, const Meta& m,
+                                              uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+                                              BitsEmitSmem& sm) {
+  const int lane = threadIdx.x & 31;
+  const int nw = bo >= 0 ? (t.n + 31) >> 5 : 0;
+  int incl = nw;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int total = __shfl_sync(kFullMask, incl, 31);
+  if (total == 0) return 0;
+  sm.incl[lane] = incl;
+  sm.done[lane] = 0;
+  sm.bo[lane] = bo;
+  sm.w[lane] = t.w;
+  sm.tx0[lane] = t.tx0;
+  sm.ty0[lane] = t.ty0;
+  sm.start[lane] = start;
+  sm.cnt[lane] = cnt;
+  sm.tbase[lane] = tbase;
+  __syncwarp();
+  for (int base = 0; base < total; base += 32) {
+    const int k = base + lane;
+    int owner = 32, wi = 0;  // 32: no word (past the end)
+    uint32_t bits = 0u;
+    if (k < total) {
+      int lo = 0, hi = 31;  // first owner whose inclusive end exceeds k
+#pragma unroll
+      for (int step = 0; step < 5; ++step) {
+        const int mid = (lo + hi) >> 1;
+        if (sm.incl[mid] > k) hi = mid;
+        else lo = mid + 1;
+      }
+      owner = lo;
+      wi = k - (owner ? sm.incl[owner - 1] : 0);
+      bits = words[sm.bo[owner] + wi];
+    }
+    const int pc = __popc(bits);
+    int pre = pc;  // inclusive prefix of the popcounts over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, pre, o);
+      if (lane >= o) pre += y;
+    }
+    const int prev = __shfl_up_sync(kFullMask, owner, 1);
+    const int next = __shfl_down_sync(kFullMask, owner, 1);
+    const unsigned heads = __ballot_sync(kFullMask, lane == 0 || owner != prev);
+    const unsigned le = (lane == 31) ? 0xffffffffu : ((2u << lane) - 1u);
+    const int seg0 = 31 - __clz(heads & le);
+    const int before_seg = __shfl_sync(kFullMask, pre, seg0 > 0 ? seg0 - 1 : 0);
+    const int seg_base = seg0 > 0 ? before_seg : 0;  // popcounts of earlier segments in this round
+    const int done = owner < 32 ? sm.done[owner] : 0;
+    sm.rbits[lane] = bits;
+    sm.rpre[lane] = pre;
+    sm.rowner[lane] = owner;
+    sm.rwi[lane] = wi;
+    sm.rslot[lane] = done + (pre - pc - seg_base);
+    __syncwarp();
+    if (owner < 32 && (lane == 31 || next != owner)) sm.done[owner] = done + (pre - seg_base);
+    const int round_pairs = __shfl_sync(kFullMask, pre, 31);
+    for (int q = lane; q < round_pairs; q += 32) {
+      int lo = 0, hi = 31;  // first word whose inclusive prefix exceeds q
+#pragma unroll
+      for (int step = 0; step < 5; ++step) {
+        const int mid = (lo + hi) >> 1;
+        if (sm.rpre[mid] > q) hi = mid;
+        else lo = mid + 1;
+      }
+      const uint32_t wb = sm.rbits[lo];
+      const int j = q - (sm.rpre[lo] - __popc(wb));  // rank of the pair's bit within its word
+      const int o = sm.rowner[lo];
+      const int slot = sm.rslot[lo] + j;
+      if (slot < sm.cnt[o]) {
+        int b0 = 0, b1 = 31;  // lowest bit position p with more than j set bits in wb[0..p]
+#pragma unroll
+        for (int step = 0; step < 5; ++step) {
+          const int mid = (b0 + b1) >> 1;
+          if (__popc(wb & ((2u << mid) - 1u)) > j) b1 = mid;
+          else b0 = mid + 1;
+        }
+        const int local = sm.rwi[lo] * 32 + b0;
+        const int w = sm.w[o];
+        const int row = cand_row(local, w);
+        const int tx = sm.tx0[o] + (local - row * w), ty = sm.ty0[o] + row;
+        keys[(int64_t)sm.start[o] + slot] = sm.tbase[o] + (uint32_t)(ty * m.tiles_x + tx);
+        vals[(int64_t)sm.start[o] + slot] = (uint32_t)(r0 + o);
+      }
+    }
+    __syncwarp();
+  }
+  return sm.done[lane];
+}
+
 __global__ void __launch_bounds__(256)
     k_emit(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ pair_offsets,
            const unsigned long long* __restrict__ masks, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
-           uint32_t* __restrict__ status, ZeroList zero) {
+           uint32_t* __restrict__ status, ZeroList zero, BigBits big) {
   pdl_wait();
   pdl_trigger();
   __shared__ WarpTilesSmem s_warp[8];
+  __shared__ BitsEmitSmem s_bits[8];
   __shared__ int s_start[8][32], s_cnt[8][32];
   __shared__ uint32_t s_tbase[8][32];
   zero_words(zero);  // the tile sort's scratch
@@ -411,8 +587,14 @@ __global__ void __launch_bounds__(256)
     if (cnt > 0) t = splat_tiles(p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, m);
   }
   // A splat with a recorded hit mask writes its pairs straight from it (the
-  // set bits in row-major candidate order); the others are tested again.
+  // set bits in row-major candidate order); a larger one with hit bits reads
+  // them in warp_tiles; the others are tested again.
   int own_hits = -1;
+  int bigoff = -1;
+  if (masks && big.words && t.n > kMaskCands) {
+    const unsigned long long v = masks[r];
+    if (v != kNoBigMask) bigoff = (int)v;
+  }
   if (masks && t.n > 0 && t.n <= kMaskCands) {
     unsigned long long bits = masks[r];
     own_hits = __popcll(bits);
@@ -431,15 +613,25 @@ __global__ void __launch_bounds__(256)
   s_start[warp][lane] = start;
   s_cnt[warp][lane] = cnt;
   s_tbase[warp][lane] = tbase;
-  WarpTilesSmem& sm = s_warp[warp];
   const int r0 = r - lane;
-  warp_tiles(t, m, sm, [&](int owner, int tx, int ty, int slot, int) {
-    if (slot < s_cnt[warp][owner]) {
-      const int64_t idx = (int64_t)s_start[warp][owner] + slot;
-      keys[idx] = s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx);
-      vals[idx] = (uint32_t)(r0 + owner);
+  // Larger splats with hit bits: their pairs straight from the bits.
+  if (big.words) {
+    const int bit_hits = warp_emit_bits(bigoff, t, start, cnt, tbase, r0, big.words, m, keys, vals, s_bits[warp]);
+    if (bigoff >= 0) {
+      own_hits = bit_hits;
+      t.n = 0;
     }
-  });
+  }
+  WarpTilesSmem& sm = s_warp[warp];
+  warp_tiles(
+      t, m, sm,
+      [&](int owner, int tx, int ty, int slot, int) {
+        if (slot < s_cnt[warp][owner]) {
+          const int64_t idx = (int64_t)s_start[warp][owner] + slot;
+          keys[idx] = s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx);
+          vals[idx] = (uint32_t)(r0 + owner);
+        }
+      });
   const int hits = own_hits >= 0 ? own_hits : sm.hits[lane];
   if (valid && hits != cnt) raise_error(status, GSB_DEVERR_PAIR_OVERFLOW, kSiteEmit);
 }
@@ -539,9 +731,31 @@ extern "C" size_t gsb_bin_prepare_workspace_size(const gsb_raster_meta* meta) {
   return c.off + 256;
 }
 
+namespace {
+// Words of the hit-bit region that follows the B*G slots of tile_masks.
+uint32_t big_mask_capacity(const Meta& m) {
+  return (uint32_t)std::min<uint64_t>((uint64_t)m.BG * kBigMaskWords, 0x7fffffffull);
+}
+BigBits big_bits_of(const Meta& m, uint64_t* tile_masks, uint32_t* status) {
+  BigBits b;
+  if (tile_masks && m.BG > 0) {
+    b.words = reinterpret_cast<uint32_t*>(tile_masks + m.BG);
+    b.capacity = big_mask_capacity(m);
+    b.cursor = status + GSB_STATUS_MASK_WORDS;
+  }
+  return b;
+}
+}  // namespace
+
+extern "C" size_t gsb_bin_tile_masks_size(const gsb_raster_meta* meta) {
+  Meta m;
+  if (make_meta(meta, &m) != GSB_OK) return 0;
+  return (size_t)m.BG * sizeof(uint64_t) + (size_t)big_mask_capacity(m) * sizeof(uint32_t);
+}
+
 extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, const float* conics,
-                             const float* opacities, const float* depths, uint32_t* status, void* workspace,
-                             size_t workspace_bytes, void* stream_) {
+                             const float* opacities, const float* depths, uint64_t* tile_masks, uint32_t* status,
+                             void* workspace, size_t workspace_bytes, void* stream_) {
   Meta m;
   int rc = make_meta(meta, &m);
   if (rc != GSB_OK) return rc;
@@ -567,13 +781,13 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   zero.ptr[2] = sz.ptr;
   zero.words[2] = sz.words;
   if (depth_keys32(m))
-    launch_pdl(k_prepare<uint32_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d), conics,
-                                                               opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in),
-                                                               w.vals_in, w.counts, w.masks, status, zero);
+    launch_pdl(k_prepare<uint32_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d),
+               conics, opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in), w.vals_in, w.counts, w.masks,
+               status, zero, big_bits_of(m, tile_masks, status));
   else
-    launch_pdl(k_prepare<uint64_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d), conics,
-                                                               opacities, depths, w.keys_in, w.vals_in, w.counts,
-                                                               w.masks, status, zero);
+    launch_pdl(k_prepare<uint64_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d),
+               conics, opacities, depths, w.keys_in, w.vals_in, w.counts, w.masks, status, zero,
+               big_bits_of(m, tile_masks, status));
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
@@ -628,7 +842,8 @@ extern "C" int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d
                                const float* colors, const float* opacities, const float* depths, int32_t* perm,
                                float* rec, int32_t* pair_offsets, uint32_t* status, void* workspace,
                                size_t workspace_bytes, void* stream) {
-  int rc = gsb_bin_count(meta, means2d, conics, opacities, depths, status, workspace, workspace_bytes, stream);
+  int rc = gsb_bin_count(meta, means2d, conics, opacities, depths, /*tile_masks=*/nullptr, status, workspace,
+                         workspace_bytes, stream);
   if (rc != GSB_OK) return rc;
   return gsb_bin_sort_scan(meta, means2d, conics, colors, opacities, depths, perm, rec, pair_offsets,
                            /*tile_masks=*/nullptr, status, workspace, workspace_bytes, stream);
@@ -688,8 +903,8 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   zero.ptr[1] = zero.ptr[2] = nullptr;
   zero.words[1] = zero.words[2] = 0;
   launch_pdl(k_emit, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float4*>(rec), pair_offsets,
-                                                reinterpret_cast<const unsigned long long*>(tile_masks), w.keys,
-                                                w.vals, status, zero);
+             reinterpret_cast<const unsigned long long*>(tile_masks), w.keys, w.vals, status, zero,
+             big_bits_of(m, const_cast<uint64_t*>(tile_masks), status));
   note_launches(1);
   cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
                                    total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true);

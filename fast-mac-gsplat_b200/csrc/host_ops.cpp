@@ -266,14 +266,15 @@ Binned bin_impl(const gsb_raster_meta& meta, const Tensor& means2d, const Tensor
   r.perm = empty({B, G}, at::kInt, dev);
   r.rec = empty({BG, GSB_REC_FLOATS}, at::kFloat, dev);
   Tensor pair_offsets = empty({BG + 1}, at::kInt, dev);
-  Tensor tile_masks = empty({BG}, at::kLong, dev);
+  // Hit masks / hit bits of each splat's candidate tiles (gsb_bin_tile_masks_size bytes).
+  Tensor tile_masks = empty({static_cast<int64_t>((gsb_bin_tile_masks_size(&meta) + 7) / 8)}, at::kLong, dev);
   Tensor ws = empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 1))}, at::kByte, dev);
   auto cur = at::cuda::getCurrentCUDAStream(dev.index());
   PairRead& pr = pair_read();
   {
     Phase ph("bin_prepare", means2d);
     check(gsb_bin_count(&meta, ptr<float>(m2), ptr<float>(q2), ptr<float>(o2), ptr<float>(d2),
-                        ptr<uint32_t>(r.status), ws.data_ptr(), ws_bytes, stream),
+                        ptr<uint64_t>(tile_masks), ptr<uint32_t>(r.status), ws.data_ptr(), ws_bytes, stream),
           "gsb_bin_count");
     // The pair total is read on the side stream as soon as the count kernel is
     // done, while the depth sort and scan run on the compute stream.

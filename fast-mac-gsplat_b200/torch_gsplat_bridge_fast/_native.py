@@ -21,6 +21,7 @@ GSB_STATUS_ERROR = 1
 GSB_STATUS_MAX_TILE_COUNT = 2
 GSB_STATUS_ERROR_SITE = 3
 GSB_STATUS_PAIR_TOTAL64 = 4
+GSB_STATUS_MASK_WORDS = 6
 GSB_STATUS_WORDS = 8
 GSB_REC_FLOATS = 12
 GSB_PEER_MAX_RANKS = 8
@@ -40,6 +41,7 @@ EXPORTED = (
     "gsb_bin_prepare_workspace_size",
     "gsb_bin_prepare",
     "gsb_bin_count",
+    "gsb_bin_tile_masks_size",
     "gsb_bin_sort_scan",
     "gsb_bin_emit_workspace_size",
     "gsb_bin_emit",
@@ -106,7 +108,8 @@ def load() -> C.CDLL:
         "gsb_kernel_launches": (C.c_uint64, []),
         "gsb_bin_prepare_workspace_size": (sz, [M]),
         "gsb_bin_prepare": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
-        "gsb_bin_count": (C.c_int, [M, p, p, p, p, p, p, sz, p]),
+        "gsb_bin_count": (C.c_int, [M, p, p, p, p, p, p, p, sz, p]),
+        "gsb_bin_tile_masks_size": (sz, [M]),
         "gsb_bin_sort_scan": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_bin_emit_workspace_size": (sz, [M, i64]),
         "gsb_bin_emit": (C.c_int, [M, p, p, p, i64, p, p, p, p, p, sz, p]),

@@ -404,15 +404,15 @@ def _bin(config: RasterConfig, means2d_b: Tensor, conics_b: Tensor, colors_b: Te
     st.perm = torch.empty((B, G), dtype=torch.int32, device=dev)
     st.rec = torch.empty((BG, N.GSB_REC_FLOATS), dtype=torch.float32, device=dev)
     st.pair_offsets = torch.empty(BG + 1, dtype=torch.int32, device=dev)
-    tile_masks = torch.empty(BG, dtype=torch.int64, device=dev)
+    tile_masks = torch.empty((int(L.gsb_bin_tile_masks_size(meta)) + 7) // 8, dtype=torch.int64, device=dev)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     cur = torch.cuda.current_stream(dev)
     stream = cur.cuda_stream
     # Locals keep every (possibly copied) input alive until the launch returns.
     m2 = _aligned(means2d_b, 8)
     q2, c2, o2, d2 = (t.contiguous() for t in (conics_b, colors_b, opacities_b, depths_b))
-    N.check(L.gsb_bin_count(meta, N.ptr(m2), N.ptr(q2), N.ptr(o2), N.ptr(d2), N.ptr(st.status), N.ptr(ws),
-                            ws_bytes, stream), "gsb_bin_count")
+    N.check(L.gsb_bin_count(meta, N.ptr(m2), N.ptr(q2), N.ptr(o2), N.ptr(d2), N.ptr(tile_masks), N.ptr(st.status),
+                            N.ptr(ws), ws_bytes, stream), "gsb_bin_count")
     # The pair total is read as soon as the count kernel is done, while the depth
     # sort and scan run: the host wait overlaps GPU work.
     total_host = _pinned("total_host", 1, torch.int64)

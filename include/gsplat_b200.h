@@ -47,6 +47,7 @@ extern "C" {
 #define GSB_STATUS_MAX_TILE_COUNT 2 /* written by gsb_tile_stats */
 #define GSB_STATUS_ERROR_SITE 3     /* first kernel site that raised an error */
 #define GSB_STATUS_PAIR_TOTAL64 4   /* words 4-5: 64-bit pair total, written by gsb_bin_count */
+#define GSB_STATUS_MASK_WORDS 6     /* hit-bit words of tile_masks handed out (gsb_bin_count) */
 #define GSB_STATUS_WORDS 8
 
 #define GSB_DEVERR_LOOKBACK_TIMEOUT 1u /* decoupled look-back spin limit hit */
@@ -110,11 +111,18 @@ int gsb_bin_prepare(const gsb_raster_meta* meta, const float* means2d, const flo
  * copy of that word enqueued right after it completes while gsb_bin_sort_scan
  * (depth sort, gather, scan) still runs. */
 int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, const float* conics,
-                  const float* opacities, const float* depths, uint32_t* status, void* workspace,
-                  size_t workspace_bytes, void* stream);
-/* tile_masks (optional, [B*G] in rank order): for a splat whose snugbox holds at most 64
- * candidate tiles, bit k marks candidate k (row-major in its box) as hit; gsb_bin_emit
- * then writes its pairs from the mask instead of testing the tiles again. */
+                  const float* opacities, const float* depths, uint64_t* tile_masks, uint32_t* status,
+                  void* workspace, size_t workspace_bytes, void* stream);
+/* tile_masks (optional; NULL in all three calls, or the same buffer of
+ * gsb_bin_tile_masks_size bytes in gsb_bin_count, gsb_bin_sort_scan and
+ * gsb_bin_emit) records which candidate tiles of each splat were hit, so
+ * gsb_bin_emit writes the pairs without testing the tiles again. It starts with
+ * B*G 64-bit slots in rank order: for a splat whose snugbox holds at most 64
+ * candidate tiles, bit k marks candidate k (row-major in its box) as hit; for a
+ * larger splat, the slot is the word offset of its hit bits in the uint32 region
+ * after the slots (bit k of word offset + k/32), or all ones when the region
+ * (8 words per splat) was full and the splat is tested again. */
+size_t gsb_bin_tile_masks_size(const gsb_raster_meta* meta);
 int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const float* conics,
                       const float* colors, const float* opacities, const float* depths, int32_t* perm,
                       float* rec, int32_t* pair_offsets, uint64_t* tile_masks, uint32_t* status,

@@ -168,3 +168,28 @@ def test_emit_without_masks_matches(name):
     assert torch.equal(keys, st.keys) and torch.equal(ids, st.binned_ids) and torch.equal(toff, st.tile_offsets)
     c = cpu_bin(s)
     assert np.array_equal(keys.cpu().numpy().view(np.uint64), c["keys"])
+
+
+@pytest.mark.parametrize("sigma,G,H,W", [
+    ((20.0, 120.0), 600, 512, 640),   # hundreds to thousands of candidate tiles per splat: hit bits
+    ((150.0, 300.0), 300, 1024, 1024),  # every splat covers the frame: the bit region (8 words a splat) fills up
+])
+def test_large_splat_hit_bits_match_oracle(sigma, G, H, W):
+    """Splats with more than 64 candidate tiles keep their hit bits in the
+    region after tile_masks' slots, and k_emit reads them instead of testing the
+    tiles again; when the region is full the remaining splats are tested again.
+    Both ways, the keys, lists and ranges equal the oracle's bit for bit, and
+    the region's cursor (status word GSB_STATUS_MASK_WORDS) shows bits were
+    handed out."""
+    s = make_2d(2, G, H, W, seed=21, sigma=sigma)
+    g = gpu_bin(s)
+    c = cpu_bin(s)
+    assert_bin_equal(g, c)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV).contiguous() for t in s.tensors()))
+    torch.cuda.synchronize()
+    used = int(st.status[N.GSB_STATUS_MASK_WORDS])
+    capacity = 8 * s.B * s.G
+    assert used > 0
+    if sigma[0] >= 150.0:
+        assert used > capacity  # asked for more than the region holds: some splats re-tested
