@@ -1,8 +1,9 @@
 """Generates the golden fixtures in tests/golden/ by running the reference's OWN
-torch code (nbardy/fast-mac-gsplat) on CPU. Run where the reference checkout is
-mounted (GSPLAT_REF_ROOT, default /root/reference); the GPU box never runs this.
+torch code (nbardy/fast-mac-gsplat) on CPU. Run where a checkout of the
+reference is available, with its path in GSPLAT_REF_ROOT; the GPU box never
+runs this.
 
-    python tests/golden/make_golden.py
+    GSPLAT_REF_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 Reference functions executed:
   variants/v8_project3d/tests/reference_check.py: dense_reference (15-50),
@@ -24,7 +25,9 @@ import numpy as np
 import torch
 
 sys.dont_write_bytecode = True
-REF = Path(os.environ.get("GSPLAT_REF_ROOT", "/root/reference"))
+if "GSPLAT_REF_ROOT" not in os.environ and __name__ == "__main__":
+    sys.exit("set GSPLAT_REF_ROOT to the path of a reference checkout")
+REF = Path(os.environ.get("GSPLAT_REF_ROOT", "."))
 OUT = Path(__file__).resolve().parent
 
 
