@@ -58,6 +58,8 @@ def test_binning_bit_exact_configs(name):
     (3, 513, 70, 90, (0.5, 12.0)),
     (2, 4097, 129, 257, (1.0, 40.0)),
     (5, 3000, 31, 47, (0.5, 8.0)),
+    (2, 20001, 200, 300, (0.5, 4.0)),
+    (1, 65537, 256, 256, (0.5, 2.0)),
 ])
 def test_binning_bit_exact_ragged(B, G, H, W, sigma):
     s = make_2d(B, G, H, W, seed=B * 1000 + G, sigma=sigma)
@@ -90,6 +92,15 @@ def test_binning_edge_values():
     m[0, 190:200] = torch.tensor([5e9, -5e9])
     m[1, 300:305] = float("nan")
     m[1, 305:310] = float("inf")
+    assert_bin_equal(gpu_bin(s), cpu_bin(s))
+
+
+@pytest.mark.parametrize("B,G", [(1, 65536), (2, 30001), (3, 8192), (2, 8193)])
+def test_depth_order_with_ties(B, G):
+    """Depths drawn from 37 values: the depth order must keep input order within
+    each tie, across sort partitions and across views."""
+    s = make_2d(B, G, 96, 128, seed=G + B, sigma=(0.5, 3.0))
+    s.depths.copy_(torch.floor(s.depths / 100.0 * 37.0) + 0.5)
     assert_bin_equal(gpu_bin(s), cpu_bin(s))
 
 
