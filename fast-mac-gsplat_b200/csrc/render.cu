@@ -22,14 +22,14 @@
 // most kShortMax pairs are processed by ONE WARP each (8 pixels per lane, the
 // column terms of the exponent shared by the lane's 8 rows, backward gradients
 // summed over the lane's pixels before a single warp reduction). Longer lists
-// are appended to a device list and processed by a CTA per tile (one pixel per
-// thread), so a hot tile is spread over 8 warps. All kernels are persistent.
+// go to a CTA per tile (128 threads, two packed pixels each), which finds its
+// tiles itself by scanning tile_offsets. All kernels are persistent.
 //
 // The training forward also copies each short tile's records, in list order,
 // into pair_rec [P,12] (a by-product of its gather). The backward warp kernel
-// then prefetches a tile's records, ids and per-pixel state with cp.async one
-// tile ahead (double-buffered shared memory), so its per-tile load latency
-// overlaps the previous tile's arithmetic.
+// then prefetches a tile's per-pixel state, and for tiles of at most kBwdHalf
+// records also its records and ids, with cp.async one tile ahead, so its
+// per-tile load latency overlaps the previous tile's arithmetic.
 #include <mutex>
 
 #include "gsb_common.cuh"
@@ -38,8 +38,14 @@
 namespace gsb {
 namespace {
 
-constexpr int kShortMax = 64;   // pairs per tile handled by one warp (forward)
-constexpr int kBwdShortMax = 48;  // same in the backward: smaller record buffers let 4 CTAs share an SM
+constexpr int kShortMax = 96;   // pairs per tile handled by one warp (forward)
+// The backward warp kernel takes the same tiles (it reads the records the
+// forward warp kernel copied to pair_rec). Its record buffer holds
+// kBwdShortMax records as two halves: tiles of at most kBwdHalf records are
+// prefetched one tile ahead into alternate halves; a longer one uses both.
+constexpr int kBwdShortMax = 96;
+constexpr int kBwdHalf = kBwdShortMax / 2;
+static_assert(kBwdShortMax <= kShortMax, "the backward warp kernel reads pair_rec of forward warp-kernel tiles");
 constexpr int kWarpBatch = 32;  // records staged per warp round (forward)
 constexpr int kLanePx = 8;      // pixels per lane in the warp kernels: rows py0 + 2i
 constexpr int kWarps = 8;       // warps per CTA (forward warp kernel, CTA kernels)
@@ -103,6 +109,23 @@ __device__ __forceinline__ float warp_reduce_scatter16(float (&v)[16], int lane)
     }
   }
   return v[0] + __shfl_xor_sync(kFullMask, v[0], 1);
+}
+
+// Dynamic tile assignment of the backward warp kernel: a warp takes its next
+// tile from a counter in the status block (lane 0's atomic, broadcast), so a
+// warp that met longer lists takes fewer tiles and the kernel's tail shrinks.
+// It pays when a warp sees many tiles (c3: 28); with a few per warp (1080p
+// frames: 3.5) the claims made three tiles ahead fix most of the assignment
+// anyway, and the static grid stride measured faster, so the host chooses
+// (kMinTilesPerWarpForClaims). The counter is 0 when the warp kernel starts:
+// gsb_bin_count clears the status block, and the long-tile CTA kernel that
+// follows every backward warp kernel resets it once the warp kernel has
+// completed (it starts with griddepcontrol.wait).
+constexpr int kMinTilesPerWarpForClaims = 8;
+__device__ __forceinline__ int claim_tiles(uint32_t* counter, int count, int lane) {
+  int t = 0;
+  if (lane == 0) t = (int)atomicAdd(counter, (unsigned)count);
+  return __shfl_sync(kFullMask, t, 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -466,14 +489,14 @@ struct BwdState {
   int last[kTilePixels];
 };
 struct BwdRecs {
-  float4 rec[kBwdShortMax][3];
+  float4 rec[kBwdShortMax][3];  // rows [0, kBwdHalf) and [kBwdHalf, kBwdShortMax): the two halves
   int ids[kBwdShortMax];
 };
 constexpr int kRedChunk = 3;    // records whose gradients are reduced together
 constexpr int kRedStride = 36;  // padded row (32 lanes + 4): conflict-free 16-byte row reads
 struct BwdWarpSmem {
   BwdState st;
-  BwdRecs rec[2];
+  BwdRecs rb;
   float red[kRedChunk * kGradComps][kRedStride];
   int red_gi[kRedChunk];
 };
@@ -492,13 +515,11 @@ __device__ __forceinline__ TileOff load_off(const int32_t* __restrict__ toff, in
 }
 
 // Issues (does not wait for) the cp.async copies of one short tile's per-pixel
-// state, records and ids.
-__device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileOff off, BwdState* st,
-                                                  BwdRecs* rb, int lane, const float* __restrict__ grad,
-                                                  const float* __restrict__ final_T,
-                                                  const int32_t* __restrict__ last_idx,
-                                                  const float4* __restrict__ pair_rec,
-                                                  const int32_t* __restrict__ ids) {
+// state.
+__device__ __forceinline__ void prefetch_bwd_state(const Meta& m, int tile, TileOff off, BwdState* st, int lane,
+                                                   const float* __restrict__ grad,
+                                                   const float* __restrict__ final_T,
+                                                   const int32_t* __restrict__ last_idx) {
   if (tile >= m.total_tiles || off.n == 0 || off.n > kBwdShortMax) return;
   const TileCoord tc = tile_coord(m, tile);
   const int x0 = tc.tx * kTile, y0 = tc.ty * kTile;
@@ -535,8 +556,17 @@ __device__ __forceinline__ void prefetch_bwd_tile(const Meta& m, int tile, TileO
       }
     }
   }
-  for (int q = lane; q < 3 * off.n; q += 32) cp_async16(&rb->rec[0][0] + q, pair_rec + 3 * (size_t)off.start + q);
-  for (int q = lane; q < off.n; q += 32) cp_async4(&rb->ids[q], ids + off.start + q);
+}
+
+// Issues the cp.async copies of one short tile's records and ids into rows
+// [row0, row0 + n) of the record buffer.
+__device__ __forceinline__ void prefetch_bwd_recs(TileOff off, BwdRecs* rb, int row0, int lane,
+                                                  const float4* __restrict__ pair_rec,
+                                                  const int32_t* __restrict__ ids) {
+  if (off.n == 0 || off.n > kBwdShortMax) return;
+  for (int q = lane; q < 3 * off.n; q += 32)
+    cp_async16(&rb->rec[row0][0] + q, pair_rec + 3 * (size_t)off.start + q);
+  for (int q = lane; q < off.n; q += 32) cp_async4(&rb->ids[row0 + q], ids + off.start + q);
 }
 
 // Sums the staged gradient rows of `count` records (row = record slot x
@@ -569,23 +599,49 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                       const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
-                      float* __restrict__ grad_rec, uint32_t* __restrict__ status) {
+                      float* __restrict__ grad_rec, uint32_t* __restrict__ status, int claims) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 s_dyn[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   BwdWarpSmem& W = reinterpret_cast<BwdWarpSmem*>(s_dyn)[warp];
+  // Tiles are claimed one at a time, three ahead of use: the current tile, the
+  // next one (state and records prefetched), the one after (offsets loaded),
+  // and a claim in flight for the tile after that.
+  // Without claims (claims == 0) the k-th tile of a warp is the grid stride's.
+  uint32_t* const claim = status + GSB_STATUS_TILE_CLAIM;
   const int stride = gridDim.x * kBwdWarps;
-  int tile = blockIdx.x * kBwdWarps + warp;
+  int next_static = blockIdx.x * kBwdWarps + warp;
+  auto take = [&]() {
+    if (claims) return claim_tiles(claim, 1, lane);
+    const int t = next_static;
+    next_static += stride;
+    return t;
+  };
+  int tile = take();
+  int nxt_tile = take();
+  int nn_tile = take();
   TileOff cur = load_off(toff, tile, m.total_tiles);
-  TileOff nxt = load_off(toff, tile + stride, m.total_tiles);
-  prefetch_bwd_tile(m, tile, cur, &W.st, &W.rec[0], lane, grad, final_T, last_idx, pair_rec, ids);
+  TileOff nxt = load_off(toff, nxt_tile, m.total_tiles);
+  if (tile < m.total_tiles) prefetch_bwd_state(m, tile, cur, &W.st, lane, grad, final_T, last_idx);
+  prefetch_bwd_recs(cur, &W.rb, 0, lane, pair_rec, ids);
   cp_async_commit();
-  for (int k = 0; tile < m.total_tiles; ++k, tile += stride) {
-    const TileOff nn = load_off(toff, tile + 2 * stride, m.total_tiles);
+  int row0 = 0;          // first record row of the current tile
+  bool pending = false;  // the current tile's records are not copied yet
+  while (tile < m.total_tiles) {
+    int pend = next_static;  // the tile after nn: a claim in flight until the end of this tile
+    if (claims) pend = lane == 0 ? (int)atomicAdd(claim, 1u) : 0;
+    else next_static += stride;
+    const TileOff nn = load_off(toff, nn_tile, m.total_tiles);
     cp_async_wait<0>();
     __syncwarp();
-    const BwdRecs& R = W.rec[k & 1];
+    if (pending) {  // after or before a tile of more than kBwdHalf records: copy now, into rows from 0
+      prefetch_bwd_recs(cur, &W.rb, 0, lane, pair_rec, ids);
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncwarp();
+    }
+    const BwdRecs& R = W.rb;
     const int n = cur.n;
     const bool work = n > 0 && n <= kBwdShortMax;
     const TileCoord tc = tile_coord(m, tile);
@@ -614,17 +670,21 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
       }
     }
     __syncwarp();  // W.st is read: the next tile's prefetch may overwrite it
-    prefetch_bwd_tile(m, tile + stride, nxt, &W.st, &W.rec[(k + 1) & 1], lane, grad, final_T, last_idx, pair_rec,
-                      ids);
+    // The next tile's records go into the other half now when both tiles fit
+    // a half; otherwise they are copied when that tile starts.
+    const bool recs_now = cur.n <= kBwdHalf && nxt.n <= kBwdHalf;
+    const int next_row0 = recs_now ? kBwdHalf - row0 : 0;
+    if (nxt_tile < m.total_tiles) prefetch_bwd_state(m, nxt_tile, nxt, &W.st, lane, grad, final_T, last_idx);
+    if (recs_now) prefetch_bwd_recs(nxt, &W.rb, next_row0, lane, pair_rec, ids);
     cp_async_commit();
     if (work) {  // tiles above kBwdShortMax: k_render_bwd_cta finds them
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
       int slot = 0;
 #pragma unroll 1
       for (int j = tile_last - 1; j >= 0; --j) {
-        const float4 p0 = R.rec[j][0];
-        const float4 p1 = R.rec[j][1];
-        const float4 p2 = R.rec[j][2];
+        const float4 p0 = R.rec[row0 + j][0];
+        const float4 p1 = R.rec[row0 + j][1];
+        const float4 p2 = R.rec[row0 + j][2];
         const float dx = __fsub_rn(fx, p0.x);
         const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
         const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
@@ -655,7 +715,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
 #pragma unroll
         for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
         if (lane == 0) {
-          int gi = R.ids[j];
+          int gi = R.ids[row0 + j];
           if ((unsigned)gi >= (unsigned)m.BG) {
             raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
             gi = -1;
@@ -669,8 +729,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
       }
       if (slot > 0) flush_red(W, slot, lane, grad_rec);
     }
+    tile = nxt_tile;
+    nxt_tile = nn_tile;
+    nn_tile = claims ? __shfl_sync(kFullMask, pend, 0) : pend;
     cur = nxt;
     nxt = nn;
+    row0 = next_row0;
+    pending = !recs_now;
   }
   cp_async_wait<0>();
 }
@@ -720,6 +785,7 @@ __global__ void __launch_bounds__(kCtaThreads)
   __shared__ int s_max[kCtaThreads / 32];
   __shared__ int s_long[kCtaThreads], s_warp[kCtaThreads / 32];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  if (blockIdx.x == 0 && t == 0) status[GSB_STATUS_TILE_CLAIM] = 0u;  // the warp kernel has completed
   for (long long chunk = 0; long_chunk_live(m, chunk); ++chunk) {
     const int n_long = collect_long_tiles(m, toff, kBwdShortMax, 0x7fffffff, chunk, s_long, s_warp);
     for (int k = 0; k < n_long; ++k) {
@@ -981,13 +1047,14 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   const float4* r4 = reinterpret_cast<const float4*>(rec);
   const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
   const int cta_grid = max(1, min(g.bwd_cta, m.total_tiles));
+  const int claims = m.total_tiles >= kMinTilesPerWarpForClaims * warp_grid * kBwdWarps ? 1 : 0;
   // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
   const bool clamp_om = !(1.0f - m.max_alpha >= m.eps);
   auto bwd_warp = clamp_om ? k_render_bwd_warp<true> : k_render_bwd_warp<false>;
   auto bwd_cta = clamp_om ? k_render_bwd_cta<true> : k_render_bwd_cta<false>;
   cudaError_t e = launch_pdl(bwd_warp, warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream, m,
                              reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx,
-                             grad_rgb, grad_rec, status);
+                             grad_rgb, grad_rec, status, claims);
   if (e == cudaSuccess)
     e = launch_pdl(bwd_cta, cta_grid, kCtaThreads, 0, stream, m, r4, tile_offsets, binned_ids, final_T,
                    last_idx, grad_rgb, grad_rec, status);

@@ -22,7 +22,8 @@ GSB_STATUS_MAX_TILE_COUNT = 2
 GSB_STATUS_ERROR_SITE = 3
 GSB_STATUS_PAIR_TOTAL64 = 4
 GSB_STATUS_MASK_WORDS = 6
-GSB_STATUS_WORDS = 8
+GSB_STATUS_TILE_CLAIM = 8
+GSB_STATUS_WORDS = 16
 GSB_REC_FLOATS = 12
 GSB_PEER_MAX_RANKS = 8
 GSB_PEER_FLAG_BYTES = 256

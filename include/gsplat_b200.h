@@ -48,7 +48,8 @@ extern "C" {
 #define GSB_STATUS_ERROR_SITE 3     /* first kernel site that raised an error */
 #define GSB_STATUS_PAIR_TOTAL64 4   /* words 4-5: 64-bit pair total, written by gsb_bin_count */
 #define GSB_STATUS_MASK_WORDS 6     /* hit-bit words of tile_masks handed out (gsb_bin_count) */
-#define GSB_STATUS_WORDS 8
+#define GSB_STATUS_TILE_CLAIM 8     /* tile claim counter of the backward warp kernel (0 between calls) */
+#define GSB_STATUS_WORDS 16
 
 #define GSB_DEVERR_LOOKBACK_TIMEOUT 1u /* decoupled look-back spin limit hit */
 #define GSB_DEVERR_PAIR_OVERFLOW 2u    /* emit wrote past its scan slot / P >= 2^31 */
