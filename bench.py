@@ -228,6 +228,11 @@ def run_b200(args):
         launches0 = L.gsb_kernel_launches()
         t_bracket = time.perf_counter()
         set_kernel_timer(True)
+        # Steps are enqueued back to back: the host prepares step k+1 while the
+        # GPU runs step k (as in a training loop), and each step's events are
+        # read after the bracket's final synchronize. Host latency before a
+        # step's first launch is then not counted as device time.
+        evs = []
         for _ in range(args.steps):
             flush.zero_()  # L2 flush between timed steps (outside the step events)
             e0 = torch.cuda.Event(enable_timing=True)
@@ -235,11 +240,11 @@ def run_b200(args):
             e0.record()
             step()
             e1.record()
-            e1.synchronize()
-            step_ms.append(e0.elapsed_time(e1))
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        step_ms = [a.elapsed_time(b) for a, b in evs]
         kt = kernel_times()
         set_kernel_timer(False)
-        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         bracket_ms = (time.perf_counter() - t_bracket) * 1e3
@@ -527,6 +532,7 @@ def run_shared3d(args):
             dist.barrier()
         torch.cuda.synchronize()
         launches0 = L.gsb_kernel_launches()
+        evs = []
         for _ in range(args.steps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -534,11 +540,12 @@ def run_shared3d(args):
             e0.record()
             step((a0, a1))
             e1.record()
-            e1.synchronize()
+            evs.append((e0, e1, a0, a1))
+        torch.cuda.synchronize()  # every step's events are read after the bracket
+        for e0, e1, a0, a1 in evs:
             step_ms.append(e0.elapsed_time(e1))
             if reducer is not None:
                 ar_ms.append(a0.elapsed_time(a1))
-        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         launches = L.gsb_kernel_launches() - launches0
@@ -602,15 +609,15 @@ def _median_ms(fn, reps: int, warmup: int = 3) -> float:
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    times = []
+    evs = []
     for _ in range(reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
         e1.record()
-        e1.synchronize()
-        times.append(e0.elapsed_time(e1))
-    return statistics.median(times)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()  # back-to-back repetitions, read after the last
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
 
 
 def run_matrix(args):

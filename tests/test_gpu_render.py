@@ -179,6 +179,26 @@ def test_eval_and_train_paths_agree_and_are_deterministic():
     assert torch.equal(tr, tr2)
 
 
+@pytest.mark.parametrize("name", ["c1", "c3"])
+def test_repeated_backward_through_saved_state(name):
+    """Two backward passes through one forward (retain_graph) add the same
+    gradients twice. c3 runs the backward warp kernel with dynamic tile claims
+    (many tiles per warp), c1 with the static grid stride; the claim counter
+    must be back at zero for the second pass."""
+    s = config_2d(name, seed=5)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    ins = [t.to(DEV).clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+    out = tgb.rasterize_projected_gaussians(*ins, cfg)
+    g = grad_image(s.B, s.height, s.width, seed=6).to(DEV)
+    out.backward(g, retain_graph=True)
+    first = [t.grad.clone() for t in ins[:4]]
+    out.backward(g)
+    torch.cuda.synchronize()
+    for a, b in zip(first, ins[:4]):
+        second = b.grad - a
+        assert rel_err(np_(second), np_(a)) <= 1e-5
+
+
 def test_serial_and_flatten_batches_agree():
     s = make_2d(3, 700, 48, 80, seed=12, sigma=(1.0, 15.0))
     ins = [t.to(DEV) for t in s.tensors()]
