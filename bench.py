@@ -42,7 +42,7 @@ L2_FLUSH_BYTES = 256 << 20
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3", "c4"))
@@ -227,7 +227,6 @@ def run_b200(args):
         torch.cuda.synchronize()
         launches0 = L.gsb_kernel_launches()
         t_bracket = time.perf_counter()
-        set_kernel_timer(True)
         # Steps are enqueued back to back: the host prepares step k+1 while the
         # GPU runs step k (as in a training loop), and each step's events are
         # read after the bracket's final synchronize. Host latency before a
@@ -243,12 +242,22 @@ def run_b200(args):
             evs.append((e0, e1))
         torch.cuda.synchronize()
         step_ms = [a.elapsed_time(b) for a, b in evs]
-        kt = kernel_times()
-        set_kernel_timer(False)
         if world > 1:
             dist.barrier()
         bracket_ms = (time.perf_counter() - t_bracket) * 1e3
         launches = L.gsb_kernel_launches() - launches0
+        # Per-kernel durations (the rooflines' denominators): the same K steps
+        # again with the host runtime's per-phase events on. An event recorded
+        # between two kernels ends their programmatic launch overlap (about
+        # 26 us per c3 step for the 10 events), so the step time above is taken
+        # without them.
+        set_kernel_timer(True)
+        for _ in range(args.steps):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        kt = kernel_times()
+        set_kernel_timer(False)
     clock = clocks.summary()
     ms = statistics.mean(step_ms)
     ms_med = statistics.median(step_ms)
@@ -314,6 +323,9 @@ def run_b200(args):
                        "parallelism": f"views sharded, {world} rank(s), no collective"},
             "gpu_launches": int(launches),
             "kernels": kernels,
+            "kernel_timing": "per-phase CUDA events on the launching stream, over a second run of the same K "
+                             "steps right after the timed one (the events end the programmatic launch overlap "
+                             "between kernels, so the timed steps run without them)",
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": f"{peak_kind} copy bandwidth", "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "algorithmic_bytes_per_launch": alg,
