@@ -52,6 +52,7 @@ constexpr int kWarps = 8;       // warps per CTA (forward warp kernel, CTA kerne
 constexpr int kBwdWarps = 4;    // warps per CTA (backward warp kernel)
 constexpr int kBatch = 256;     // records staged per CTA round (long kernels)
 constexpr int kCtaThreads = 128;  // threads per long tile in the CTA kernels (2 pixels each)
+constexpr int kDenseSplatsPerTile = 4;  // B*G / tiles from which the CTA kernels get one CTA per tile
 constexpr int kGradComps = 9;
 
 struct TileCoord {
@@ -978,6 +979,18 @@ extern "C" size_t gsb_render_workspace_size(const gsb_raster_meta* meta) {
 namespace gsb {
 namespace {
 
+// Grid of the long-tile CTA kernels. Each CTA scans a strided slice of the
+// tiles and renders the long ones it finds, one after another. Where long tiles
+// are common (many splats per tile: clustered or dense scenes), one CTA per
+// tile instead gives every long tile its own CTA, and the hardware block
+// scheduler hands them to SMs as slots free up, which balances tiles of very
+// different lengths; the extra CTAs exit after two loads. With about one
+// splat per tile (c2, c3) a slice per resident CTA keeps the scan cheap.
+int long_tile_grid(const Meta& m, int resident) {
+  if ((int64_t)m.BG >= kDenseSplatsPerTile * (int64_t)m.total_tiles) return max(1, m.total_tiles);
+  return max(1, min(resident, m.total_tiles));
+}
+
 // The forward's two launches: warp per short tile, then CTA per long tile.
 int launch_forward(const Meta& m, const float* rec, const int32_t* tile_offsets, const int32_t* binned_ids,
                    float* out_rgb, float* final_T, int32_t* last_idx, float* pair_rec, uint32_t* status,
@@ -986,7 +999,7 @@ int launch_forward(const Meta& m, const float* rec, const int32_t* tile_offsets,
   const float4* r4 = reinterpret_cast<const float4*>(rec);
   float4* pr4 = reinterpret_cast<float4*>(pair_rec);
   const int warp_grid = max(1, min(g.fwd_warp[final_T ? 1 : 0], (m.total_tiles + kWarps - 1) / kWarps));
-  const int cta_grid = max(1, min(g.fwd_cta[final_T ? 1 : 0], m.total_tiles));
+  const int cta_grid = long_tile_grid(m, g.fwd_cta[final_T ? 1 : 0]);
   cudaError_t e;
   if (final_T) {
     e = launch_pdl(k_render_fwd_warp<true>, warp_grid, kWarps * 32, 0, stream, m, r4, tile_offsets, binned_ids,
@@ -1046,7 +1059,7 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
   const GridCache& g = grids();
   const float4* r4 = reinterpret_cast<const float4*>(rec);
   const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
-  const int cta_grid = max(1, min(g.bwd_cta, m.total_tiles));
+  const int cta_grid = long_tile_grid(m, g.bwd_cta);
   const int claims = m.total_tiles >= kMinTilesPerWarpForClaims * warp_grid * kBwdWarps ? 1 : 0;
   // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
   const bool clamp_om = !(1.0f - m.max_alpha >= m.eps);
