@@ -23,7 +23,9 @@
 // column terms of the exponent shared by the lane's 8 rows, backward gradients
 // summed over the lane's pixels before a single warp reduction). Longer lists
 // go to a CTA per tile (128 threads, two packed pixels each), which finds its
-// tiles itself by scanning tile_offsets. All kernels are persistent.
+// tiles itself by scanning tile_offsets. The warp kernels are persistent; the
+// CTA kernels run a slice of tiles per resident CTA, or one CTA per tile in
+// dense scenes (long_tile_grid).
 //
 // The training forward also copies each short tile's records, in list order,
 // into pair_rec [P,12] (a by-product of its gather). The backward warp kernel

@@ -41,7 +41,10 @@ extern "C" {
 #define GSB_ERR_CUDA 6             /* a CUDA runtime call failed */
 #define GSB_ERR_DEVICE_BOUNDS 7    /* a device-side bounds check fired */
 
-/* ---- device status block (caller-owned, GSB_STATUS_WORDS x uint32) ------ */
+/* ---- device status block (caller-owned, GSB_STATUS_WORDS x uint32) ------ *
+ * gsb_bin_count clears it; the render and backward calls of that binning use
+ * it too (error flags, the backward's tile claim counter), so calls sharing a
+ * status block must be ordered on one stream.                              */
 #define GSB_STATUS_TOTAL_PAIRS 0    /* written by gsb_bin_prepare */
 #define GSB_STATUS_ERROR 1          /* OR of GSB_DEVERR_* flags */
 #define GSB_STATUS_MAX_TILE_COUNT 2 /* written by gsb_tile_stats */
