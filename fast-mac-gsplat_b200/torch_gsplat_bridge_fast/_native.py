@@ -33,6 +33,7 @@ GSB_DEVERR_PEER_TIMEOUT = 8
 DEVERR_LOOKBACK_TIMEOUT = 1
 DEVERR_PAIR_OVERFLOW = 2
 DEVERR_BOUNDS = 4
+DEVERR_PEER_TIMEOUT = GSB_DEVERR_PEER_TIMEOUT
 
 # Every symbol include/gsplat_b200.h declares (checked by the ABI test).
 EXPORTED = (
@@ -177,4 +178,6 @@ def decode_device_error(flags: int, site: int) -> str:
         parts.append("pair count overflow (emit/scan mismatch or > 2^31 pairs)")
     if flags & DEVERR_BOUNDS:
         parts.append("index out of bounds")
+    if flags & DEVERR_PEER_TIMEOUT:
+        parts.append("a peer rank did not reach the gradient-sum barrier in time")
     return f"gsplat_b200 device error (flags={flags}, site={site}): " + "; ".join(parts or ["unknown"])

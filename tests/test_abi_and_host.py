@@ -31,6 +31,36 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(N.EXPORTED)
 
 
+def _header_defines():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return {k: int(v) for k, v in re.findall(r"#define\s+(GSB_[A-Z0-9_]+)\s+(\d+)u?\b", text)}
+
+
+def test_binding_constants_match_the_header():
+    """The ctypes binding mirrors the header's constants (status-block layout,
+    record size, peer buffer layout, device error flags) with the same values."""
+    defines = _header_defines()
+    must = [k for k in defines if k.startswith(("GSB_STATUS_", "GSB_REC_", "GSB_PEER_"))]
+    assert "GSB_STATUS_WORDS" in must and "GSB_STATUS_TILE_CLAIM" in must
+    for name in must:
+        assert getattr(N, name) == defines[name], name
+    for name, value in defines.items():
+        if hasattr(N, name):
+            assert getattr(N, name) == value, name
+        if name.startswith("GSB_DEVERR_"):
+            assert getattr(N, name[4:]) == value, name  # DEVERR_* in the binding
+    words = [v for k, v in defines.items() if k.startswith("GSB_STATUS_") and k != "GSB_STATUS_WORDS"]
+    assert max(words) + 1 <= defines["GSB_STATUS_WORDS"]
+
+
+def test_device_error_decoding_names_every_flag():
+    for flag, text in [(N.DEVERR_LOOKBACK_TIMEOUT, "look-back"), (N.DEVERR_PAIR_OVERFLOW, "pair count"),
+                       (N.DEVERR_BOUNDS, "out of bounds"), (N.DEVERR_PEER_TIMEOUT, "peer rank")]:
+        msg = N.decode_device_error(flag, 3)
+        assert text in msg and "unknown" not in msg, msg
+    assert "unknown" in N.decode_device_error(0, 0)
+
+
 def test_version_and_status_strings():
     L = N.load()
     assert L.gsb_version() >= 100
