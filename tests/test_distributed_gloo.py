@@ -98,3 +98,54 @@ def test_shared_gradient_allreduce_matches_single_process():
     for _, _, grads in results:
         for g, r in zip(grads, ref):
             assert torch.allclose(g, r.grad, rtol=1e-5, atol=1e-6)
+
+
+def _silent_worker(rank, world, port, out_q):
+    """Rank 1 joins the group and then never takes part in the all-reduce (a
+    rank that hangs); rank 0 must get an error from the process group's
+    timeout instead of waiting for ever."""
+    sys.path[:0] = [str(ROOT), str(ROOT / "fast-mac-gsplat_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import time
+
+    from torch_gsplat_bridge_fast.distributed import SharedGradAllReduce
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    err = None
+    t0 = time.perf_counter()
+    try:
+        if rank == 0:
+            p = torch.zeros(64, requires_grad=True)
+            p.grad = torch.ones(64)
+            try:
+                SharedGradAllReduce([p])()
+            except Exception as e:  # the expected outcome
+                err = type(e).__name__
+        else:
+            time.sleep(12)
+    finally:
+        out_q.put((rank, err, time.perf_counter() - t0))
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_rank_that_never_joins_the_allreduce_is_detected():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_silent_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        results = {r: (err, t) for r, err, t in (q.get(timeout=120) for _ in procs)}
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    err, waited = results[0]
+    assert err is not None, "rank 0 returned from an all-reduce its peer never joined"
+    assert waited < 30.0, waited
