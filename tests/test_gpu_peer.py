@@ -106,3 +106,44 @@ def test_peer_allreduce_two_ranks_matches_cpu_sum(views):
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
 def test_peer_allreduce_four_ranks_matches_cpu_sum():
     _run(4)
+
+
+def test_peer_allreduce_wait_times_out_and_reports():
+    """Failure detection without a GPU fault: rank 0 of a 2-rank sum whose
+    second buffer (on the same GPU) belongs to a rank that never launches.
+    Its flags are never set, so the kernel's bounded waits (10 s at the start
+    barrier, 10 s at the end barrier) run out; it records
+    GSB_DEVERR_PEER_TIMEOUT in the status block and returns. Only this one
+    kernel waits, so no two waiting kernels share the GPU. The context stays
+    usable afterwards."""
+    import ctypes as C
+    import time
+
+    from torch_gsplat_bridge_fast import _native as N
+
+    L = N.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = 4096
+    bases = []
+    for _ in range(2):
+        b = C.c_void_p()
+        N.check(L.gsb_peer_buffer_alloc(n * 4, C.byref(b)), "gsb_peer_buffer_alloc")
+        bases.append(b.value)
+    try:
+        status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
+        arr = (C.c_void_p * 2)(*bases)
+        t0 = time.perf_counter()
+        N.check(L.gsb_peer_allreduce_sum(0, 2, arr, n, 1, N.ptr(status), N.stream_ptr(dev)), "gsb_peer_allreduce_sum")
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+        flags = int(status[N.GSB_STATUS_ERROR].item())
+        assert flags & N.GSB_DEVERR_PEER_TIMEOUT, flags
+        assert int(status[N.GSB_STATUS_ERROR_SITE].item()) in (7, 8)  # start or end barrier
+        assert 9.0 < waited < 60.0, waited
+        assert "peer rank" in N.decode_device_error(flags, int(status[N.GSB_STATUS_ERROR_SITE].item()))
+        x = torch.arange(10, device=dev, dtype=torch.float32)
+        assert float(x.sum().item()) == 45.0  # the context is still usable
+    finally:
+        for b in bases:
+            L.gsb_peer_buffer_free(C.c_void_p(b))
