@@ -3,6 +3,8 @@
 // Replaces the per-tile threadgroup bitonic sort of the reference
 // (variants/v8_project3d/csrc/metal/gsplat_v8_project3d_kernels.metal:594-617, capped at
 // GSP_FAST_CAP entries per tile) with one global, stable, uncapped sort.
+#include <mutex>
+
 #include "gsb_common.cuh"
 #include "gsb_host.cuh"
 #include "radix_sort.cuh"
@@ -264,9 +266,11 @@ int grid_for(int64_t n, int threads, int max_blocks) {
 template <typename K>
 static cudaError_t onesweep_smem_optin() {
   static bool done[64] = {false};
+  static std::mutex mu;  // host threads may sort concurrently
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
   if (done[dev & 63]) return cudaSuccess;
   e = cudaFuncSetAttribute(rs_onesweep<K, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)sizeof(OnesweepSmem<K, 16>));

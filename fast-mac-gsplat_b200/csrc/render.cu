@@ -939,8 +939,10 @@ struct GridCache {
 
 const GridCache& grids() {
   static GridCache cache[64];
+  static std::mutex mu;  // host threads may launch concurrently: fill each entry once, under the lock
   int dev = 0;
   cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
   GridCache& g = cache[dev & 63];
   if (g.sms == 0) {
     int sms = 148;
