@@ -179,8 +179,9 @@ int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int
  * reference. For callers that cannot allocate device memory themselves (a host
  * that owns all device memory and gives this library only its inputs and
  * outputs): it takes no workspace arguments, since the compositing kernels need
- * no scratch, and allocates nothing. Calls on different streams do not
- * interfere. Same arguments and results as gsb_render_forward otherwise. */
+ * no scratch, and allocates nothing; it has no size limit beyond
+ * gsb_render_forward's. Concurrent calls must use separate status blocks.
+ * Same arguments and results as gsb_render_forward otherwise. */
 int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec,
                                const int32_t* tile_offsets, const int32_t* binned_ids,
                                float* out_rgb, float* final_T, int32_t* last_idx, float* pair_rec,
