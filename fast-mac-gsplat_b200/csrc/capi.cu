@@ -19,7 +19,9 @@ extern "C" const char* gsb_status_string(int code) {
     case GSB_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer, bad shape or bad config)";
     case GSB_ERR_UNSUPPORTED: return "unsupported configuration (tile_size must be 16)";
     case GSB_ERR_WORKSPACE: return "workspace smaller than the *_workspace_size query";
-    case GSB_ERR_CAPACITY: return "pair count exceeds the supported index range";
+    case GSB_ERR_CAPACITY:
+      return "size exceeds capacity (pair count beyond the int32 index range, or beyond the fixed maximum "
+             "of an allocation-free entry point)";
     case GSB_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait ran out";
     case GSB_ERR_CUDA: return "CUDA runtime error";
     case GSB_ERR_DEVICE_BOUNDS: return "device-side bounds check failed";

@@ -402,3 +402,71 @@ extern "C" int gsb_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* val
                                               status, static_cast<cudaStream_t>(stream), false);
   return e == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free sort (gsb_radix_sort_pairs_noalloc): the same sort with its
+// scratch (temporary keys and values, digit histograms, partition counters and
+// look-back words) in a fixed device array of this library instead of a
+// caller-provided workspace. It serves callers that cannot allocate device
+// memory at all, such as a host application that budgets every byte of GPU
+// memory itself and hands a plugin only the buffers of each call.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this
+// library holds kNoallocScratchBytes of it until the process exits. Its name is
+// only a host-side stand-in in host code, so the host looks its device address
+// up once per device (cudaGetSymbolAddress, with that device current) and
+// passes that address to the kernels.
+// ---------------------------------------------------------------------------
+namespace gsb {
+namespace {
+
+constexpr int64_t kNoallocMaxPairs = GSB_SORT_NOALLOC_MAX_PAIRS;
+// Scratch of the largest allowed sort (2^18 pairs, 64 key bits: 8 passes of
+// 1,024-key partitions) is 2 MiB of keys, 1 MiB of values and 2.1 MB of
+// histograms and look-back words; the set-up checks that it fits.
+constexpr size_t kNoallocScratchBytes = GSB_SORT_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoallocMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_sort_scratch[kNoallocScratchBytes];
+
+// Device address of g_sort_scratch on the current device, looked up on the
+// first call for that device (under a lock: host threads may sort at once).
+int noalloc_scratch(void** out) {
+  static void* addr[kNoallocMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GSB_ERR_CUDA;
+  if (dev < 0 || dev >= kNoallocMaxDevices) return GSB_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_sort_scratch) != cudaSuccess || p == nullptr) return GSB_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return GSB_OK;
+}
+
+}  // namespace
+}  // namespace gsb
+
+extern "C" int gsb_radix_sort_pairs_noalloc(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
+                                            uint32_t* vals_out, int64_t n, int begin_bit, int end_bit,
+                                            uint32_t* status, void* stream) {
+  if (n < 0 || begin_bit < 0 || end_bit > 64 || end_bit < begin_bit) return GSB_ERR_INVALID_ARGUMENT;
+  if (n > gsb::kNoallocMaxPairs) return GSB_ERR_CAPACITY;
+  if (n > 0 && (!keys_in || !vals_in || !keys_out || !vals_out || !status)) return GSB_ERR_INVALID_ARGUMENT;
+  if (keys_in == keys_out && n > 0) return GSB_ERR_INVALID_ARGUMENT;
+  if (gsb_radix_sort_pairs_workspace_size(n, begin_bit, end_bit) > gsb::kNoallocScratchBytes)
+    return GSB_ERR_CAPACITY;
+  if (n == 0) return GSB_OK;
+  void* scratch = nullptr;
+  const int rc = gsb::noalloc_scratch(&scratch);
+  if (rc != GSB_OK) return rc;
+  // scratch_zeroed = false: the sort clears its histograms, counters and
+  // look-back words (left over from the previous call) with a memset first.
+  gsb::Carver c(scratch);
+  const cudaError_t e = gsb::radix_sort_pairs(c, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit,
+                                              status, static_cast<cudaStream_t>(stream), false);
+  return e == cudaSuccess ? GSB_OK : GSB_ERR_CUDA;
+}

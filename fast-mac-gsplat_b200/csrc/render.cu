@@ -1094,15 +1094,3 @@ extern "C" int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm
   note_launches(1);
   return cuda_status(e);
 }
-
-// ---------------------------------------------------------------------------
-// Allocation-free forward: the compositing forward needs no scratch, so this is
-// gsb_render_forward without the (unused) workspace arguments. Meant for hosts
-// that own all device memory and give a plugin no way to allocate.
-// ---------------------------------------------------------------------------
-extern "C" int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
-                                          const int32_t* binned_ids, float* out_rgb, float* final_T,
-                                          int32_t* last_idx, float* pair_rec, uint32_t* status, void* stream_) {
-  return gsb_render_forward(meta, rec, tile_offsets, binned_ids, out_rgb, final_T, last_idx, pair_rec, status,
-                            nullptr, 0, stream_);
-}

@@ -28,6 +28,8 @@ GSB_REC_FLOATS = 12
 GSB_PEER_MAX_RANKS = 8
 GSB_PEER_FLAG_BYTES = 256
 GSB_PEER_HANDLE_BYTES = 64
+GSB_SORT_NOALLOC_MAX_PAIRS = 262144
+GSB_SORT_NOALLOC_SCRATCH_BYTES = 6 << 20
 GSB_DEVERR_PEER_TIMEOUT = 8
 
 DEVERR_LOOKBACK_TIMEOUT = 1
@@ -51,12 +53,12 @@ EXPORTED = (
     "gsb_render_workspace_size",
     "gsb_render_forward",
     "gsb_render_backward",
-    "gsb_render_forward_noalloc",
     "gsb_unsort_grads",
     "gsb_project_forward",
     "gsb_project_backward",
     "gsb_radix_sort_pairs_workspace_size",
     "gsb_radix_sort_pairs",
+    "gsb_radix_sort_pairs_noalloc",
     "gsb_sh_forward",
     "gsb_sh_backward",
     "gsb_peer_buffer_alloc",
@@ -119,12 +121,12 @@ def load() -> C.CDLL:
         "gsb_render_workspace_size": (sz, [M]),
         "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_render_backward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
-        "gsb_render_forward_noalloc": (C.c_int, [M, p, p, p, p, p, p, p, p, p]),
         "gsb_unsort_grads": (C.c_int, [M, p, p, p, p, p, p, p]),
         "gsb_project_forward": (C.c_int, [i32, i32, p, p, p, p, p, p, f32, p, p, p, p, p]),
         "gsb_project_backward": (C.c_int, [i32, i32] + [p] * 10 + [f32] + [p] * 7),
         "gsb_radix_sort_pairs_workspace_size": (sz, [i64, C.c_int, C.c_int]),
         "gsb_radix_sort_pairs": (C.c_int, [p, p, p, p, i64, C.c_int, C.c_int, p, p, sz, p]),
+        "gsb_radix_sort_pairs_noalloc": (C.c_int, [p, p, p, p, i64, C.c_int, C.c_int, p, p]),
         "gsb_sh_forward": (C.c_int, [i32, i32, i32, p, p, p, p, p]),
         "gsb_sh_backward": (C.c_int, [i32, i32, i32, p, p, p, p, p, p, p, p, p]),
         "gsb_peer_buffer_alloc": (C.c_int, [sz, C.POINTER(p)]),

@@ -36,7 +36,8 @@ extern "C" {
 #define GSB_ERR_INVALID_ARGUMENT 1 /* bad pointer / shape / config */
 #define GSB_ERR_UNSUPPORTED 2      /* e.g. tile_size != 16 */
 #define GSB_ERR_WORKSPACE 3        /* workspace smaller than *_workspace_size */
-#define GSB_ERR_CAPACITY 4         /* pair count exceeds the int32 index range */
+#define GSB_ERR_CAPACITY 4         /* pair count beyond the int32 index range, or a size beyond
+                                      an allocation-free entry point's fixed maximum */
 #define GSB_ERR_DEVICE_TIMEOUT 5   /* a bounded device-side wait ran out */
 #define GSB_ERR_CUDA 6             /* a CUDA runtime call failed */
 #define GSB_ERR_DEVICE_BOUNDS 7    /* a device-side bounds check fired */
@@ -175,18 +176,6 @@ int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int
                         const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
                         void* workspace, size_t workspace_bytes, void* stream);
 
-/* Allocation-free variant of gsb_render_forward, with no counterpart in the
- * reference. For callers that cannot allocate device memory themselves (a host
- * that owns all device memory and gives this library only its inputs and
- * outputs): it takes no workspace arguments, since the compositing kernels need
- * no scratch, and allocates nothing; it has no size limit beyond
- * gsb_render_forward's. Concurrent calls must use separate status blocks.
- * Same arguments and results as gsb_render_forward otherwise. */
-int gsb_render_forward_noalloc(const gsb_raster_meta* meta, const float* rec,
-                               const int32_t* tile_offsets, const int32_t* binned_ids,
-                               float* out_rgb, float* final_T, int32_t* last_idx, float* pair_rec,
-                               uint32_t* status, void* stream);
-
 /* Replaces the un-sort scatter of the autograd backward
  * (torch_gsplat_bridge_fast/rasterize.py:96-105; …/v8_project3d/…/rasterize.py:583-591, 847-851).
  * Any output pointer may be NULL (that gradient is skipped). */
@@ -268,6 +257,28 @@ size_t gsb_radix_sort_pairs_workspace_size(int64_t n, int begin_bit, int end_bit
 int gsb_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
                          uint32_t* vals_out, int64_t n, int begin_bit, int end_bit,
                          uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Allocation-free variant of gsb_radix_sort_pairs. It has no counterpart in the
+ * reference. Some callers cannot allocate device memory: a host application that
+ * budgets all GPU memory itself and gives a plugin only the buffers of each call,
+ * or a loop that must not reach cudaFree, which synchronizes the device. This
+ * entry point takes no workspace and allocates nothing: its scratch is a fixed
+ * array of GSB_SORT_NOALLOC_SCRATCH_BYTES inside the library, which every GPU
+ * that loads the library holds until the process exits. Sorts of more than
+ * GSB_SORT_NOALLOC_MAX_PAIRS pairs are refused with GSB_ERR_CAPACITY.
+ *
+ * The first call on a device looks up that device's address of the array (a
+ * cudaGetSymbolAddress call, made with that device current); make that first
+ * call before any stream capture. All calls on a device share the one array,
+ * and each call clears the parts that must start at zero, so calls that can
+ * overlap on the GPU (on different streams, or from different host threads
+ * without ordering) race and corrupt each other: order them on one stream.
+ * Same arguments and results as gsb_radix_sort_pairs otherwise. */
+#define GSB_SORT_NOALLOC_MAX_PAIRS 262144
+#define GSB_SORT_NOALLOC_SCRATCH_BYTES (6u << 20)
+int gsb_radix_sort_pairs_noalloc(const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
+                                 uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
+                                 void* stream);
 
 #ifdef __cplusplus
 }

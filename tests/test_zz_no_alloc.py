@@ -1,68 +1,105 @@
-"""The allocation-free forward entry point (gsb_render_forward_noalloc) against the
-regular one (gsb_render_forward, caller-provided workspace), through the C ABI.
+"""The allocation-free sort entry point (gsb_radix_sort_pairs_noalloc) against the
+regular one (gsb_radix_sort_pairs, caller-provided workspace), through the C ABI.
 
-Some callers cannot allocate device memory: a host that owns all of it and hands
-this library only input and output buffers. The compositing forward needs no
-scratch (the CTA kernel for long tiles finds them itself), so that entry point
-takes no workspace. This test runs it twice in a row on a scene with long tiles
-and checks both results against the workspace entry point at the tolerance the
-compositing tests use.
+Some callers of this library cannot allocate device memory: a host application
+that budgets all GPU memory itself and hands a plugin only the buffers of each
+call, or a loop that must not reach cudaFree, which synchronizes the device.
+gsb_radix_sort_pairs_noalloc serves them: its scratch is a fixed device array
+inside the library, shared by every call on a device. These tests run it twice
+in a row (the second call finds the first call's leftovers in that array) and
+check both results bit for bit against the workspace entry point, since a sort
+of integers must be exact. They also check that the call takes no device memory
+and that sizes above the fixed maximum are refused.
+
+This file is collected last, so a run that stops at its first failure has run
+every other test before it.
 """
 from __future__ import annotations
-
-import ctypes as C
 
 import numpy as np
 import pytest
 import torch
 
-import torch_gsplat_bridge_fast as tgb
-from helpers import IMAGE_ATOL, max_abs, np_
 from torch_gsplat_bridge_fast import _native as N
-from torch_gsplat_bridge_fast.rasterize import _bin, _render_forward
-from workloads import config_2d
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")
 
 
-def _noalloc_forward(st, cfg, B):
+def _device_tensors(keys: np.ndarray, vals: np.ndarray):
+    k_in = torch.from_numpy(keys.view(np.int64)).to(DEV)
+    v_in = torch.from_numpy(vals.view(np.int32)).to(DEV)
+    return k_in, v_in, torch.empty_like(k_in), torch.empty_like(v_in)
+
+
+def _sort_workspace(keys, vals, begin, end):
     L = N.load()
-    H, W = cfg.height, cfg.width
-    out = torch.full((B, H, W, 3), float("nan"), device=DEV)
-    final_T = torch.full((B, H, W), float("nan"), device=DEV)
-    last_idx = torch.full((B, H, W), -7, dtype=torch.int32, device=DEV)
-    pair_rec = torch.empty((max(st.P, 1), N.GSB_REC_FLOATS), device=DEV)
+    k_in, v_in, k_out, v_out = _device_tensors(keys, vals)
     status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
-    rc = L.gsb_render_forward_noalloc(st.meta, N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids),
-                                      N.ptr(out), N.ptr(final_T), N.ptr(last_idx), N.ptr(pair_rec),
-                                      N.ptr(status), N.stream_ptr(DEV))
-    N.check(rc, "gsb_render_forward_noalloc")
+    ws_n = L.gsb_radix_sort_pairs_workspace_size(keys.size, begin, end)
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=DEV)
+    N.check(L.gsb_radix_sort_pairs(N.ptr(k_in), N.ptr(v_in), N.ptr(k_out), N.ptr(v_out), keys.size, begin, end,
+                                   N.ptr(status), N.ptr(ws), ws_n, N.stream_ptr(DEV)), "gsb_radix_sort_pairs")
     torch.cuda.synchronize()
     assert int(status[N.GSB_STATUS_ERROR]) == 0
-    return out, final_T, last_idx
+    return k_out.cpu().numpy().view(np.uint64), v_out.cpu().numpy().view(np.uint32)
 
 
-def test_noalloc_forward_matches_workspace_forward_twice():
-    s = config_2d("c1", seed=0)  # clustered: has tiles above the warp-kernel cap (the CTA kernel's share)
-    cfg = tgb.RasterConfig(s.height, s.width)
-    st = _bin(cfg, *(t.to(DEV) for t in s.tensors()))
-    counts = np.diff(st.tile_offsets.cpu().numpy())
-    assert counts.max() > 64
-    ref_out, ref_T, ref_last, _ = _render_forward(st, cfg, s.B, save_state=True)
-    torch.cuda.synchronize()
-    for _ in range(2):
-        out, final_T, last_idx = _noalloc_forward(st, cfg, s.B)
-        assert max_abs(np_(out), np_(ref_out)) <= IMAGE_ATOL
-        assert max_abs(np_(final_T), np_(ref_T)) <= IMAGE_ATOL
-        assert np.array_equal(np_(last_idx), np_(ref_last))
+def _free_device_bytes() -> int:
+    free, _total = torch.cuda.mem_get_info(DEV)
+    return int(free)
 
 
-def test_noalloc_forward_has_no_tile_cap():
-    """The compositing kernels need no scratch, so a frame of 4 x 4112^2 pixels
-    (264,196 tiles) is not refused for capacity; with no buffers the call fails
-    its argument check instead."""
+def _sort_noalloc(keys, vals, begin, end, check_memory: bool):
+    """One call of the allocation-free entry point; with check_memory, asserts
+    that neither torch's allocator nor the device lost memory across it."""
     L = N.load()
-    meta = N.make_meta(4112, 4112, 4, 1, 1 / 255, 1e-4, (0.0, 0.0, 0.0))
-    rc = L.gsb_render_forward_noalloc(C.byref(meta), None, None, None, None, None, None, None, None, None)
-    assert rc == 1  # GSB_ERR_INVALID_ARGUMENT, not GSB_ERR_CAPACITY (4)
+    k_in, v_in, k_out, v_out = _device_tensors(keys, vals)
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    alloc0, reserved0, free0 = torch.cuda.memory_allocated(DEV), torch.cuda.memory_reserved(DEV), _free_device_bytes()
+    rc = L.gsb_radix_sort_pairs_noalloc(N.ptr(k_in), N.ptr(v_in), N.ptr(k_out), N.ptr(v_out), keys.size, begin, end,
+                                        N.ptr(status), N.stream_ptr(DEV))
+    N.check(rc, "gsb_radix_sort_pairs_noalloc")
+    torch.cuda.synchronize()
+    if check_memory:
+        assert torch.cuda.memory_allocated(DEV) == alloc0
+        assert torch.cuda.memory_reserved(DEV) == reserved0
+        # A workspace of this sort is several MB; the driver's free count moves
+        # in 2 MiB pages, so a drop of less than that is not an allocation.
+        assert _free_device_bytes() > free0 - (2 << 20)
+    assert int(status[N.GSB_STATUS_ERROR]) == 0
+    return k_out.cpu().numpy().view(np.uint64), v_out.cpu().numpy().view(np.uint32)
+
+
+def _keys(n: int, seed: int):
+    rng = np.random.default_rng(seed)
+    keys = rng.integers(0, 2**63, n, dtype=np.uint64) | (rng.integers(0, 2, n, dtype=np.uint64) << np.uint64(63))
+    keys[: n // 3] &= np.uint64(0xFFFF0000FFFF00FF)  # many ties: stability matters
+    return keys, np.arange(n, dtype=np.uint32)
+
+
+@pytest.mark.parametrize("n,begin,end", [(N.GSB_SORT_NOALLOC_MAX_PAIRS, 0, 64), (100_003, 32, 45), (4097, 5, 19)])
+def test_noalloc_sort_matches_workspace_sort_twice(n, begin, end):
+    keys, vals = _keys(n, seed=n + begin)
+    ref_k, ref_v = _sort_workspace(keys, vals, begin, end)
+    # Two calls in a row: the second meets the first call's histograms and
+    # look-back words in the shared scratch and must clear them itself. The
+    # first call on the device also looks up the array's address; memory is
+    # checked on the second.
+    for call in range(2):
+        k, v = _sort_noalloc(keys, vals, begin, end, check_memory=call == 1)
+        assert np.array_equal(k, ref_k), f"keys differ on call {call}"
+        assert np.array_equal(v, ref_v), f"values differ on call {call}"
+
+
+def test_noalloc_sort_refuses_sizes_above_its_maximum():
+    L = N.load()
+    n = N.GSB_SORT_NOALLOC_MAX_PAIRS + 1
+    keys, vals = _keys(n, seed=1)
+    k_in, v_in, k_out, v_out = _device_tensors(keys, vals)
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    rc = L.gsb_radix_sort_pairs_noalloc(N.ptr(k_in), N.ptr(v_in), N.ptr(k_out), N.ptr(v_out), n, 0, 64,
+                                        N.ptr(status), N.stream_ptr(DEV))
+    assert rc == 4, rc  # GSB_ERR_CAPACITY
+    assert b"allocation-free" in L.gsb_status_string(rc)
