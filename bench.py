@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--config", default=CONFIG_NAME, choices=("c0", "c1", "c2", "c3", "c4"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-splits", action="store_true",
+                    help="skip the c2 (views split over ranks) and c4 (shared scene + gradient sum) lines")
     ap.add_argument("--trace", default="",
                     help="replay a recorded batch (torch.save'd dict of means2d/conics/colors/opacities/depths) "
                          "instead of the synthetic config; with --height/--width")
@@ -179,6 +181,217 @@ def algorithmic_bytes(kernel: str, B: int, H: int, W: int, G: int, P: int) -> in
     return 0
 
 
+def fp32_probe(dev, reps: int = 5):
+    """Measured FP32 peak (TFLOP/s): the library's FFMA and FFMA2 probe kernels
+    (gsb_fma_probe) on a full-occupancy grid, best of `reps` launches each after
+    a warm-up, CUDA events on the launching stream (a burst figure, like the
+    compositing kernels' launches of a fraction of a millisecond)."""
+    from torch_gsplat_bridge_fast import _native
+
+    L = _native.load()
+    blocks, iters = 8, 65536
+    n = int(L.gsb_fma_probe_out_floats(blocks))
+    out = torch.empty(n, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    res = {}
+    for packed, name in ((0, "ffma"), (1, "ffma2")):
+        flops = n * iters * 8 * 2 * (2 if packed else 1)
+        _native.check(L.gsb_fma_probe(packed, blocks, iters, _native.ptr(out), stream), "gsb_fma_probe")
+        best = None
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            _native.check(L.gsb_fma_probe(packed, blocks, iters, _native.ptr(out), stream), "gsb_fma_probe")
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        res[name] = round(flops / (best * 1e-3) / 1e12, 2)
+    return res
+
+
+def cpu_model() -> str:
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.startswith("Model name:"):
+                return line.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return "unknown"
+
+
+def time_steps_back_to_back(step, steps: int, flush):
+    """K steps enqueued back to back, an L2 flush before each (outside the step
+    events); every step's events are read after the final synchronize."""
+    evs = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def _max_over_ranks(x: float, dev, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(x: float, dev, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def bench_c2_sharded(dev, rank: int, world: int, steps: int, flush):
+    """Config 2 (B=4 independent 1024x512 views) with its views split over the
+    ranks (torch_gsplat_bridge_fast.distributed.shard_views, round robin): each
+    rank renders and differentiates its views as one batch, no collective.
+    Strong scaling: the 4 views are fixed, so ranks beyond 4 have none. Time =
+    max over ranks of the mean step."""
+    import torch_gsplat_bridge_fast as tgb
+    from torch_gsplat_bridge_fast.distributed import shard_views
+    from torch_gsplat_bridge_fast.rasterize import _bin
+    from workloads import config_2d, grad_image
+
+    s = config_2d("c2", seed=0)
+    views = shard_views(s.B, world, rank)
+    E_mine, ms = 0.0, 0.0
+    if views:
+        idx = torch.tensor(views)
+        base = [t[idx].contiguous().to(dev) for t in s.tensors()]
+        g = grad_image(s.B, s.height, s.width, seed=1000)[idx].contiguous().to(dev)
+        cfg = tgb.RasterConfig(s.height, s.width)
+        st = _bin(cfg, *base)
+        E_mine = float(tiled_work(st.tile_offsets, len(views), s.height, s.width))
+        del st
+
+        def step():
+            ins = [t.detach().requires_grad_(i < 4) for i, t in enumerate(base)]
+            tgb.rasterize_projected_gaussians(*ins, cfg).backward(g)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    if views:
+        ms = statistics.mean(time_steps_back_to_back(step, steps, flush))
+    ms_max = _max_over_ranks(ms, dev, world)
+    E_all = _sum_over_ranks(E_mine, dev, world)
+    return {"workload": "c2: B=4 views, 1024x512, G=2,048 per view, fwd+bwd; views split over ranks",
+            "ranks_with_views": min(world, s.B), "views_rank0": len(shard_views(s.B, world, 0)),
+            "ms_per_step": round(ms_max, 4), "value": round(E_all / (ms_max * 1e-3) / 1e9, 3),
+            "unit": UNIT, "scaling": "strong (4 views in total)"}
+
+
+def bench_c4_shared(dev, rank: int, world: int, steps: int, flush, allreduce: str = "peer", sh_degree: int = 3):
+    """Config 4's shared-scene training step: 2^20 Gaussians on every rank,
+    rank r renders camera r mod 8 (projection, SH colours, binning, compositing
+    fwd+bwd, projection VJP), then the per-Gaussian gradients (59 floats with
+    SH degree 3) are summed across ranks by PeerGradAllReduce (the library's
+    NVLink peer-memory kernel) or NCCL. Weak scaling: one view per rank."""
+    import torch_gsplat_bridge_fast as tgb
+    from torch_gsplat_bridge_fast.distributed import PeerGradAllReduce, SharedGradAllReduce
+    from torch_gsplat_bridge_fast.rasterize import _bin
+    from workloads import config_3d, grad_image
+
+    sc = config_3d(seed=0)
+    view = rank % sc.camera_to_world.shape[0]
+    H, W, G = sc.height, sc.width, sc.means3d.shape[0]
+    cfg = tgb.RasterConfig(H, W)
+    fx, fy, cx, cy = (float(v) for v in sc.camera_params[view])
+    c2w = sc.camera_to_world[view].to(dev)
+    params = [t.to(dev).requires_grad_(True) for t in (sc.means3d, sc.scales, sc.quats, sc.opacities, sc.colors)]
+    deg = sh_degree
+    if deg >= 0:  # colour from SH: (deg+1)^2 x 3 coefficients per Gaussian replace the RGB
+        K = (deg + 1) ** 2
+        gsh = torch.Generator().manual_seed(11)
+        sh = torch.randn(G, K, 3, generator=gsh) * 0.2
+        sh[:, 0] = (sc.colors - 0.5) / 0.28209479177387814  # degree-0 term reproduces the RGB
+        params[4] = sh.to(dev).requires_grad_(True)
+
+    def colors_of(p):
+        return tgb.spherical_harmonics_colors(p[4], p[0], c2w, degree=deg) if deg >= 0 else p[4]
+
+    gimg = grad_image(1, H, W, seed=2000 + rank)[0].to(dev)
+    with torch.no_grad():
+        m2, q2, o2, d2 = tgb.project_pinhole_gaussians(*params[:4], fx, fy, cx, cy, camera_to_world=c2w)
+        st = _bin(cfg, m2[None].contiguous(), q2[None].contiguous(), colors_of(params)[None].contiguous(),
+                  o2[None].contiguous(), d2[None].contiguous())
+        E = float(tiled_work(st.tile_offsets, 1, H, W))
+        del st
+    reducer = None
+    if world > 1:
+        reducer = PeerGradAllReduce(params) if allreduce == "peer" else SharedGradAllReduce(params)
+    floats_per_gaussian = sum(p[0].numel() for p in params)
+    nbytes = sum(p.numel() for p in params) * 4
+    ex_evs = []
+
+    def step(record=False):
+        for p in params:
+            p.grad = None
+        img = tgb.rasterize_pinhole_gaussians(*params[:4], colors_of(params), fx, fy, cx, cy, camera_to_world=c2w,
+                                              config=cfg)
+        img.backward(gimg)
+        if reducer is not None:
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            reducer()
+            a1.record()
+            if record:
+                ex_evs.append((a0, a1))
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    step_ms = time_steps_back_to_back(lambda: step(True), steps, flush)
+    ms = statistics.mean(step_ms)
+    ex_ms = statistics.mean(a.elapsed_time(b) for a, b in ex_evs) if ex_evs else 0.0
+    if isinstance(reducer, PeerGradAllReduce):
+        reducer.check_errors()
+    ms_max = _max_over_ranks(ms, dev, world)
+    ex_max = _max_over_ranks(ex_ms, dev, world)
+    E_all = _sum_over_ranks(E, dev, world)
+    out = {"workload": f"c4: G={G} shared 3D Gaussians, SH degree {deg} colours, one {W}x{H} camera per rank "
+                       f"(view = rank mod 8), fwd+bwd + gradient sum over ranks",
+           "ms_per_step": round(ms_max, 4), "value": round(E_all / (ms_max * 1e-3) / 1e9, 3), "unit": UNIT,
+           "scaling": "weak (one view per rank)", "grad_floats_per_gaussian": floats_per_gaussian,
+           "exchange": None}
+    if reducer is not None:
+        out["exchange"] = {"impl": "NVLink peer-memory kernel (gsb_peer_allreduce_sum)" if allreduce == "peer"
+                           else "NCCL all-reduce", "bytes": nbytes, "ms": round(ex_max, 4),
+                           "share_of_step": round(ex_max / ms_max, 4),
+                           "busbw_GBs": round(2 * (world - 1) / world * nbytes / (ex_max * 1e-3) / 1e9, 1),
+                           "includes": "pack of the .grad tensors into the flat buffer and the sum"}
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        if isinstance(reducer, PeerGradAllReduce):
+            reducer.close()
+    return out
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -216,6 +429,7 @@ def run_b200(args):
         return ins
 
     for _ in range(max(args.warmup, 3)):
+        flush.zero_()  # the flush's first launch is warm too before the bracket
         step()
     torch.cuda.synchronize()
 
@@ -246,6 +460,19 @@ def run_b200(args):
             dist.barrier()
         bracket_ms = (time.perf_counter() - t_bracket) * 1e3
         launches = L.gsb_kernel_launches() - launches0
+        # Forward only (the no-grad path, BASELINE config 3's first figure).
+
+        def fwd_only():
+            with torch.no_grad():
+                tgb.rasterize_projected_gaussians(*base, cfg)
+
+        for _ in range(3):
+            flush.zero_()
+            fwd_only()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        fwd_ms = statistics.mean(time_steps_back_to_back(fwd_only, args.steps, flush))
         # Per-kernel durations (the rooflines' denominators): the same K steps
         # again with the host runtime's per-phase events on. An event recorded
         # between two kernels ends their programmatic launch overlap (about
@@ -262,12 +489,11 @@ def run_b200(args):
     ms = statistics.mean(step_ms)
     ms_med = statistics.median(step_ms)
 
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = _max_over_ranks(ms, dev, world)
+    fwd_ms_max = _max_over_ranks(fwd_ms, dev, world)
+    wall_ms = _max_over_ranks(bracket_ms / args.steps, dev, world)
     value = world * E / (ms_max * 1e-3) / 1e9
+    probe = fp32_probe(dev)
 
     # Dominant kernel roofline (HBM-bound compositing / binning kernels).
     totals = {k: sum(v) for k, v in kt.items()}
@@ -281,15 +507,25 @@ def run_b200(args):
                    "share": totals[k] / max(sum(totals.values()), 1e-9)} for k, v in kt.items()}
     # The compositing kernels are FP32-issue bound, not HBM bound: their second
     # roofline is the FP32 pipe (algorithmic FLOPs per Gsplat-px eval x E).
-    fp32_peak = 148 * 128 * 2 * float(clock.get("sm_max_mhz") or 1965.0) * 1e6 / 1e12
+    # Peak: the measured FFMA / FFMA2 probe (the better of the two), with the
+    # nominal 148 SMs x 128 lanes x 2 x max clock for context.
+    fp32_peak = max(probe.values())
+    fp32_nominal = 148 * 128 * 2 * float(clock.get("sm_max_mhz") or 1965.0) * 1e6 / 1e12
     roof_fp32 = {}
     for k, fpe in FLOPS_PER_EVAL.items():
         if k in kt:
             tf = fpe * E / (statistics.mean(kt[k]) * 1e-3) / 1e12
             roof_fp32[k] = {"bound": "fp32", "achieved": round(tf, 2), "peak": round(fp32_peak, 1),
-                            "peak_kind": "nominal: 148 SMs x 128 FP32 lanes x 2 x max SM clock", "unit": "TFLOP/s",
+                            "peak_kind": "measured: FFMA/FFMA2 probe kernel (gsb_fma_probe), burst, this run",
+                            "nominal_peak": round(fp32_nominal, 1), "unit": "TFLOP/s",
                             "frac": round(tf / fp32_peak, 4), "flops_per_eval": fpe,
                             "avg_launch_ms": round(statistics.mean(kt[k]), 4)}
+
+    splits = None
+    if not args.no_splits and not args.trace:
+        splits = {"c2_views_sharded": bench_c2_sharded(dev, rank, world, min(args.steps, 50), flush),
+                  "c4_shared_scene": bench_c4_shared(dev, rank, world, min(args.steps, 10), flush,
+                                                     allreduce=args.allreduce)}
 
     e2e = None
     if not args.no_e2e:
@@ -310,7 +546,11 @@ def run_b200(args):
             "warmup": max(args.warmup, 3),
             "ms_per_step": round(ms_max, 4),
             "ms_per_step_median": round(ms_med, 4),
+            "wall_ms_per_step": round(wall_ms, 4),
             "bracket_ms": round(bracket_ms, 2),
+            "forward_only": {"ms_per_step": round(fwd_ms_max, 4),
+                             "value": round(world * E / (fwd_ms_max * 1e-3) / 1e9, 3), "unit": UNIT,
+                             "path": "no-grad forward (binning + compositing), same inputs and flush"},
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
@@ -331,6 +571,8 @@ def run_b200(args):
                          "frac": round(achieved / peak, 4), "algorithmic_bytes_per_launch": alg,
                          "traffic": traffic, "avg_launch_ms": round(dom_ms, 4)},
             "roofline_fp32": roof_fp32,
+            "fp32_probe_tflops": probe,
+            "multi_gpu_splits": splits,
             "clocks": clock,
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -423,8 +665,39 @@ def cpu_baseline(config: str, seed: int, steps: int = 1):
     t = statistics.mean(times)
     cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     return {"value": round(E / t / 1e9, 4), "unit": UNIT, "cores": cores, "kind": "port",
-            "seconds_per_step": round(t, 3),
-            "sample": f"one full {config} fwd+bwd step (C oracle: binning + composite + reverse backward)"}
+            "seconds_per_step": round(t, 3), "cpu_model": cpu_model(),
+            "sample": f"one full {config} fwd+bwd step (C oracle: binning + composite + reverse backward)",
+            "torch_reference_c0": torch_reference_c0()}
+
+
+def torch_reference_c0():
+    """The reference's own torch CPU path on config 0 (the only config under
+    its 64M-evaluation torch work limit): dense_torch_reference
+    (benchmarks/benchmark_full_matrix.py:128-152, restated in
+    oracle/torch_ref.dense_reference and pinned to the original's output by
+    tests/golden/c0like_dense_torch_direct.npz), forward + autograd backward of
+    a N(0,1) grad_image, all host threads. Dense work: every pixel x splat."""
+    from oracle import torch_ref as TR
+    from workloads import config_2d, grad_image
+
+    s = config_2d("c0", seed=0)
+    g = grad_image(1, s.height, s.width, seed=1000)
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        ins = [t.clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+        t0 = time.perf_counter()
+        out = TR.dense_reference(*ins, s.height, s.width)
+        t1 = time.perf_counter()
+        out.backward(g)
+        t2 = time.perf_counter()
+    finally:
+        torch.set_num_threads(prev)
+    dense = s.B * s.height * s.width * s.G
+    return {"seconds_fwd": round(t1 - t0, 2), "seconds_fwd_bwd": round(t2 - t0, 2), "threads": threads,
+            "dense_evals": dense, "dense_evals_per_s": round(dense / (t2 - t0) / 1e9, 4),
+            "sample": "c0 (512x512, G=512) fwd+bwd, one run"}
 
 
 def run_reference(args):
@@ -470,6 +743,7 @@ def run_reference(args):
         "config": {"workload": f"{args.config}: B={s.B}, {s.width}x{s.height}, G={s.G} 2D splats, fwd+bwd",
                    "evals_per_view_E": E},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                         "cpu_model": cpu_model(),
                          "sample": f"one full {args.config} fwd+bwd step per timed step"},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

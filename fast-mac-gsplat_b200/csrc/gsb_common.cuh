@@ -363,6 +363,43 @@ __device__ __forceinline__ float vis_select_fwd(float T, float t_thr, float powe
       : "f"(T), "f"(t_thr), "f"(power), "f"(vis_thr), "f"(value), "r"(consumed));
   return r;
 }
+// vis_select_fwd that also reports vis (0/1), for the guarded loops below.
+__device__ __forceinline__ float vis_select_fwd_v(float T, float t_thr, float power, float vis_thr, float value,
+                                                  int consumed, int& last, int& vis) {
+  float r;
+  asm("{\n\t.reg .pred pl, pv;\n\t"
+      "setp.gt.f32 pl, %3, %4;\n\t"
+      "setp.le.and.f32 pv, %5, 0f00000000, pl;\n\t"
+      "setp.ge.and.f32 pv, %5, %6, pv;\n\t"
+      "selp.f32 %0, %7, 0f00000000, pv;\n\t"
+      "selp.b32 %1, %8, %1, pl;\n\t"
+      "selp.b32 %2, 1, 0, pv;\n\t}"
+      : "=f"(r), "+r"(last), "=r"(vis)
+      : "f"(T), "f"(t_thr), "f"(power), "f"(vis_thr), "f"(value), "r"(consumed));
+  return r;
+}
+
+// Non-finite colours. The branch-free loops give a pixel that does not see a
+// splat alpha = 0 and still evaluate w*c (forward) and alpha*(<g,c> - gT)
+// (backward); with a NaN or infinite colour those products are NaN although
+// w or alpha is 0, and the NaN would spread to every pixel of the tile. The
+// reference skips such pixels (a per-pixel branch), so a pixel that does not
+// see the splat keeps its state. The loops therefore check the colours of each
+// staged batch of records (a warp- or CTA-uniform decision) and run a guarded
+// form of the body, which selects the updated value only where the splat is
+// visible, when one of them is not finite. Finite colours take the unguarded
+// body; for them both forms give the same values.
+__device__ __forceinline__ bool finite_rgb(float r, float g, float b) {
+  return (fabsf(r) <= 3.402823466e38f) & (fabsf(g) <= 3.402823466e38f) & (fabsf(b) <= 3.402823466e38f);
+}
+// Per half: vis ? v : keep.
+__device__ __forceinline__ F2 select2(int vis_lo, int vis_hi, F2 v, F2 keep) {
+  float vl, vh, kl, kh;
+  split(v, vl, vh);
+  split(keep, kl, kh);
+  return f2(vis_lo ? vl : kl, vis_hi ? vh : kh);
+}
+
 // Backward form: vis = j < last && power <= 0 && power >= vis_thr; returns
 // vis ? value : 0 and pass = (vis && power < sat_thr) as 0/1.
 __device__ __forceinline__ float vis_select_bwd(int j, int last, float power, float vis_thr, float sat_thr,
@@ -376,6 +413,22 @@ __device__ __forceinline__ float vis_select_bwd(int j, int last, float power, fl
       "selp.f32 %0, %7, 0f00000000, pv;\n\t"
       "selp.b32 %1, 1, 0, ps;\n\t}"
       : "=f"(r), "=r"(pass)
+      : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  return r;
+}
+// vis_select_bwd that also reports vis (0/1), for the guarded loops.
+__device__ __forceinline__ float vis_select_bwd_v(int j, int last, float power, float vis_thr, float sat_thr,
+                                                  float value, int& pass, int& vis) {
+  float r;
+  asm("{\n\t.reg .pred pv, ps;\n\t"
+      "setp.lt.s32 pv, %3, %4;\n\t"
+      "setp.le.and.f32 pv, %5, 0f00000000, pv;\n\t"
+      "setp.ge.and.f32 pv, %5, %6, pv;\n\t"
+      "setp.lt.and.f32 ps, %5, %7, pv;\n\t"
+      "selp.f32 %0, %8, 0f00000000, pv;\n\t"
+      "selp.b32 %1, 1, 0, ps;\n\t"
+      "selp.b32 %2, 1, 0, pv;\n\t}"
+      : "=f"(r), "=r"(pass), "=r"(vis)
       : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
   return r;
 }

@@ -139,7 +139,56 @@ __device__ __forceinline__ int claim_tiles(uint32_t* counter, int count, int lan
 // per-pixel branches: an invisible or finished pixel gets alpha = 0, which
 // leaves its colour and transmittance bit-for-bit unchanged (w = T*0 = 0,
 // T*(1-0) = T), so the 8 pixels' chains interleave. The results equal those of
-// a per-pixel `if (visible)` loop exactly.
+// a per-pixel `if (visible)` loop exactly, for finite colours; kGuard (a batch
+// holding a non-finite colour) adds w*c only where the splat is visible.
+template <bool kGuard>
+__device__ __forceinline__ void fwd_warp_batch(const Meta& m, const float4 (*recs)[3], int cnt, int base, float fx,
+                                               const F2 (&fy)[kLanePx / 2], F2 (&T)[kLanePx / 2],
+                                               F2 (&cr)[kLanePx / 2], F2 (&cg)[kLanePx / 2], F2 (&cb)[kLanePx / 2],
+                                               int (&last)[kLanePx]) {
+  const F2 one = f2(1.0f), log2e = f2(kLog2e);
+#pragma unroll 1
+  for (int j = 0; j < cnt; ++j) {
+    const float4 p0 = recs[j][0];
+    const float4 p1 = recs[j][1];
+    const float4 p2 = recs[j][2];
+    const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
+    const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
+    const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x);
+    const int consumed = base + j + 1;
+#pragma unroll
+    for (int q = 0; q < kLanePx / 2; ++q) {
+      const F2 power = power_at2(ta, tb, ch, sub2(fy[q], mu_y));
+      float pl, ph, tl, th, xl, xh;
+      split(power, pl, ph);
+      split(T[q], tl, th);
+      split(mul2(power, log2e), xl, xh);
+      const float vl_ = fminf(m.max_alpha, p1.y * ex2_approx(xl)), vh_ = fminf(m.max_alpha, p1.y * ex2_approx(xh));
+      float al, ah;
+      int vis_l = 1, vis_h = 1;
+      if (kGuard) {
+        al = vis_select_fwd_v(tl, m.T_thr, pl, p2.z, vl_, consumed, last[2 * q], vis_l);
+        ah = vis_select_fwd_v(th, m.T_thr, ph, p2.z, vh_, consumed, last[2 * q + 1], vis_h);
+      } else {
+        al = vis_select_fwd(tl, m.T_thr, pl, p2.z, vl_, consumed, last[2 * q]);
+        ah = vis_select_fwd(th, m.T_thr, ph, p2.z, vh_, consumed, last[2 * q + 1]);
+      }
+      const F2 alpha = f2(al, ah);
+      const F2 w = mul2(T[q], alpha);
+      if (kGuard) {
+        cr[q] = select2(vis_l, vis_h, fma2(w, col_r, cr[q]), cr[q]);
+        cg[q] = select2(vis_l, vis_h, fma2(w, col_g, cg[q]), cg[q]);
+        cb[q] = select2(vis_l, vis_h, fma2(w, col_b, cb[q]), cb[q]);
+      } else {
+        cr[q] = fma2(w, col_r, cr[q]);
+        cg[q] = fma2(w, col_g, cg[q]);
+        cb[q] = fma2(w, col_b, cb[q]);
+      }
+      T[q] = mul2(T[q], sub2(one, alpha));
+    }
+  }
+}
+
 template <bool kSave>
 __global__ void __launch_bounds__(kWarps * 32, 2)
     k_render_fwd_warp(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
@@ -187,12 +236,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       if (!__any_sync(kFullMask, live)) break;
       const int cnt = min(kWarpBatch, n - base);
       __syncwarp();
+      bool bad_color = false;
       if (lane < cnt) {
         float4 r[3];
         load_rec(rec, load_gi(ids, start + base + lane, m.BG, status, kSiteRender), r);
         my[lane][0] = r[0];
         my[lane][1] = r[1];
         my[lane][2] = r[2];
+        bad_color = !finite_rgb(r[1].z, r[1].w, r[2].x);
         if (kSave) {
           float4* dst = pair_rec + 3 * (size_t)(start + base + lane);
           dst[0] = r[0];
@@ -200,36 +251,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
           dst[2] = r[2];
         }
       }
+      const bool guard = __any_sync(kFullMask, bad_color);
       __syncwarp();
       if (!live) continue;
-      #pragma unroll 1
-      for (int j = 0; j < cnt; ++j) {
-        const float4 p0 = my[j][0];
-        const float4 p1 = my[j][1];
-        const float4 p2 = my[j][2];
-        const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
-        const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
-        const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x);
-        const int consumed = base + j + 1;
-#pragma unroll
-        for (int q = 0; q < kLanePx / 2; ++q) {
-          const F2 power = power_at2(ta, tb, ch, sub2(fy[q], mu_y));
-          float pl, ph, tl, th, xl, xh;
-          split(power, pl, ph);
-          split(T[q], tl, th);
-          split(mul2(power, log2e), xl, xh);
-          const float al = vis_select_fwd(tl, m.T_thr, pl, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xl)), consumed,
-                                          last[2 * q]);
-          const float ah = vis_select_fwd(th, m.T_thr, ph, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xh)), consumed,
-                                          last[2 * q + 1]);
-          const F2 alpha = f2(al, ah);
-          const F2 w = mul2(T[q], alpha);
-          cr[q] = fma2(w, col_r, cr[q]);
-          cg[q] = fma2(w, col_g, cg[q]);
-          cb[q] = fma2(w, col_b, cb[q]);
-          T[q] = mul2(T[q], sub2(one, alpha));
-        }
-      }
+      if (guard)
+        fwd_warp_batch<true>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
+      else
+        fwd_warp_batch<false>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
     }
     if (px < m.W) {
       const size_t pix0 = ((size_t)tc.b * m.H + py0) * m.W + px;
@@ -291,13 +319,57 @@ __device__ __forceinline__ bool long_chunk_live(const Meta& m, long long chunk) 
   return (long long)blockIdx.x + chunk * blockDim.x * (long long)gridDim.x < m.total_tiles;
 }
 
+// One staged batch of the CTA kernel over a thread's 2 packed pixels (kGuard:
+// as fwd_warp_batch). A warp leaves the batch once its 64 pixels are finished.
+template <bool kGuard>
+__device__ __forceinline__ void fwd_cta_batch(const Meta& m, const float4 (*recs)[3], int cnt, int base, float fx,
+                                              F2 fy, F2& T, F2& cr, F2& cg, F2& cb, int& last_l, int& last_h) {
+  const F2 one = f2(1.0f), log2e = f2(kLog2e);
+#pragma unroll 1
+  for (int j = 0; j < cnt; ++j) {
+    const float4 p0 = recs[j][0];
+    const float4 p1 = recs[j][1];
+    const float4 p2 = recs[j][2];
+    const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
+    const F2 power = power_at2(f2(pc.ta), f2(pc.tb), f2(pc.ch), sub2(fy, f2(p0.y)));
+    const int consumed = base + j + 1;
+    float pl, ph, xl, xh, tl, th;
+    split(T, tl, th);
+    if (!__any_sync(kFullMask, (tl > m.T_thr) | (th > m.T_thr))) break;
+    split(power, pl, ph);
+    split(mul2(power, log2e), xl, xh);
+    const float vl_ = fminf(m.max_alpha, p1.y * ex2_approx(xl)), vh_ = fminf(m.max_alpha, p1.y * ex2_approx(xh));
+    float al, ah;
+    int vis_l = 1, vis_h = 1;
+    if (kGuard) {
+      al = vis_select_fwd_v(tl, m.T_thr, pl, p2.z, vl_, consumed, last_l, vis_l);
+      ah = vis_select_fwd_v(th, m.T_thr, ph, p2.z, vh_, consumed, last_h, vis_h);
+    } else {
+      al = vis_select_fwd(tl, m.T_thr, pl, p2.z, vl_, consumed, last_l);
+      ah = vis_select_fwd(th, m.T_thr, ph, p2.z, vh_, consumed, last_h);
+    }
+    const F2 alpha = f2(al, ah);
+    const F2 w = mul2(T, alpha);
+    if (kGuard) {
+      cr = select2(vis_l, vis_h, fma2(w, f2(p1.z), cr), cr);
+      cg = select2(vis_l, vis_h, fma2(w, f2(p1.w), cg), cg);
+      cb = select2(vis_l, vis_h, fma2(w, f2(p2.x), cb), cb);
+    } else {
+      cr = fma2(w, f2(p1.z), cr);
+      cg = fma2(w, f2(p1.w), cg);
+      cb = fma2(w, f2(p2.x), cb);
+    }
+    T = mul2(T, sub2(one, alpha));
+  }
+}
+
 // CTA of kCtaThreads per long tile. A thread owns 2 pixels of one column (rows
 // r and r + 8), packed as one f32x2 pair, and runs the warp kernel's
 // branch-free record body on them, so the per-record work is amortised over 2
 // pixels and done with packed instructions. Records are staged kBatch at a time
 // in shared memory; the CTA stops early once no pixel is live.
 template <bool kSave>
-__global__ void __launch_bounds__(kCtaThreads)
+__global__ void __launch_bounds__(kCtaThreads, 8)
     k_render_fwd_cta(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                      const int32_t* __restrict__ ids, float* __restrict__ out, float* __restrict__ final_T,
                      int32_t* __restrict__ last_idx, uint32_t* __restrict__ status) {
@@ -327,34 +399,15 @@ __global__ void __launch_bounds__(kCtaThreads)
         const bool live = (tl > m.T_thr) | (th > m.T_thr);
         if (__syncthreads_count(live) == 0) break;
         const int cnt = min(kBatch, n - base);
-        for (int i = t; i < cnt; i += kCtaThreads)
+        bool bad_color = false;
+        for (int i = t; i < cnt; i += kCtaThreads) {
           load_rec(rec, load_gi(ids, start + base + i, m.BG, status, kSiteRender), s_rec[i]);
-        __syncthreads();
-#pragma unroll 1
-          for (int j = 0; j < cnt; ++j) {
-            const float4 p0 = s_rec[j][0];
-            const float4 p1 = s_rec[j][1];
-            const float4 p2 = s_rec[j][2];
-            const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
-            const F2 power = power_at2(f2(pc.ta), f2(pc.tb), f2(pc.ch), sub2(fy, f2(p0.y)));
-            const int consumed = base + j + 1;
-            float pl, ph, xl, xh;
-            split(T, tl, th);
-            // The warp leaves the batch once its 64 pixels are all finished.
-            if (!__any_sync(kFullMask, (tl > m.T_thr) | (th > m.T_thr))) break;
-            split(power, pl, ph);
-            split(mul2(power, log2e), xl, xh);
-            const float al =
-                vis_select_fwd(tl, m.T_thr, pl, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xl)), consumed, last_l);
-            const float ah =
-                vis_select_fwd(th, m.T_thr, ph, p2.z, fminf(m.max_alpha, p1.y * ex2_approx(xh)), consumed, last_h);
-            const F2 alpha = f2(al, ah);
-            const F2 w = mul2(T, alpha);
-            cr = fma2(w, f2(p1.z), cr);
-            cg = fma2(w, f2(p1.w), cg);
-            cb = fma2(w, f2(p2.x), cb);
-            T = mul2(T, sub2(one, alpha));
-          }
+          bad_color |= !finite_rgb(s_rec[i][1].z, s_rec[i][1].w, s_rec[i][2].x);
+        }
+        if (__syncthreads_or(bad_color))
+          fwd_cta_batch<true>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
+        else
+          fwd_cta_batch<false>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
         __syncthreads();  // s_rec is refilled by the next batch
       }
       float tv[2], rv[2], gv[2], bv[2];
@@ -422,9 +475,12 @@ __device__ __forceinline__ void pixel_vjp(const Meta& m, float dy, float power, 
 // (T_cur * rcp(1 - 0) = T_cur; gT + 0 * d = gT) and adds nothing to S.
 // gT advances as gT + alpha (dot_gc - gT), the same value as
 // alpha dot_gc + (1 - alpha) gT up to rounding. S[t] holds per-half partial sums.
+// Only gT can carry a non-finite colour into a pixel that does not see the
+// splat (the other terms are selected or multiplied by finite zeros); kGuard
+// selects it.
 // kClampOm: clamp 1 - alpha at eps (only needed when max_alpha > 1 - eps;
 // otherwise 1 - alpha >= 1 - max_alpha >= eps already).
-template <bool kClampOm>
+template <bool kClampOm, bool kGuard = false>
 __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int last_h, F2 dy, float pl, float ph,
                                            F2 op, float vis_thr, float sat_thr, F2 col_r, F2 col_g, F2 col_b,
                                            F2 gr, F2 gg, F2 gb, F2& T_cur, F2& gT, F2 (&S)[7]) {
@@ -433,9 +489,15 @@ __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int
   const F2 e = f2(ex2_approx(xl), ex2_approx(xh));
   float rl, rh;
   split(mul2(op, e), rl, rh);
-  int pass_l, pass_h;
-  const float al = vis_select_bwd(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l);
-  const float ah = vis_select_bwd(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h);
+  int pass_l, pass_h, vis_l = 1, vis_h = 1;
+  float al, ah;
+  if (kGuard) {
+    al = vis_select_bwd_v(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l, vis_l);
+    ah = vis_select_bwd_v(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h, vis_h);
+  } else {
+    al = vis_select_bwd(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l);
+    ah = vis_select_bwd(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h);
+  }
   const F2 alpha = f2(al, ah);
   float oml, omh;
   split(sub2(f2(1.0f), alpha), oml, omh);
@@ -462,7 +524,9 @@ __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int
   S[4] = fma2(gr, wc, S[4]);
   S[5] = fma2(gg, wc, S[5]);
   S[6] = fma2(gb, wc, S[6]);
-  gT = fma2(alpha, d, gT);
+  // kGuard (a non-finite colour among the staged records): d is NaN for every
+  // pixel, so gT moves only where the splat is visible.
+  gT = kGuard ? select2(vis_l, vis_h, fma2(alpha, d, gT), gT) : fma2(alpha, d, gT);
   T_cur = T_prev;
 }
 
@@ -597,6 +661,68 @@ __device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, f
   __syncwarp();
 }
 
+// The reverse walk over one short tile's records (rows row0 .. row0 + tile_last
+// of the warp's record buffer) for a lane's 8 pixels, with the per-record
+// gradient reduction. kGuard: a record's colour is not finite (pixel_vjp2).
+template <bool kClampOm, bool kGuard>
+__device__ __forceinline__ void bwd_warp_records(const Meta& m, BwdWarpSmem& W, int row0, int tile_last, int lane,
+                                                 float fx, const F2 (&fy)[kLanePx / 2], const F2 (&gr)[kLanePx / 2],
+                                                 const F2 (&gg)[kLanePx / 2], const F2 (&gb)[kLanePx / 2],
+                                                 F2 (&Tc)[kLanePx / 2], F2 (&gT)[kLanePx / 2],
+                                                 const int (&last)[kLanePx], uint32_t* __restrict__ status,
+                                                 float* __restrict__ grad_rec) {
+  const BwdRecs& R = W.rb;
+  int slot = 0;
+#pragma unroll 1
+  for (int j = tile_last - 1; j >= 0; --j) {
+    const float4 p0 = R.rec[row0 + j][0];
+    const float4 p1 = R.rec[row0 + j][1];
+    const float4 p2 = R.rec[row0 + j][2];
+    const float dx = __fsub_rn(fx, p0.x);
+    const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
+    const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
+    const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x), op = f2(p1.y);
+    F2 S[7];
+#pragma unroll
+    for (int t = 0; t < 7; ++t) S[t] = f2(0.0f);
+#pragma unroll
+    for (int q = 0; q < kLanePx / 2; ++q) {
+      const F2 dy = sub2(fy[q], mu_y);
+      const F2 power = power_at2(ta, tb, ch, dy);
+      float pl, ph;
+      split(power, pl, ph);
+      pixel_vjp2<kClampOm, kGuard>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z, p2.w, col_r, col_g,
+                                   col_b, gr[q], gg[q], gb[q], Tc[q], gT[q], S);
+    }
+    float Sv[7];
+#pragma unroll
+    for (int t = 0; t < 7; ++t) {
+      float lo, hi;
+      split(S[t], lo, hi);
+      Sv[t] = lo + hi;
+    }
+    float v[16];
+    vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
+    // Stage this splat's 9 lane values; every kRedChunk splats the warp
+    // sums the staged rows (one row per lane) and adds them to grad_rec.
+#pragma unroll
+    for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
+    if (lane == 0) {
+      int gi = R.ids[row0 + j];
+      if ((unsigned)gi >= (unsigned)m.BG) {
+        raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
+        gi = -1;
+      }
+      W.red_gi[slot] = gi;
+    }
+    if (++slot == kRedChunk) {
+      flush_red(W, slot, lane, grad_rec);
+      slot = 0;
+    }
+  }
+  if (slot > 0) flush_red(W, slot, lane, grad_rec);
+}
+
 template <bool kClampOm>
 __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
@@ -682,55 +808,16 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     cp_async_commit();
     if (work) {  // tiles above kBwdShortMax: k_render_bwd_cta finds them
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
-      int slot = 0;
-#pragma unroll 1
-      for (int j = tile_last - 1; j >= 0; --j) {
-        const float4 p0 = R.rec[row0 + j][0];
-        const float4 p1 = R.rec[row0 + j][1];
-        const float4 p2 = R.rec[row0 + j][2];
-        const float dx = __fsub_rn(fx, p0.x);
-        const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
-        const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
-        const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x), op = f2(p1.y);
-        F2 S[7];
-#pragma unroll
-        for (int t = 0; t < 7; ++t) S[t] = f2(0.0f);
-#pragma unroll
-        for (int q = 0; q < kLanePx / 2; ++q) {
-          const F2 dy = sub2(fy[q], mu_y);
-          const F2 power = power_at2(ta, tb, ch, dy);
-          float pl, ph;
-          split(power, pl, ph);
-          pixel_vjp2<kClampOm>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z, p2.w, col_r, col_g, col_b,
-                               gr[q], gg[q], gb[q], Tc[q], gT[q], S);
-        }
-        float Sv[7];
-#pragma unroll
-        for (int t = 0; t < 7; ++t) {
-          float lo, hi;
-          split(S[t], lo, hi);
-          Sv[t] = lo + hi;
-        }
-        float v[16];
-        vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
-        // Stage this splat's 9 lane values; every kRedChunk splats the warp
-        // sums the staged rows (one row per lane) and adds them to grad_rec.
-#pragma unroll
-        for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
-        if (lane == 0) {
-          int gi = R.ids[row0 + j];
-          if ((unsigned)gi >= (unsigned)m.BG) {
-            raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
-            gi = -1;
-          }
-          W.red_gi[slot] = gi;
-        }
-        if (++slot == kRedChunk) {
-          flush_red(W, slot, lane, grad_rec);
-          slot = 0;
-        }
-      }
-      if (slot > 0) flush_red(W, slot, lane, grad_rec);
+      // A non-finite colour among the records this tile walks takes the guarded body.
+      bool bad_color = false;
+      for (int q = lane; q < tile_last; q += 32)
+        bad_color |= !finite_rgb(W.rb.rec[row0 + q][1].z, W.rb.rec[row0 + q][1].w, W.rb.rec[row0 + q][2].x);
+      if (__any_sync(kFullMask, bad_color))
+        bwd_warp_records<kClampOm, true>(m, W, row0, tile_last, lane, fx, fy, gr, gg, gb, Tc, gT, last, status,
+                                         grad_rec);
+      else
+        bwd_warp_records<kClampOm, false>(m, W, row0, tile_last, lane, fx, fy, gr, gg, gb, Tc, gT, last, status,
+                                          grad_rec);
     }
     tile = nxt_tile;
     nxt_tile = nn_tile;
@@ -826,13 +913,16 @@ __global__ void __launch_bounds__(kCtaThreads)
       for (int bend = tile_last; bend > 0; bend -= kBatch) {
         const int bstart = max(0, bend - kBatch);
         const int cnt = bend - bstart;
+        bool bad_color = false;
         for (int i = t; i < cnt; i += kCtaThreads) {
           const int gi = load_gi(ids, start + bstart + i, m.BG, status, kSiteRenderBwd);
           s_gi[i] = gi;
           load_rec(rec, gi, s_rec[i]);
+          bad_color |= !finite_rgb(s_rec[i][1].z, s_rec[i][1].w, s_rec[i][2].x);
         }
         for (int i = t; i < cnt * kGradComps; i += kCtaThreads) (&s_acc[0][0])[i] = 0.0f;
-        __syncthreads();
+        // A non-finite colour in the batch: the guarded per-pixel VJP (CTA-uniform).
+        const bool guard = __syncthreads_or(bad_color);
         int slot = 0;
 #pragma unroll 1
         for (int jj = cnt - 1; jj >= 0; --jj) {
@@ -853,8 +943,12 @@ __global__ void __launch_bounds__(kCtaThreads)
           F2 S[7];
 #pragma unroll
           for (int q = 0; q < 7; ++q) S[q] = f2(0.0f);
-          pixel_vjp2<kClampOm>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w, f2(p1.z), f2(p1.w),
-                               f2(p2.x), gr, gg, gb, Tc, gT, S);
+          if (guard)
+            pixel_vjp2<kClampOm, true>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w, f2(p1.z),
+                                       f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
+          else
+            pixel_vjp2<kClampOm, false>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w, f2(p1.z),
+                                        f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
           float Sv[7];
 #pragma unroll
           for (int q = 0; q < 7; ++q) {

@@ -42,6 +42,8 @@ EXPORTED = (
     "gsb_version",
     "gsb_status_string",
     "gsb_kernel_launches",
+    "gsb_fma_probe_out_floats",
+    "gsb_fma_probe",
     "gsb_bin_prepare_workspace_size",
     "gsb_bin_prepare",
     "gsb_bin_count",
@@ -110,6 +112,8 @@ def load() -> C.CDLL:
         "gsb_version": (C.c_int, []),
         "gsb_status_string": (C.c_char_p, [C.c_int]),
         "gsb_kernel_launches": (C.c_uint64, []),
+        "gsb_fma_probe_out_floats": (i64, [i32]),
+        "gsb_fma_probe": (C.c_int, [i32, i32, i32, p, p]),
         "gsb_bin_prepare_workspace_size": (sz, [M]),
         "gsb_bin_prepare": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_bin_count": (C.c_int, [M, p, p, p, p, p, p, p, sz, p]),
@@ -134,7 +138,7 @@ def load() -> C.CDLL:
         "gsb_peer_handle": (C.c_int, [p, p]),
         "gsb_peer_open": (C.c_int, [p, C.POINTER(p)]),
         "gsb_peer_close": (C.c_int, [p]),
-        "gsb_peer_allreduce_sum": (C.c_int, [i32, i32, C.POINTER(p), i64, C.c_uint32, p, p]),
+        "gsb_peer_allreduce_sum": (C.c_int, [i32, i32, C.POINTER(p), i64, C.c_uint32, C.c_uint64, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

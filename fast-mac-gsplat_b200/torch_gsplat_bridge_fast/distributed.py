@@ -126,10 +126,16 @@ class PeerGradAllReduce(_FlatGrads):
     grads_as_views: after a call each parameter's .grad is a view into the
     summed buffer (no copy back), valid until the next call, as with DDP's
     gradient_as_bucket_view. False copies the sums into the .grad tensors.
+    wait_s: bound of each barrier wait inside the kernel. A rank that waits
+    longer, or that meets a peer that gave up, raises the kernel's error flag
+    (the sums of that call are then not valid on that rank). Each call copies
+    the flag to host memory without waiting, and the next call (or
+    check_errors()) raises RuntimeError before touching the buffer, so a failed
+    sum never reaches a second step silently.
     """
 
     def __init__(self, params: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None,
-                 grads_as_views: bool = True):
+                 grads_as_views: bool = True, wait_s: float = 10.0):
         from . import _native as N
 
         self._N = N
@@ -168,27 +174,46 @@ class PeerGradAllReduce(_FlatGrads):
         self._init_flat(params, flat=data[:total])
         self._data = data
         self.status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
+        self._status_host = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, pin_memory=True)
+        self._status_copied = torch.cuda.Event()
+        self._pending = False
         self.epoch = 0
+        self.wait_ns = max(1, int(wait_s * 1e9))
         self.grads_as_views = grads_as_views
 
     def __call__(self) -> None:
+        self._raise_if_failed(sync=False)
         self._pack()
         self.epoch += 1
-        stream = torch.cuda.current_stream(self._data.device).cuda_stream
+        dev = self._data.device
+        stream = torch.cuda.current_stream(dev)
         self._N.check(self._L.gsb_peer_allreduce_sum(self.rank, self.world, self._bases, self.padded,
-                                                     self.epoch & 0xFFFFFFFF, self._N.ptr(self.status), stream),
+                                                     self.epoch & 0xFFFFFFFF, self.wait_ns,
+                                                     self._N.ptr(self.status), stream.cuda_stream),
                       "gsb_peer_allreduce_sum")
+        self._status_host.copy_(self.status, non_blocking=True)
+        self._status_copied.record(stream)
+        self._pending = True
         if self.grads_as_views:
             self._unpack_views()
         else:
             self._unpack()
 
-    def check_errors(self) -> None:
-        """Raises if a call timed out waiting for a peer (synchronizes)."""
-        flags = int(self.status[self._N.GSB_STATUS_ERROR].item())
+    def _raise_if_failed(self, sync: bool) -> None:
+        if not self._pending:
+            return
+        if sync or not self._status_copied.query():
+            self._status_copied.synchronize()
+        self._pending = False
+        flags = int(self._status_host[self._N.GSB_STATUS_ERROR]) & 0xFFFFFFFF
         if flags:
-            raise RuntimeError(f"gsplat_b200 peer all-reduce: a rank did not reach a barrier in time "
-                               f"(device error flags {flags})")
+            raise RuntimeError(f"gsplat_b200 peer all-reduce (epoch {self.epoch}): a rank did not reach a barrier "
+                               f"in time or gave up the call; its sums are not valid (device error flags {flags})")
+
+    def check_errors(self) -> None:
+        """Raises if the last call timed out waiting for a peer or met a peer
+        that gave up (waits for that call's status copy)."""
+        self._raise_if_failed(sync=True)
 
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (collective: every rank calls it)."""

@@ -67,18 +67,26 @@ def get_runtime_shader_config() -> RuntimeShaderConfig:
 @dataclass(frozen=True)
 class RasterConfig:
     """Superset of the reference configs (root rasterize.py:15-23; v8_project3d
-    rasterize.py:55-67; v8 rasterize.py:65-82). `max_tile_pairs` is the root API's
-    name for the per-tile cap and overrides `max_fast_pairs` when given. Tiles
-    over the cap are rendered exactly (what the reference's overflow fallback
-    produces); with `enable_overflow_fallback=False` the reference's error is
-    raised instead. The v8 scheduling knobs (active tiles, stop-count mode,
-    pair budgets) are accepted and have no effect: they tune Metal launch
-    overhead, which the B200 pipeline does not have."""
+    rasterize.py:55-67; v8 rasterize.py:65-82).
+
+    Positional order follows the root API, whose package name this one keeps:
+    the 4th field is the root's per-tile cap `max_tile_pairs` (default 4096), so
+    `RasterConfig(h, w, 16, 4096)` works as it does there. The v8 name of the
+    cap, `max_fast_pairs` (default 2048), is a keyword field at the end; as in
+    v8 it is checked against the runtime fast cap (GSP_FAST_CAP). Fields 5 and
+    on keep both versions' positions. The cap in force (`pair_cap`) is the
+    smaller of the two. Tiles over the cap are rendered exactly (what the
+    reference's overflow fallback produces, and what the root kernel would
+    refuse); with `enable_overflow_fallback=False` the v8 error is raised
+    instead. The v8 scheduling knobs (active tiles, stop-count mode, pair
+    budgets) are accepted and have no effect: they tune Metal launch overhead
+    and per-tile capacities that the B200 pipeline (one global sort, per-pixel
+    stop state) does not have."""
 
     height: int
     width: int
     tile_size: int = 16
-    max_fast_pairs: int = 2048
+    max_tile_pairs: int = 4096
     alpha_threshold: float = 1.0 / 255.0
     transmittance_threshold: float = 1e-4
     background: Tuple[float, float, float] = (0.0, 0.0, 0.0)
@@ -86,17 +94,17 @@ class RasterConfig:
     batch_strategy: str = "auto"  # auto | flatten | serial
     batch_launch_limit_tiles: int = 262144
     batch_launch_limit_gaussians: int = 262144
-    max_tile_pairs: Optional[int] = None
     use_active_tiles: bool = False
     active_policy: str = "off"
     sort_active_tiles_by_count: bool = True
     stop_count_mode: str = "adaptive"
     stop_count_dense_threshold: int = 64
     max_pairs_per_launch: int = 0
+    max_fast_pairs: int = 2048
 
     @property
     def pair_cap(self) -> int:
-        return int(self.max_tile_pairs if self.max_tile_pairs is not None else self.max_fast_pairs)
+        return int(min(self.max_tile_pairs, self.max_fast_pairs))
 
 
 _validated: Dict[Any, RuntimeShaderConfig] = {}
@@ -131,13 +139,23 @@ def _runtime_validate_uncached(config: RasterConfig) -> RuntimeShaderConfig:
         )
     if config.tile_size != 16:
         raise ValueError("The B200 kernels are specialized for 16x16 tiles.")
-    if config.max_tile_pairs is None and config.max_fast_pairs > rt.fast_cap:
+    if config.max_fast_pairs > rt.fast_cap:
         raise ValueError(
             f"RasterConfig.max_fast_pairs={config.max_fast_pairs} exceeds compiled fast cap {rt.fast_cap}. "
             "Lower the runtime cap or set GSP_FAST_CAP before import."
         )
     if config.batch_strategy not in ("auto", "flatten", "serial"):
         raise ValueError("batch_strategy must be one of: auto, flatten, serial")
+    # The v8 policy knobs have no effect here, but invalid values are refused
+    # with v8's messages (variants/v8/torch_gsplat_bridge_v8/rasterize.py:97-106).
+    if config.active_policy not in ("off", "on", "auto"):
+        raise ValueError("active_policy must be one of: off, on, auto")
+    if config.stop_count_mode not in ("always", "never", "adaptive"):
+        raise ValueError("stop_count_mode must be one of: always, never, adaptive")
+    if config.stop_count_dense_threshold <= 0:
+        raise ValueError("stop_count_dense_threshold must be positive")
+    if config.max_pairs_per_launch < 0:
+        raise ValueError("max_pairs_per_launch must be non-negative")
     if config.height <= 0 or config.width <= 0:
         raise ValueError("height and width must be positive")
     return rt
@@ -679,17 +697,20 @@ def rasterize_pinhole_gaussians(means3d: Tensor, scales: Tensor, quats: Tensor, 
 # ---------------------------------------------------------------------------
 # Profiling (…/v8_project3d/…/rasterize.py:1006-1096)
 # ---------------------------------------------------------------------------
-def _tile_stop_counts(final_T: Tensor, last_idx: Tensor, counts: Tensor, config: RasterConfig) -> Tensor:
-    """Reference per-tile stop count from per-pixel state: max over valid pixels
-    of (saturated ? break index + 1 : tile count) (…kernels.metal:899-923)."""
-    B, H, W = final_T.shape
+def _tile_stop_counts(last_idx: Tensor, counts: Tensor, config: RasterConfig) -> Tensor:
+    """The reference's per-tile stop count (…kernels.metal:875-923) from the
+    per-pixel state: the max over the tile's in-image pixels of last_idx (the
+    entries a pixel walked: the saturating index + 1, or the tile's count), and
+    0 for an empty tile or one above the pair cap, which the reference's fast
+    kernel leaves to its overflow path (:876-884)."""
+    B, H, W = last_idx.shape
     ty, tx = (H + 15) // 16, (W + 15) // 16
     cnt = counts.view(B, ty, tx).to(torch.int64)
-    cnt_px = cnt.repeat_interleave(16, 1).repeat_interleave(16, 2)[:, :H, :W]
-    stop = torch.where(final_T <= config.transmittance_threshold, last_idx.to(torch.int64), cnt_px)
-    pad = torch.zeros((B, ty * 16, tx * 16), dtype=torch.int64, device=stop.device)
-    pad[:, :H, :W] = stop
-    return pad.view(B, ty, 16, tx, 16).amax(dim=(2, 4)).reshape(-1)
+    pad = torch.zeros((B, ty * 16, tx * 16), dtype=torch.int64, device=last_idx.device)
+    pad[:, :H, :W] = last_idx.to(torch.int64)
+    stop = pad.view(B, ty, 16, tx, 16).amax(dim=(2, 4))
+    stop = torch.where((cnt > 0) & (cnt <= int(config.pair_cap)), stop, torch.zeros_like(stop))
+    return stop.reshape(-1)
 
 
 @torch.no_grad()
@@ -715,7 +736,7 @@ def profile_projected_gaussians(means2d: Tensor, conics: Tensor, colors: Tensor,
             out, final_T, last_idx, _ = _render_forward(st, config, b1 - b0, save_state=True)
             if return_image:
                 images.append(out)
-            all_stops.append(_tile_stop_counts(final_T, last_idx, counts, config).cpu().to(torch.float32))
+            all_stops.append(_tile_stop_counts(last_idx, counts, config).cpu().to(torch.float32))
     counts_cpu = torch.cat(all_counts) if all_counts else torch.zeros(0)
     stats: Dict[str, Any] = {
         "batch_size": int(B),

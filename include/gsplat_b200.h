@@ -91,6 +91,13 @@ const char* gsb_status_string(int code);
 /* Number of kernels this library has launched in this process (all devices);
  * a diagnostic for launch accounting, no reference counterpart. */
 uint64_t gsb_kernel_launches(void);
+/* FP32 throughput probe, a measurement diagnostic with no reference counterpart:
+ * blocks_per_sm x SMs blocks of 256 threads, each thread running 8 independent
+ * chains of `iters` fused multiply-adds (packed != 0: fma.rn.f32x2, two per
+ * instruction). FLOPs per launch = gsb_fma_probe_out_floats(blocks_per_sm) x
+ * iters x 8 x 2 (x 2 packed). out receives one float per thread. */
+int64_t gsb_fma_probe_out_floats(int32_t blocks_per_sm);
+int gsb_fma_probe(int32_t packed, int32_t blocks_per_sm, int32_t iters, float* out, void* stream);
 
 /* ---- binning, phase 1 ---------------------------------------------------
  * Replaces: the depth sort + gathers of
@@ -243,11 +250,15 @@ int gsb_peer_close(void* base);
  * buffer. One kernel: a start barrier (every rank's data is final), rank r
  * adds shard r of all buffers over NVLink and stores the sum into all of them,
  * then an end barrier. Every rank calls it with the same n_floats and epoch;
- * epoch counts the calls from 1 and grows by one per call. Barrier waits are
- * bounded (about 10 s): a rank that does not arrive raises
- * GSB_DEVERR_PEER_TIMEOUT in status[GSB_STATUS_ERROR] and the kernel returns. */
+ * epoch counts the calls from 1 and grows by one per call. Each barrier wait is
+ * bounded by wait_ns nanoseconds (0: 10 s). A rank whose wait runs out, that
+ * finds a peer already at a later epoch, or that finds a peer's abort mark for
+ * this epoch, gives up the call: it marks its abort in every peer's buffer,
+ * raises GSB_DEVERR_PEER_TIMEOUT in status[GSB_STATUS_ERROR] and returns. After
+ * a call that raised it, the buffer's contents are undefined on every rank that
+ * reports it, and the group must not call again. */
 int gsb_peer_allreduce_sum(int32_t rank, int32_t world, void* const* bases, int64_t n_floats, uint32_t epoch,
-                           uint32_t* status, void* stream);
+                           uint64_t wait_ns, uint32_t* status, void* stream);
 
 /* ---- building blocks, exported for parity tests -------------------------
  * Stable LSD radix sort of (uint64 key, uint32 value) pairs on key bits

@@ -192,3 +192,35 @@ def full_forward_backward(meta: Meta, means2d, conics, colors, opacities, depths
     grads = unsort_grads(meta, perm, grad_rec)
     return dict(perm=perm, rec=rec, pair_offsets=off, P=P, keys=keys, ids=ids, tile_offsets=toff, image=img,
                 final_T=T, last_idx=last, grad_rec=grad_rec, grads=grads)
+
+
+def tile_stop_counts(meta: Meta, tile_offsets, last_idx, max_fast_pairs: int) -> np.ndarray:
+    """Per-tile stop count as tile_fast_forward_state writes it
+    (variants/v8_project3d/csrc/metal/gsplat_v8_project3d_kernels.metal:875-923): 0 for an
+    empty tile and for a tile above max_fast_pairs (left to the overflow path,
+    :876-884); otherwise the max over the tile's in-image pixels of local_stop,
+    the number of list entries the pixel walked (chunk_start + j + 1 up to and
+    including the entry that saturated it, :903-916). last_idx [B,H,W] is the C
+    oracle's per-pixel count of consumed entries, which is that local_stop."""
+    B, H, W = meta.batch_size, meta.height, meta.width
+    tx, ty = (W + 15) // 16, (H + 15) // 16
+    counts = np.diff(np.asarray(tile_offsets, dtype=np.int64)).reshape(B, ty, tx)
+    pad = np.zeros((B, ty * 16, tx * 16), dtype=np.int64)
+    pad[:, :H, :W] = np.asarray(last_idx, dtype=np.int64).reshape(B, H, W)
+    stop = pad.reshape(B, ty, 16, tx, 16).max(axis=(2, 4))
+    stop[(counts == 0) | (counts > int(max_fast_pairs))] = 0
+    return stop.reshape(-1)
+
+
+def profile_stop_stats(counts, stops) -> dict:
+    """The stop statistics of profile_projected_gaussians
+    (variants/v8_project3d/torch_gsplat_bridge_v8_project3d/rasterize.py:1070-1085) from
+    per-tile pair counts and stop counts."""
+    import torch
+
+    c = torch.as_tensor(np.asarray(counts), dtype=torch.float32)
+    s = torch.as_tensor(np.asarray(stops), dtype=torch.float32)
+    ratio = torch.where(c > 0, s / torch.clamp(c, min=1.0), torch.zeros_like(s))
+    return {"mean_stop_count": float(s.mean().item()), "p95_stop_count": float(torch.quantile(s, 0.95).item()),
+            "max_stop_count": int(s.max().item()), "mean_stop_ratio": float(ratio.mean().item()),
+            "p95_stop_ratio": float(torch.quantile(ratio, 0.95).item())}

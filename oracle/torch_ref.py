@@ -212,3 +212,51 @@ def sh_colors_reference(sh: Tensor, means3d: Tensor, camera_to_world: Tensor, de
     Y = sh_basis(d, degree)
     K = Y.shape[-1]
     return torch.clamp_min((Y[..., None] * sh[None, :, :K]).sum(-2) + 0.5, 0.0)
+
+
+# ---------------------------------------------------------------------------
+# The reference benchmark harness's accuracy check (benchmarks/benchmark_full_matrix.py),
+# so a renderer entry written for that harness can be driven here.
+# ---------------------------------------------------------------------------
+def clone_inputs(inputs, backward: bool):
+    """benchmark_full_matrix.py:155-161: detached contiguous copies, the four
+    differentiable inputs requiring grad when the mode has a backward."""
+    out = []
+    for i, t in enumerate(inputs):
+        c = t.detach().clone().contiguous()
+        c.requires_grad_(backward and i < 4)
+        out.append(c)
+    return tuple(out)
+
+
+def harness_measure_accuracy(run_renderer, renderer: str, base_inputs, height: int, width: int,
+                             mode: str = "forward_backward", max_work_items: int = 64_000_000):
+    """measure_accuracy (benchmark_full_matrix.py:380-427) for one renderer: the
+    renderer's image and (forward_backward) its gradients of out.square().mean()
+    against the dense torch reference on clones of the same inputs."""
+    B, G = base_inputs[0].shape[:2]
+    work = B * height * width * G
+    if work > max_work_items:
+        return {"accuracy_status": "skipped",
+                "accuracy_reason": f"work_items {work} exceeds accuracy limit {max_work_items}"}
+    backward = mode == "forward_backward"
+    run_inputs = clone_inputs(base_inputs, backward)
+    ref_inputs = clone_inputs(base_inputs, backward)
+    out = run_renderer(renderer, run_inputs, height, width)
+    ref = dense_reference(*ref_inputs, height, width)
+    err = (out - ref).detach().abs()
+    result = {"accuracy_status": "ok", "image_max_abs_error": float(err.max().item()),
+              "image_mean_abs_error": float(err.mean().item())}
+    if backward:
+        out.square().mean().backward()
+        ref.square().mean().backward()
+        worst = []
+        for name, got, want in zip(("means2d", "conics", "colors", "opacities"), run_inputs[:4], ref_inputs[:4]):
+            if got.grad is None or want.grad is None:
+                continue
+            e = (got.grad - want.grad).detach().abs()
+            result[f"grad_{name}_max_abs_error"] = float(e.max().item())
+            result[f"grad_{name}_mean_abs_error"] = float(e.mean().item())
+            worst.append(float(e.max().item()))
+        result["grad_max_abs_error"] = max(worst) if worst else 0.0
+    return result

@@ -106,12 +106,35 @@ def test_argument_validation_without_gpu():
 
 
 def test_raster_config_defaults_and_aliases():
+    from torch_gsplat_bridge_fast.rasterize import _runtime_validate
+
     cfg = tgb.RasterConfig(height=32, width=48)
     assert cfg.tile_size == 16 and cfg.max_fast_pairs == 2048 and cfg.enable_overflow_fallback
-    assert cfg.pair_cap == 2048
-    assert tgb.RasterConfig(32, 48, 16, 4096).pair_cap == 4096  # root positional order
-    assert tgb.RasterConfig(32, 48, max_tile_pairs=4096).pair_cap == 4096
-    tgb.RasterConfig(32, 48, use_active_tiles=True, active_policy="auto", stop_count_mode="always")
+    assert cfg.max_tile_pairs == 4096 and cfg.pair_cap == 2048
+    # The root API's positional form (torch_gsplat_bridge_fast/rasterize.py:15-23):
+    # the 4th field is max_tile_pairs = 4096, and the config validates.
+    root = tgb.RasterConfig(32, 48, 16, 4096, 1.0 / 255.0, 1e-4, (0.0, 0.0, 0.0))
+    assert root.max_tile_pairs == 4096 and root.background == (0.0, 0.0, 0.0)
+    _runtime_validate(root)
+    assert tgb.RasterConfig(32, 48, 16, 1000).pair_cap == 1000
+    # v8's fields 5-17 keep their positions (variants/v8/…/rasterize.py:65-82).
+    v8 = tgb.RasterConfig(32, 48, 16, 2048, 0.01, 1e-3, (1.0, 1.0, 1.0), False, "serial", 100, 200, True, "auto",
+                          False, "never", 32, 1000)
+    assert (v8.alpha_threshold, v8.transmittance_threshold, v8.background) == (0.01, 1e-3, (1.0, 1.0, 1.0))
+    assert (v8.enable_overflow_fallback, v8.batch_strategy, v8.batch_launch_limit_tiles) == (False, "serial", 100)
+    assert (v8.batch_launch_limit_gaussians, v8.use_active_tiles, v8.active_policy) == (200, True, "auto")
+    assert (v8.sort_active_tiles_by_count, v8.stop_count_mode, v8.stop_count_dense_threshold) == (False, "never", 32)
+    assert v8.max_pairs_per_launch == 1000 and v8.pair_cap == 2048
+    _runtime_validate(v8)
+    # v8's keyword cap, checked against the runtime fast cap as v8 does.
+    assert tgb.RasterConfig(32, 48, max_fast_pairs=512).pair_cap == 512
+    with pytest.raises(ValueError, match="exceeds compiled fast cap"):
+        _runtime_validate(tgb.RasterConfig(32, 48, max_fast_pairs=4096))
+    for bad, msg in ((dict(active_policy="sometimes"), "active_policy"), (dict(stop_count_mode="x"), "stop_count_mode"),
+                     (dict(stop_count_dense_threshold=0), "stop_count_dense_threshold"),
+                     (dict(max_pairs_per_launch=-1), "max_pairs_per_launch")):
+        with pytest.raises(ValueError, match=msg):
+            _runtime_validate(tgb.RasterConfig(32, 48, **bad))
 
 
 def test_runtime_shader_config_env(monkeypatch):

@@ -111,7 +111,10 @@ def _silent_worker(rank, world, port, out_q):
 
     from torch_gsplat_bridge_fast.distributed import SharedGradAllReduce
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    # The rendezvous may wait for a slow peer start; only the all-reduce's group
+    # has the short timeout under test.
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=4))
     err = None
     t0 = time.perf_counter()
     try:
@@ -119,7 +122,7 @@ def _silent_worker(rank, world, port, out_q):
             p = torch.zeros(64, requires_grad=True)
             p.grad = torch.ones(64)
             try:
-                SharedGradAllReduce([p])()
+                SharedGradAllReduce([p], group=group)()
             except Exception as e:  # the expected outcome
                 err = type(e).__name__
         else:

@@ -108,14 +108,29 @@ def test_peer_allreduce_four_ranks_matches_cpu_sum():
     _run(4)
 
 
-def test_peer_allreduce_wait_times_out_and_reports():
+class _RawInt32:
+    """A raw device allocation seen by torch.as_tensor as int32 (no copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+@pytest.mark.parametrize("case", ["timeout", "poisoned", "ahead"])
+def test_peer_allreduce_gives_up_and_reports(case):
     """Failure detection without a GPU fault: rank 0 of a 2-rank sum whose
-    second buffer (on the same GPU) belongs to a rank that never launches.
-    Its flags are never set, so the kernel's bounded waits (10 s at the start
-    barrier, 10 s at the end barrier) run out; it records
-    GSB_DEVERR_PEER_TIMEOUT in the status block and returns. Only this one
-    kernel waits, so no two waiting kernels share the GPU. The context stays
-    usable afterwards."""
+    second buffer (on the same GPU) belongs to a rank that never launches, so
+    only this one kernel waits and no two waiting kernels share the GPU.
+
+    timeout:  the peer's flags are never set; the start barrier's bounded wait
+              (1 s here) runs out.
+    poisoned: the peer has marked an abort of this epoch in rank 0's buffer
+              (it gave up the call); rank 0 must give up at once.
+    ahead:    the peer's start slot already holds a later epoch (it left this
+              call without rank 0); rank 0 must give up at once.
+    In every case the kernel records GSB_DEVERR_PEER_TIMEOUT at the start
+    barrier, marks its own abort in both buffers, leaves the data untouched and
+    returns; the context stays usable."""
     import ctypes as C
     import time
 
@@ -124,24 +139,44 @@ def test_peer_allreduce_wait_times_out_and_reports():
     L = N.load()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    n = 4096
+    n, epoch = 4096, 5
     bases = []
     for _ in range(2):
         b = C.c_void_p()
         N.check(L.gsb_peer_buffer_alloc(n * 4, C.byref(b)), "gsb_peer_buffer_alloc")
         bases.append(b.value)
     try:
+        flags = [torch.as_tensor(_RawInt32(b, N.GSB_PEER_FLAG_BYTES // 4), device=dev) for b in bases]
+        data = [torch.as_tensor(_RawInt32(b + N.GSB_PEER_FLAG_BYTES, n), device=dev).view(torch.float32)
+                for b in bases]
+        for r, d in enumerate(data):
+            d.copy_(torch.arange(n, device=dev, dtype=torch.float32) + 1000.0 * r)
+        if case == "poisoned":
+            flags[0][16 + 1] = epoch  # rank 1's abort slot in rank 0's buffer
+        elif case == "ahead":
+            flags[0][0 + 1] = epoch + 1  # rank 1's start slot in rank 0's buffer
+        torch.cuda.synchronize()
         status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=dev)
         arr = (C.c_void_p * 2)(*bases)
+        wait_ns = 1_000_000_000 if case == "timeout" else 4_000_000_000
         t0 = time.perf_counter()
-        N.check(L.gsb_peer_allreduce_sum(0, 2, arr, n, 1, N.ptr(status), N.stream_ptr(dev)), "gsb_peer_allreduce_sum")
+        N.check(L.gsb_peer_allreduce_sum(0, 2, arr, n, epoch, wait_ns, N.ptr(status), N.stream_ptr(dev)),
+                "gsb_peer_allreduce_sum")
         torch.cuda.synchronize()
         waited = time.perf_counter() - t0
-        flags = int(status[N.GSB_STATUS_ERROR].item())
-        assert flags & N.GSB_DEVERR_PEER_TIMEOUT, flags
-        assert int(status[N.GSB_STATUS_ERROR_SITE].item()) in (7, 8)  # start or end barrier
-        assert 9.0 < waited < 60.0, waited
-        assert "peer rank" in N.decode_device_error(flags, int(status[N.GSB_STATUS_ERROR_SITE].item()))
+        err = int(status[N.GSB_STATUS_ERROR].item())
+        assert err & N.GSB_DEVERR_PEER_TIMEOUT, err
+        assert int(status[N.GSB_STATUS_ERROR_SITE].item()) == 7  # the start barrier
+        if case == "timeout":
+            assert 0.9 < waited < 30.0, waited
+        else:
+            assert waited < 2.0, waited  # no wait for the 4 s limit
+        for f in flags:  # rank 0's abort mark for this epoch, in both buffers
+            assert int(f[16 + 0].item()) == epoch
+        assert int(flags[0][32].item()) == 0 and int(flags[0][33].item()) == 0  # counter and failure word reset
+        for r, d in enumerate(data):
+            assert torch.equal(d, torch.arange(n, device=dev, dtype=torch.float32) + 1000.0 * r)
+        assert "peer rank" in N.decode_device_error(err, 7)
         x = torch.arange(10, device=dev, dtype=torch.float32)
         assert float(x.sum().item()) == 45.0  # the context is still usable
     finally:

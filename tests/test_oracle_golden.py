@@ -230,3 +230,26 @@ def test_pixel_sampled_saturating_matches_reference(name, bg):
     assert max_abs(out.detach(), c["image"]) <= 1e-5
     for t, key in zip(ins[:4], ("g_means2d", "g_conics", "g_colors", "g_opacities")):
         assert rel_err(t.grad, c[key]) <= 1e-4, key
+
+
+def test_tile_stop_counts_follow_the_reference_definition():
+    """oracle.tile_stop_counts / profile_stop_stats restate the per-tile stop count
+    of tile_fast_forward_state (…kernels.metal:875-923: max over in-image pixels,
+    0 for empty tiles and tiles above max_fast_pairs) and the statistics of
+    profile_projected_gaussians (…/rasterize.py:1070-1085)."""
+    meta = O.Meta(20, 40, 1, 1)  # 2 x 3 tiles; the bottom row of tiles is 4 pixels high
+    counts = np.array([5, 0, 3000, 7, 2, 9], dtype=np.int64)
+    toff = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    last = np.zeros((1, 20, 40), dtype=np.int32)
+    last[0, 3, 5], last[0, 9, 1] = 4, 5  # tile 0 -> 5
+    last[0, 2, 20] = 1  # tile 1 is empty -> 0
+    last[0, 0, 33] = 3000  # tile 2 is above the cap -> 0
+    last[0, 17, 3] = 6  # tile 3 -> 6
+    last[0, 19, 39] = 9  # tile 5 -> 9 (tile 4 stays 0)
+    stops = O.tile_stop_counts(meta, toff, last, 2048)
+    assert stops.tolist() == [5, 0, 0, 6, 0, 9]
+    st = O.profile_stop_stats(counts, stops)
+    assert st["max_stop_count"] == 9 and abs(st["mean_stop_count"] - 20 / 6) < 1e-6
+    ratio = np.array([5 / 5, 0, 0, 6 / 7, 0, 9 / 9])
+    assert abs(st["mean_stop_ratio"] - ratio.mean()) < 1e-6
+    assert abs(st["p95_stop_ratio"] - float(np.quantile(ratio, 0.95))) < 1e-6
