@@ -400,36 +400,56 @@ __device__ __forceinline__ F2 select2(int vis_lo, int vis_hi, F2 v, F2 keep) {
   return f2(vis_lo ? vl : kl, vis_hi ? vh : kh);
 }
 
-// Backward form: vis = j < last && power <= 0 && power >= vis_thr; returns
-// vis ? value : 0 and pass = (vis && power < sat_thr) as 0/1.
+// Backward form: vis = j < last && power <= 0 && power >= vis_thr (kCheckLast
+// false drops the j < last term, for records every pixel of the warp reaches);
+// returns vis ? value : 0, and pass_mask = all ones when vis && power < sat_thr
+// else 0 (the caller ANDs it into the bits of a float, a select that also
+// clears a NaN). kWantVis also reports vis as 0/1 (the guarded loops).
+template <bool kCheckLast, bool kWantVis>
 __device__ __forceinline__ float vis_select_bwd(int j, int last, float power, float vis_thr, float sat_thr,
-                                                float value, int& pass) {
+                                                float value, unsigned& pass_mask, int& vis) {
   float r;
-  asm("{\n\t.reg .pred pv, ps;\n\t"
-      "setp.lt.s32 pv, %2, %3;\n\t"
-      "setp.le.and.f32 pv, %4, 0f00000000, pv;\n\t"
-      "setp.ge.and.f32 pv, %4, %5, pv;\n\t"
-      "setp.lt.and.f32 ps, %4, %6, pv;\n\t"
-      "selp.f32 %0, %7, 0f00000000, pv;\n\t"
-      "selp.b32 %1, 1, 0, ps;\n\t}"
-      : "=f"(r), "=r"(pass)
-      : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
-  return r;
-}
-// vis_select_bwd that also reports vis (0/1), for the guarded loops.
-__device__ __forceinline__ float vis_select_bwd_v(int j, int last, float power, float vis_thr, float sat_thr,
-                                                  float value, int& pass, int& vis) {
-  float r;
-  asm("{\n\t.reg .pred pv, ps;\n\t"
-      "setp.lt.s32 pv, %3, %4;\n\t"
-      "setp.le.and.f32 pv, %5, 0f00000000, pv;\n\t"
-      "setp.ge.and.f32 pv, %5, %6, pv;\n\t"
-      "setp.lt.and.f32 ps, %5, %7, pv;\n\t"
-      "selp.f32 %0, %8, 0f00000000, pv;\n\t"
-      "selp.b32 %1, 1, 0, ps;\n\t"
-      "selp.b32 %2, 1, 0, pv;\n\t}"
-      : "=f"(r), "=r"(pass), "=r"(vis)
-      : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  if (kCheckLast && kWantVis) {
+    asm("{\n\t.reg .pred pv, ps;\n\t"
+        "setp.lt.s32 pv, %3, %4;\n\t"
+        "setp.le.and.f32 pv, %5, 0f00000000, pv;\n\t"
+        "setp.ge.and.f32 pv, %5, %6, pv;\n\t"
+        "setp.lt.and.f32 ps, %5, %7, pv;\n\t"
+        "selp.f32 %0, %8, 0f00000000, pv;\n\t"
+        "selp.b32 %1, -1, 0, ps;\n\t"
+        "selp.b32 %2, 1, 0, pv;\n\t}"
+        : "=f"(r), "=r"(pass_mask), "=r"(vis)
+        : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  } else if (kCheckLast) {
+    asm("{\n\t.reg .pred pv, ps;\n\t"
+        "setp.lt.s32 pv, %2, %3;\n\t"
+        "setp.le.and.f32 pv, %4, 0f00000000, pv;\n\t"
+        "setp.ge.and.f32 pv, %4, %5, pv;\n\t"
+        "setp.lt.and.f32 ps, %4, %6, pv;\n\t"
+        "selp.f32 %0, %7, 0f00000000, pv;\n\t"
+        "selp.b32 %1, -1, 0, ps;\n\t}"
+        : "=f"(r), "=r"(pass_mask)
+        : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  } else if (kWantVis) {
+    asm("{\n\t.reg .pred pv, ps;\n\t"
+        "setp.le.f32 pv, %3, 0f00000000;\n\t"
+        "setp.ge.and.f32 pv, %3, %4, pv;\n\t"
+        "setp.lt.and.f32 ps, %3, %5, pv;\n\t"
+        "selp.f32 %0, %6, 0f00000000, pv;\n\t"
+        "selp.b32 %1, -1, 0, ps;\n\t"
+        "selp.b32 %2, 1, 0, pv;\n\t}"
+        : "=f"(r), "=r"(pass_mask), "=r"(vis)
+        : "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  } else {
+    asm("{\n\t.reg .pred pv, ps;\n\t"
+        "setp.le.f32 pv, %2, 0f00000000;\n\t"
+        "setp.ge.and.f32 pv, %2, %3, pv;\n\t"
+        "setp.lt.and.f32 ps, %2, %4, pv;\n\t"
+        "selp.f32 %0, %5, 0f00000000, pv;\n\t"
+        "selp.b32 %1, -1, 0, ps;\n\t}"
+        : "=f"(r), "=r"(pass_mask)
+        : "f"(power), "f"(vis_thr), "f"(sat_thr), "f"(value));
+  }
   return r;
 }
 

@@ -50,6 +50,7 @@ template <typename K, int ITEMS>
 struct OnesweepSmem {
   K keys[kSortThreads * ITEMS];
   uint32_t vals[kSortThreads * ITEMS];
+  uint32_t vstage[kSortThreads * ITEMS];  // the partition's values in input order (cp.async)
   uint32_t warp_hist[kSortWarps][kRadix];  // per-warp digit counts, then exclusive over warps
   uint32_t local_base[kRadix];             // exclusive scan of the partition's digit counts
   uint32_t global_base[kRadix];            // digit base + look-back exclusive prefix
@@ -67,7 +68,7 @@ struct OnesweepSmem {
 // look-back resolves), then written out by consecutive threads, so each
 // digit's run leaves the CTA as contiguous stores.
 template <typename K, int ITEMS>
-__global__ void __launch_bounds__(kSortThreads)
+__global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
     rs_onesweep(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                 K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
                 int shift, int bits, const uint32_t* __restrict__ hist,
@@ -89,14 +90,17 @@ __global__ void __launch_bounds__(kSortThreads)
   const int64_t tile0 = (int64_t)part * kTile;
   const int64_t seg = tile0 + (int64_t)warp * (32 * ITEMS);
   K k[ITEMS];
-  uint32_t v[ITEMS];
   uint32_t rank[ITEMS];
   const uint32_t lt_mask = (1u << lane) - 1u;
+  {
+    const int valid = (int)min((int64_t)kTile, n - tile0);
+    for (int e = tid; e < valid; e += kSortThreads) cp_async4(&sm.vstage[e], vals_in + tile0 + e);
+    cp_async_commit();
+  }
 #pragma unroll
   for (int i = 0; i < ITEMS; ++i) {
     const int64_t idx = seg + i * 32 + lane;
     k[i] = idx < n ? keys_in[idx] : K(0);
-    v[i] = idx < n ? vals_in[idx] : 0u;
   }
   // Exclusive digit bases of this pass (the histogram load overlaps the key loads).
   uint32_t digit_base;
@@ -175,6 +179,7 @@ __global__ void __launch_bounds__(kSortThreads)
     for (int w = 0; w < kSortWarps; ++w) wsum += (w < warp) ? sm.scan[w] : 0u;
     sm.local_base[t] = wsum + x - sum;
   }
+  cp_async_wait<0>();
   __syncthreads();
   // Stage the partition in digit order.
 #pragma unroll
@@ -184,7 +189,7 @@ __global__ void __launch_bounds__(kSortThreads)
       const uint32_t d = (uint32_t)(k[i] >> shift) & dmask;
       const uint32_t lp = sm.local_base[d] + sm.warp_hist[warp][d] + rank[i];
       sm.keys[lp] = k[i];
-      sm.vals[lp] = v[i];
+      sm.vals[lp] = sm.vstage[warp * 32 * ITEMS + i * 32 + lane];
     }
   }
   // Decoupled look-back for digit t.

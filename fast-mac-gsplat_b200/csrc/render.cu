@@ -198,10 +198,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   pdl_wait();
   pdl_trigger();
   __shared__ float4 s_rec[kWarps][kWarpBatch][3];
+  __shared__ __align__(16) float s_out[kWarps][kTilePixels * 3];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float4(*my)[3] = s_rec[warp];
+  float* srgb = s_out[warp];
   const int stride = gridDim.x * kWarps;
-  const F2 one = f2(1.0f), log2e = f2(kLog2e);
   for (int tile = blockIdx.x * kWarps + warp; tile < m.total_tiles; tile += stride) {
     const int start = __ldg(&toff[tile]);
     const int n = __ldg(&toff[tile + 1]) - start;
@@ -259,7 +260,39 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       else
         fwd_warp_batch<false>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
     }
-    if (px < m.W) {
+    const bool full = (tc.tx * kTile + kTile <= m.W) && (tc.ty * kTile + kTile <= m.H) && ((m.W & 3) == 0);
+    if (full) {
+      const size_t pix0 = ((size_t)tc.b * m.H + py0) * m.W + px;
+#pragma unroll
+      for (int q = 0; q < kLanePx / 2; ++q) {
+        float tv[2], rv[2], gv[2], bv[2];
+        split(T[q], tv[0], tv[1]);
+        split(cr[q], rv[0], rv[1]);
+        split(cg[q], gv[0], gv[1]);
+        split(cb[q], bv[0], bv[1]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int idx = ((lane >> 4) + 4 * q + 2 * h) * kTile + (lane & 15);
+          srgb[3 * idx + 0] = fmaf(tv[h], m.bg_r, rv[h]);
+          srgb[3 * idx + 1] = fmaf(tv[h], m.bg_g, gv[h]);
+          srgb[3 * idx + 2] = fmaf(tv[h], m.bg_b, bv[h]);
+          if (kSave) {
+            const size_t pix = pix0 + (size_t)(4 * q + 2 * h) * (size_t)m.W;
+            final_T[pix] = tv[h];
+            last_idx[pix] = last[2 * q + h];
+          }
+        }
+      }
+      __syncwarp();
+      const size_t row0 = ((size_t)tc.b * m.H + tc.ty * kTile) * m.W + tc.tx * kTile;
+#pragma unroll
+      for (int i = 0; i < 6; ++i) {  // 16 rows x 12 float4 = 192 = 6 per lane
+        const int qq = lane + 32 * i, r = qq / 12, k = qq - r * 12;
+        const float4 v = *reinterpret_cast<const float4*>(&srgb[r * 48 + 4 * k]);
+        *reinterpret_cast<float4*>(out + 3 * (row0 + (size_t)r * m.W) + 4 * k) = v;
+      }
+      __syncwarp();
+    } else if (px < m.W) {
       const size_t pix0 = ((size_t)tc.b * m.H + py0) * m.W + px;
 #pragma unroll
       for (int q = 0; q < kLanePx / 2; ++q) {
@@ -289,7 +322,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 
 // The CTA kernels find their long tiles themselves (no list, counter or
 // memset between the warp and CTA kernels): in chunk k, thread i of CTA b
-// checks tile b + (256k + i) * gridDim.x, so the long tiles of a clustered
+// checks tile b + (blockDim.x * k + i) * gridDim.x (blockDim.x = kCtaThreads),
+// so the long tiles of a clustered
 // scene spread over all CTAs. The tiles found are compacted into s_long (one
 // ballot per warp); a tile is long when short_max < pairs <= long_max. Returns
 // how many. All threads call it; it ends with a barrier.
@@ -480,7 +514,7 @@ __device__ __forceinline__ void pixel_vjp(const Meta& m, float dy, float power, 
 // selects it.
 // kClampOm: clamp 1 - alpha at eps (only needed when max_alpha > 1 - eps;
 // otherwise 1 - alpha >= 1 - max_alpha >= eps already).
-template <bool kClampOm, bool kGuard = false>
+template <bool kClampOm, bool kGuard, bool kCheckLast, bool kFirst>
 __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int last_h, F2 dy, float pl, float ph,
                                            F2 op, float vis_thr, float sat_thr, F2 col_r, F2 col_g, F2 col_b,
                                            F2 gr, F2 gg, F2 gb, F2& T_cur, F2& gT, F2 (&S)[7]) {
@@ -489,15 +523,12 @@ __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int
   const F2 e = f2(ex2_approx(xl), ex2_approx(xh));
   float rl, rh;
   split(mul2(op, e), rl, rh);
-  int pass_l, pass_h, vis_l = 1, vis_h = 1;
-  float al, ah;
-  if (kGuard) {
-    al = vis_select_bwd_v(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l, vis_l);
-    ah = vis_select_bwd_v(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h, vis_h);
-  } else {
-    al = vis_select_bwd(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl), pass_l);
-    ah = vis_select_bwd(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh), pass_h);
-  }
+  unsigned pass_l, pass_h;
+  int vis_l = 1, vis_h = 1;
+  const float al = vis_select_bwd<kCheckLast, kGuard>(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl),
+                                                      pass_l, vis_l);
+  const float ah = vis_select_bwd<kCheckLast, kGuard>(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh),
+                                                      pass_h, vis_h);
   const F2 alpha = f2(al, ah);
   float oml, omh;
   split(sub2(f2(1.0f), alpha), oml, omh);
@@ -511,19 +542,30 @@ __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int
   const F2 g_alpha = mul2(T_prev, d);
   const F2 wc = mul2(T_prev, alpha);
   // raw < max_alpha (power below the saturation log-threshold) passes g_alpha
-  // to raw: d op = g_alpha e, d power = g_alpha raw = (g_alpha e) op.
+  // to raw: d op = g_alpha e, d power = g_alpha raw = (g_alpha e) op. The gate
+  // is an AND of the float bits with the pass mask.
   float gel, geh;
   split(mul2(g_alpha, e), gel, geh);
-  const F2 ge = f2(pass_l ? gel : 0.0f, pass_h ? geh : 0.0f);
+  const F2 ge = f2(__uint_as_float(__float_as_uint(gel) & pass_l), __uint_as_float(__float_as_uint(geh) & pass_h));
   const F2 gp = mul2(ge, op);
-  S[0] = add2(S[0], gp);
   const F2 gpdy = mul2(gp, dy);
-  S[1] = add2(S[1], gpdy);
-  S[2] = fma2(gpdy, dy, S[2]);
-  S[3] = add2(S[3], ge);
-  S[4] = fma2(gr, wc, S[4]);
-  S[5] = fma2(gg, wc, S[5]);
-  S[6] = fma2(gb, wc, S[6]);
+  if (kFirst) {  // the lane's first pixel pair of this record starts the sums
+    S[0] = gp;
+    S[1] = gpdy;
+    S[2] = mul2(gpdy, dy);
+    S[3] = ge;
+    S[4] = mul2(gr, wc);
+    S[5] = mul2(gg, wc);
+    S[6] = mul2(gb, wc);
+  } else {
+    S[0] = add2(S[0], gp);
+    S[1] = add2(S[1], gpdy);
+    S[2] = fma2(gpdy, dy, S[2]);
+    S[3] = add2(S[3], ge);
+    S[4] = fma2(gr, wc, S[4]);
+    S[5] = fma2(gg, wc, S[5]);
+    S[6] = fma2(gb, wc, S[6]);
+  }
   // kGuard (a non-finite colour among the staged records): d is NaN for every
   // pixel, so gT moves only where the splat is visible.
   gT = kGuard ? select2(vis_l, vis_h, fma2(alpha, d, gT), gT) : fma2(alpha, d, gT);
@@ -661,65 +703,89 @@ __device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, f
   __syncwarp();
 }
 
-// The reverse walk over one short tile's records (rows row0 .. row0 + tile_last
-// of the warp's record buffer) for a lane's 8 pixels, with the per-record
-// gradient reduction. kGuard: a record's colour is not finite (pixel_vjp2).
-template <bool kClampOm, bool kGuard>
-__device__ __forceinline__ void bwd_warp_records(const Meta& m, BwdWarpSmem& W, int row0, int tile_last, int lane,
-                                                 float fx, const F2 (&fy)[kLanePx / 2], const F2 (&gr)[kLanePx / 2],
-                                                 const F2 (&gg)[kLanePx / 2], const F2 (&gb)[kLanePx / 2],
-                                                 F2 (&Tc)[kLanePx / 2], F2 (&gT)[kLanePx / 2],
-                                                 const int (&last)[kLanePx], uint32_t* __restrict__ status,
-                                                 float* __restrict__ grad_rec) {
+// One record (row row0 + j of the warp's record buffer) of the reverse walk for
+// a lane's 8 pixels, with the per-record gradient reduction staged every
+// kRedChunk records. kGuard: a record's colour is not finite (pixel_vjp2).
+// kCheckLast: some pixel of the warp stops before this record (j >= the
+// warp's smallest last_idx), so each pixel tests j < last.
+template <bool kClampOm, bool kGuard, bool kCheckLast>
+__device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, int row0, int j, int lane, float fx,
+                                                const F2 (&fy)[kLanePx / 2], const F2 (&gr)[kLanePx / 2],
+                                                const F2 (&gg)[kLanePx / 2], const F2 (&gb)[kLanePx / 2],
+                                                F2 (&Tc)[kLanePx / 2], F2 (&gT)[kLanePx / 2],
+                                                const int (&last)[kLanePx], int& slot, uint32_t* __restrict__ status,
+                                                float* __restrict__ grad_rec) {
   const BwdRecs& R = W.rb;
-  int slot = 0;
-#pragma unroll 1
-  for (int j = tile_last - 1; j >= 0; --j) {
-    const float4 p0 = R.rec[row0 + j][0];
-    const float4 p1 = R.rec[row0 + j][1];
-    const float4 p2 = R.rec[row0 + j][2];
-    const float dx = __fsub_rn(fx, p0.x);
-    const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
-    const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
-    const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x), op = f2(p1.y);
-    F2 S[7];
+  const float4 p0 = R.rec[row0 + j][0];
+  const float4 p1 = R.rec[row0 + j][1];
+  const float4 p2 = R.rec[row0 + j][2];
+  const float dx = __fsub_rn(fx, p0.x);
+  const PowerCol pc = power_col(p0.z, p0.w, p1.x, dx);
+  const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
+  const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x), op = f2(p1.y);
+  F2 S[7];
 #pragma unroll
-    for (int t = 0; t < 7; ++t) S[t] = f2(0.0f);
-#pragma unroll
-    for (int q = 0; q < kLanePx / 2; ++q) {
-      const F2 dy = sub2(fy[q], mu_y);
-      const F2 power = power_at2(ta, tb, ch, dy);
-      float pl, ph;
-      split(power, pl, ph);
-      pixel_vjp2<kClampOm, kGuard>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z, p2.w, col_r, col_g,
-                                   col_b, gr[q], gg[q], gb[q], Tc[q], gT[q], S);
-    }
-    float Sv[7];
-#pragma unroll
-    for (int t = 0; t < 7; ++t) {
-      float lo, hi;
-      split(S[t], lo, hi);
-      Sv[t] = lo + hi;
-    }
-    float v[16];
-    vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
-    // Stage this splat's 9 lane values; every kRedChunk splats the warp
-    // sums the staged rows (one row per lane) and adds them to grad_rec.
-#pragma unroll
-    for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
-    if (lane == 0) {
-      int gi = R.ids[row0 + j];
-      if ((unsigned)gi >= (unsigned)m.BG) {
-        raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
-        gi = -1;
-      }
-      W.red_gi[slot] = gi;
-    }
-    if (++slot == kRedChunk) {
-      flush_red(W, slot, lane, grad_rec);
-      slot = 0;
-    }
+  for (int q = 0; q < kLanePx / 2; ++q) {
+    const F2 dy = sub2(fy[q], mu_y);
+    const F2 power = power_at2(ta, tb, ch, dy);
+    float pl, ph;
+    split(power, pl, ph);
+    if (q == 0)
+      pixel_vjp2<kClampOm, kGuard, kCheckLast, true>(m, j, last[0], last[1], dy, pl, ph, op, p2.z, p2.w, col_r,
+                                                     col_g, col_b, gr[0], gg[0], gb[0], Tc[0], gT[0], S);
+    else
+      pixel_vjp2<kClampOm, kGuard, kCheckLast, false>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z,
+                                                      p2.w, col_r, col_g, col_b, gr[q], gg[q], gb[q], Tc[q], gT[q],
+                                                      S);
   }
+  float Sv[7];
+#pragma unroll
+  for (int t = 0; t < 7; ++t) {
+    float lo, hi;
+    split(S[t], lo, hi);
+    Sv[t] = lo + hi;
+  }
+  float v[16];
+  vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
+  // Stage this splat's 9 lane values; every kRedChunk splats the warp
+  // sums the staged rows (one row per lane) and adds them to grad_rec.
+#pragma unroll
+  for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
+  if (lane == 0) {
+    int gi = R.ids[row0 + j];
+    if ((unsigned)gi >= (unsigned)m.BG) {
+      raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
+      gi = -1;
+    }
+    W.red_gi[slot] = gi;
+  }
+  if (++slot == kRedChunk) {
+    flush_red(W, slot, lane, grad_rec);
+    slot = 0;
+  }
+}
+
+// The reverse walk over one short tile's records (rows row0 .. row0 +
+// tile_last of the warp's record buffer). Records at or past lmin (the warp's
+// smallest last_idx) test each pixel's stop; the ones before it are reached by
+// every pixel and skip that test.
+template <bool kClampOm, bool kGuard>
+__device__ __forceinline__ void bwd_warp_records(const Meta& m, BwdWarpSmem& W, int row0, int tile_last, int lmin,
+                                                 int lane, float fx, const F2 (&fy)[kLanePx / 2],
+                                                 const F2 (&gr)[kLanePx / 2], const F2 (&gg)[kLanePx / 2],
+                                                 const F2 (&gb)[kLanePx / 2], F2 (&Tc)[kLanePx / 2],
+                                                 F2 (&gT)[kLanePx / 2], const int (&last)[kLanePx],
+                                                 uint32_t* __restrict__ status, float* __restrict__ grad_rec) {
+  int slot = 0;
+  int j = tile_last - 1;
+#pragma unroll 1
+  for (; j >= lmin; --j)
+    bwd_warp_record<kClampOm, kGuard, true>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
+                                            grad_rec);
+#pragma unroll 1
+  for (; j >= 0; --j)
+    bwd_warp_record<kClampOm, kGuard, false>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
+                                             grad_rec);
   if (slot > 0) flush_red(W, slot, lane, grad_rec);
 }
 
@@ -781,7 +847,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     // Pair q holds rows py0 + 4q and py0 + 4q + 2 (see the forward kernel).
     F2 fy[kLanePx / 2], gr[kLanePx / 2], gg[kLanePx / 2], gb[kLanePx / 2], Tc[kLanePx / 2], gT[kLanePx / 2];
     int last[kLanePx];
-    int lmax = 0;
+    int lmax = 0, lmin = n;
     if (work) {
 #pragma unroll
       for (int q = 0; q < kLanePx / 2; ++q) {
@@ -796,6 +862,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
         last[2 * q] = min(W.st.last[pl], n);
         last[2 * q + 1] = min(W.st.last[ph], n);
         lmax = max(lmax, max(last[2 * q], last[2 * q + 1]));
+        lmin = min(lmin, min(last[2 * q], last[2 * q + 1]));
       }
     }
     __syncwarp();  // W.st is read: the next tile's prefetch may overwrite it
@@ -808,16 +875,17 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     cp_async_commit();
     if (work) {  // tiles above kBwdShortMax: k_render_bwd_cta finds them
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
+      const int warp_lmin = __reduce_min_sync(kFullMask, lmin);
       // A non-finite colour among the records this tile walks takes the guarded body.
       bool bad_color = false;
       for (int q = lane; q < tile_last; q += 32)
         bad_color |= !finite_rgb(W.rb.rec[row0 + q][1].z, W.rb.rec[row0 + q][1].w, W.rb.rec[row0 + q][2].x);
       if (__any_sync(kFullMask, bad_color))
-        bwd_warp_records<kClampOm, true>(m, W, row0, tile_last, lane, fx, fy, gr, gg, gb, Tc, gT, last, status,
-                                         grad_rec);
+        bwd_warp_records<kClampOm, true>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT, last,
+                                         status, grad_rec);
       else
-        bwd_warp_records<kClampOm, false>(m, W, row0, tile_last, lane, fx, fy, gr, gg, gb, Tc, gT, last, status,
-                                          grad_rec);
+        bwd_warp_records<kClampOm, false>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT, last,
+                                          status, grad_rec);
     }
     tile = nxt_tile;
     nxt_tile = nn_tile;
@@ -941,14 +1009,12 @@ __global__ void __launch_bounds__(kCtaThreads)
           const bool vis = ((j < lastv[0]) & (pl <= 0.0f) & (pl >= p2.z)) | ((j < lastv[1]) & (ph <= 0.0f) & (ph >= p2.z));
           if (!__any_sync(kFullMask, vis)) continue;
           F2 S[7];
-#pragma unroll
-          for (int q = 0; q < 7; ++q) S[q] = f2(0.0f);
           if (guard)
-            pixel_vjp2<kClampOm, true>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w, f2(p1.z),
-                                       f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
+            pixel_vjp2<kClampOm, true, true, true>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w,
+                                                   f2(p1.z), f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
           else
-            pixel_vjp2<kClampOm, false>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w, f2(p1.z),
-                                        f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
+            pixel_vjp2<kClampOm, false, true, true>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w,
+                                                    f2(p1.z), f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
           float Sv[7];
 #pragma unroll
           for (int q = 0; q < 7; ++q) {
