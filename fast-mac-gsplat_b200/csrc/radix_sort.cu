@@ -18,7 +18,12 @@ constexpr uint32_t kValueMask = 0x3fffffffu;
 constexpr int kMaxPasses = 8;
 constexpr int kLookWin = 8;  // predecessors read per look-back step
 
-// Histograms of every digit pass in one read of the keys.
+// Histograms of every digit pass in one read of the keys. A thread takes
+// kHistItems consecutive keys per round and counts runs of equal digits before
+// touching the shared histogram, so clustered keys (a tile sort's high digit is
+// constant over long stretches) cost one shared atomic per run instead of one
+// per key on a few hot counters.
+constexpr int kHistItems = 16;
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads)
     rs_histogram(const K* __restrict__ keys, int64_t n, int begin_bit, int passes,
@@ -28,13 +33,45 @@ __global__ void __launch_bounds__(kSortThreads)
   __shared__ uint32_t s_hist[kMaxPasses][kRadix];
   for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) s_hist[i / kRadix][i % kRadix] = 0;
   __syncthreads();
-  const int64_t stride = (int64_t)gridDim.x * kSortThreads;
-  for (int64_t i = (int64_t)blockIdx.x * kSortThreads + threadIdx.x; i < n; i += stride) {
-    const K k = keys[i];
+  const int64_t stride = (int64_t)gridDim.x * kSortThreads * kHistItems;
+  // 16-byte loads need a 16-byte aligned key array (a caller's pointer to the
+  // exported sort may not be); otherwise the keys are read one by one.
+  const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15u) == 0u;
+  for (int64_t i0 = ((int64_t)blockIdx.x * kSortThreads + threadIdx.x) * kHistItems; i0 < n; i0 += stride) {
+    K k[kHistItems];
+    const int cnt = (int)min((int64_t)kHistItems, n - i0);
+    if (cnt == kHistItems && vec) {
+      constexpr int kPer = 16 / sizeof(K);
+#pragma unroll
+      for (int v = 0; v < kHistItems / kPer; ++v) {
+        const uint4 q = reinterpret_cast<const uint4*>(keys + i0)[v];
+        const K* qk = reinterpret_cast<const K*>(&q);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) k[v * kPer + u] = qk[u];
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < kHistItems; ++u) k[u] = u < cnt ? keys[i0 + u] : K(0);
+    }
     for (int p = 0; p < passes; ++p) {
       const int bits = (p == passes - 1) ? last_bits : kRadixBits;
-      const uint32_t d = (uint32_t)(k >> (begin_bit + p * kRadixBits)) & ((1u << bits) - 1u);
-      atomicAdd(&s_hist[p][d], 1u);
+      const int sh = begin_bit + p * kRadixBits;
+      const uint32_t dm = (1u << bits) - 1u;
+      uint32_t run_d = (uint32_t)(k[0] >> sh) & dm, run_n = 1;
+#pragma unroll
+      for (int u = 1; u < kHistItems; ++u) {
+        if (u < cnt) {
+          const uint32_t d = (uint32_t)(k[u] >> sh) & dm;
+          if (d == run_d) {
+            ++run_n;
+          } else {
+            atomicAdd(&s_hist[p][run_d], run_n);
+            run_d = d;
+            run_n = 1;
+          }
+        }
+      }
+      atomicAdd(&s_hist[p][run_d], run_n);
     }
   }
   __syncthreads();
@@ -325,7 +362,7 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
     if (e != cudaSuccess) return e;
   }
-  launch_pdl(rs_histogram<K>, grid_for(n, kSortThreads, 148 * 4), kSortThreads, 0, stream, keys_in, n, begin_bit, passes,
+  launch_pdl(rs_histogram<K>, grid_for((n + kHistItems - 1) / kHistItems, kSortThreads, 148 * 4), kSortThreads, 0, stream, keys_in, n, begin_bit, passes,
                                                                                    last_bits, hist);
   note_launches(1);
   // Ping-pong so the last pass writes keys_out: pass p writes out when

@@ -204,3 +204,29 @@ def test_large_splat_hit_bits_match_oracle(sigma, G, H, W):
     assert used > 0
     if sigma[0] >= 150.0:
         assert used > capacity  # asked for more than the region holds: some splats re-tested
+
+
+def test_radix_sort_accepts_keys_that_are_not_16_byte_aligned():
+    """The exported sort takes a caller's pointers: keys one element into a
+    tensor are 8-byte but not 16-byte aligned, so the histogram pass must read
+    them one by one instead of with 16-byte loads."""
+    L = N.load()
+    n = 100_001
+    rng = np.random.default_rng(11)
+    keys = rng.integers(0, 2**40, n + 1, dtype=np.uint64)
+    vals = np.arange(n + 1, dtype=np.uint32)
+    k_all = torch.from_numpy(keys.view(np.int64)).to(DEV)
+    v_all = torch.from_numpy(vals.view(np.int32)).to(DEV)
+    k_in, v_in = k_all[1:], v_all[1:]
+    assert k_in.data_ptr() % 16 == 8
+    k_out, v_out = torch.empty_like(k_in), torch.empty_like(v_in)
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    ws_n = L.gsb_radix_sort_pairs_workspace_size(n, 0, 40)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=DEV)
+    N.check(L.gsb_radix_sort_pairs(N.ptr(k_in), N.ptr(v_in), N.ptr(k_out), N.ptr(v_out), n, 0, 40, N.ptr(status),
+                                   N.ptr(ws), ws_n, N.stream_ptr(DEV)), "sort")
+    torch.cuda.synchronize()
+    assert int(status[N.GSB_STATUS_ERROR]) == 0
+    order = np.argsort(keys[1:], kind="stable")
+    assert np.array_equal(k_out.cpu().numpy().view(np.uint64), keys[1:][order])
+    assert np.array_equal(v_out.cpu().numpy().view(np.uint32), vals[1:][order])
