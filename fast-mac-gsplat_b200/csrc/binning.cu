@@ -449,13 +449,18 @@ struct BitsEmitSmem {
   int incl[32];  // inclusive scan of the owners' bit-word counts
   int done[32];  // pairs written per owner so far
   int bo[32], w[32], tx0[32], ty0[32], start[32], cnt[32];
+  uint32_t mlo[32], mhi[32];  // an owner's 64-bit hit mask (bo == kMaskWords) as two words
   uint32_t tbase[32];
   // The round's 32 words: bits, inclusive popcount prefix, owner, word index, first slot.
   uint32_t rbits[32];
   int rpre[32], rowner[32], rwi[32], rslot[32];
 };
 
-// Writes the pairs of the warp's splats that kept hit bits (bo >= 0). Their bit
+// Writes the pairs of the warp's splats that kept hit bits: bo >= 0 for a
+// larger splat's words in the hit-bit region, bo == kMaskWords for a small
+// splat whose 64-bit hit mask (`mask`) stands for its one or two words. The 32
+// splats of a warp own one contiguous range of pair slots, so all their pairs
+// leave as consecutive stores. The bit
 // words are taken 32 at a time (round r covers words 32r .. 32r+31 of the
 // concatenated lists); a word's first pair slot is its owner's pairs so far
 // plus the popcounts of the owner's earlier words in the round (a segmented
@@ -465,12 +470,13 @@ struct BitsEmitSmem {
 // each splat's pairs keep row-major candidate order. Costs one round per 32
 // words instead of one per 32 candidates. Returns the number of pairs of this
 // lane's splat.
-__device__ __forceinline__ int warp_emit_bits(int bo, const SplatTiles& t, int start, int cnt, uint32_t tbase,
-                                              int r0, const uint32_t* __restrict__ words, const Meta& m,
-                                              uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
-                                              BitsEmitSmem& sm) {
+constexpr int kMaskWords = -2;
+__device__ __forceinline__ int warp_emit_bits(int bo, unsigned long long mask, const SplatTiles& t, int start, int cnt,
+                                              uint32_t tbase, int r0, const uint32_t* __restrict__ words,
+                                              const Meta& m, uint32_t* __restrict__ keys,
+                                              uint32_t* __restrict__ vals, BitsEmitSmem& sm) {
   const int lane = threadIdx.x & 31;
-  const int nw = bo >= 0 ? (t.n + 31) >> 5 : 0;
+  const int nw = (bo >= 0 || bo == kMaskWords) ? (t.n + 31) >> 5 : 0;
   int incl = nw;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -488,6 +494,8 @@ __device__ __forceinline__ int warp_emit_bits(int bo, const SplatTiles& t, int s
   sm.start[lane] = start;
   sm.cnt[lane] = cnt;
   sm.tbase[lane] = tbase;
+  sm.mlo[lane] = (uint32_t)mask;
+  sm.mhi[lane] = (uint32_t)(mask >> 32);
   __syncwarp();
   for (int base = 0; base < total; base += 32) {
     const int k = base + lane;
@@ -503,7 +511,8 @@ __device__ __forceinline__ int warp_emit_bits(int bo, const SplatTiles& t, int s
       }
       owner = lo;
       wi = k - (owner ? sm.incl[owner - 1] : 0);
-      bits = words[sm.bo[owner] + wi];
+      const int ob = sm.bo[owner];
+      bits = ob >= 0 ? words[ob + wi] : (wi == 0 ? sm.mlo[owner] : sm.mhi[owner]);
     }
     const int pc = __popc(bits);
     int pre = pc;  // inclusive prefix of the popcounts over the warp
@@ -590,37 +599,27 @@ __global__ void __launch_bounds__(256)
   // set bits in row-major candidate order); a larger one with hit bits reads
   // them in warp_tiles; the others are tested again.
   int own_hits = -1;
-  int bigoff = -1;
+  int bo = -1;  // where this splat's hit bits are: region offset, kMaskWords, or none (-1)
+  unsigned long long mask = 0ull;
   if (masks && big.words && t.n > kMaskCands) {
     const unsigned long long v = masks[r];
-    if (v != kNoBigMask) bigoff = (int)v;
+    if (v != kNoBigMask) bo = (int)v;
   }
   if (masks && t.n > 0 && t.n <= kMaskCands) {
-    unsigned long long bits = masks[r];
-    own_hits = __popcll(bits);
-    int slot = 0;
-    while (bits && slot < cnt) {
-      const int local = __ffsll(bits) - 1;
-      bits &= bits - 1;
-      const int row = cand_row(local, t.w);
-      const int tx = t.tx0 + (local - row * t.w), ty = t.ty0 + row;
-      keys[(int64_t)start + slot] = tbase + (uint32_t)(ty * m.tiles_x + tx);
-      vals[(int64_t)start + slot] = (uint32_t)r;
-      ++slot;
-    }
-    t.n = 0;
+    mask = masks[r];
+    own_hits = __popcll(mask);
+    bo = kMaskWords;
   }
   s_start[warp][lane] = start;
   s_cnt[warp][lane] = cnt;
   s_tbase[warp][lane] = tbase;
   const int r0 = r - lane;
-  // Larger splats with hit bits: their pairs straight from the bits.
-  if (big.words) {
-    const int bit_hits = warp_emit_bits(bigoff, t, start, cnt, tbase, r0, big.words, m, keys, vals, s_bits[warp]);
-    if (bigoff >= 0) {
-      own_hits = bit_hits;
-      t.n = 0;
-    }
+  // Splats with hit bits (a mask or region words): their pairs straight from
+  // the bits, written by the whole warp.
+  if (masks) {
+    const int bit_hits = warp_emit_bits(bo, mask, t, start, cnt, tbase, r0, big.words, m, keys, vals, s_bits[warp]);
+    if (bo >= 0) own_hits = bit_hits;
+    if (bo != -1) t.n = 0;
   }
   WarpTilesSmem& sm = s_warp[warp];
   warp_tiles(
