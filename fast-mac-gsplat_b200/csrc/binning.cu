@@ -32,14 +32,23 @@ constexpr int kLookWin = 8;  // predecessors read per look-back step
 // ellipse_rect do not depend on the tile and are taken once here; the test
 // then evaluates the same correctly rounded operation sequence per tile.
 struct SplatTiles {
-  float mx, my, a, b, c, tau, kc, ka;
+  float mx, my, a, b, c, tau, kc, ka, b2;  // b2 = 2b (exact: a power-of-two product)
   int tx0, ty0, w, n;  // candidates [tx0, tx0 + w) x [ty0, ty0 + n / w); n = 0: none
 };
+
+// quad_form with its constant factor 2b taken once per splat: the same
+// correctly rounded operation sequence, so the same value bit for bit.
+__device__ __forceinline__ float quad_form_b2(float a, float b2, float c, float dx, float dy) {
+  const float t0 = __fmul_rn(__fmul_rn(a, dx), dx);
+  const float t1 = __fmul_rn(__fmul_rn(b2, dx), dy);
+  const float t2 = __fmul_rn(__fmul_rn(c, dy), dy);
+  return __fadd_rn(__fadd_rn(t0, t1), t2);
+}
 
 __device__ __forceinline__ SplatTiles splat_tiles(float mx, float my, float a, float b, float c, float op,
                                                   const Meta& m) {
   SplatTiles s;
-  s.mx = mx, s.my = my, s.a = a, s.b = b, s.c = c;
+  s.mx = mx, s.my = my, s.a = a, s.b = b, s.c = c, s.b2 = __fmul_rn(2.0f, b);
   s.tau = 0.0f, s.kc = 0.0f, s.ka = 0.0f;
   s.tx0 = 0, s.ty0 = 0, s.w = 1, s.n = 0;
   float tau;
@@ -66,21 +75,21 @@ __device__ __forceinline__ bool tile_hit(const SplatTiles& s, int tx, int ty, co
   const float dy0 = __fsub_rn(ry0, s.my);
   const float dy1 = __fsub_rn(ry1, s.my);
   float qmin = __int_as_float(0x7f800000);
-  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx0, dy0));
-  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx0, dy1));
-  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx1, dy0));
-  qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx1, dy1));
+  qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx0, dy0));
+  qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx0, dy1));
+  qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx1, dy0));
+  qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx1, dy1));
   if (s.c > 1e-8f) {
     float dy = fminf(fmaxf(__fmul_rn(s.kc, dx0), dy0), dy1);
-    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx0, dy));
+    qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx0, dy));
     dy = fminf(fmaxf(__fmul_rn(s.kc, dx1), dy0), dy1);
-    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx1, dy));
+    qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx1, dy));
   }
   if (s.a > 1e-8f) {
     float dx = fminf(fmaxf(__fmul_rn(s.ka, dy0), dx0), dx1);
-    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx, dy0));
+    qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx, dy0));
     dx = fminf(fmaxf(__fmul_rn(s.ka, dy1), dx0), dx1);
-    qmin = fminf(qmin, quad_form(s.a, s.b, s.c, dx, dy1));
+    qmin = fminf(qmin, quad_form_b2(s.a, s.b2, s.c, dx, dy1));
   }
   return qmin <= s.tau;
 }
@@ -126,12 +135,14 @@ struct BigBits {
 // visit(owner, tx, ty, slot) runs for each hit with slot = its index in the
 // owner's list and local = its candidate index in the owner's row-major box.
 // On return sm.hits[j] is splat j's hit count.
-// kMasks (k_prepare): record hit masks, and hit bits of larger splats in
-// `big` when it has room.
+// kMasks (k_prepare): record hit masks; a larger splat that gets room in `big`
+// is first walked by the whole warp on its own, writing its hit bits a word
+// per round, and takes no part in the shared rounds.
 template <bool kMasks = false, typename Visit>
 __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m, WarpTilesSmem& sm,
                                            Visit&& visit, BigBits big = BigBits()) {
   const int lane = threadIdx.x & 31;
+  SplatTiles coop = mine;  // the candidates walked cooperatively below
   if (kMasks) {
     // One cursor atomic per warp: the lanes' word counts are summed, and each
     // lane takes its piece of the warp's range (if the range fits, else none).
@@ -149,37 +160,63 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
       uint32_t at = 0u;
       if (lane == 0 && warp_words) at = atomicAdd(big.cursor, warp_words);
       at = __shfl_sync(kFullMask, at, 0);
-      if (words && at <= big.capacity && warp_words <= big.capacity - at) {
-        for (uint32_t w = 0; w < words; ++w) big.words[at + excl + w] = 0u;
-        b = (int)(at + excl);
-      }
+      if (words && at <= big.capacity && warp_words <= big.capacity - at) b = (int)(at + excl);
     }
-    sm.big[lane] = b;  // read by other lanes after the __syncwarp below
+    sm.big[lane] = b;
+    sm.t[lane] = mine;
+    __syncwarp();
+    // A splat that got hit-bit words is walked by the whole warp, 32 candidates
+    // per round in row-major order: no owner search and no segments, and the
+    // round's ballot is the splat's hit word for those 32 candidates (every
+    // word is written whole, so the region needs no clearing).
+    unsigned walk = __ballot_sync(kFullMask, b >= 0);
+    while (walk) {
+      const int j = __ffs(walk) - 1;
+      walk &= walk - 1;
+      const SplatTiles& s = sm.t[j];
+      const int bj = sm.big[j];
+      int hits = 0;
+      for (int base = 0; base < s.n; base += 32) {
+        const int local = base + lane;
+        bool hit = false;
+        if (local < s.n) {
+          const int row = cand_row(local, s.w);
+          hit = tile_hit(s, s.tx0 + (local - row * s.w), s.ty0 + row, m);
+        }
+        const unsigned bal = __ballot_sync(kFullMask, hit);
+        hits += __popc(bal);
+        if (lane == 0) big.words[bj + (base >> 5)] = bal;
+      }
+      if (lane == 0) sm.hits[j] = hits;
+    }
+    if (b >= 0) coop.n = 0;
+    __syncwarp();
   }
-  long long incl = mine.n;
+  long long incl = coop.n;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const long long y = __shfl_up_sync(kFullMask, incl, o);
     if (lane >= o) incl += y;
   }
   const long long total = __shfl_sync(kFullMask, incl, 31);
-  sm.hits[lane] = 0;
-  sm.t[lane] = mine;
+  if (!(kMasks && sm.big[lane] >= 0)) sm.hits[lane] = 0;  // a walked splat keeps its count
+  sm.t[lane] = coop;
   if (kMasks) sm.mask[lane] = 0ull;
   if (total > 0x7fffffffll) {
-    // Beyond int range for the warp: each lane walks its own candidates.
-    int cnt = 0;
-    for (int local = 0; local < mine.n; ++local) {
-      const int row = cand_row(local, mine.w);
-      const int tx = mine.tx0 + (local - row * mine.w), ty = mine.ty0 + row;
-      const int bb = kMasks ? sm.big[lane] : -1;
-      if (tile_hit(mine, tx, ty, m)) {
-        if (kMasks && mine.n <= kMaskCands) sm.mask[lane] |= 1ull << local;
-        if (kMasks && bb >= 0) atomicOr(&big.words[bb + (local >> 5)], 1u << (local & 31));
-        visit(lane, tx, ty, cnt++, local);
+    // Beyond int range for the warp: each lane walks its own remaining
+    // candidates (splats the warp walked above have none left).
+    if (coop.n > 0) {
+      int cnt = 0;
+      for (int local = 0; local < coop.n; ++local) {
+        const int row = cand_row(local, coop.w);
+        const int tx = coop.tx0 + (local - row * coop.w), ty = coop.ty0 + row;
+        if (tile_hit(coop, tx, ty, m)) {
+          if (kMasks && coop.n <= kMaskCands) sm.mask[lane] |= 1ull << local;
+          visit(lane, tx, ty, cnt++, local);
+        }
       }
+      sm.hits[lane] = cnt;
     }
-    sm.hits[lane] = cnt;
     __syncwarp();
     return;
   }
@@ -221,16 +258,6 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
       // The segment's lanes hold consecutive candidates local, local+1, ...
       if (kMasks && sm.t[owner].n <= kMaskCands)
         sm.mask[owner] |= (unsigned long long)((hits & seg) >> seg0) << local;
-      const int bb = kMasks ? sm.big[owner] : -1;
-      if (kMasks && bb >= 0) {
-        // The segment's hits are candidates local .. local + len - 1: at most two words.
-        const uint32_t bits = (hits & seg) >> seg0;
-        const int w0 = local >> 5, off = local & 31;
-        if (bits) {
-          atomicOr(&big.words[bb + w0], bits << off);
-          if (off && (bits >> (32 - off))) atomicOr(&big.words[bb + w0 + 1], bits >> (32 - off));
-        }
-      }
     }
     if (hit) visit(owner, tx, ty, base_slot + before, local);
     __syncwarp();
