@@ -1058,7 +1058,9 @@ __global__ void __launch_bounds__(kCtaThreads)
   }
 }
 
-// grad_rec (depth-rank order, packed) -> user layout in input order.
+// grad_rec (depth-rank order, packed) -> user layout in input order, one
+// thread per rank scattering its values (for small splat counts, where one
+// launch is all the time there is).
 __global__ void __launch_bounds__(256)
     k_unsort(Meta m, const int32_t* __restrict__ perm, const float4* __restrict__ grad_rec,
              float* __restrict__ g_means2d, float* __restrict__ g_conics, float* __restrict__ g_colors,
@@ -1088,6 +1090,56 @@ __global__ void __launch_bounds__(256)
     g_colors[3 * o + 2] = q2.x;
   }
 }
+
+// The same as a gather, for large splat counts: scattering each rank's 9 values to a random input position cost one
+// partly written 32-byte sector per value. First the inverse permutation is
+// written, one 4-byte slot per splat, into the first requested output tensor
+// (its element o * inv_stride); then the thread of input position o reads its
+// rank there, loads that rank's packed gradients and writes all of o's outputs
+// with consecutive stores, its own inverse slot included (no other thread
+// reads that slot).
+__global__ void __launch_bounds__(256)
+    k_unsort_invert(Meta m, const int32_t* __restrict__ perm, int32_t* __restrict__ inv, int inv_stride) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= m.BG) return;
+  const int b = fast_div(r, m.div_G);
+  inv[(size_t)(b * m.G + perm[r]) * inv_stride] = r;
+}
+
+__global__ void __launch_bounds__(256)
+    k_unsort_gather(Meta m, const int32_t* inv, int inv_stride, const float4* __restrict__ grad_rec,
+                    float* g_means2d, float* g_conics, float* g_colors, float* g_opac) {  // inv aliases an output
+  pdl_wait();
+  pdl_trigger();
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= m.BG) return;
+  const int r = inv[(size_t)o * inv_stride];
+  if ((unsigned)r >= (unsigned)m.BG) return;  // perm is a permutation: every slot was written
+  const float4 q0 = grad_rec[3 * r + 0];
+  const float4 q1 = grad_rec[3 * r + 1];
+  const float4 q2 = grad_rec[3 * r + 2];
+  if (g_means2d) {
+    g_means2d[2 * o + 0] = q0.x;
+    g_means2d[2 * o + 1] = q0.y;
+  }
+  if (g_conics) {
+    g_conics[3 * o + 0] = q0.z;
+    g_conics[3 * o + 1] = q0.w;
+    g_conics[3 * o + 2] = q1.x;
+  }
+  if (g_opac) g_opac[o] = q1.y;
+  if (g_colors) {
+    g_colors[3 * o + 0] = q1.z;
+    g_colors[3 * o + 1] = q1.w;
+    g_colors[3 * o + 2] = q2.x;
+  }
+}
+
+// From this many splats the un-sort runs as invert + gather (c4's 2^20:
+// 93 -> 38 us); below it one scatter launch is as fast (65,536: 10.8 us).
+constexpr int kGatherUnsortMin = 1 << 18;
 
 constexpr size_t kBwdWarpSmem = sizeof(BwdWarpSmem) * kBwdWarps;
 
@@ -1247,10 +1299,27 @@ extern "C" int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm
   if (rc != GSB_OK) return rc;
   if (m.BG == 0) return GSB_OK;
   if (!perm || !grad_rec) return GSB_ERR_INVALID_ARGUMENT;
+  // The inverse permutation's slots: the first requested output (opacities
+  // have one float per splat, the others two or three).
+  int32_t* inv = nullptr;
+  int stride = 0;
+  if (g_opacities) inv = reinterpret_cast<int32_t*>(g_opacities), stride = 1;
+  else if (g_means2d) inv = reinterpret_cast<int32_t*>(g_means2d), stride = 2;
+  else if (g_conics) inv = reinterpret_cast<int32_t*>(g_conics), stride = 3;
+  else if (g_colors) inv = reinterpret_cast<int32_t*>(g_colors), stride = 3;
+  if (!inv) return GSB_OK;  // no gradient requested
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  const cudaError_t e = launch_pdl(k_unsort, grid1d(m.BG, 256), 256, 0, stream, m, perm,
-                                   reinterpret_cast<const float4*>(grad_rec), g_means2d, g_conics, g_colors,
-                                   g_opacities);
-  note_launches(1);
+  if (m.BG < kGatherUnsortMin) {
+    const cudaError_t e1 = launch_pdl(k_unsort, grid1d(m.BG, 256), 256, 0, stream, m, perm,
+                                      reinterpret_cast<const float4*>(grad_rec), g_means2d, g_conics, g_colors,
+                                      g_opacities);
+    note_launches(1);
+    return cuda_status(e1);
+  }
+  cudaError_t e = launch_pdl(k_unsort_invert, grid1d(m.BG, 256), 256, 0, stream, m, perm, inv, stride);
+  if (e == cudaSuccess)
+    e = launch_pdl(k_unsort_gather, grid1d(m.BG, 256), 256, 0, stream, m, static_cast<const int32_t*>(inv), stride,
+                   reinterpret_cast<const float4*>(grad_rec), g_means2d, g_conics, g_colors, g_opacities);
+  note_launches(2);
   return cuda_status(e);
 }

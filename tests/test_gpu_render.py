@@ -501,3 +501,31 @@ def test_reference_harness_entry_measures_accuracy(mode):
         assert all(f"grad_{k}_max_abs_error" in res for k in ("means2d", "conics", "colors", "opacities"))
     with pytest.raises(ValueError, match="unknown renderer"):
         run_renderer("nope", base, s.height, s.width)
+
+
+@pytest.mark.parametrize("G", [70_000, 300_000])
+def test_unsort_grads_with_any_subset_of_outputs(G):
+    """gsb_unsort_grads (the un-sort of the autograd backward, …/rasterize.py:583-591)
+    through the C ABI: each requested output gets its gradients in input order
+    exactly, whichever outputs are NULL. Below 2^18 splats it scatters; above,
+    it writes the inverse permutation into the first requested output and
+    gathers, so both paths and every choice of that output are covered."""
+    from torch_gsplat_bridge_fast import _native as N
+
+    L = N.load()
+    meta = N.make_meta(64, 64, 1, G, 1 / 255, 1e-4, (0.0, 0.0, 0.0))
+    gen = torch.Generator().manual_seed(G)
+    perm = torch.randperm(G, generator=gen).to(torch.int32)
+    grad_rec = torch.randn(G, 12, generator=gen)
+    want = np.zeros((G, 12), np.float32)
+    want[perm.numpy()] = grad_rec.numpy()
+    cols = [(0, 2), (2, 5), (6, 9), (5, 6)]  # means2d, conics, colors, opacities in the packed record
+    shapes = [(G, 2), (G, 3), (G, 3), (G,)]
+    for sel in [(0, 1, 2, 3), (0,), (1,), (2,), (3,), (1, 2), (0, 3)]:
+        outs = [torch.full(sh, float("nan"), device=DEV) if k in sel else None for k, sh in enumerate(shapes)]
+        N.check(L.gsb_unsort_grads(meta, N.ptr(perm.to(DEV)), N.ptr(grad_rec.to(DEV)), *(N.ptr(t) for t in outs),
+                                   N.stream_ptr(DEV)), "gsb_unsort_grads")
+        torch.cuda.synchronize()
+        for k in sel:
+            a, b = cols[k]
+            assert np.array_equal(np_(outs[k]).reshape(G, -1), want[:, a:b]), (sel, k)
