@@ -33,6 +33,7 @@ constexpr int kLookWin = 8;  // predecessors read per look-back step
 // then evaluates the same correctly rounded operation sequence per tile.
 struct SplatTiles {
   float mx, my, a, b, c, tau, kc, ka, b2;  // b2 = 2b (exact: a power-of-two product)
+  float rw;  // 1 / w, correctly rounded (cand_row)
   int tx0, ty0, w, n;  // candidates [tx0, tx0 + w) x [ty0, ty0 + n / w); n = 0: none
 };
 
@@ -50,6 +51,7 @@ __device__ __forceinline__ SplatTiles splat_tiles(float mx, float my, float a, f
   SplatTiles s;
   s.mx = mx, s.my = my, s.a = a, s.b = b, s.c = c, s.b2 = __fmul_rn(2.0f, b);
   s.tau = 0.0f, s.kc = 0.0f, s.ka = 0.0f;
+  s.rw = 1.0f;
   s.tx0 = 0, s.ty0 = 0, s.w = 1, s.n = 0;
   float tau;
   if (!support_tau(op, m.alpha_thr, m.eps, &tau)) return s;
@@ -60,6 +62,7 @@ __device__ __forceinline__ SplatTiles splat_tiles(float mx, float my, float a, f
   s.ty0 = bb.y0 / kTile;
   s.w = bb.x1 / kTile - s.tx0 + 1;
   s.n = s.w * (bb.y1 / kTile - s.ty0 + 1);
+  s.rw = __frcp_rn((float)s.w);
   if (c > 1e-8f) s.kc = -__fdiv_rn(b, c);
   if (a > 1e-8f) s.ka = -__fdiv_rn(b, a);
   return s;
@@ -94,12 +97,110 @@ __device__ __forceinline__ bool tile_hit(const SplatTiles& s, int tx, int ty, co
   return qmin <= s.tau;
 }
 
-// Row of candidate `local` (0 <= local < n) of a splat whose box is w tiles wide.
-__device__ __forceinline__ int cand_row(int local, int w) {
-  int r = (int)(((float)local + 0.5f) * __frcp_rn((float)w));
+// Row of candidate `local` (0 <= local < n) of a splat whose box is w tiles
+// wide; rw = 1 / w (the estimate is corrected to the exact quotient).
+__device__ __forceinline__ int cand_row(int local, int w, float rw) {
+  int r = (int)(((float)local + 0.5f) * rw);
   while (r > 0 && r * w > local) --r;
   while ((r + 1) * w <= local) ++r;
   return r;
+}
+__device__ __forceinline__ int cand_row(int local, int w) { return cand_row(local, w, __frcp_rn((float)w)); }
+
+// Hit tiles of a splat row by row (k_prepare). Within one row of tiles (a
+// horizontal strip of pixel centres [ry0, ry1]) the support ellipse q <= T is
+// convex, so the row's tiles that meet it are the ones whose column range
+// [rx0, rx1] meets the ellipse's x-extent inside the strip: one run of tiles.
+// For T_in = tau (1 - 2^-7) and T_out = tau (1 + 2^-7) that gives, per row,
+// the tiles that surely hit and the only ones that can; the tiles between the
+// two runs (one or two at each end of a row) go to the exact tile_hit. So the
+// hit sets stay exactly the reference's while the work is per row, not per
+// candidate tile.
+//
+// Why it is sound. Let q(p) = d^T A d (d = p - mean, A = [[a, b], [b, c]]).
+// For a positive definite A with a, c > 1e-8 the points tile_hit evaluates
+// (the mean when it lies in the rectangle, the 4 corners, and the minimum of q
+// on each edge at the clamped stationary point) include a minimiser of q over
+// the rectangle, so its float minimum differs from the exact minimum only by
+// rounding. Each evaluated q is a sum of three products of correctly rounded
+// factors, within about 9 eps (a dx^2 + 2|b dx dy| + c dy^2) <= 18 eps k q of
+// its exact value, with k = (a + c) / lambda_min <= (a + c)^2 / det. The float
+// rectangle corners (rx - mx rounded) move the evaluated points by at most
+// eps (|d| + 32) px, which changes q by a relative 3 eps (R_major + 32) /
+// R_minor at the threshold (R = sqrt(tau / lambda)). span_geom admits a splat
+// only when k <= 2^12 and lambda_max <= a + c <= 2^8 tau (R_minor >= 1/16 px),
+// which bounds both effects by 4.5e-3 of tau, below the 2^-7 (7.8e-3) between
+// tau and T_in, T_out. A tile that meets the ellipse at T_in therefore has a
+// float minimum below tau (a hit); one that misses it at T_out has every
+// evaluated q above tau (a miss). The extents are computed in double: an error
+// dD in D = a T - det e^2 moves the boundary point where dq/dx = 2 sqrt(D), so
+// q changes by about dD / a ~ 2^-51 T, far inside the margin; the tile columns
+// are then found by exact comparisons with rx0 and rx1.
+constexpr double kSpanMargin = 0x1p-7;
+// Splats with fewer candidate tiles take the exact test for each: for them the
+// row walk's setup costs more than the tests it saves.
+constexpr int kSpanMinCands = 12;
+
+struct SpanGeom {
+  double mx, my, b, det, ia, bc;  // ia = 1 / a, bc = b / c
+  double E[2], XR[2], aT[2];      // per threshold (0: T_in, 1: T_out): y and x half extents, a T
+};
+
+// The constants of the row walk, or false when the splat is outside the
+// conditions above (it then takes the exact test for every candidate).
+__device__ __forceinline__ bool span_geom(const SplatTiles& s, SpanGeom& g) {
+  if (s.n < kSpanMinCands) return false;
+  const float a = s.a, b = s.b, c = s.c;
+  if (!(a > 1e-8f) || !(c > 1e-8f) || !(a < 1e30f) || !(c < 1e30f) || !(fabsf(b) < 1e30f)) return false;
+  if (!(fabsf(s.mx) < 0x1p22f) || !(fabsf(s.my) < 0x1p22f)) return false;
+  const double da = a, db = b, dc = c;
+  const double det = da * dc - db * db;  // products exact in double
+  const double tr = da + dc;
+  if (!(det > 0.0) || !(tr * tr <= 4096.0 * det) || !(tr <= 256.0 * (double)s.tau)) return false;
+  g.mx = s.mx, g.my = s.my, g.b = db, g.det = det, g.ia = 1.0 / da, g.bc = db / dc;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const double T = (double)s.tau * (k ? 1.0 + kSpanMargin : 1.0 - kSpanMargin);
+    g.E[k] = sqrt(da * T / det);
+    g.XR[k] = sqrt(dc * T / det);
+    g.aT[k] = da * T;
+  }
+  return true;
+}
+
+// x-extent [xl, xr] (relative to the mean) of the ellipse q <= T_k within the
+// strip e in [e0, e1] (relative to the mean); false when they do not meet.
+// The right boundary x(e) = (-b e + sqrt(a T - det e^2)) / a is concave with its
+// maximum XR at e = -(b / c) XR, the left one convex with its minimum -XR at
+// e = (b / c) XR; off those points the extreme is at an end of the strip.
+__device__ __forceinline__ bool strip_extent(const SpanGeom& g, int k, double e0, double e1, double& xl, double& xr) {
+  const double lo = fmax(e0, -g.E[k]), hi = fmin(e1, g.E[k]);
+  if (!(lo <= hi)) return false;
+  const double es = g.bc * g.XR[k];
+  const double sl = sqrt(fmax(g.aT[k] - g.det * lo * lo, 0.0));
+  const double sh = sqrt(fmax(g.aT[k] - g.det * hi * hi, 0.0));
+  const double cl = -g.b * lo, ch = -g.b * hi;
+  xr = (-es >= lo && -es <= hi) ? g.XR[k] : fmax(cl + sl, ch + sh) * g.ia;
+  xl = (es >= lo && es <= hi) ? -g.XR[k] : fmin(cl - sl, ch - sh) * g.ia;
+  return true;
+}
+
+// First column t in [t0, t1] whose rectangle reaches right of X (rx1 >= X), or
+// t1 + 1; last column in [t0, t1] reaching left of X (rx0 <= X), or t0 - 1.
+// Exact: the estimate is corrected against the float rectangle edges.
+__device__ __forceinline__ int first_col_reaching(double X, int t0, int t1, int W) {
+  const double f = ceil((X - 15.5) * 0.0625);
+  int t = f <= (double)t0 ? t0 : (f > (double)t1 ? t1 + 1 : (int)f);
+  while (t > t0 && (double)tile_rx1(t - 1, W) >= X) --t;
+  while (t <= t1 && (double)tile_rx1(t, W) < X) ++t;
+  return t;
+}
+__device__ __forceinline__ int last_col_reaching(double X, int t0, int t1) {
+  const double f = floor((X - 0.5) * 0.0625);
+  int t = f >= (double)t1 ? t1 : (f < (double)t0 ? t0 - 1 : (int)f);
+  while (t < t1 && (double)tile_rx0(t + 1) <= X) ++t;
+  while (t >= t0 && (double)tile_rx0(t) > X) --t;
+  return t;
 }
 
 constexpr int kMaskCands = 64;  // splats with at most this many candidate tiles keep a hit mask
@@ -110,12 +211,12 @@ constexpr int kMaskCands = 64;  // splats with at most this many candidate tiles
 constexpr uint32_t kBigMaskWords = 8;
 constexpr unsigned long long kNoBigMask = ~0ull;
 
-// Per-warp shared state of warp_tiles.
+// Per-warp shared state of warp_tiles and warp_count_tiles.
 struct WarpTilesSmem {
   SplatTiles t[32];
   int incl[32];                  // inclusive scan of the candidate counts
   int hits[32];                  // running hit count per owner
-  unsigned long long mask[32];   // hit mask per owner with <= kMaskCands candidates (kMasks)
+  unsigned long long mask[32];   // hit mask per owner with <= kMaskCands candidates (warp_count_tiles)
   int big[32];                   // word offset of a larger owner's hit bits, or -1
 };
 
@@ -127,96 +228,47 @@ struct BigBits {
   uint32_t* cursor = nullptr; // words handed out so far (k_prepare)
 };
 
+// Owner of concatenated candidate k (0 <= k < the warp's total): the first
+// lane whose inclusive candidate count exceeds k.
+__device__ __forceinline__ int find_owner(const int* incl, int k) {
+  int lo = 0, hi = 31;
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int mid = (lo + hi) >> 1;
+    if (incl[mid] > k) hi = mid;
+    else lo = mid + 1;
+  }
+  return lo;
+}
+
 // Visits every candidate tile of the warp's 32 splats (lane j owns splat j),
 // spread evenly over the lanes: round r tests candidates 32r .. 32r+31 of the
 // warp's concatenated row-major candidate lists, so a warp costs its total
 // candidate count / 32 rounds however unevenly the splats are sized. Hits are
 // numbered per owner in row-major tile order (the reference's loop order):
 // visit(owner, tx, ty, slot) runs for each hit with slot = its index in the
-// owner's list and local = its candidate index in the owner's row-major box.
-// On return sm.hits[j] is splat j's hit count.
-// kMasks (k_prepare): record hit masks; a larger splat that gets room in `big`
-// is first walked by the whole warp on its own, writing its hit bits a word
-// per round, and takes no part in the shared rounds.
-template <bool kMasks = false, typename Visit>
-__device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m, WarpTilesSmem& sm,
-                                           Visit&& visit, BigBits big = BigBits()) {
+// owner's list. On return sm.hits[j] is splat j's hit count.
+template <typename Visit>
+__device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m, WarpTilesSmem& sm, Visit&& visit) {
   const int lane = threadIdx.x & 31;
-  SplatTiles coop = mine;  // the candidates walked cooperatively below
-  if (kMasks) {
-    // One cursor atomic per warp: the lanes' word counts are summed, and each
-    // lane takes its piece of the warp's range (if the range fits, else none).
-    int b = -1;
-    if (big.words) {
-      const uint32_t words = mine.n > kMaskCands ? ((uint32_t)mine.n + 31u) >> 5 : 0u;
-      uint32_t excl = words;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(kFullMask, excl, o);
-        if (lane >= o) excl += y;
-      }
-      const uint32_t warp_words = __shfl_sync(kFullMask, excl, 31);
-      excl -= words;
-      uint32_t at = 0u;
-      if (lane == 0 && warp_words) at = atomicAdd(big.cursor, warp_words);
-      at = __shfl_sync(kFullMask, at, 0);
-      if (words && at <= big.capacity && warp_words <= big.capacity - at) b = (int)(at + excl);
-    }
-    sm.big[lane] = b;
-    sm.t[lane] = mine;
-    __syncwarp();
-    // A splat that got hit-bit words is walked by the whole warp, 32 candidates
-    // per round in row-major order: no owner search and no segments, and the
-    // round's ballot is the splat's hit word for those 32 candidates (every
-    // word is written whole, so the region needs no clearing).
-    unsigned walk = __ballot_sync(kFullMask, b >= 0);
-    while (walk) {
-      const int j = __ffs(walk) - 1;
-      walk &= walk - 1;
-      const SplatTiles& s = sm.t[j];
-      const int bj = sm.big[j];
-      int hits = 0;
-      for (int base = 0; base < s.n; base += 32) {
-        const int local = base + lane;
-        bool hit = false;
-        if (local < s.n) {
-          const int row = cand_row(local, s.w);
-          hit = tile_hit(s, s.tx0 + (local - row * s.w), s.ty0 + row, m);
-        }
-        const unsigned bal = __ballot_sync(kFullMask, hit);
-        hits += __popc(bal);
-        if (lane == 0) big.words[bj + (base >> 5)] = bal;
-      }
-      if (lane == 0) sm.hits[j] = hits;
-    }
-    if (b >= 0) coop.n = 0;
-    __syncwarp();
-  }
-  long long incl = coop.n;
+  long long incl = mine.n;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const long long y = __shfl_up_sync(kFullMask, incl, o);
     if (lane >= o) incl += y;
   }
   const long long total = __shfl_sync(kFullMask, incl, 31);
-  if (!(kMasks && sm.big[lane] >= 0)) sm.hits[lane] = 0;  // a walked splat keeps its count
-  sm.t[lane] = coop;
-  if (kMasks) sm.mask[lane] = 0ull;
+  sm.hits[lane] = 0;
+  sm.t[lane] = mine;
   if (total > 0x7fffffffll) {
-    // Beyond int range for the warp: each lane walks its own remaining
-    // candidates (splats the warp walked above have none left).
-    if (coop.n > 0) {
-      int cnt = 0;
-      for (int local = 0; local < coop.n; ++local) {
-        const int row = cand_row(local, coop.w);
-        const int tx = coop.tx0 + (local - row * coop.w), ty = coop.ty0 + row;
-        if (tile_hit(coop, tx, ty, m)) {
-          if (kMasks && coop.n <= kMaskCands) sm.mask[lane] |= 1ull << local;
-          visit(lane, tx, ty, cnt++, local);
-        }
-      }
-      sm.hits[lane] = cnt;
+    // Beyond int range for the warp: each lane walks its own candidates.
+    int cnt = 0;
+    for (int local = 0; local < mine.n; ++local) {
+      const int row = cand_row(local, mine.w, mine.rw);
+      const int tx = mine.tx0 + (local - row * mine.w), ty = mine.ty0 + row;
+      if (tile_hit(mine, tx, ty, m)) visit(lane, tx, ty, cnt++);
     }
+    sm.hits[lane] = cnt;
     __syncwarp();
     return;
   }
@@ -224,20 +276,13 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
   __syncwarp();
   for (int base = 0; base < (int)total; base += 32) {
     const int k = base + lane;
-    int owner = -1, tx = 0, ty = 0, local = 0;
+    int owner = -1, tx = 0, ty = 0;
     bool hit = false;
     if (k < (int)total) {
-      int lo = 0, hi = 31;  // first owner whose inclusive end exceeds k
-#pragma unroll
-      for (int step = 0; step < 5; ++step) {
-        const int mid = (lo + hi) >> 1;
-        if (sm.incl[mid] > k) hi = mid;
-        else lo = mid + 1;
-      }
-      owner = lo;
+      owner = find_owner(sm.incl, k);
       const SplatTiles& s = sm.t[owner];
-      local = k - (owner ? sm.incl[owner - 1] : 0);
-      const int row = cand_row(local, s.w);
+      const int local = k - (owner ? sm.incl[owner - 1] : 0);
+      const int row = cand_row(local, s.w, s.rw);
       tx = s.tx0 + (local - row * s.w);
       ty = s.ty0 + row;
       hit = tile_hit(s, tx, ty, m);
@@ -253,15 +298,240 @@ __device__ __forceinline__ void warp_tiles(const SplatTiles& mine, const Meta& m
     const int before = __popc(hits & seg & ((1u << lane) - 1u));
     const int base_slot = owner >= 0 ? sm.hits[owner] : 0;
     __syncwarp();
-    if (lane == seg0 && owner >= 0) {
-      sm.hits[owner] = base_slot + __popc(hits & seg);
-      // The segment's lanes hold consecutive candidates local, local+1, ...
-      if (kMasks && sm.t[owner].n <= kMaskCands)
-        sm.mask[owner] |= (unsigned long long)((hits & seg) >> seg0) << local;
-    }
-    if (hit) visit(owner, tx, ty, base_slot + before, local);
+    if (lane == seg0 && owner >= 0) sm.hits[owner] = base_slot + __popc(hits & seg);
+    if (hit) visit(owner, tx, ty, base_slot + before);
     __syncwarp();
   }
+}
+
+// k_prepare's per-warp shared state: warp_tiles' arrays, the row-walk
+// constants of the lanes' splats, and the queue of tiles left to the exact test.
+struct CountSmem {
+  WarpTilesSmem t;
+  SpanGeom g[32];
+  int qlocal[64];
+  unsigned char qowner[64];
+};
+
+// Hit counts (sm.hits), hit masks (sm.mask, splats with <= kMaskCands
+// candidates) and hit-bit words (`big`) of the warp's 32 splats, for k_prepare.
+// Splats that meet span_geom's conditions are walked row by row (rounds of 32
+// rows of the warp's splats, one row per lane): the sure run of each row is
+// counted and its bits are ORed in at once, and the unsure tiles at the ends of
+// the runs are queued and run through tile_hit 32 at a time. The others take
+// tile_hit for every candidate: a larger one with hit-bit words is walked by
+// the whole warp on its own, 32 candidates per round in row-major order (the
+// round's ballot is its hit word, written whole), the rest share rounds of 32
+// candidates as in warp_tiles.
+__device__ __forceinline__ void warp_count_tiles(const SplatTiles& mine, const Meta& m, CountSmem& cs, BigBits big) {
+  WarpTilesSmem& sm = cs.t;
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  SpanGeom geom;
+  const bool span = span_geom(mine, geom);
+  // One cursor atomic per warp: the lanes' word counts are summed, and each
+  // lane takes its piece of the warp's range (if the range fits, else none).
+  int b = -1;
+  if (big.words) {
+    const uint32_t words = mine.n > kMaskCands ? ((uint32_t)mine.n + 31u) >> 5 : 0u;
+    uint32_t excl = words;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFullMask, excl, o);
+      if (lane >= o) excl += y;
+    }
+    const uint32_t warp_words = __shfl_sync(kFullMask, excl, 31);
+    excl -= words;
+    uint32_t at = 0u;
+    if (lane == 0 && warp_words) at = atomicAdd(big.cursor, warp_words);
+    at = __shfl_sync(kFullMask, at, 0);
+    if (words && at <= big.capacity && warp_words <= big.capacity - at) b = (int)(at + excl);
+  }
+  sm.big[lane] = b;
+  sm.t[lane] = mine;
+  sm.mask[lane] = 0ull;
+  sm.hits[lane] = 0;
+  if (span) cs.g[lane] = geom;
+  __syncwarp();
+
+  // 1. Exact walk of the larger splats outside the row walk that got words.
+  unsigned walk = __ballot_sync(kFullMask, b >= 0 && !span);
+  while (walk) {
+    const int j = __ffs(walk) - 1;
+    walk &= walk - 1;
+    const SplatTiles& s = sm.t[j];
+    const int bj = sm.big[j];
+    int hits = 0;
+    for (int base = 0; base < s.n; base += 32) {
+      const int local = base + lane;
+      bool hit = false;
+      if (local < s.n) {
+        const int row = cand_row(local, s.w, s.rw);
+        hit = tile_hit(s, s.tx0 + (local - row * s.w), s.ty0 + row, m);
+      }
+      const unsigned bal = __ballot_sync(kFullMask, hit);
+      hits += __popc(bal);
+      if (lane == 0) big.words[bj + (base >> 5)] = bal;
+    }
+    if (lane == 0) sm.hits[j] = hits;
+  }
+  // 2. The words of the row-walked splats are cleared (their runs are ORed in).
+  unsigned clear = __ballot_sync(kFullMask, b >= 0 && span);
+  while (clear) {
+    const int j = __ffs(clear) - 1;
+    clear &= clear - 1;
+    uint32_t* const w = big.words + sm.big[j];
+    for (int i = lane; i < (sm.t[j].n + 31) >> 5; i += 32) w[i] = 0u;
+  }
+  __syncwarp();
+
+  // 3. Exact shared rounds for the other splats outside the row walk.
+  {
+    const int n = (!span && b < 0) ? mine.n : 0;
+    long long incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const long long total = __shfl_sync(kFullMask, incl, 31);
+    if (total > 0x7fffffffll) {
+      // Beyond int range for the warp: each lane tests its own candidates.
+      int cnt = 0;
+      unsigned long long mask = 0ull;
+      for (int local = 0; local < n; ++local) {
+        const int row = cand_row(local, mine.w, mine.rw);
+        if (tile_hit(mine, mine.tx0 + (local - row * mine.w), mine.ty0 + row, m)) {
+          if (n <= kMaskCands) mask |= 1ull << local;
+          ++cnt;
+        }
+      }
+      if (n > 0) sm.hits[lane] = cnt, sm.mask[lane] = mask;
+    } else if (total > 0) {
+      sm.incl[lane] = (int)incl;
+      __syncwarp();
+      for (int base = 0; base < (int)total; base += 32) {
+        const int k = base + lane;
+        int owner = -1, local = 0;
+        bool hit = false;
+        if (k < (int)total) {
+          owner = find_owner(sm.incl, k);
+          const SplatTiles& s = sm.t[owner];
+          local = k - (owner ? sm.incl[owner - 1] : 0);
+          const int row = cand_row(local, s.w, s.rw);
+          hit = tile_hit(s, s.tx0 + (local - row * s.w), s.ty0 + row, m);
+        }
+        // Owners are non-decreasing across lanes: the first lane of each
+        // segment of equal owner adds the segment's hits.
+        const int prev = __shfl_up_sync(kFullMask, owner, 1);
+        const unsigned starts = __ballot_sync(kFullMask, lane == 0 || owner != prev);
+        const unsigned hits = __ballot_sync(kFullMask, hit);
+        const unsigned le = (lane == 31) ? 0xffffffffu : ((2u << lane) - 1u);
+        const int seg0 = 31 - __clz(starts & le);
+        const unsigned above = starts & ~le;
+        const unsigned seg = (above ? ((1u << (__ffs(above) - 1)) - 1u) : 0xffffffffu) & ~((1u << seg0) - 1u);
+        if (lane == seg0 && owner >= 0) {
+          sm.hits[owner] += __popc(hits & seg);
+          // The segment's lanes hold consecutive candidates local, local+1, ...
+          if (sm.t[owner].n <= kMaskCands) sm.mask[owner] |= (unsigned long long)((hits & seg) >> seg0) << local;
+        }
+        __syncwarp();
+      }
+    }
+    __syncwarp();
+  }
+
+  // 4. Row walk of the splats that meet span_geom's conditions.
+  const int rows = span ? mine.n / mine.w : 0;
+  int incl = rows;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int total = __shfl_sync(kFullMask, incl, 31);
+  if (total == 0) return;
+  sm.incl[lane] = incl;
+  __syncwarp();
+  int qn = 0;
+  // The exact test of up to 32 queued tiles.
+  auto flush = [&]() {
+    __syncwarp();
+    const int take = min(qn, 32);
+    if (lane < take) {
+      const int local = cs.qlocal[lane], owner = cs.qowner[lane];
+      const SplatTiles& s = sm.t[owner];
+      const int row = cand_row(local, s.w, s.rw);
+      if (tile_hit(s, s.tx0 + (local - row * s.w), s.ty0 + row, m)) {
+        atomicAdd(&sm.hits[owner], 1);
+        if (s.n <= kMaskCands) atomicOr(&sm.mask[owner], 1ull << local);
+        else if (sm.big[owner] >= 0) atomicOr(big.words + sm.big[owner] + (local >> 5), 1u << (local & 31));
+      }
+    }
+    const int rest = qn - take;
+    int mv = 0, mo = 0;
+    if (lane < rest) mv = cs.qlocal[32 + lane], mo = cs.qowner[32 + lane];
+    __syncwarp();
+    if (lane < rest) cs.qlocal[lane] = mv, cs.qowner[lane] = (unsigned char)mo;
+    __syncwarp();
+    qn = rest;
+  };
+  for (int base = 0; base < total; base += 32) {
+    const int k = base + lane;
+    int owner = 0, row0 = 0, t0 = 0;
+    int pl = 0, ph = -1, hl = 0, hh = -1;  // possible and sure column runs
+    if (k < total) {
+      owner = find_owner(sm.incl, k);
+      const SplatTiles& s = sm.t[owner];
+      const SpanGeom& g = cs.g[owner];
+      const int r = k - (owner ? sm.incl[owner - 1] : 0);
+      const int ty = s.ty0 + r;
+      const double e0 = (double)tile_rx0(ty) - g.my, e1 = (double)tile_rx1(ty, m.H) - g.my;
+      t0 = s.tx0;
+      row0 = r * s.w;
+      const int t1 = s.tx0 + s.w - 1;
+      double xl, xr;
+      if (strip_extent(g, 1, e0, e1, xl, xr)) {
+        pl = first_col_reaching(g.mx + xl, t0, t1, m.W);
+        ph = last_col_reaching(g.mx + xr, t0, t1);
+        if (pl <= ph && strip_extent(g, 0, e0, e1, xl, xr)) {
+          hl = first_col_reaching(g.mx + xl, t0, t1, m.W);
+          hh = last_col_reaching(g.mx + xr, t0, t1);
+        }
+      }
+      if (hl <= hh) {
+        atomicAdd(&sm.hits[owner], hh - hl + 1);
+        const int l0 = row0 + (hl - t0), l1 = row0 + (hh - t0);
+        if (s.n <= kMaskCands) {
+          atomicOr(&sm.mask[owner], (~0ull >> (63 - (l1 - l0))) << l0);
+        } else if (sm.big[owner] >= 0) {
+          uint32_t* const wd = big.words + sm.big[owner];
+          for (int wi = l0 >> 5; wi <= (l1 >> 5); ++wi) {
+            const int lo = max(l0 - 32 * wi, 0), hi = min(l1 - 32 * wi, 31);
+            atomicOr(&wd[wi], (0xffffffffu >> (31 - (hi - lo))) << lo);
+          }
+        }
+      }
+    }
+    // The unsure columns: [pl, ph] minus the sure run [hl, hh].
+    int a0 = pl, a1 = ph, b0 = 0, b1 = -1;
+    if (hl <= hh) a1 = hl - 1, b0 = hh + 1, b1 = ph;
+    const int na = max(a1 - a0 + 1, 0), u = na + max(b1 - b0 + 1, 0);
+    for (int i = 0; __any_sync(kFullMask, i < u); ++i) {
+      const bool has = i < u;
+      const unsigned bal = __ballot_sync(kFullMask, has);
+      if (has) {
+        const int col = i < na ? a0 + i : b0 + (i - na);
+        const int at = qn + __popc(bal & lt);
+        cs.qlocal[at] = row0 + (col - t0);
+        cs.qowner[at] = (unsigned char)owner;
+      }
+      qn += __popc(bal);
+      if (qn >= 32) flush();
+    }
+  }
+  while (qn > 0) flush();
+  __syncwarp();
 }
 
 // Scratch that later kernels of the same phase need cleared, zeroed by the
@@ -291,7 +561,7 @@ __global__ void __launch_bounds__(256)
               ZeroList zero, BigBits big) {
   pdl_wait();
   pdl_trigger();
-  __shared__ WarpTilesSmem s_warp[8];
+  __shared__ CountSmem s_count[8];
   zero_words(zero);  // the depth sort's and the scan's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -305,11 +575,10 @@ __global__ void __launch_bounds__(256)
     const float2 mu = means2d[i];
     t = splat_tiles(mu.x, mu.y, conics[3 * i + 0], conics[3 * i + 1], conics[3 * i + 2], opacities[i], m);
   }
-  WarpTilesSmem& sm = s_warp[warp];
   // Splats with at most kMaskCands candidates also record which ones hit, so
   // k_emit writes their pairs without testing the tiles again.
-  warp_tiles<true>(t, m, sm, [](int, int, int, int, int) {}, big);
-  __syncwarp();
+  warp_count_tiles(t, m, s_count[warp], big);
+  const WarpTilesSmem& sm = s_count[warp].t;
   const uint32_t n = valid ? (uint32_t)sm.hits[lane] : 0u;
   if (valid) {
     counts[i] = n;
@@ -651,7 +920,7 @@ __global__ void __launch_bounds__(256)
   WarpTilesSmem& sm = s_warp[warp];
   warp_tiles(
       t, m, sm,
-      [&](int owner, int tx, int ty, int slot, int) {
+      [&](int owner, int tx, int ty, int slot) {
         if (slot < s_cnt[warp][owner]) {
           const int64_t idx = (int64_t)s_start[warp][owner] + slot;
           keys[idx] = s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx);

@@ -95,6 +95,40 @@ def test_binning_edge_values():
     assert_bin_equal(gpu_bin(s), cpu_bin(s))
 
 
+def test_binning_row_walk_edges():
+    """k_prepare finds most hit tiles row by row from the support ellipse's
+    extent in each tile row (with margins on both sides of the threshold) and
+    sends only the tiles between the sure and the possible runs to the exact
+    ellipse-rectangle test. Splats near the limits of that walk must bin
+    exactly as the oracle does: axis ratios around the admitted 64:1 (k =
+    4096), minor radii down to a few hundredths of a pixel, opacities just
+    above the alpha threshold (tiny tau), means on tile edges, pixel centres
+    and tile centres, and frames whose last tile row and column are one pixel
+    wide."""
+    B, G, H, W = 2, 6000, 16 * 20 + 1, 16 * 24 + 1
+    g = torch.Generator().manual_seed(4242)
+    s = make_2d(B, G, H, W, seed=4243)
+    major = torch.exp(torch.rand(B, G, generator=g) * (np.log(80.0) - np.log(0.03)) + np.log(0.03))
+    ratios = torch.tensor([1.0, 8.0, 32.0, 60.0, 63.9, 64.0, 64.1, 66.0, 80.0, 200.0, 1000.0])
+    ratio = ratios[torch.randint(0, len(ratios), (B, G), generator=g)]
+    theta = torch.rand(B, G, generator=g) * np.pi
+    theta[:, ::7] = 0.0
+    theta[:, 1::7] = np.pi / 4
+    from workloads import conic_from_sigma
+    s.conics.copy_(conic_from_sigma(torch.stack([major, major / ratio], -1), theta))
+    m = s.means2d
+    third = G // 3
+    k = torch.randint(0, 24, (B, third), generator=g).float() * 16.0
+    off = torch.tensor([0.0, 0.5, 8.0, 15.5, 16.0])[torch.randint(0, 5, (B, third), generator=g)]
+    m[:, :third, 0] = k + off
+    m[:, :third, 1] = torch.randint(0, 20, (B, third), generator=g).float() * 16.0 + 8.0
+    m[:, third:2 * third] = torch.floor(m[:, third:2 * third]) + 0.5
+    o = s.opacities
+    o[:, ::5] = (1.0 / 255.0) * (1.0 + 1e-6)
+    o[:, 1::5] = 1.0
+    assert_bin_equal(gpu_bin(s), cpu_bin(s))
+
+
 @pytest.mark.parametrize("B,G", [(1, 65536), (2, 30001), (3, 8192), (2, 8193)])
 def test_depth_order_with_ties(B, G):
     """Depths drawn from 37 values: the depth order must keep input order within
