@@ -740,40 +740,52 @@ __global__ void __launch_bounds__(kScanThreads, 2)
 // k_prepare) and writes its pairs at its scan slot, in row-major tile order:
 // key = global tile index (32 bits), value = rank index. The stable sort on
 // the tile key then leaves each tile's list in rank (= depth) order.
-// Per-warp shared state of warp_emit_bits.
+// Per-warp shared state of warp_emit_bits (the owners' constants) and of k_emit.
 struct BitsEmitSmem {
-  int incl[32];  // inclusive scan of the owners' bit-word counts
+  int incl[32];  // inclusive scan of the owners' half-word counts
   int done[32];  // pairs written per owner so far
   int bo[32], w[32], tx0[32], ty0[32], start[32], cnt[32];
+  float rw[32];
   uint32_t mlo[32], mhi[32];  // an owner's 64-bit hit mask (bo == kMaskWords) as two words
   uint32_t tbase[32];
-  // The round's 32 words: bits, inclusive popcount prefix, owner, word index, first slot.
-  uint32_t rbits[32];
-  int rpre[32], rowner[32], rwi[32], rslot[32];
+};
+// One round's staged pairs (in slot order) and, per half-word of the round,
+// its owner, first staged pair and that pair's slot.
+constexpr int kEmitStage = 512;  // 32 half-words x 16 candidates
+struct EmitStage {
+  uint32_t key[kEmitStage];
+  unsigned char lane[kEmitStage];
+  int owner[32], q0[32], slot0[32];
+};
+struct EmitSmem {
+  BitsEmitSmem bits;
+  union {  // the bit writer, then warp_tiles for the splats without bits
+    EmitStage stage;
+    WarpTilesSmem tiles;
+  } u;
 };
 
 // Writes the pairs of the warp's splats that kept hit bits: bo >= 0 for a
 // larger splat's words in the hit-bit region, bo == kMaskWords for a small
-// splat whose 64-bit hit mask (`mask`) stands for its one or two words. The 32
-// splats of a warp own one contiguous range of pair slots, so all their pairs
-// leave as consecutive stores. The bit
-// words are taken 32 at a time (round r covers words 32r .. 32r+31 of the
-// concatenated lists); a word's first pair slot is its owner's pairs so far
-// plus the popcounts of the owner's earlier words in the round (a segmented
-// warp scan). The round's pairs are then written by consecutive lanes: pair q
-// finds its word by a binary search over the popcount prefix and its bit as the
-// (q - word start)-th set bit, so consecutive lanes write consecutive slots and
-// each splat's pairs keep row-major candidate order. Costs one round per 32
-// words instead of one per 32 candidates. Returns the number of pairs of this
-// lane's splat.
+// splat whose 64-bit hit mask (`mask`) stands for its words. The 32 splats of
+// a warp own one contiguous range of pair slots, so all their pairs leave as
+// consecutive stores. The bits are taken as half-words of 16 candidates, 32 per
+// round (round r covers half-words 32r .. 32r+31 of the warp's concatenated
+// lists). Lane L expands half-word L: it walks the set bits in order, steps the
+// tile row and column from the previous bit, and stages each pair's key at its
+// place among the round's pairs (the popcount prefix over the lanes). The warp
+// then writes the staged pairs with consecutive lanes on consecutive slots.
+// Each splat's pairs keep row-major candidate order. Returns the number of
+// pairs of this lane's splat (sm.start, sm.cnt and sm.tbase are set by the
+// caller).
 constexpr int kMaskWords = -2;
-__device__ __forceinline__ int warp_emit_bits(int bo, unsigned long long mask, const SplatTiles& t, int start, int cnt,
-                                              uint32_t tbase, int r0, const uint32_t* __restrict__ words,
-                                              const Meta& m, uint32_t* __restrict__ keys,
-                                              uint32_t* __restrict__ vals, BitsEmitSmem& sm) {
+__device__ __forceinline__ int warp_emit_bits(int bo, unsigned long long mask, const SplatTiles& t, int r0,
+                                              const uint32_t* __restrict__ words, const Meta& m,
+                                              uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+                                              BitsEmitSmem& sm, EmitStage& st) {
   const int lane = threadIdx.x & 31;
-  const int nw = (bo >= 0 || bo == kMaskWords) ? (t.n + 31) >> 5 : 0;
-  int incl = nw;
+  const int nh = (bo >= 0 || bo == kMaskWords) ? (t.n + 15) >> 4 : 0;
+  int incl = nh;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(kFullMask, incl, o);
@@ -785,30 +797,22 @@ __device__ __forceinline__ int warp_emit_bits(int bo, unsigned long long mask, c
   sm.done[lane] = 0;
   sm.bo[lane] = bo;
   sm.w[lane] = t.w;
+  sm.rw[lane] = t.rw;
   sm.tx0[lane] = t.tx0;
   sm.ty0[lane] = t.ty0;
-  sm.start[lane] = start;
-  sm.cnt[lane] = cnt;
-  sm.tbase[lane] = tbase;
   sm.mlo[lane] = (uint32_t)mask;
   sm.mhi[lane] = (uint32_t)(mask >> 32);
   __syncwarp();
   for (int base = 0; base < total; base += 32) {
     const int k = base + lane;
-    int owner = 32, wi = 0;  // 32: no word (past the end)
+    int owner = 32, hw = 0;  // 32: no half-word (past the end)
     uint32_t bits = 0u;
     if (k < total) {
-      int lo = 0, hi = 31;  // first owner whose inclusive end exceeds k
-#pragma unroll
-      for (int step = 0; step < 5; ++step) {
-        const int mid = (lo + hi) >> 1;
-        if (sm.incl[mid] > k) hi = mid;
-        else lo = mid + 1;
-      }
-      owner = lo;
-      wi = k - (owner ? sm.incl[owner - 1] : 0);
+      owner = find_owner(sm.incl, k);
+      hw = k - (owner ? sm.incl[owner - 1] : 0);
       const int ob = sm.bo[owner];
-      bits = ob >= 0 ? words[ob + wi] : (wi == 0 ? sm.mlo[owner] : sm.mhi[owner]);
+      const uint32_t word = ob >= 0 ? words[ob + (hw >> 1)] : ((hw >> 1) == 0 ? sm.mlo[owner] : sm.mhi[owner]);
+      bits = (hw & 1) ? (word >> 16) : (word & 0xffffu);
     }
     const int pc = __popc(bits);
     int pre = pc;  // inclusive prefix of the popcounts over the warp
@@ -825,40 +829,42 @@ __device__ __forceinline__ int warp_emit_bits(int bo, unsigned long long mask, c
     const int before_seg = __shfl_sync(kFullMask, pre, seg0 > 0 ? seg0 - 1 : 0);
     const int seg_base = seg0 > 0 ? before_seg : 0;  // popcounts of earlier segments in this round
     const int done = owner < 32 ? sm.done[owner] : 0;
-    sm.rbits[lane] = bits;
-    sm.rpre[lane] = pre;
-    sm.rowner[lane] = owner;
-    sm.rwi[lane] = wi;
-    sm.rslot[lane] = done + (pre - pc - seg_base);
+    const int q0 = pre - pc;
+    st.owner[lane] = owner;
+    st.q0[lane] = q0;
+    st.slot0[lane] = done + (q0 - seg_base);
     __syncwarp();
     if (owner < 32 && (lane == 31 || next != owner)) sm.done[owner] = done + (pre - seg_base);
+    if (bits) {
+      const int w = sm.w[owner];
+      const int local0 = hw * 16;
+      const int row = cand_row(local0, w, sm.rw[owner]);
+      int col = local0 - row * w, at = 0, q = q0;
+      uint32_t key = sm.tbase[owner] + (uint32_t)((sm.ty0[owner] + row) * m.tiles_x + sm.tx0[owner]);
+      while (bits) {
+        const int b = __ffs(bits) - 1;
+        bits &= bits - 1;
+        col += b - at;
+        at = b;
+        while (col >= w) {
+          col -= w;
+          key += (uint32_t)m.tiles_x;
+        }
+        st.key[q] = key + (uint32_t)col;
+        st.lane[q] = (unsigned char)lane;
+        ++q;
+      }
+    }
+    __syncwarp();
     const int round_pairs = __shfl_sync(kFullMask, pre, 31);
     for (int q = lane; q < round_pairs; q += 32) {
-      int lo = 0, hi = 31;  // first word whose inclusive prefix exceeds q
-#pragma unroll
-      for (int step = 0; step < 5; ++step) {
-        const int mid = (lo + hi) >> 1;
-        if (sm.rpre[mid] > q) hi = mid;
-        else lo = mid + 1;
-      }
-      const uint32_t wb = sm.rbits[lo];
-      const int j = q - (sm.rpre[lo] - __popc(wb));  // rank of the pair's bit within its word
-      const int o = sm.rowner[lo];
-      const int slot = sm.rslot[lo] + j;
+      const int l = st.lane[q];
+      const int o = st.owner[l];
+      const int slot = st.slot0[l] + (q - st.q0[l]);
       if (slot < sm.cnt[o]) {
-        int b0 = 0, b1 = 31;  // lowest bit position p with more than j set bits in wb[0..p]
-#pragma unroll
-        for (int step = 0; step < 5; ++step) {
-          const int mid = (b0 + b1) >> 1;
-          if (__popc(wb & ((2u << mid) - 1u)) > j) b1 = mid;
-          else b0 = mid + 1;
-        }
-        const int local = sm.rwi[lo] * 32 + b0;
-        const int w = sm.w[o];
-        const int row = cand_row(local, w);
-        const int tx = sm.tx0[o] + (local - row * w), ty = sm.ty0[o] + row;
-        keys[(int64_t)sm.start[o] + slot] = sm.tbase[o] + (uint32_t)(ty * m.tiles_x + tx);
-        vals[(int64_t)sm.start[o] + slot] = (uint32_t)(r0 + o);
+        const int64_t idx = (int64_t)sm.start[o] + slot;
+        keys[idx] = st.key[q];
+        vals[idx] = (uint32_t)(r0 + o);
       }
     }
     __syncwarp();
@@ -872,10 +878,7 @@ __global__ void __launch_bounds__(256)
            uint32_t* __restrict__ status, ZeroList zero, BigBits big) {
   pdl_wait();
   pdl_trigger();
-  __shared__ WarpTilesSmem s_warp[8];
-  __shared__ BitsEmitSmem s_bits[8];
-  __shared__ int s_start[8][32], s_cnt[8][32];
-  __shared__ uint32_t s_tbase[8][32];
+  __shared__ EmitSmem s_emit[8];
   zero_words(zero);  // the tile sort's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -893,7 +896,7 @@ __global__ void __launch_bounds__(256)
   }
   // A splat with a recorded hit mask writes its pairs straight from it (the
   // set bits in row-major candidate order); a larger one with hit bits reads
-  // them in warp_tiles; the others are tested again.
+  // them from the region; the others are tested again.
   int own_hits = -1;
   int bo = -1;  // where this splat's hit bits are: region offset, kMaskWords, or none (-1)
   unsigned long long mask = 0ull;
@@ -906,24 +909,26 @@ __global__ void __launch_bounds__(256)
     own_hits = __popcll(mask);
     bo = kMaskWords;
   }
-  s_start[warp][lane] = start;
-  s_cnt[warp][lane] = cnt;
-  s_tbase[warp][lane] = tbase;
+  EmitSmem& es = s_emit[warp];
+  es.bits.start[lane] = start;
+  es.bits.cnt[lane] = cnt;
+  es.bits.tbase[lane] = tbase;
   const int r0 = r - lane;
   // Splats with hit bits (a mask or region words): their pairs straight from
   // the bits, written by the whole warp.
   if (masks) {
-    const int bit_hits = warp_emit_bits(bo, mask, t, start, cnt, tbase, r0, big.words, m, keys, vals, s_bits[warp]);
+    const int bit_hits = warp_emit_bits(bo, mask, t, r0, big.words, m, keys, vals, es.bits, es.u.stage);
     if (bo >= 0) own_hits = bit_hits;
     if (bo != -1) t.n = 0;
   }
-  WarpTilesSmem& sm = s_warp[warp];
+  __syncwarp();  // the stage is reused by warp_tiles
+  WarpTilesSmem& sm = es.u.tiles;
   warp_tiles(
       t, m, sm,
       [&](int owner, int tx, int ty, int slot) {
-        if (slot < s_cnt[warp][owner]) {
-          const int64_t idx = (int64_t)s_start[warp][owner] + slot;
-          keys[idx] = s_tbase[warp][owner] + (uint32_t)(ty * m.tiles_x + tx);
+        if (slot < es.bits.cnt[owner]) {
+          const int64_t idx = (int64_t)es.bits.start[owner] + slot;
+          keys[idx] = es.bits.tbase[owner] + (uint32_t)(ty * m.tiles_x + tx);
           vals[idx] = (uint32_t)(r0 + owner);
         }
       });
