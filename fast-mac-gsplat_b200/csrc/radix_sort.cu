@@ -96,6 +96,39 @@ struct OnesweepSmem {
   long long fence_sink;
 };
 
+// Ranks one warp's ITEMS x 32 keys by digit, stably in (item, lane) order,
+// counting into the warp's digit histogram. The lanes holding the same digit
+// come from one ballot per digit bit (cheaper than match.any): NB ballots on
+// bits 0 .. NB-1 (a digit has no set bit above its pass's width), and with
+// kSentinel one more on bit kRadixBits, set only in the invalid lanes' digit
+// kRadix (past the end of the keys).
+template <int NB, bool kSentinel, typename K, int ITEMS>
+__device__ __forceinline__ void rank_items(const K (&k)[ITEMS], uint32_t (&rank)[ITEMS], int64_t seg, int64_t n,
+                                           int shift, uint32_t dmask, int lane, uint32_t lt_mask,
+                                           uint32_t* __restrict__ warp_hist) {
+#pragma unroll
+  for (int i = 0; i < ITEMS; ++i) {
+    const int64_t idx = seg + i * 32 + lane;
+    const bool valid = !kSentinel || idx < n;
+    const uint32_t d = valid ? ((uint32_t)(k[i] >> shift) & dmask) : kRadix;
+    uint32_t peers = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < NB + (kSentinel ? 1 : 0); ++b) {
+      const int bit = b < NB ? b : kRadixBits;
+      const bool on = (d >> bit) & 1u;
+      const uint32_t bal = __ballot_sync(kFullMask, on);
+      peers &= on ? bal : ~bal;
+    }
+    uint32_t cnt_before = 0;
+    if (valid) cnt_before = warp_hist[d];
+    __syncwarp();
+    rank[i] = cnt_before + __popc(peers & lt_mask);
+    const int leader = 31 - __clz(peers);
+    if (valid && lane == leader) warp_hist[d] = cnt_before + __popc(peers);
+    __syncwarp();
+  }
+}
+
 // One digit pass. Keys are held warp-striped: warp w owns the contiguous
 // segment [tile + w*32*ITEMS, +32*ITEMS) and lane l holds its items i*32+l, so
 // (item, lane) order is input order and the lane-order ranking is stable. Each
@@ -165,27 +198,19 @@ __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
     if (tid == 0) sm.fence_sink = c;
   }
 
-#pragma unroll
-  for (int i = 0; i < ITEMS; ++i) {
-    const int64_t idx = seg + i * 32 + lane;
-    const bool valid = idx < n;
-    const uint32_t d = valid ? ((uint32_t)(k[i] >> shift) & dmask) : kRadix;  // sentinel group
-    // Lanes holding the same digit, from one ballot per digit bit (the
-    // invalid-lane sentinel differs in bit 8). Cheaper than match.any.
-    uint32_t peers = 0xffffffffu;
-#pragma unroll
-    for (int b = 0; b <= kRadixBits; ++b) {
-      const bool on = (d >> b) & 1u;
-      const uint32_t bal = __ballot_sync(kFullMask, on);
-      peers &= on ? bal : ~bal;
+  // A full partition ballots exactly the pass's digit bits (a last pass of
+  // fewer bits takes fewer ballots); the last, partial one also sets its
+  // invalid lanes apart by the sentinel bit.
+  if (tile0 + kTile <= n) {
+    switch (bits) {
+      case 7: rank_items<7, false>(k, rank, seg, n, shift, dmask, lane, lt_mask, sm.warp_hist[warp]); break;
+      case 6: rank_items<6, false>(k, rank, seg, n, shift, dmask, lane, lt_mask, sm.warp_hist[warp]); break;
+      case 5: rank_items<5, false>(k, rank, seg, n, shift, dmask, lane, lt_mask, sm.warp_hist[warp]); break;
+      case 4: rank_items<4, false>(k, rank, seg, n, shift, dmask, lane, lt_mask, sm.warp_hist[warp]); break;
+      default: rank_items<kRadixBits, false>(k, rank, seg, n, shift, dmask, lane, lt_mask, sm.warp_hist[warp]); break;
     }
-    uint32_t cnt_before = 0;
-    if (valid) cnt_before = sm.warp_hist[warp][d];
-    __syncwarp();
-    rank[i] = cnt_before + __popc(peers & lt_mask);
-    const int leader = 31 - __clz(peers);
-    if (valid && lane == leader) sm.warp_hist[warp][d] = cnt_before + __popc(peers);
-    __syncwarp();
+  } else {
+    rank_items<kRadixBits, true>(k, rank, seg, n, shift, dmask, lane, lt_mask, sm.warp_hist[warp]);
   }
   __syncthreads();
 
