@@ -938,37 +938,34 @@ __global__ void __launch_bounds__(256)
 
 // tile_offsets[t] = index of the first sorted pair of tile t (= exclusive
 // prefix of per-tile counts); every entry is written by exactly one thread.
-// A thread takes 4 consecutive sorted pairs at a time (one 16-byte load of
-// keys), striding over the list: a grid of a few CTAs per SM, since a CTA per
-// 1024 pairs made the launch bound by CTA scheduling (150 us for 60M pairs).
+// A thread takes 4 consecutive sorted pairs (one 16-byte load of keys).
 // keys64 (optional) receives (tile << 32) | depth_key of each sorted pair.
 __global__ void __launch_bounds__(256)
     k_ranges(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, const float4* __restrict__ rec,
              int64_t n_pairs, int total_tiles, int32_t* __restrict__ tile_offsets, uint64_t* __restrict__ keys64) {
   pdl_wait();
   pdl_trigger();
-  const int64_t stride = 4 * (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); i0 < n_pairs; i0 += stride) {
-    uint32_t k[4];
-    if (i0 + 4 <= n_pairs) {
-      const uint4 q = *reinterpret_cast<const uint4*>(keys + i0);  // keys is 256-byte aligned
-      k[0] = q.x, k[1] = q.y, k[2] = q.z, k[3] = q.w;
-    } else {
+  const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i0 >= n_pairs) return;
+  uint32_t k[4];
+  if (i0 + 4 <= n_pairs) {
+    const uint4 q = *reinterpret_cast<const uint4*>(keys + i0);  // keys is 256-byte aligned
+    k[0] = q.x, k[1] = q.y, k[2] = q.z, k[3] = q.w;
+  } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) k[u] = (i0 + u < n_pairs) ? keys[i0 + u] : 0u;
-    }
-    int64_t prev = (i0 == 0) ? -1 : (int64_t)keys[i0 - 1];
+    for (int u = 0; u < 4; ++u) k[u] = (i0 + u < n_pairs) ? keys[i0 + u] : 0u;
+  }
+  int64_t prev = (i0 == 0) ? -1 : (int64_t)keys[i0 - 1];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t i = i0 + u;
-      if (i < n_pairs) {
-        const int64_t t = k[u];
-        for (int64_t s = prev + 1; s <= t; ++s) tile_offsets[s] = (int32_t)i;
-        if (i == n_pairs - 1)
-          for (int64_t s = t + 1; s <= total_tiles; ++s) tile_offsets[s] = (int32_t)n_pairs;
-        if (keys64) keys64[i] = ((uint64_t)t << 32) | __float_as_uint(rec[3 * (size_t)vals[i] + 2].y);
-        prev = t;
-      }
+  for (int u = 0; u < 4; ++u) {
+    const int64_t i = i0 + u;
+    if (i < n_pairs) {
+      const int64_t t = k[u];
+      for (int64_t s = prev + 1; s <= t; ++s) tile_offsets[s] = (int32_t)i;
+      if (i == n_pairs - 1)
+        for (int64_t s = t + 1; s <= total_tiles; ++s) tile_offsets[s] = (int32_t)n_pairs;
+      if (keys64) keys64[i] = ((uint64_t)t << 32) | __float_as_uint(rec[3 * (size_t)vals[i] + 2].y);
+      prev = t;
     }
   }
 }
@@ -1212,7 +1209,7 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
                                    total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
-  launch_pdl(k_ranges, std::min(grid1d((total_pairs + 3) / 4, 256), 148 * 8), 256, 0, stream, w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
+  launch_pdl(k_ranges, grid1d((total_pairs + 3) / 4, 256), 256, 0, stream, w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
                                                          reinterpret_cast<const float4*>(rec), total_pairs,
                                                          m.total_tiles, tile_offsets, keys);
   note_launches(1);
