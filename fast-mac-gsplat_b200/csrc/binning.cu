@@ -142,8 +142,8 @@ constexpr double kSpanMargin = 0x1p-7;
 constexpr int kSpanMinCands = 32;
 
 struct SpanGeom {
-  double mx, my, b, det, ia, bc;  // ia = 1 / a, bc = b / c
-  double E[2], XR[2], aT[2];      // per threshold (0: T_in, 1: T_out): y and x half extents, a T
+  double det, ia, bc;          // ia = 1 / a, bc = b / c (the mean and b: the splat's floats)
+  double E[2], XR[2], aT[2];  // per threshold (0: T_in, 1: T_out): y and x half extents, a T
 };
 
 // The constants of the row walk, or false when the splat is outside the
@@ -157,7 +157,7 @@ __device__ __forceinline__ bool span_geom(const SplatTiles& s, SpanGeom& g) {
   const double det = da * dc - db * db;  // products exact in double
   const double tr = da + dc;
   if (!(det > 0.0) || !(tr * tr <= 4096.0 * det) || !(tr <= 256.0 * (double)s.tau)) return false;
-  g.mx = s.mx, g.my = s.my, g.b = db, g.det = det, g.ia = 1.0 / da, g.bc = db / dc;
+  g.det = det, g.ia = 1.0 / da, g.bc = db / dc;
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const double T = (double)s.tau * (k ? 1.0 + kSpanMargin : 1.0 - kSpanMargin);
@@ -173,13 +173,14 @@ __device__ __forceinline__ bool span_geom(const SplatTiles& s, SpanGeom& g) {
 // The right boundary x(e) = (-b e + sqrt(a T - det e^2)) / a is concave with its
 // maximum XR at e = -(b / c) XR, the left one convex with its minimum -XR at
 // e = (b / c) XR; off those points the extreme is at an end of the strip.
-__device__ __forceinline__ bool strip_extent(const SpanGeom& g, int k, double e0, double e1, double& xl, double& xr) {
+__device__ __forceinline__ bool strip_extent(const SpanGeom& g, double b, int k, double e0, double e1, double& xl,
+                                             double& xr) {
   const double lo = fmax(e0, -g.E[k]), hi = fmin(e1, g.E[k]);
   if (!(lo <= hi)) return false;
   const double es = g.bc * g.XR[k];
   const double sl = sqrt(fmax(g.aT[k] - g.det * lo * lo, 0.0));
   const double sh = sqrt(fmax(g.aT[k] - g.det * hi * hi, 0.0));
-  const double cl = -g.b * lo, ch = -g.b * hi;
+  const double cl = -b * lo, ch = -b * hi;
   xr = (-es >= lo && -es <= hi) ? g.XR[k] : fmax(cl + sl, ch + sh) * g.ia;
   xl = (es >= lo && es <= hi) ? -g.XR[k] : fmin(cl - sl, ch - sh) * g.ia;
   return true;
@@ -486,17 +487,18 @@ __device__ __forceinline__ void warp_count_tiles(const SplatTiles& mine, const M
       const SpanGeom& g = cs.g[owner];
       const int r = k - (owner ? sm.incl[owner - 1] : 0);
       const int ty = s.ty0 + r;
-      const double e0 = (double)tile_rx0(ty) - g.my, e1 = (double)tile_rx1(ty, m.H) - g.my;
+      const double gmx = s.mx, gmy = s.my, gb = s.b;
+      const double e0 = (double)tile_rx0(ty) - gmy, e1 = (double)tile_rx1(ty, m.H) - gmy;
       t0 = s.tx0;
       row0 = r * s.w;
       const int t1 = s.tx0 + s.w - 1;
       double xl, xr;
-      if (strip_extent(g, 1, e0, e1, xl, xr)) {
-        pl = first_col_reaching(g.mx + xl, t0, t1, m.W);
-        ph = last_col_reaching(g.mx + xr, t0, t1);
-        if (pl <= ph && strip_extent(g, 0, e0, e1, xl, xr)) {
-          hl = first_col_reaching(g.mx + xl, t0, t1, m.W);
-          hh = last_col_reaching(g.mx + xr, t0, t1);
+      if (strip_extent(g, gb, 1, e0, e1, xl, xr)) {
+        pl = first_col_reaching(gmx + xl, t0, t1, m.W);
+        ph = last_col_reaching(gmx + xr, t0, t1);
+        if (pl <= ph && strip_extent(g, gb, 0, e0, e1, xl, xr)) {
+          hl = first_col_reaching(gmx + xl, t0, t1, m.W);
+          hh = last_col_reaching(gmx + xr, t0, t1);
         }
       }
       if (hl <= hh) {
@@ -534,6 +536,30 @@ __device__ __forceinline__ void warp_count_tiles(const SplatTiles& mine, const M
   __syncwarp();
 }
 
+// The depth sort's digit histogram (radix_sort_pairs' digit_hist) is counted
+// by k_prepare, which writes the depth keys, instead of a histogram launch
+// over them: counts in shared memory per CTA, added to the global counts once
+// per CTA; the global counts are cleared by k_clear_words in the launch before.
+// (The tile keys are not counted in k_emit: their low digits differ from pair
+// to pair, one shared atomic each, which made the c4 emit phase 52 us slower
+// than the separate histogram pass.)
+constexpr int kDepthHistPasses = kSortMaxPasses;  // 64-bit depth keys
+
+__global__ void k_clear_words(uint32_t* __restrict__ a, int na, uint32_t* __restrict__ b, int nb) {
+  pdl_wait();
+  pdl_trigger();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < na) a[i] = 0u;
+  if (i < nb) b[i] = 0u;
+}
+
+__device__ __forceinline__ void flush_hist(const uint32_t* s, uint32_t* g, int words) {
+  for (int i = threadIdx.x; i < words; i += blockDim.x) {
+    const uint32_t v = s[i];
+    if (v) atomicAdd(&g[i], v);
+  }
+}
+
 // Scratch that later kernels of the same phase need cleared, zeroed by the
 // phase's first kernel instead of separate memset launches.
 struct ZeroList {
@@ -558,10 +584,13 @@ __global__ void __launch_bounds__(256)
               const float* __restrict__ opacities, const float* __restrict__ depths,
               K* __restrict__ sort_keys, uint32_t* __restrict__ sort_vals,
               uint32_t* __restrict__ counts, unsigned long long* __restrict__ masks, uint32_t* __restrict__ status,
-              ZeroList zero, BigBits big) {
+              ZeroList zero, BigBits big, uint32_t* __restrict__ depth_hist, int depth_passes) {
   pdl_wait();
   pdl_trigger();
   __shared__ CountSmem s_count[8];
+  __shared__ uint32_t s_hist[(sizeof(K) == 4 ? 4 : kDepthHistPasses) * kRadix];  // the depth keys' digit counts
+  for (int i = threadIdx.x; i < depth_passes * kRadix; i += blockDim.x) s_hist[i] = 0u;
+  __syncthreads();
   zero_words(zero);  // the depth sort's and the scan's scratch
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -570,8 +599,10 @@ __global__ void __launch_bounds__(256)
   if (valid) {
     const int b = fast_div(i, m.div_G);
     // One view: the 32-bit depth key alone; several: the view in the high word.
-    sort_keys[i] = (K)(((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]));
+    const K key = (K)(((uint64_t)(uint32_t)b << 32) | depth_key(depths[i]));
+    sort_keys[i] = key;
     sort_vals[i] = (uint32_t)i;
+    for (int p = 0; p < depth_passes; ++p) atomicAdd(&s_hist[p * kRadix + ((uint32_t)(key >> (8 * p)) & 255u)], 1u);
     const float2 mu = means2d[i];
     t = splat_tiles(mu.x, mu.y, conics[3 * i + 0], conics[3 * i + 1], conics[3 * i + 2], opacities[i], m);
   }
@@ -591,6 +622,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(kFullMask, wsum, o);
   if (lane == 0 && wsum) atomicAdd(reinterpret_cast<unsigned long long*>(status + GSB_STATUS_PAIR_TOTAL64), wsum);
+  __syncthreads();
+  flush_hist(s_hist, depth_hist, depth_passes * kRadix);
 }
 
 // Gathers splats into depth-rank order (packed 48-byte records), and turns the
@@ -998,6 +1031,7 @@ struct PrepareWs {
   unsigned long long* masks;  // hit masks of splats with <= kMaskCands candidates, input order
   unsigned long long* lookback;
   uint32_t* counter;
+  uint32_t* depth_hist;  // digit counts of the depth keys (k_prepare -> depth sort)
 };
 
 void carve_prepare(Carver& c, const Meta& m, PrepareWs* w) {
@@ -1010,10 +1044,12 @@ void carve_prepare(Carver& c, const Meta& m, PrepareWs* w) {
   w->masks = c.take<unsigned long long>(n);
   w->lookback = c.take<unsigned long long>((n + kScanTile - 1) / kScanTile + 1);
   w->counter = c.take<uint32_t>(1);
+  w->depth_hist = c.take<uint32_t>((size_t)kDepthHistPasses * kRadix);
 }
 
 int depth_sort_end_bit(const Meta& m) { return 32 + (m.B > 1 ? bits_for(m.B - 1) : 0); }
 bool depth_keys32(const Meta& m) { return m.B == 1; }
+int depth_passes(const Meta& m) { return sort_passes(0, depth_keys32(m) ? 32 : depth_sort_end_bit(m)); }
 
 }  // namespace
 }  // namespace gsb
@@ -1065,11 +1101,15 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   if (workspace_bytes < gsb_bin_prepare_workspace_size(meta) || (m.BG > 0 && !workspace))
     return GSB_ERR_WORKSPACE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  if (cudaMemsetAsync(status, 0, sizeof(uint32_t) * GSB_STATUS_WORDS, stream) != cudaSuccess) return GSB_ERR_CUDA;
-  if (m.BG == 0) return GSB_OK;
+  if (m.BG == 0) return cuda_status(cudaMemsetAsync(status, 0, sizeof(uint32_t) * GSB_STATUS_WORDS, stream));
   Carver c(workspace);
   PrepareWs w;
   carve_prepare(c, m, &w);
+  // The status block and the depth keys' digit counts start at zero.
+  const int dpasses = depth_passes(m);
+  launch_pdl(k_clear_words, grid1d(std::max(GSB_STATUS_WORDS, dpasses * kRadix), 256), 256, 0, stream, status,
+             GSB_STATUS_WORDS, w.depth_hist, dpasses * kRadix);
+  note_launches(1);
   const int parts = (m.BG + kScanTile - 1) / kScanTile;
   const ZeroRegion sz = radix_sort_zero_region(c, m.BG, 0, depth_keys32(m) ? 32 : depth_sort_end_bit(m),
                                                depth_keys32(m));
@@ -1083,11 +1123,11 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   if (depth_keys32(m))
     launch_pdl(k_prepare<uint32_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d),
                conics, opacities, depths, reinterpret_cast<uint32_t*>(w.keys_in), w.vals_in, w.counts, w.masks,
-               status, zero, big_bits_of(m, tile_masks, status));
+               status, zero, big_bits_of(m, tile_masks, status), w.depth_hist, dpasses);
   else
     launch_pdl(k_prepare<uint64_t>, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float2*>(means2d),
                conics, opacities, depths, w.keys_in, w.vals_in, w.counts, w.masks, status, zero,
-               big_bits_of(m, tile_masks, status));
+               big_bits_of(m, tile_masks, status), w.depth_hist, dpasses);
   note_launches(1);
   return cuda_status(cudaGetLastError());
 }
@@ -1119,7 +1159,8 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
     uint32_t* k32_sorted = reinterpret_cast<uint32_t*>(w.keys_sorted);
     // 32-bit keys in the 64-bit key buffers; the sort's scratch (carved after
     // them) is smaller than the 64-bit sort's that the workspace is sized for.
-    e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream, true);
+    e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream, true,
+                         w.depth_hist);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
     launch_pdl(k_gather_scan<uint32_t>, parts, kScanThreads, 0, stream, 
         m, k32_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities, w.counts,
@@ -1127,7 +1168,7 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
         pair_offsets, w.lookback, w.counter, status);
   } else {
     e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
-                         status, stream, true);
+                         status, stream, true, w.depth_hist);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
     launch_pdl(k_gather_scan<uint64_t>, parts, kScanThreads, 0, stream, 
         m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,

@@ -15,7 +15,7 @@ namespace {
 constexpr uint32_t kFlagAgg = 0x40000000u;  // partition aggregate published
 constexpr uint32_t kFlagInc = 0x80000000u;  // inclusive prefix published
 constexpr uint32_t kValueMask = 0x3fffffffu;
-constexpr int kMaxPasses = 8;
+constexpr int kMaxPasses = kSortMaxPasses;
 constexpr int kLookWin = 8;  // predecessors read per look-back step
 
 // Histograms of every digit pass in one read of the keys. A thread takes
@@ -359,7 +359,7 @@ static int sort_items(int64_t n) {
 template <typename K>
 static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32_t* vals_in, K* keys_out,
                                       uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                                      cudaStream_t stream, bool scratch_zeroed) {
+                                      cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist) {
   const int passes = sort_passes(begin_bit, end_bit);
   const int items = sort_items(n);
   const int64_t tile = (int64_t)kSortThreads * items;
@@ -370,8 +370,8 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
   uint32_t* v_tmp = ws.take<uint32_t>(passes > 1 ? (size_t)n : 0);
   const size_t zero_words = (size_t)kMaxPasses * kRadix + kMaxPasses + (size_t)passes * (size_t)parts * kRadix;
   uint32_t* zeroed = ws.take<uint32_t>(zero_words);
-  uint32_t* hist = zeroed;
-  uint32_t* counters = hist + (size_t)kMaxPasses * kRadix;
+  uint32_t* hist = digit_hist ? const_cast<uint32_t*>(digit_hist) : zeroed;
+  uint32_t* counters = zeroed + (size_t)kMaxPasses * kRadix;
   uint32_t* lookback = counters + kMaxPasses;
   if (ws.base == nullptr) return cudaSuccess;
   if (n <= 0) return cudaSuccess;
@@ -387,9 +387,11 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
     if (e != cudaSuccess) return e;
   }
-  launch_pdl(rs_histogram<K>, grid_for((n + kHistItems - 1) / kHistItems, kSortThreads, 148 * 4), kSortThreads, 0, stream, keys_in, n, begin_bit, passes,
-                                                                                   last_bits, hist);
-  note_launches(1);
+  if (!digit_hist) {
+    launch_pdl(rs_histogram<K>, grid_for((n + kHistItems - 1) / kHistItems, kSortThreads, 148 * 4), kSortThreads, 0,
+               stream, keys_in, n, begin_bit, passes, last_bits, hist);
+    note_launches(1);
+  }
   // Ping-pong so the last pass writes keys_out: pass p writes out when
   // (passes-1-p) is even, else tmp.
   const K* ki = keys_in;
@@ -414,16 +416,16 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
 
 cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in, uint64_t* keys_out,
                              uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                             cudaStream_t stream, bool scratch_zeroed) {
+                             cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist) {
   return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream,
-                            scratch_zeroed);
+                            scratch_zeroed, digit_hist);
 }
 
 cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                              uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                             cudaStream_t stream, bool scratch_zeroed) {
+                             cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist) {
   return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream,
-                            scratch_zeroed);
+                            scratch_zeroed, digit_hist);
 }
 
 template <typename K>

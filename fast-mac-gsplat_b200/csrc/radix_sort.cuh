@@ -19,6 +19,7 @@ constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kRadix = 256;
 constexpr int kRadixBits = 8;
 constexpr int64_t kSortMaxN = (int64_t(1) << 30) - 1;  // 30-bit look-back payload
+constexpr int kSortMaxPasses = 8;                     // 64-bit keys
 
 inline int sort_passes(int begin_bit, int end_bit) {
   return end_bit > begin_bit ? (end_bit - begin_bit + kRadixBits - 1) / kRadixBits : 0;
@@ -29,13 +30,18 @@ inline int sort_passes(int begin_bit, int end_bit) {
 // when running (base != nullptr); measuring mode launches nothing.
 // scratch_zeroed: the caller has already cleared the sort's zero-initialised
 // scratch (radix_sort_zero_region) in an earlier kernel, saving a memset launch.
+// digit_hist: when given, the kernel that wrote the keys has already counted
+// their digits there (pass p's 256 counts at digit_hist + 256 p, digits of
+// bits begin_bit + 8p ...), so the histogram launch is skipped.
 cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t* vals_in,
                              uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
-                             int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed);
+                             int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed,
+                             const uint32_t* digit_hist = nullptr);
 // 32-bit keys (end_bit <= 32): 8 bytes per pair moved per pass instead of 12.
 cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in,
                              uint32_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
-                             int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed);
+                             int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed,
+                             const uint32_t* digit_hist = nullptr);
 
 // The words a radix_sort_pairs call carved from `ws` (at its current offset)
 // needs cleared before it runs (histograms, partition counters, look-back).
