@@ -392,6 +392,16 @@ __device__ __forceinline__ float vis_select_fwd_v(float T, float t_thr, float po
 __device__ __forceinline__ bool finite_rgb(float r, float g, float b) {
   return (fabsf(r) <= 3.402823466e38f) & (fabsf(g) <= 3.402823466e38f) & (fabsf(b) <= 3.402823466e38f);
 }
+// Saturation. alpha = min(max_alpha, op * exp(power)), and the backward passes
+// the gradient to op * exp(power) only below max_alpha. A visible splat has
+// power <= 0, where ex2.approx returns at most 1 + 2^-22, so a splat with
+// op < max_alpha (1 - 2^-20) never reaches max_alpha: for a batch of records
+// that all satisfy this (a warp- or CTA-uniform check, like the colour check),
+// the loops drop the min and the saturation test (kSat false) with the same
+// results bit for bit.
+constexpr float kNoSatMargin = 1.0f - 0x1p-20f;
+__device__ __forceinline__ bool may_saturate(float op, float max_alpha) { return !(op < max_alpha * kNoSatMargin); }
+
 // Per half: vis ? v : keep.
 __device__ __forceinline__ F2 select2(int vis_lo, int vis_hi, F2 v, F2 keep) {
   float vl, vh, kl, kh;
@@ -405,10 +415,53 @@ __device__ __forceinline__ F2 select2(int vis_lo, int vis_hi, F2 v, F2 keep) {
 // returns vis ? value : 0, and pass_mask = all ones when vis && power < sat_thr
 // else 0 (the caller ANDs it into the bits of a float, a select that also
 // clears a NaN). kWantVis also reports vis as 0/1 (the guarded loops).
-template <bool kCheckLast, bool kWantVis>
+// kSat false: no record of the batch can saturate (opacity below max_alpha by
+// a margin, see kNoSatMargin), so sat_thr > 0 >= power and pass_mask = vis.
+template <bool kCheckLast, bool kWantVis, bool kSat = true>
 __device__ __forceinline__ float vis_select_bwd(int j, int last, float power, float vis_thr, float sat_thr,
                                                 float value, unsigned& pass_mask, int& vis) {
   float r;
+  if (!kSat) {
+    if (kCheckLast && kWantVis) {
+      asm("{\n\t.reg .pred pv;\n\t"
+          "setp.lt.s32 pv, %3, %4;\n\t"
+          "setp.le.and.f32 pv, %5, 0f00000000, pv;\n\t"
+          "setp.ge.and.f32 pv, %5, %6, pv;\n\t"
+          "selp.f32 %0, %7, 0f00000000, pv;\n\t"
+          "selp.b32 %1, -1, 0, pv;\n\t"
+          "selp.b32 %2, 1, 0, pv;\n\t}"
+          : "=f"(r), "=r"(pass_mask), "=r"(vis)
+          : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(value));
+    } else if (kCheckLast) {
+      asm("{\n\t.reg .pred pv;\n\t"
+          "setp.lt.s32 pv, %2, %3;\n\t"
+          "setp.le.and.f32 pv, %4, 0f00000000, pv;\n\t"
+          "setp.ge.and.f32 pv, %4, %5, pv;\n\t"
+          "selp.f32 %0, %6, 0f00000000, pv;\n\t"
+          "selp.b32 %1, -1, 0, pv;\n\t}"
+          : "=f"(r), "=r"(pass_mask)
+          : "r"(j), "r"(last), "f"(power), "f"(vis_thr), "f"(value));
+    } else if (kWantVis) {
+      asm("{\n\t.reg .pred pv;\n\t"
+          "setp.le.f32 pv, %3, 0f00000000;\n\t"
+          "setp.ge.and.f32 pv, %3, %4, pv;\n\t"
+          "selp.f32 %0, %5, 0f00000000, pv;\n\t"
+          "selp.b32 %1, -1, 0, pv;\n\t"
+          "selp.b32 %2, 1, 0, pv;\n\t}"
+          : "=f"(r), "=r"(pass_mask), "=r"(vis)
+          : "f"(power), "f"(vis_thr), "f"(value));
+    } else {
+      asm("{\n\t.reg .pred pv;\n\t"
+          "setp.le.f32 pv, %2, 0f00000000;\n\t"
+          "setp.ge.and.f32 pv, %2, %3, pv;\n\t"
+          "selp.f32 %0, %4, 0f00000000, pv;\n\t"
+          "selp.b32 %1, -1, 0, pv;\n\t}"
+          : "=f"(r), "=r"(pass_mask)
+          : "f"(power), "f"(vis_thr), "f"(value));
+    }
+    (void)sat_thr;
+    return r;
+  }
   if (kCheckLast && kWantVis) {
     asm("{\n\t.reg .pred pv, ps;\n\t"
         "setp.lt.s32 pv, %3, %4;\n\t"

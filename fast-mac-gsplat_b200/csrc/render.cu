@@ -141,7 +141,7 @@ __device__ __forceinline__ int claim_tiles(uint32_t* counter, int count, int lan
 // T*(1-0) = T), so the 8 pixels' chains interleave. The results equal those of
 // a per-pixel `if (visible)` loop exactly, for finite colours; kGuard (a batch
 // holding a non-finite colour) adds w*c only where the splat is visible.
-template <bool kGuard>
+template <bool kGuard, bool kSat>
 __device__ __forceinline__ void fwd_warp_batch(const Meta& m, const float4 (*recs)[3], int cnt, int base, float fx,
                                                const F2 (&fy)[kLanePx / 2], F2 (&T)[kLanePx / 2],
                                                F2 (&cr)[kLanePx / 2], F2 (&cg)[kLanePx / 2], F2 (&cb)[kLanePx / 2],
@@ -154,7 +154,7 @@ __device__ __forceinline__ void fwd_warp_batch(const Meta& m, const float4 (*rec
     const float4 p2 = recs[j][2];
     const PowerCol pc = power_col(p0.z, p0.w, p1.x, __fsub_rn(fx, p0.x));
     const F2 ta = f2(pc.ta), tb = f2(pc.tb), ch = f2(pc.ch), mu_y = f2(p0.y);
-    const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x);
+    const F2 col_r = f2(p1.z), col_g = f2(p1.w), col_b = f2(p2.x), op = f2(p1.y);
     const int consumed = base + j + 1;
 #pragma unroll
     for (int q = 0; q < kLanePx / 2; ++q) {
@@ -163,7 +163,13 @@ __device__ __forceinline__ void fwd_warp_batch(const Meta& m, const float4 (*rec
       split(power, pl, ph);
       split(T[q], tl, th);
       split(mul2(power, log2e), xl, xh);
-      const float vl_ = fminf(m.max_alpha, p1.y * ex2_approx(xl)), vh_ = fminf(m.max_alpha, p1.y * ex2_approx(xh));
+      float vl_, vh_;  // op * exp(power), capped at max_alpha where a record may saturate
+      if (kSat) {
+        vl_ = fminf(m.max_alpha, p1.y * ex2_approx(xl));
+        vh_ = fminf(m.max_alpha, p1.y * ex2_approx(xh));
+      } else {
+        split(mul2(op, f2(ex2_approx(xl), ex2_approx(xh))), vl_, vh_);
+      }
       float al, ah;
       int vis_l = 1, vis_h = 1;
       if (kGuard) {
@@ -237,7 +243,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       if (!__any_sync(kFullMask, live)) break;
       const int cnt = min(kWarpBatch, n - base);
       __syncwarp();
-      bool bad_color = false;
+      bool bad_color = false, sat = false;
       if (lane < cnt) {
         float4 r[3];
         load_rec(rec, load_gi(ids, start + base + lane, m.BG, status, kSiteRender), r);
@@ -245,6 +251,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         my[lane][1] = r[1];
         my[lane][2] = r[2];
         bad_color = !finite_rgb(r[1].z, r[1].w, r[2].x);
+        sat = may_saturate(r[1].y, m.max_alpha);
         if (kSave) {
           float4* dst = pair_rec + 3 * (size_t)(start + base + lane);
           dst[0] = r[0];
@@ -252,13 +259,15 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
           dst[2] = r[2];
         }
       }
-      const bool guard = __any_sync(kFullMask, bad_color);
+      const bool guard = __any_sync(kFullMask, bad_color), any_sat = __any_sync(kFullMask, sat);
       __syncwarp();
       if (!live) continue;
       if (guard)
-        fwd_warp_batch<true>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
+        fwd_warp_batch<true, true>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
+      else if (any_sat)
+        fwd_warp_batch<false, true>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
       else
-        fwd_warp_batch<false>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
+        fwd_warp_batch<false, false>(m, my, cnt, base, fx, fy, T, cr, cg, cb, last);
     }
     const bool full = (tc.tx * kTile + kTile <= m.W) && (tc.ty * kTile + kTile <= m.H) && ((m.W & 3) == 0);
     if (full) {
@@ -355,7 +364,7 @@ __device__ __forceinline__ bool long_chunk_live(const Meta& m, long long chunk) 
 
 // One staged batch of the CTA kernel over a thread's 2 packed pixels (kGuard:
 // as fwd_warp_batch). A warp leaves the batch once its 64 pixels are finished.
-template <bool kGuard>
+template <bool kGuard, bool kSat>
 __device__ __forceinline__ void fwd_cta_batch(const Meta& m, const float4 (*recs)[3], int cnt, int base, float fx,
                                               F2 fy, F2& T, F2& cr, F2& cg, F2& cb, int& last_l, int& last_h) {
   const F2 one = f2(1.0f), log2e = f2(kLog2e);
@@ -372,7 +381,13 @@ __device__ __forceinline__ void fwd_cta_batch(const Meta& m, const float4 (*recs
     if (!__any_sync(kFullMask, (tl > m.T_thr) | (th > m.T_thr))) break;
     split(power, pl, ph);
     split(mul2(power, log2e), xl, xh);
-    const float vl_ = fminf(m.max_alpha, p1.y * ex2_approx(xl)), vh_ = fminf(m.max_alpha, p1.y * ex2_approx(xh));
+    float vl_, vh_;  // op * exp(power), capped at max_alpha where a record may saturate
+    if (kSat) {
+      vl_ = fminf(m.max_alpha, p1.y * ex2_approx(xl));
+      vh_ = fminf(m.max_alpha, p1.y * ex2_approx(xh));
+    } else {
+      split(mul2(f2(p1.y), f2(ex2_approx(xl), ex2_approx(xh))), vl_, vh_);
+    }
     float al, ah;
     int vis_l = 1, vis_h = 1;
     if (kGuard) {
@@ -433,15 +448,19 @@ __global__ void __launch_bounds__(kCtaThreads, 8)
         const bool live = (tl > m.T_thr) | (th > m.T_thr);
         if (__syncthreads_count(live) == 0) break;
         const int cnt = min(kBatch, n - base);
-        bool bad_color = false;
+        bool bad_color = false, sat = false;
         for (int i = t; i < cnt; i += kCtaThreads) {
           load_rec(rec, load_gi(ids, start + base + i, m.BG, status, kSiteRender), s_rec[i]);
           bad_color |= !finite_rgb(s_rec[i][1].z, s_rec[i][1].w, s_rec[i][2].x);
+          sat |= may_saturate(s_rec[i][1].y, m.max_alpha);
         }
-        if (__syncthreads_or(bad_color))
-          fwd_cta_batch<true>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
+        const bool guard = __syncthreads_or(bad_color);
+        if (guard)
+          fwd_cta_batch<true, true>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
+        else if (__syncthreads_or(sat))
+          fwd_cta_batch<false, true>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
         else
-          fwd_cta_batch<false>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
+          fwd_cta_batch<false, false>(m, s_rec, cnt, base, fx, fy, T, cr, cg, cb, last_l, last_h);
         __syncthreads();  // s_rec is refilled by the next batch
       }
       float tv[2], rv[2], gv[2], bv[2];
@@ -514,7 +533,7 @@ __device__ __forceinline__ void pixel_vjp(const Meta& m, float dy, float power, 
 // selects it.
 // kClampOm: clamp 1 - alpha at eps (only needed when max_alpha > 1 - eps;
 // otherwise 1 - alpha >= 1 - max_alpha >= eps already).
-template <bool kClampOm, bool kGuard, bool kCheckLast, bool kFirst>
+template <bool kClampOm, bool kGuard, bool kCheckLast, bool kFirst, bool kSat = true>
 __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int last_h, F2 dy, float pl, float ph,
                                            F2 op, float vis_thr, float sat_thr, F2 col_r, F2 col_g, F2 col_b,
                                            F2 gr, F2 gg, F2 gb, F2& T_cur, F2& gT, F2 (&S)[7]) {
@@ -525,10 +544,10 @@ __device__ __forceinline__ void pixel_vjp2(const Meta& m, int j, int last_l, int
   split(mul2(op, e), rl, rh);
   unsigned pass_l, pass_h;
   int vis_l = 1, vis_h = 1;
-  const float al = vis_select_bwd<kCheckLast, kGuard>(j, last_l, pl, vis_thr, sat_thr, fminf(m.max_alpha, rl),
-                                                      pass_l, vis_l);
-  const float ah = vis_select_bwd<kCheckLast, kGuard>(j, last_h, ph, vis_thr, sat_thr, fminf(m.max_alpha, rh),
-                                                      pass_h, vis_h);
+  const float al = vis_select_bwd<kCheckLast, kGuard, kSat>(j, last_l, pl, vis_thr, sat_thr,
+                                                            kSat ? fminf(m.max_alpha, rl) : rl, pass_l, vis_l);
+  const float ah = vis_select_bwd<kCheckLast, kGuard, kSat>(j, last_h, ph, vis_thr, sat_thr,
+                                                            kSat ? fminf(m.max_alpha, rh) : rh, pass_h, vis_h);
   const F2 alpha = f2(al, ah);
   float oml, omh;
   split(sub2(f2(1.0f), alpha), oml, omh);
@@ -708,7 +727,7 @@ __device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, f
 // kRedChunk records. kGuard: a record's colour is not finite (pixel_vjp2).
 // kCheckLast: some pixel of the warp stops before this record (j >= the
 // warp's smallest last_idx), so each pixel tests j < last.
-template <bool kClampOm, bool kGuard, bool kCheckLast>
+template <bool kClampOm, bool kGuard, bool kCheckLast, bool kSat>
 __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, int row0, int j, int lane, float fx,
                                                 const F2 (&fy)[kLanePx / 2], const F2 (&gr)[kLanePx / 2],
                                                 const F2 (&gg)[kLanePx / 2], const F2 (&gb)[kLanePx / 2],
@@ -731,10 +750,10 @@ __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, i
     float pl, ph;
     split(power, pl, ph);
     if (q == 0)
-      pixel_vjp2<kClampOm, kGuard, kCheckLast, true>(m, j, last[0], last[1], dy, pl, ph, op, p2.z, p2.w, col_r,
+      pixel_vjp2<kClampOm, kGuard, kCheckLast, true, kSat>(m, j, last[0], last[1], dy, pl, ph, op, p2.z, p2.w, col_r,
                                                      col_g, col_b, gr[0], gg[0], gb[0], Tc[0], gT[0], S);
     else
-      pixel_vjp2<kClampOm, kGuard, kCheckLast, false>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z,
+      pixel_vjp2<kClampOm, kGuard, kCheckLast, false, kSat>(m, j, last[2 * q], last[2 * q + 1], dy, pl, ph, op, p2.z,
                                                       p2.w, col_r, col_g, col_b, gr[q], gg[q], gb[q], Tc[q], gT[q],
                                                       S);
   }
@@ -769,7 +788,7 @@ __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, i
 // tile_last of the warp's record buffer). Records at or past lmin (the warp's
 // smallest last_idx) test each pixel's stop; the ones before it are reached by
 // every pixel and skip that test.
-template <bool kClampOm, bool kGuard>
+template <bool kClampOm, bool kGuard, bool kSat>
 __device__ __forceinline__ void bwd_warp_records(const Meta& m, BwdWarpSmem& W, int row0, int tile_last, int lmin,
                                                  int lane, float fx, const F2 (&fy)[kLanePx / 2],
                                                  const F2 (&gr)[kLanePx / 2], const F2 (&gg)[kLanePx / 2],
@@ -780,11 +799,11 @@ __device__ __forceinline__ void bwd_warp_records(const Meta& m, BwdWarpSmem& W, 
   int j = tile_last - 1;
 #pragma unroll 1
   for (; j >= lmin; --j)
-    bwd_warp_record<kClampOm, kGuard, true>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
+    bwd_warp_record<kClampOm, kGuard, true, kSat>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
                                             grad_rec);
 #pragma unroll 1
   for (; j >= 0; --j)
-    bwd_warp_record<kClampOm, kGuard, false>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
+    bwd_warp_record<kClampOm, kGuard, false, kSat>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
                                              grad_rec);
   if (slot > 0) flush_red(W, slot, lane, grad_rec);
 }
@@ -876,16 +895,23 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     if (work) {  // tiles above kBwdShortMax: k_render_bwd_cta finds them
       const int tile_last = __reduce_max_sync(kFullMask, lmax);
       const int warp_lmin = __reduce_min_sync(kFullMask, lmin);
-      // A non-finite colour among the records this tile walks takes the guarded body.
-      bool bad_color = false;
-      for (int q = lane; q < tile_last; q += 32)
+      // A non-finite colour among the records this tile walks takes the guarded
+      // body; a record that may saturate takes the body with the saturation test.
+      bool bad_color = false, sat = false;
+      for (int q = lane; q < tile_last; q += 32) {
         bad_color |= !finite_rgb(W.rb.rec[row0 + q][1].z, W.rb.rec[row0 + q][1].w, W.rb.rec[row0 + q][2].x);
-      if (__any_sync(kFullMask, bad_color))
-        bwd_warp_records<kClampOm, true>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT, last,
-                                         status, grad_rec);
+        sat |= may_saturate(W.rb.rec[row0 + q][1].y, m.max_alpha);
+      }
+      const bool guard = __any_sync(kFullMask, bad_color), any_sat = __any_sync(kFullMask, sat);
+      if (guard)
+        bwd_warp_records<kClampOm, true, true>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT,
+                                               last, status, grad_rec);
+      else if (any_sat)
+        bwd_warp_records<kClampOm, false, true>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT,
+                                                last, status, grad_rec);
       else
-        bwd_warp_records<kClampOm, false>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT, last,
-                                          status, grad_rec);
+        bwd_warp_records<kClampOm, false, false>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc,
+                                                 gT, last, status, grad_rec);
     }
     tile = nxt_tile;
     nxt_tile = nn_tile;
@@ -981,16 +1007,19 @@ __global__ void __launch_bounds__(kCtaThreads)
       for (int bend = tile_last; bend > 0; bend -= kBatch) {
         const int bstart = max(0, bend - kBatch);
         const int cnt = bend - bstart;
-        bool bad_color = false;
+        bool bad_color = false, sat = false;
         for (int i = t; i < cnt; i += kCtaThreads) {
           const int gi = load_gi(ids, start + bstart + i, m.BG, status, kSiteRenderBwd);
           s_gi[i] = gi;
           load_rec(rec, gi, s_rec[i]);
           bad_color |= !finite_rgb(s_rec[i][1].z, s_rec[i][1].w, s_rec[i][2].x);
+          sat |= may_saturate(s_rec[i][1].y, m.max_alpha);
         }
         for (int i = t; i < cnt * kGradComps; i += kCtaThreads) (&s_acc[0][0])[i] = 0.0f;
-        // A non-finite colour in the batch: the guarded per-pixel VJP (CTA-uniform).
+        // A non-finite colour in the batch: the guarded per-pixel VJP; a record
+        // that may saturate: the saturation test (both CTA-uniform).
         const bool guard = __syncthreads_or(bad_color);
+        const bool any_sat = __syncthreads_or(sat);
         int slot = 0;
 #pragma unroll 1
         for (int jj = cnt - 1; jj >= 0; --jj) {
@@ -1012,9 +1041,12 @@ __global__ void __launch_bounds__(kCtaThreads)
           if (guard)
             pixel_vjp2<kClampOm, true, true, true>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w,
                                                    f2(p1.z), f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
-          else
+          else if (any_sat)
             pixel_vjp2<kClampOm, false, true, true>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z, p2.w,
                                                     f2(p1.z), f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
+          else
+            pixel_vjp2<kClampOm, false, true, true, false>(m, j, lastv[0], lastv[1], dy, pl, ph, f2(p1.y), p2.z,
+                                                           p2.w, f2(p1.z), f2(p1.w), f2(p2.x), gr, gg, gb, Tc, gT, S);
           float Sv[7];
 #pragma unroll
           for (int q = 0; q < 7; ++q) {
