@@ -369,6 +369,43 @@ def test_edge_geometry_matches_c_oracle(alpha_threshold):
         assert rel_err(got, want) <= GRAD_RTOL, key
 
 
+def test_saturation_boundary_matches_c_oracle():
+    """Batches whose records all have opacity below max_alpha (1 - 2^-20) skip
+    the alpha cap and the saturation test; the others keep them. View 0 mixes
+    opacities on both sides of that bound (and at, and above, max_alpha) in
+    every tile; view 1 has only opacities just below it, so its batches take
+    the shortened body with values where the cap would matter soonest. Both
+    must match the C oracle (which always applies the cap and the test) with
+    the usual gates."""
+    from workloads import Splats2D, conic_from_sigma
+
+    B, G, H, W = 2, 2000, 96, 112
+    g = torch.Generator().manual_seed(31)
+    lim = np.float32(np.float32(0.99) * np.float32(1.0 - 2.0 ** -20))
+    below = np.float32(np.nextafter(lim, np.float32(0.0)))
+    mix = torch.tensor([np.nextafter(below, np.float32(0.0)), below, lim, np.nextafter(lim, np.float32(1.0)),
+                        0.99, 0.995, 0.6], dtype=torch.float32)
+    opac = torch.empty(B, G)
+    opac[0] = mix[torch.randint(0, len(mix), (G,), generator=g)]
+    opac[1] = torch.tensor([float(np.nextafter(below, np.float32(0.0))), float(below), 0.98999],
+                           dtype=torch.float32)[torch.randint(0, 3, (G,), generator=g)]
+    means = torch.rand(B, G, 2, generator=g) * torch.tensor([float(W), float(H)])
+    sig = torch.rand(B, G, 2, generator=g) * 4.5 + 1.5
+    theta = torch.rand(B, G, generator=g) * np.pi
+    s = Splats2D(means.contiguous(), conic_from_sigma(sig, theta), torch.rand(B, G, 3, generator=g),
+                 opac.contiguous(), (torch.rand(B, G, generator=g) * 50 + 0.1).contiguous(), H, W)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    gimg = grad_image(s.B, s.height, s.width, seed=32)
+    meta = O.Meta(s.height, s.width, s.B, s.G)
+    ref = O.full_forward_backward(meta, *(t.numpy() for t in s.tensors()), gimg.numpy())
+    ins = [t.to(DEV).clone().requires_grad_(i < 4) for i, t in enumerate(s.tensors())]
+    img = tgb.rasterize_projected_gaussians(*ins, cfg)
+    img.backward(gimg.to(DEV))
+    assert max_abs(np_(img), ref["image"]) <= IMAGE_ATOL
+    for t, want, key in zip(ins[:4], ref["grads"], GRAD_KEYS):
+        assert rel_err(np_(t.grad).reshape(want.shape), want) <= GRAD_RTOL, key
+
+
 def _finite_split(got, want):
     """The non-finite entries of got and want must be the same ones; returns
     both restricted to the finite entries."""
