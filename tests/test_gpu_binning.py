@@ -172,7 +172,8 @@ def _sort(keys: np.ndarray, vals: np.ndarray, begin: int, end: int):
 
 
 @pytest.mark.parametrize("n,begin,end", [(1, 0, 8), (4095, 0, 32), (4096, 32, 48), (4097, 5, 19),
-                                         (100_000, 0, 64), (1_000_003, 32, 45), (300_000, 0, 0)])
+                                         (100_000, 0, 64), (1_000_003, 32, 45), (300_000, 0, 0),
+                                         (2_000_001, 10, 11), (700_001, 40, 51)])
 def test_radix_sort_is_stable_and_exact(n, begin, end):
     rng = np.random.default_rng(n + begin)
     keys = rng.integers(0, 2**63, n, dtype=np.uint64) | (rng.integers(0, 2, n, dtype=np.uint64) << np.uint64(63))
