@@ -132,22 +132,23 @@ __device__ __forceinline__ int cand_row(int local, int w) { return cand_row(loca
 // which bounds both effects by 4.5e-3 of tau, below the 2^-7 (7.8e-3) between
 // tau and T_in, T_out. A tile that meets the ellipse at T_in therefore has a
 // float minimum below tau (a hit); one that misses it at T_out has every
-// evaluated q above tau (a miss). The extents are computed in double: an error
-// dD in D = a T - det e^2 moves the boundary point where dq/dx = 2 sqrt(D), so
-// q changes by about dD / a ~ 2^-51 T, far inside the margin; the tile columns
-// are then found by exact comparisons with rx0 and rx1.
+// evaluated q above tau (a miss). The extents are computed in float relative
+// to the mean (strip_extent bounds their effect on q at 1e-4 tau, far inside
+// the margin), and the tile columns are found by comparisons with the float
+// rectangle edges.
 constexpr double kSpanMargin = 0x1p-7;
 // Splats with fewer candidate tiles take the exact test for each: for them the
 // row walk's setup costs more than the tests it saves.
 constexpr int kSpanMinCands = 32;
 
 struct SpanGeom {
-  double det, ia, bc;          // ia = 1 / a, bc = b / c (the mean and b: the splat's floats)
-  double E[2], XR[2], aT[2];  // per threshold (0: T_in, 1: T_out): y and x half extents, a T
+  float det, ia, bc;          // ia = 1 / a, bc = b / c (the mean and b: the splat's floats)
+  float E[2], XR[2], aT[2];  // per threshold (0: T_in, 1: T_out): y and x half extents, a T
 };
 
 // The constants of the row walk, or false when the splat is outside the
-// conditions above (it then takes the exact test for every candidate).
+// conditions above (it then takes the exact test for every candidate). The
+// admission test is done in double; the constants are rounded to float.
 __device__ __forceinline__ bool span_geom(const SplatTiles& s, SpanGeom& g) {
   if (s.n < kSpanMinCands) return false;
   const float a = s.a, b = s.b, c = s.c;
@@ -157,13 +158,13 @@ __device__ __forceinline__ bool span_geom(const SplatTiles& s, SpanGeom& g) {
   const double det = da * dc - db * db;  // products exact in double
   const double tr = da + dc;
   if (!(det > 0.0) || !(tr * tr <= 4096.0 * det) || !(tr <= 256.0 * (double)s.tau)) return false;
-  g.det = det, g.ia = 1.0 / da, g.bc = db / dc;
+  g.det = (float)det, g.ia = (float)(1.0 / da), g.bc = (float)(db / dc);
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const double T = (double)s.tau * (k ? 1.0 + kSpanMargin : 1.0 - kSpanMargin);
-    g.E[k] = sqrt(da * T / det);
-    g.XR[k] = sqrt(dc * T / det);
-    g.aT[k] = da * T;
+    g.E[k] = (float)sqrt(da * T / det);
+    g.XR[k] = (float)sqrt(dc * T / det);
+    g.aT[k] = (float)(da * T);
   }
   return true;
 }
@@ -173,34 +174,49 @@ __device__ __forceinline__ bool span_geom(const SplatTiles& s, SpanGeom& g) {
 // The right boundary x(e) = (-b e + sqrt(a T - det e^2)) / a is concave with its
 // maximum XR at e = -(b / c) XR, the left one convex with its minimum -XR at
 // e = (b / c) XR; off those points the extreme is at an end of the strip.
-__device__ __forceinline__ bool strip_extent(const SpanGeom& g, double b, int k, double e0, double e1, double& xl,
-                                             double& xr) {
-  const double lo = fmax(e0, -g.E[k]), hi = fmin(e1, g.E[k]);
+// In float: an error dD in D = a T - det e^2 (at most about 2^-22 a T here)
+// moves the boundary where dq/dx = 2 sqrt(D), so q changes by at most 2 dD / a
+// (2^-21 T); the -b e / a term, the square root and the division add relative
+// errors of a few 2^-24 in x, which change q by at most 2^-18 T (|b| <= 32
+// sqrt(det) under the k <= 2^12 admission); the strip ends and the column
+// edges are taken relative to the mean (fl(r - m), off by 2^-24 |r - m|), which
+// changes q by at most 2^-23 (R + 16) / R_minor < 4e-5 T. All stay far inside
+// the 2^-7 margin.
+__device__ __forceinline__ bool strip_extent(const SpanGeom& g, float b, int k, float e0, float e1, float& xl,
+                                             float& xr) {
+  const float lo = fmaxf(e0, -g.E[k]), hi = fminf(e1, g.E[k]);
   if (!(lo <= hi)) return false;
-  const double es = g.bc * g.XR[k];
-  const double sl = sqrt(fmax(g.aT[k] - g.det * lo * lo, 0.0));
-  const double sh = sqrt(fmax(g.aT[k] - g.det * hi * hi, 0.0));
-  const double cl = -b * lo, ch = -b * hi;
-  xr = (-es >= lo && -es <= hi) ? g.XR[k] : fmax(cl + sl, ch + sh) * g.ia;
-  xl = (es >= lo && es <= hi) ? -g.XR[k] : fmin(cl - sl, ch - sh) * g.ia;
+  const float es = g.bc * g.XR[k];
+  const float sl = sqrtf(fmaxf(fmaf(-g.det * lo, lo, g.aT[k]), 0.0f));
+  const float sh = sqrtf(fmaxf(fmaf(-g.det * hi, hi, g.aT[k]), 0.0f));
+  const float cl = -b * lo, ch = -b * hi;
+  xr = (-es >= lo && -es <= hi) ? g.XR[k] : fmaxf(cl + sl, ch + sh) * g.ia;
+  xl = (es >= lo && es <= hi) ? -g.XR[k] : fminf(cl - sl, ch - sh) * g.ia;
   return true;
 }
 
-// First column t in [t0, t1] whose rectangle reaches right of X (rx1 >= X), or
-// t1 + 1; last column in [t0, t1] reaching left of X (rx0 <= X), or t0 - 1.
-// Exact: the estimate is corrected against the float rectangle edges.
-__device__ __forceinline__ int first_col_reaching(double X, int t0, int t1, int W) {
-  const double f = ceil((X - 15.5) * 0.0625);
-  int t = f <= (double)t0 ? t0 : (f > (double)t1 ? t1 + 1 : (int)f);
-  while (t > t0 && (double)tile_rx1(t - 1, W) >= X) --t;
-  while (t <= t1 && (double)tile_rx1(t, W) < X) ++t;
+// Column rectangle edges as tile_rx0 / tile_rx1 compute them (the same float
+// values), with (float)t formed as (2^23 + t) - 2^23, exact for 0 <= t < 2^23,
+// instead of a conversion instruction.
+__device__ __forceinline__ float col_float(int t) { return __int_as_float(0x4B000000 | t) - 8388608.0f; }
+__device__ __forceinline__ float col_rx0(int t) { return fmaf(16.0f, col_float(t), 0.5f); }
+__device__ __forceinline__ float col_rx1(int t, float rmax) { return fminf(rmax, fmaf(16.0f, col_float(t), 15.5f)); }
+
+// First column t in [t0, t1] whose rectangle reaches right of x (rx1 - mx >= x,
+// relative to the mean mx), or t1 + 1; last column in [t0, t1] reaching left of
+// x (rx0 - mx <= x), or t0 - 1. rmax = tile_rx1's image clip, (W - 1) + 0.5.
+// The estimate is corrected by the comparisons themselves, which are monotone
+// in t.
+__device__ __forceinline__ int first_col_reaching(float x, float mx, int t0, int t1, float rmax) {
+  int t = min(max(__float2int_ru((mx + x - 15.5f) * 0.0625f), t0), t1 + 1);
+  while (t > t0 && col_rx1(t - 1, rmax) - mx >= x) --t;
+  while (t <= t1 && col_rx1(t, rmax) - mx < x) ++t;
   return t;
 }
-__device__ __forceinline__ int last_col_reaching(double X, int t0, int t1) {
-  const double f = floor((X - 0.5) * 0.0625);
-  int t = f >= (double)t1 ? t1 : (f < (double)t0 ? t0 - 1 : (int)f);
-  while (t < t1 && (double)tile_rx0(t + 1) <= X) ++t;
-  while (t >= t0 && (double)tile_rx0(t) > X) --t;
+__device__ __forceinline__ int last_col_reaching(float x, float mx, int t0, int t1) {
+  int t = min(max(__float2int_rd((mx + x - 0.5f) * 0.0625f), t0 - 1), t1);
+  while (t < t1 && col_rx0(t + 1) - mx <= x) ++t;
+  while (t >= t0 && col_rx0(t) - mx > x) --t;
   return t;
 }
 
@@ -487,18 +503,18 @@ __device__ __forceinline__ void warp_count_tiles(const SplatTiles& mine, const M
       const SpanGeom& g = cs.g[owner];
       const int r = k - (owner ? sm.incl[owner - 1] : 0);
       const int ty = s.ty0 + r;
-      const double gmx = s.mx, gmy = s.my, gb = s.b;
-      const double e0 = (double)tile_rx0(ty) - gmy, e1 = (double)tile_rx1(ty, m.H) - gmy;
+      const float e0 = tile_rx0(ty) - s.my, e1 = tile_rx1(ty, m.H) - s.my;
+      const float rmax = (float)(m.W - 1) + 0.5f;
       t0 = s.tx0;
       row0 = r * s.w;
       const int t1 = s.tx0 + s.w - 1;
-      double xl, xr;
-      if (strip_extent(g, gb, 1, e0, e1, xl, xr)) {
-        pl = first_col_reaching(gmx + xl, t0, t1, m.W);
-        ph = last_col_reaching(gmx + xr, t0, t1);
-        if (pl <= ph && strip_extent(g, gb, 0, e0, e1, xl, xr)) {
-          hl = first_col_reaching(gmx + xl, t0, t1, m.W);
-          hh = last_col_reaching(gmx + xr, t0, t1);
+      float xl, xr;
+      if (strip_extent(g, s.b, 1, e0, e1, xl, xr)) {
+        pl = first_col_reaching(xl, s.mx, t0, t1, rmax);
+        ph = last_col_reaching(xr, s.mx, t0, t1);
+        if (pl <= ph && strip_extent(g, s.b, 0, e0, e1, xl, xr)) {
+          hl = first_col_reaching(xl, s.mx, t0, t1, rmax);
+          hh = last_col_reaching(xr, s.mx, t0, t1);
         }
       }
       if (hl <= hh) {
