@@ -358,8 +358,16 @@ std::vector<Tensor> render_fwd_impl(const gsb_raster_meta& meta, const Tensor& r
 
 // Reverse-order VJP and un-sort into input order (reference:
 // tile_fast_backward_saved, …/gsplat_v8_project3d_kernels.metal:931-1063;
-// _unsort_batched, …/rasterize.py:583-591). Gradients whose needs flag is
-// false come back undefined (None in Python).
+// _unsort_batched, …/rasterize.py:583-591). From 2^18 splats the un-sort is
+// folded into the backward's atomics (gsb_render_backward_inputs), which then
+// target slices of one zeroed buffer; below, the atomics go to packed records
+// in rank order and gsb_unsort_grads scatters them: there the input-order
+// targets (four arrays, at permuted positions) cost the backward more L2
+// traffic than the un-sort launch it saves (c3: +40 us against 11 us), while
+// at 2^20 splats the un-sort is the dearer part (c4: -60 us). Gradients
+// whose needs flag is false come back undefined (None in Python).
+constexpr int64_t kFoldUnsortMinSplats = int64_t(1) << 18;
+
 std::tuple<Tensor, Tensor, Tensor, Tensor> render_bwd_impl(const gsb_raster_meta& meta, const Tensor& perm,
                                                            const Tensor& rec, const Tensor& tile_offsets,
                                                            const Tensor& binned_ids, const Tensor& final_T,
@@ -370,26 +378,59 @@ std::tuple<Tensor, Tensor, Tensor, Tensor> render_bwd_impl(const gsb_raster_meta
   const int64_t B = meta.batch_size, G = meta.gaussians_per_batch;
   void* stream = stream_of(rec);
   const Tensor g = aligned(grad_out.to(at::kFloat), 16);
-  const size_t ws_bytes = gsb_render_workspace_size(&meta);
-  Tensor grad_rec = empty({B * G, GSB_REC_FLOATS}, at::kFloat, dev);
-  Tensor ws = empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 1))}, at::kByte, dev);
+  const int64_t BG = B * G;
+  if (BG < kFoldUnsortMinSplats) {
+    const size_t ws_bytes = gsb_render_workspace_size(&meta);
+    Tensor grad_rec = empty({BG, GSB_REC_FLOATS}, at::kFloat, dev);
+    Tensor ws = empty({static_cast<int64_t>(std::max<size_t>(ws_bytes, 1))}, at::kByte, dev);
+    {
+      Phase ph("render_bwd", rec);
+      check(gsb_render_backward(&meta, ptr<float>(rec), ptr<int32_t>(tile_offsets), ptr<int32_t>(binned_ids),
+                                ptr<float>(final_T), ptr<int32_t>(last_idx), ptr<float>(pair_rec), ptr<float>(g),
+                                ptr<float>(grad_rec), ptr<uint32_t>(status), ws.data_ptr(), ws_bytes, stream),
+            "gsb_render_backward");
+    }
+    Tensor gm, gc, gcol, go;
+    if (needs[0]) gm = empty({B, G, 2}, at::kFloat, dev);
+    if (needs[1]) gc = empty({B, G, 3}, at::kFloat, dev);
+    if (needs[2]) gcol = empty({B, G, 3}, at::kFloat, dev);
+    if (needs[3]) go = empty({B, G}, at::kFloat, dev);
+    {
+      Phase ph("unsort", rec);
+      check(gsb_unsort_grads(&meta, ptr<int32_t>(perm), ptr<float>(grad_rec), ptr<float>(gm), ptr<float>(gc),
+                             ptr<float>(gcol), ptr<float>(go), stream),
+            "gsb_unsort_grads");
+    }
+    if (debug_checks())
+      read_status(status);
+    else
+      errors().defer(status);
+    return {gm, gc, gcol, go};
+  }
+  // Slices of one buffer, in the order means2d (2), conics (3), colours (3),
+  // opacities (1) floats per splat, only for the requested gradients.
+  const int64_t widths[4] = {2, 3, 3, 1};
+  int64_t floats = 0;
+  for (int i = 0; i < 4; ++i) floats += needs[i] ? widths[i] * BG : 0;
+  Tensor buf = at::zeros({std::max<int64_t>(floats, 1)}, at::TensorOptions().dtype(at::kFloat).device(dev));
+  Tensor gm, gc, gcol, go;
+  int64_t off = 0;
+  auto take = [&](int i, std::vector<int64_t> shape) {
+    Tensor t = buf.narrow(0, off, widths[i] * BG).view(shape);
+    off += widths[i] * BG;
+    return t;
+  };
+  if (needs[0]) gm = take(0, {B, G, 2});
+  if (needs[1]) gc = take(1, {B, G, 3});
+  if (needs[2]) gcol = take(2, {B, G, 3});
+  if (needs[3]) go = take(3, {B, G});
   {
     Phase ph("render_bwd", rec);
-    check(gsb_render_backward(&meta, ptr<float>(rec), ptr<int32_t>(tile_offsets), ptr<int32_t>(binned_ids),
-                              ptr<float>(final_T), ptr<int32_t>(last_idx), ptr<float>(pair_rec), ptr<float>(g),
-                              ptr<float>(grad_rec), ptr<uint32_t>(status), ws.data_ptr(), ws_bytes, stream),
-          "gsb_render_backward");
-  }
-  Tensor gm, gc, gcol, go;
-  if (needs[0]) gm = empty({B, G, 2}, at::kFloat, dev);
-  if (needs[1]) gc = empty({B, G, 3}, at::kFloat, dev);
-  if (needs[2]) gcol = empty({B, G, 3}, at::kFloat, dev);
-  if (needs[3]) go = empty({B, G}, at::kFloat, dev);
-  {
-    Phase ph("unsort", rec);
-    check(gsb_unsort_grads(&meta, ptr<int32_t>(perm), ptr<float>(grad_rec), ptr<float>(gm), ptr<float>(gc),
-                           ptr<float>(gcol), ptr<float>(go), stream),
-          "gsb_unsort_grads");
+    check(gsb_render_backward_inputs(&meta, ptr<float>(rec), ptr<int32_t>(tile_offsets), ptr<int32_t>(binned_ids),
+                                     ptr<float>(final_T), ptr<int32_t>(last_idx), ptr<float>(pair_rec), ptr<float>(g),
+                                     ptr<int32_t>(perm), ptr<float>(gm), ptr<float>(gc), ptr<float>(gcol),
+                                     ptr<float>(go), ptr<uint32_t>(status), stream),
+          "gsb_render_backward_inputs");
   }
   if (debug_checks())
     read_status(status);

@@ -629,6 +629,57 @@ struct BwdWarpSmem {
   int red_gi[kRedChunk];
 };
 
+// Where the backward adds its per-splat gradients. The sink type is a template
+// argument of the backward kernels, so each mode compiles without the other's
+// branches.
+//
+// RecSink: the packed records grad_rec [B*G*12] in depth-rank order (the
+// un-sort is a separate launch); the staged target index is the rank itself.
+struct RecSink {
+  float* rec;
+  __device__ __forceinline__ int index(const Meta&, int r) const { return r; }
+  // Adds gradient component comp (0-8, grad-record order) of target idx.
+  __device__ __forceinline__ void add(int idx, int comp, float v) const {
+    atomicAdd(rec + (size_t)idx * GSB_REC_FLOATS + comp, v);
+  }
+  // All 9 components of one target (the CTA kernel's per-thread totals).
+  __device__ __forceinline__ void add9(int idx, const float (&a)[kGradComps]) const {
+    float4* g4 = reinterpret_cast<float4*>(rec + (size_t)idx * GSB_REC_FLOATS);
+    atomicAdd(g4 + 0, make_float4(a[0], a[1], a[2], a[3]));
+    atomicAdd(g4 + 1, make_float4(a[4], a[5], a[6], a[7]));
+    atomicAdd(rec + (size_t)idx * GSB_REC_FLOATS + 8, a[8]);
+  }
+};
+
+// InputSink: straight into the input-order outputs (the un-sort folded into
+// the atomics): splat rank r goes to o = (r / G) G + perm[r], components 0-1
+// to means2d [o*2], 2-4 to conics [o*3], 5 to opacities [o], 6-8 to colors
+// [o*3]; a null output is skipped. The targets are zeroed beforehand.
+struct InputSink {
+  const int32_t* perm;
+  float* means2d;
+  float* conics;
+  float* colors;
+  float* opacities;
+  // -1 stays -1 (an id out of range).
+  __device__ __forceinline__ int index(const Meta& m, int r) const {
+    return r < 0 ? r : fast_div(r, m.div_G) * m.G + __ldg(&perm[r]);
+  }
+  __device__ __forceinline__ void add(int idx, int comp, float v) const {
+    float* dst;
+    if (comp < 2) dst = means2d ? means2d + 2 * (size_t)idx + comp : nullptr;
+    else if (comp < 5) dst = conics ? conics + 3 * (size_t)idx + (comp - 2) : nullptr;
+    else if (comp == 5) dst = opacities ? opacities + idx : nullptr;
+    else dst = colors ? colors + 3 * (size_t)idx + (comp - 6) : nullptr;
+    if (dst) atomicAdd(dst, v);
+  }
+  __device__ __forceinline__ void add9(int idx, const float (&a)[kGradComps]) const {
+#pragma unroll
+    for (int q = 0; q < kGradComps; ++q)
+      if (a[q] != 0.0f) add(idx, q, a[q]);
+  }
+};
+
 struct TileOff {
   int start, n;
 };
@@ -698,9 +749,10 @@ __device__ __forceinline__ void prefetch_bwd_recs(TileOff off, BwdRecs* rb, int 
 }
 
 // Sums the staged gradient rows of `count` records (row = record slot x
-// component, one value per lane) and adds each nonzero total to grad_rec: lane
+// component, one value per lane) and adds each nonzero total to the sink: lane
 // L takes row L, reads it with 16-byte loads and sums it as packed pairs.
-__device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, float* __restrict__ grad_rec) {
+template <class Sink>
+__device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, const Sink& sink) {
   __syncwarp();
   if (lane < count * kGradComps) {
     const float4* row = reinterpret_cast<const float4*>(&W.red[lane][0]);
@@ -717,7 +769,7 @@ __device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, f
     const float total = (a0 + a1) + (a2 + a3);
     const int slot = lane / kGradComps, comp = lane - slot * kGradComps;
     const int gi = W.red_gi[slot];
-    if (gi >= 0 && total != 0.0f) atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + comp, total);
+    if (gi >= 0 && total != 0.0f) sink.add(gi, comp, total);
   }
   __syncwarp();
 }
@@ -727,13 +779,13 @@ __device__ __forceinline__ void flush_red(BwdWarpSmem& W, int count, int lane, f
 // kRedChunk records. kGuard: a record's colour is not finite (pixel_vjp2).
 // kCheckLast: some pixel of the warp stops before this record (j >= the
 // warp's smallest last_idx), so each pixel tests j < last.
-template <bool kClampOm, bool kGuard, bool kCheckLast, bool kSat>
+template <bool kClampOm, bool kGuard, bool kCheckLast, bool kSat, class Sink>
 __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, int row0, int j, int lane, float fx,
                                                 const F2 (&fy)[kLanePx / 2], const F2 (&gr)[kLanePx / 2],
                                                 const F2 (&gg)[kLanePx / 2], const F2 (&gb)[kLanePx / 2],
                                                 F2 (&Tc)[kLanePx / 2], F2 (&gT)[kLanePx / 2],
                                                 const int (&last)[kLanePx], int& slot, uint32_t* __restrict__ status,
-                                                float* __restrict__ grad_rec) {
+                                                const Sink& sink) {
   const BwdRecs& R = W.rb;
   const float4 p0 = R.rec[row0 + j][0];
   const float4 p1 = R.rec[row0 + j][1];
@@ -767,7 +819,7 @@ __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, i
   float v[16];
   vjp_expand(Sv, dx, p0.z, p0.w, p1.x, v);
   // Stage this splat's 9 lane values; every kRedChunk splats the warp
-  // sums the staged rows (one row per lane) and adds them to grad_rec.
+  // sums the staged rows (one row per lane) and adds them to the sink.
 #pragma unroll
   for (int t = 0; t < kGradComps; ++t) W.red[slot * kGradComps + t][lane] = v[t];
   if (lane == 0) {
@@ -776,10 +828,10 @@ __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, i
       raise_error(status, GSB_DEVERR_BOUNDS, kSiteRenderBwd);
       gi = -1;
     }
-    W.red_gi[slot] = gi;
+    W.red_gi[slot] = sink.index(m, gi);
   }
   if (++slot == kRedChunk) {
-    flush_red(W, slot, lane, grad_rec);
+    flush_red(W, slot, lane, sink);
     slot = 0;
   }
 }
@@ -788,32 +840,32 @@ __device__ __forceinline__ void bwd_warp_record(const Meta& m, BwdWarpSmem& W, i
 // tile_last of the warp's record buffer). Records at or past lmin (the warp's
 // smallest last_idx) test each pixel's stop; the ones before it are reached by
 // every pixel and skip that test.
-template <bool kClampOm, bool kGuard, bool kSat>
+template <bool kClampOm, bool kGuard, bool kSat, class Sink>
 __device__ __forceinline__ void bwd_warp_records(const Meta& m, BwdWarpSmem& W, int row0, int tile_last, int lmin,
                                                  int lane, float fx, const F2 (&fy)[kLanePx / 2],
                                                  const F2 (&gr)[kLanePx / 2], const F2 (&gg)[kLanePx / 2],
                                                  const F2 (&gb)[kLanePx / 2], F2 (&Tc)[kLanePx / 2],
                                                  F2 (&gT)[kLanePx / 2], const int (&last)[kLanePx],
-                                                 uint32_t* __restrict__ status, float* __restrict__ grad_rec) {
+                                                 uint32_t* __restrict__ status, const Sink& sink) {
   int slot = 0;
   int j = tile_last - 1;
 #pragma unroll 1
   for (; j >= lmin; --j)
     bwd_warp_record<kClampOm, kGuard, true, kSat>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
-                                            grad_rec);
+                                            sink);
 #pragma unroll 1
   for (; j >= 0; --j)
     bwd_warp_record<kClampOm, kGuard, false, kSat>(m, W, row0, j, lane, fx, fy, gr, gg, gb, Tc, gT, last, slot, status,
-                                             grad_rec);
-  if (slot > 0) flush_red(W, slot, lane, grad_rec);
+                                             sink);
+  if (slot > 0) flush_red(W, slot, lane, sink);
 }
 
-template <bool kClampOm>
+template <bool kClampOm, class Sink>
 __global__ void __launch_bounds__(kBwdWarps * 32, 4)
     k_render_bwd_warp(Meta m, const float4* __restrict__ pair_rec, const int32_t* __restrict__ toff,
                       const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                       const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
-                      float* __restrict__ grad_rec, uint32_t* __restrict__ status, int claims) {
+                      Sink sink, uint32_t* __restrict__ status, int claims) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 s_dyn[];
@@ -905,13 +957,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 4)
       const bool guard = __any_sync(kFullMask, bad_color), any_sat = __any_sync(kFullMask, sat);
       if (guard)
         bwd_warp_records<kClampOm, true, true>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT,
-                                               last, status, grad_rec);
+                                               last, status, sink);
       else if (any_sat)
         bwd_warp_records<kClampOm, false, true>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc, gT,
-                                                last, status, grad_rec);
+                                                last, status, sink);
       else
         bwd_warp_records<kClampOm, false, false>(m, W, row0, tile_last, warp_lmin, lane, fx, fy, gr, gg, gb, Tc,
-                                                 gT, last, status, grad_rec);
+                                                 gT, last, status, sink);
     }
     tile = nxt_tile;
     nxt_tile = nn_tile;
@@ -953,12 +1005,12 @@ __device__ __forceinline__ void flush_red_cta(float (*red)[kRedStride], const in
 // thread sums its pair's moments, expands them once, and the warp reduces the
 // 9 gradient components of its 64 pixels (one reduce-scatter) into shared
 // accumulators; each batch of records ends with one vector atomic per record.
-template <bool kClampOm>
+template <bool kClampOm, class Sink>
 __global__ void __launch_bounds__(kCtaThreads)
     k_render_bwd_cta(Meta m, const float4* __restrict__ rec, const int32_t* __restrict__ toff,
                      const int32_t* __restrict__ ids, const float* __restrict__ final_T,
                      const int32_t* __restrict__ last_idx, const float* __restrict__ grad,
-                     float* __restrict__ grad_rec, uint32_t* __restrict__ status) {
+                     Sink sink, uint32_t* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
   __shared__ float4 s_rec[kBatch][3];
@@ -1010,7 +1062,7 @@ __global__ void __launch_bounds__(kCtaThreads)
         bool bad_color = false, sat = false;
         for (int i = t; i < cnt; i += kCtaThreads) {
           const int gi = load_gi(ids, start + bstart + i, m.BG, status, kSiteRenderBwd);
-          s_gi[i] = gi;
+          s_gi[i] = sink.index(m, gi);
           load_rec(rec, gi, s_rec[i]);
           bad_color |= !finite_rgb(s_rec[i][1].z, s_rec[i][1].w, s_rec[i][2].x);
           sat |= may_saturate(s_rec[i][1].y, m.max_alpha);
@@ -1078,10 +1130,7 @@ __global__ void __launch_bounds__(kCtaThreads)
             nz |= (acc[q] != 0.0f);
           }
           if (nz && gi >= 0) {
-            float4* g4 = reinterpret_cast<float4*>(grad_rec + (size_t)gi * GSB_REC_FLOATS);
-            atomicAdd(g4 + 0, make_float4(acc[0], acc[1], acc[2], acc[3]));
-            atomicAdd(g4 + 1, make_float4(acc[4], acc[5], acc[6], acc[7]));
-            atomicAdd(grad_rec + (size_t)gi * GSB_REC_FLOATS + 8, acc[8]);
+            sink.add9(gi, acc);
           }
         }
         __syncthreads();  // s_rec / s_acc are refilled by the next batch
@@ -1191,10 +1240,10 @@ const GridCache& grids() {
   if (g.sms == 0) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute((const void*)k_render_bwd_warp<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kBwdWarpSmem);
-    cudaFuncSetAttribute((const void*)k_render_bwd_warp<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)kBwdWarpSmem);
+    for (const void* fn : {(const void*)k_render_bwd_warp<true, RecSink>, (const void*)k_render_bwd_warp<false, RecSink>,
+                           (const void*)k_render_bwd_warp<true, InputSink>,
+                           (const void*)k_render_bwd_warp<false, InputSink>})
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdWarpSmem);
     auto occ = [&](const void* fn, int threads, size_t smem) {
       int b = 1;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, threads, smem) != cudaSuccess || b < 1) b = 1;
@@ -1204,8 +1253,11 @@ const GridCache& grids() {
     g.fwd_warp[1] = occ((const void*)k_render_fwd_warp<true>, kWarps * 32, 0);
     g.fwd_cta[0] = occ((const void*)k_render_fwd_cta<false>, kCtaThreads, 0);
     g.fwd_cta[1] = occ((const void*)k_render_fwd_cta<true>, kCtaThreads, 0);
-    g.bwd_warp = occ((const void*)k_render_bwd_warp<false>, kBwdWarps * 32, kBwdWarpSmem);
-    g.bwd_cta = occ((const void*)k_render_bwd_cta<false>, kCtaThreads, 0);
+    // One grid for both sinks: the smaller residency of the two.
+    g.bwd_warp = min(occ((const void*)k_render_bwd_warp<false, RecSink>, kBwdWarps * 32, kBwdWarpSmem),
+                     occ((const void*)k_render_bwd_warp<false, InputSink>, kBwdWarps * 32, kBwdWarpSmem));
+    g.bwd_cta = min(occ((const void*)k_render_bwd_cta<false, RecSink>, kCtaThreads, 0),
+                    occ((const void*)k_render_bwd_cta<false, InputSink>, kCtaThreads, 0));
     g.sms = sms;
   }
   return g;
@@ -1286,6 +1338,34 @@ extern "C" int gsb_render_forward(const gsb_raster_meta* meta, const float* rec,
                         static_cast<cudaStream_t>(stream_));
 }
 
+namespace gsb {
+namespace {
+// Launches both backward kernels into `sink` (zeroed by the caller).
+template <class Sink>
+int render_backward_launch(const Meta& m, const float* rec, const int32_t* tile_offsets, const int32_t* binned_ids,
+                           const float* final_T, const int32_t* last_idx, const float* pair_rec,
+                           const float* grad_rgb, const Sink& sink, uint32_t* status, cudaStream_t stream) {
+  const GridCache& g = grids();
+  const float4* r4 = reinterpret_cast<const float4*>(rec);
+  const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
+  const int cta_grid = long_tile_grid(m, g.bwd_cta);
+  const int claims = m.total_tiles >= kMinTilesPerWarpForClaims * warp_grid * kBwdWarps ? 1 : 0;
+  // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
+  const bool clamp_om = !(1.0f - m.max_alpha >= m.eps);
+  auto bwd_warp = clamp_om ? k_render_bwd_warp<true, Sink> : k_render_bwd_warp<false, Sink>;
+  auto bwd_cta = clamp_om ? k_render_bwd_cta<true, Sink> : k_render_bwd_cta<false, Sink>;
+  cudaError_t e = launch_pdl(bwd_warp, warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream, m,
+                             reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx,
+                             grad_rgb, sink, status, claims);
+  if (e == cudaSuccess)
+    e = launch_pdl(bwd_cta, cta_grid, kCtaThreads, 0, stream, m, r4, tile_offsets, binned_ids, final_T,
+                   last_idx, grad_rgb, sink, status);
+  note_launches(2);
+  return cuda_status(e);
+}
+}  // namespace
+}  // namespace gsb
+
 extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
                                    const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
                                    const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
@@ -1304,23 +1384,25 @@ extern "C" int gsb_render_backward(const gsb_raster_meta* meta, const float* rec
     cudaError_t e = cudaMemsetAsync(grad_rec, 0, sizeof(float) * GSB_REC_FLOATS * (size_t)m.BG, stream);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
   }
-  const GridCache& g = grids();
-  const float4* r4 = reinterpret_cast<const float4*>(rec);
-  const int warp_grid = max(1, min(g.bwd_warp, (m.total_tiles + kBwdWarps - 1) / kBwdWarps));
-  const int cta_grid = long_tile_grid(m, g.bwd_cta);
-  const int claims = m.total_tiles >= kMinTilesPerWarpForClaims * warp_grid * kBwdWarps ? 1 : 0;
-  // 1 - alpha needs the eps clamp only when max_alpha > 1 - eps.
-  const bool clamp_om = !(1.0f - m.max_alpha >= m.eps);
-  auto bwd_warp = clamp_om ? k_render_bwd_warp<true> : k_render_bwd_warp<false>;
-  auto bwd_cta = clamp_om ? k_render_bwd_cta<true> : k_render_bwd_cta<false>;
-  cudaError_t e = launch_pdl(bwd_warp, warp_grid, kBwdWarps * 32, kBwdWarpSmem, stream, m,
-                             reinterpret_cast<const float4*>(pair_rec), tile_offsets, binned_ids, final_T, last_idx,
-                             grad_rgb, grad_rec, status, claims);
-  if (e == cudaSuccess)
-    e = launch_pdl(bwd_cta, cta_grid, kCtaThreads, 0, stream, m, r4, tile_offsets, binned_ids, final_T,
-                   last_idx, grad_rgb, grad_rec, status);
-  note_launches(2);
-  return cuda_status(e);
+  const RecSink sink{grad_rec};
+  return render_backward_launch(m, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, grad_rgb, sink,
+                                status, stream);
+}
+
+extern "C" int gsb_render_backward_inputs(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
+                                          const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
+                                          const float* pair_rec, const float* grad_rgb, const int32_t* perm,
+                                          float* g_means2d, float* g_conics, float* g_colors, float* g_opacities,
+                                          uint32_t* status, void* stream_) {
+  Meta m;
+  int rc = make_meta(meta, &m);
+  if (rc != GSB_OK) return rc;
+  if (!tile_offsets || !final_T || !last_idx || !grad_rgb || !status) return GSB_ERR_INVALID_ARGUMENT;
+  if (m.BG > 0 && (!rec || !pair_rec || !perm)) return GSB_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(pair_rec) & 15u) return GSB_ERR_INVALID_ARGUMENT;
+  const InputSink sink{perm, g_means2d, g_conics, g_colors, g_opacities};
+  return render_backward_launch(m, rec, tile_offsets, binned_ids, final_T, last_idx, pair_rec, grad_rgb, sink,
+                                status, static_cast<cudaStream_t>(stream_));
 }
 
 extern "C" int gsb_unsort_grads(const gsb_raster_meta* meta, const int32_t* perm, const float* grad_rec,

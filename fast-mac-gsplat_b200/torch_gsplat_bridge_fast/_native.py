@@ -55,6 +55,7 @@ EXPORTED = (
     "gsb_render_workspace_size",
     "gsb_render_forward",
     "gsb_render_backward",
+    "gsb_render_backward_inputs",
     "gsb_unsort_grads",
     "gsb_project_forward",
     "gsb_project_backward",
@@ -125,6 +126,7 @@ def load() -> C.CDLL:
         "gsb_render_workspace_size": (sz, [M]),
         "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_render_backward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, sz, p]),
+        "gsb_render_backward_inputs": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, p, p, p, p]),
         "gsb_unsort_grads": (C.c_int, [M, p, p, p, p, p, p, p]),
         "gsb_project_forward": (C.c_int, [i32, i32, p, p, p, p, p, p, f32, p, p, p, p, p]),
         "gsb_project_backward": (C.c_int, [i32, i32] + [p] * 10 + [f32] + [p] * 7),

@@ -183,6 +183,19 @@ int gsb_render_backward(const gsb_raster_meta* meta, const float* rec, const int
                         const float* pair_rec, const float* grad_rgb, float* grad_rec, uint32_t* status,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* gsb_render_backward with the un-sort folded into its atomics (no reference
+ * counterpart of its own): each splat's gradients are added straight at its
+ * input position (view b, index perm[r] of rank r), so no grad_rec and no
+ * gsb_unsort_grads launch are needed. The outputs must be zeroed by the
+ * caller; any output pointer may be NULL (that gradient is skipped). The
+ * permuted targets cost the atomics more L2 traffic, so it pays for large
+ * splat counts (this library's host runtime uses it from 2^18 splats). */
+int gsb_render_backward_inputs(const gsb_raster_meta* meta, const float* rec, const int32_t* tile_offsets,
+                               const int32_t* binned_ids, const float* final_T, const int32_t* last_idx,
+                               const float* pair_rec, const float* grad_rgb, const int32_t* perm,
+                               float* g_means2d, float* g_conics, float* g_colors, float* g_opacities,
+                               uint32_t* status, void* stream);
+
 /* Replaces the un-sort scatter of the autograd backward
  * (torch_gsplat_bridge_fast/rasterize.py:96-105; …/v8_project3d/…/rasterize.py:583-591, 847-851).
  * Any output pointer may be NULL (that gradient is skipped). */

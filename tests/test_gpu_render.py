@@ -540,6 +540,45 @@ def test_reference_harness_entry_measures_accuracy(mode):
         run_renderer("nope", base, s.height, s.width)
 
 
+@pytest.mark.parametrize("name", ["c1", "c2"])
+def test_backward_into_inputs_matches_records_and_unsort(name):
+    """gsb_render_backward_inputs (the backward with the un-sort folded into its
+    atomics, which the host runtime uses) against gsb_render_backward followed
+    by gsb_unsort_grads, through the C ABI, for every output and for subsets
+    with NULL outputs: the same gradients up to the order of the float atomics.
+    c1 has long tiles (the CTA kernel), c2 four views (the view offset of the
+    input position)."""
+    from torch_gsplat_bridge_fast import _native as N
+    from torch_gsplat_bridge_fast.rasterize import _bin, _render_forward
+
+    L = N.load()
+    s = config_2d(name, seed=5)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV).contiguous() for t in s.tensors()))
+    _, T, last, pair_rec = _render_forward(st, cfg, s.B, save_state=True)
+    g = grad_image(s.B, s.height, s.width, seed=6).to(DEV).contiguous()
+    meta = st.meta
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    args = [N.ptr(st.rec), N.ptr(st.tile_offsets), N.ptr(st.binned_ids), N.ptr(T), N.ptr(last), N.ptr(pair_rec),
+            N.ptr(g)]
+    BG = s.B * s.G
+    grad_rec = torch.empty(BG, 12, device=DEV)
+    N.check(L.gsb_render_backward(meta, *args, N.ptr(grad_rec), N.ptr(status), None, 0, N.stream_ptr(DEV)),
+            "gsb_render_backward")
+    shapes = [(s.B, s.G, 2), (s.B, s.G, 3), (s.B, s.G, 3), (s.B, s.G)]
+    want = [torch.zeros(sh, device=DEV) for sh in shapes]
+    N.check(L.gsb_unsort_grads(meta, N.ptr(st.perm), N.ptr(grad_rec), *(N.ptr(t) for t in want), N.stream_ptr(DEV)),
+            "gsb_unsort_grads")
+    for sel in [(0, 1, 2, 3), (3,), (0, 2)]:
+        got = [torch.zeros(sh, device=DEV) if k in sel else None for k, sh in enumerate(shapes)]
+        N.check(L.gsb_render_backward_inputs(meta, *args, N.ptr(st.perm), *(N.ptr(t) for t in got), N.ptr(status),
+                                             N.stream_ptr(DEV)), "gsb_render_backward_inputs")
+        torch.cuda.synchronize()
+        assert int(status[N.GSB_STATUS_ERROR]) == 0
+        for k in sel:
+            assert rel_err(np_(got[k]), np_(want[k])) <= 1e-5, (name, sel, k)
+
+
 @pytest.mark.parametrize("G", [70_000, 300_000])
 def test_unsort_grads_with_any_subset_of_outputs(G):
     """gsb_unsort_grads (the un-sort of the autograd backward, …/rasterize.py:583-591)
