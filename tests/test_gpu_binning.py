@@ -129,10 +129,10 @@ def test_binning_row_walk_edges():
     assert_bin_equal(gpu_bin(s), cpu_bin(s))
 
 
-@pytest.mark.parametrize("B,G", [(1, 65536), (2, 30001), (3, 8192), (2, 8193)])
+@pytest.mark.parametrize("B,G", [(1, 65536), (1, 40001), (1, 65537), (2, 30001), (3, 8192), (2, 8193)])
 def test_depth_order_with_ties(B, G):
     """Depths drawn from 37 values: the depth order must keep input order within
-    each tie, across sort partitions and across views."""
+    each tie, across sort partitions and across views (one view: 32-bit keys)."""
     s = make_2d(B, G, 96, 128, seed=G + B, sigma=(0.5, 3.0))
     s.depths.copy_(torch.floor(s.depths / 100.0 * 37.0) + 0.5)
     assert_bin_equal(gpu_bin(s), cpu_bin(s))
@@ -173,8 +173,11 @@ def _sort(keys: np.ndarray, vals: np.ndarray, begin: int, end: int):
 
 @pytest.mark.parametrize("n,begin,end", [(1, 0, 8), (4095, 0, 32), (4096, 32, 48), (4097, 5, 19),
                                          (100_000, 0, 64), (1_000_003, 32, 45), (300_000, 0, 0),
-                                         (2_000_001, 10, 11), (700_001, 40, 51)])
+                                         (2_000_001, 10, 11), (700_001, 40, 51),
+                                         (28_673, 3, 40), (32_768, 0, 64), (32_769, 0, 33)])
 def test_radix_sort_is_stable_and_exact(n, begin, end):
+    """Sizes on both sides of the partition sizes (1,024 / 2,048 / 4,096 keys)
+    and of the item-count switches, full and partial last partitions."""
     rng = np.random.default_rng(n + begin)
     keys = rng.integers(0, 2**63, n, dtype=np.uint64) | (rng.integers(0, 2, n, dtype=np.uint64) << np.uint64(63))
     keys[: n // 3] &= np.uint64(0xFFFF0000FFFF00FF)  # many ties
