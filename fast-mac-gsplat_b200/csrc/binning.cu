@@ -1019,6 +1019,50 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Tile offsets from the last sort pass's key ranges (SortRanges), in place:
+// off[t] (t < tiles) holds n - (tile t's first pair position), 0 for an empty
+// tile, and block[k] the same for the first pair of 256-tile block k. An empty
+// tile starts where the next non-empty tile does (or at n), so off[t] is the
+// minimum start over tiles s >= t, and off[tiles] = n. One CTA per block: the
+// start after its block comes from the block entries to its right (the
+// largest n - position there), the rest from a block-wide suffix minimum.
+__global__ void __launch_bounds__(kRangesBlock)
+    k_ranges_fix(int32_t* __restrict__ off, const int32_t* __restrict__ block, int tiles, int32_t n) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int32_t s_red[kRangesBlock / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int blocks = (tiles + kRangesBlock - 1) / kRangesBlock;
+  // The first pair after this block: the largest block entry to the right.
+  int32_t far = 0;
+  for (int k = blockIdx.x + 1 + tid; k < blocks; k += kRangesBlock) far = max(far, block[k]);
+  far = __reduce_max_sync(kFullMask, far);
+  if (lane == 0) s_red[warp] = far;
+  __syncthreads();
+  int32_t right_v = 0;
+#pragma unroll
+  for (int w = 0; w < kRangesBlock / 32; ++w) right_v = max(right_v, s_red[w]);
+  const int32_t right = right_v > 0 ? n - right_v : n;
+  __syncthreads();  // s_red is reused
+  const int t = blockIdx.x * kRangesBlock + tid;
+  int32_t x = n;
+  if (t < tiles) {
+    const int32_t v = off[t];
+    x = v > 0 ? n - v : n;
+  }
+  // Inclusive suffix minimum within the warp, then over the warps to the right.
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_down_sync(kFullMask, x, o);
+    if (lane + o < 32) x = min(x, y);
+  }
+  if (lane == 0) s_red[warp] = x;
+  __syncthreads();
+  for (int w = warp + 1; w < kRangesBlock / 32; ++w) x = min(x, s_red[w]);
+  if (t < tiles) off[t] = min(x, right);
+  if (t == tiles - 1) off[tiles] = n;
+}
+
 __global__ void k_fill_i32(int32_t* __restrict__ p, int64_t n, int32_t v) {
   pdl_wait();
   pdl_trigger();
@@ -1211,11 +1255,13 @@ struct EmitWs {
   uint32_t* keys;         // emitted tile keys, rank order
   uint32_t* vals;
   uint32_t* keys_sorted;  // tile keys after the sort
+  int32_t* block_first;   // per 256-tile block: n - its first pair position (SortRanges.block)
 };
-void carve_emit(Carver& c, int64_t P, EmitWs* w) {
+void carve_emit(Carver& c, const Meta& m, int64_t P, EmitWs* w) {
   w->keys = c.take<uint32_t>((size_t)P);
   w->vals = c.take<uint32_t>((size_t)P);
   w->keys_sorted = c.take<uint32_t>((size_t)P);
+  w->block_first = c.take<int32_t>(((size_t)m.total_tiles + kRangesBlock - 1) / kRangesBlock);
 }
 int tile_end_bit(const Meta& m) { return m.total_tiles > 1 ? bits_for(m.total_tiles - 1) : 0; }
 }  // namespace
@@ -1225,16 +1271,17 @@ extern "C" size_t gsb_bin_emit_workspace_size(const gsb_raster_meta* meta, int64
   if (make_meta(meta, &m) != GSB_OK || total_pairs < 0) return 0;
   Carver c(nullptr);
   EmitWs w;
-  carve_emit(c, total_pairs, &w);
+  carve_emit(c, m, total_pairs, &w);
   radix_sort_pairs(c, (const uint32_t*)nullptr, nullptr, nullptr, nullptr, total_pairs, 0, tile_end_bit(m), nullptr,
                    0, false);
   return c.off + 256;
 }
 
-extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
-                            const uint64_t* tile_masks, int64_t total_pairs, uint64_t* keys, int32_t* binned_ids,
-                            int32_t* tile_offsets, uint32_t* status, void* workspace,
-                            size_t workspace_bytes, void* stream_) {
+namespace {
+// gsb_bin_emit (fold_request false) and gsb_bin_emit_ranges (true, keys NULL).
+int bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets, const uint64_t* tile_masks,
+             int64_t total_pairs, uint64_t* keys, int32_t* binned_ids, int32_t* tile_offsets, uint32_t* status,
+             void* workspace, size_t workspace_bytes, void* stream_, bool fold_request) {
   Meta m;
   int rc = make_meta(meta, &m);
   if (rc != GSB_OK) return rc;
@@ -1252,25 +1299,62 @@ extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const
   }
   Carver c(workspace);
   EmitWs w;
-  carve_emit(c, total_pairs, &w);
+  carve_emit(c, m, total_pairs, &w);
   const ZeroRegion sz = radix_sort_zero_region(c, total_pairs, 0, tile_end_bit(m), true);
+  // Folded ranges: the last tile-sort pass records each tile's first position
+  // and k_ranges_fix turns them into offsets, so the sorted tile keys are
+  // neither written nor read back (one tile: no pass, k_ranges instead).
+  const bool fold_ranges = fold_request && sort_passes(0, tile_end_bit(m)) > 0;
   ZeroList zero;
   zero.ptr[0] = sz.ptr;
   zero.words[0] = sz.words;
-  zero.ptr[1] = zero.ptr[2] = nullptr;
-  zero.words[1] = zero.words[2] = 0;
+  zero.ptr[1] = fold_ranges ? reinterpret_cast<uint32_t*>(tile_offsets) : nullptr;
+  zero.words[1] = fold_ranges ? (size_t)T1 : 0;
+  const size_t nblocks = ((size_t)m.total_tiles + kRangesBlock - 1) / kRangesBlock;
+  zero.ptr[2] = fold_ranges ? reinterpret_cast<uint32_t*>(w.block_first) : nullptr;
+  zero.words[2] = fold_ranges ? nblocks : 0;
   launch_pdl(k_emit, grid1d(m.BG, 256), 256, 0, stream, m, reinterpret_cast<const float4*>(rec), pair_offsets,
              reinterpret_cast<const unsigned long long*>(tile_masks), w.keys, w.vals, status, zero,
              big_bits_of(m, const_cast<uint64_t*>(tile_masks), status));
   note_launches(1);
+  SortRanges ranges;
+  if (fold_ranges) {
+    ranges.first = tile_offsets;
+    ranges.block = w.block_first;
+    ranges.n = m.total_tiles;
+  }
   cudaError_t e = radix_sort_pairs(c, w.keys, w.vals, w.keys_sorted, reinterpret_cast<uint32_t*>(binned_ids),
-                                   total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true);
+                                   total_pairs, 0, tile_end_bit(m), status, stream, /*scratch_zeroed=*/true,
+                                   nullptr, ranges);
   if (e != cudaSuccess) return GSB_ERR_CUDA;
+  if (fold_ranges) {
+    launch_pdl(k_ranges_fix, (unsigned)nblocks, kRangesBlock, 0, stream, tile_offsets, (const int32_t*)w.block_first,
+               m.total_tiles, (int32_t)total_pairs);
+    note_launches(1);
+    return cuda_status(cudaGetLastError());
+  }
   launch_pdl(k_ranges, grid1d((total_pairs + 3) / 4, 256), 256, 0, stream, w.keys_sorted, reinterpret_cast<const uint32_t*>(binned_ids),
                                                          reinterpret_cast<const float4*>(rec), total_pairs,
                                                          m.total_tiles, tile_offsets, keys);
   note_launches(1);
   return cuda_status(cudaGetLastError());
+}
+}  // namespace
+
+extern "C" int gsb_bin_emit(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
+                            const uint64_t* tile_masks, int64_t total_pairs, uint64_t* keys, int32_t* binned_ids,
+                            int32_t* tile_offsets, uint32_t* status, void* workspace,
+                            size_t workspace_bytes, void* stream_) {
+  return bin_emit(meta, rec, pair_offsets, tile_masks, total_pairs, keys, binned_ids, tile_offsets, status,
+                  workspace, workspace_bytes, stream_, false);
+}
+
+extern "C" int gsb_bin_emit_ranges(const gsb_raster_meta* meta, const float* rec, const int32_t* pair_offsets,
+                                   const uint64_t* tile_masks, int64_t total_pairs, int32_t* binned_ids,
+                                   int32_t* tile_offsets, uint32_t* status, void* workspace,
+                                   size_t workspace_bytes, void* stream_) {
+  return bin_emit(meta, rec, pair_offsets, tile_masks, total_pairs, nullptr, binned_ids, tile_offsets, status,
+                  workspace, workspace_bytes, stream_, true);
 }
 
 extern "C" int gsb_tile_stats(const gsb_raster_meta* meta, const int32_t* tile_offsets, uint32_t* status,

@@ -137,13 +137,20 @@ __device__ __forceinline__ void rank_items(const K (&k)[ITEMS], uint32_t (&rank)
 // ranked keys are first placed in digit order in shared memory (while the
 // look-back resolves), then written out by consecutive threads, so each
 // digit's run leaves the CTA as contiguous stores.
-template <typename K, int ITEMS>
+// kRanges (the last pass of a sort whose caller asked for key ranges): the
+// sorted keys are not written; instead the first output position of each key
+// value a partition holds is recorded as atomicMax(first[key], n - pos), so
+// first[] (zeroed beforehand) ends up holding n - (the key's first position),
+// 0 for a key value that does not occur; block[] gets the same per block of
+// kRangesBlock key values.
+template <typename K, int ITEMS, bool kRanges = false>
 __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
     rs_onesweep(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                 K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
                 int shift, int bits, const uint32_t* __restrict__ hist,
                 uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter,
-                uint32_t* __restrict__ status) {
+                uint32_t* __restrict__ status, int32_t* __restrict__ first, int32_t* __restrict__ block,
+                int64_t first_n) {
   pdl_wait();
   pdl_trigger();
   constexpr int kTile = kSortThreads * ITEMS;
@@ -301,7 +308,18 @@ __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
       const K key = sm.keys[e];
       const uint32_t d = (uint32_t)(key >> shift) & dmask;
       const uint32_t pos = sm.global_base[d] + ((uint32_t)e - sm.local_base[d]);
-      keys_out[pos] = key;
+      if (kRanges) {
+        // Staged keys of one digit keep the previous passes' order, so equal
+        // keys are adjacent and the first of a run starts the key here.
+        const K prev = e == 0 ? key : sm.keys[e - 1];
+        if ((e == 0 || prev != key) && (int64_t)key < first_n) {
+          const int32_t v = (int32_t)(n - (int64_t)pos);
+          atomicMax(&first[(size_t)key], v);
+          if (e == 0 || prev / kRangesBlock != key / kRangesBlock) atomicMax(&block[(size_t)key / kRangesBlock], v);
+        }
+      } else {
+        keys_out[pos] = key;
+      }
       vals_out[pos] = sm.vals[e];
     }
   }
@@ -344,6 +362,14 @@ static cudaError_t onesweep_smem_optin() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(rs_onesweep<K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)sizeof(OnesweepSmem<K, 8>));
+  if constexpr (sizeof(K) == 4) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(rs_onesweep<K, 16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(OnesweepSmem<K, 16>));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(rs_onesweep<K, 8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(OnesweepSmem<K, 8>));
+  }
   if (e == cudaSuccess) done[dev & 63] = true;
   return e;
 }
@@ -356,10 +382,16 @@ static int sort_items(int64_t n) {
   return 4;
 }
 
+template <typename K, bool kRanges>
+static auto onesweep_kernel(int items) {
+  return items == 16 ? rs_onesweep<K, 16, kRanges> : items == 8 ? rs_onesweep<K, 8, kRanges> : rs_onesweep<K, 4, kRanges>;
+}
+
 template <typename K>
 static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32_t* vals_in, K* keys_out,
                                       uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                                      cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist) {
+                                      cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist,
+                                      SortRanges ranges) {
   const int passes = sort_passes(begin_bit, end_bit);
   const int items = sort_items(n);
   const int64_t tile = (int64_t)kSortThreads * items;
@@ -401,12 +433,14 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     K* ko = to_out ? keys_out : k_tmp;
     uint32_t* vo = to_out ? vals_out : v_tmp;
     const int bits = (p == passes - 1) ? last_bits : kRadixBits;
-    auto kernel = items == 16 ? rs_onesweep<K, 16> : items == 8 ? rs_onesweep<K, 8> : rs_onesweep<K, 4>;
+    auto kernel = onesweep_kernel<K, false>(items);
+    if constexpr (sizeof(K) == 4)
+      if (ranges.first && p == passes - 1) kernel = onesweep_kernel<K, true>(items);
     const size_t smem = items == 16 ? sizeof(OnesweepSmem<K, 16>)
                                     : items == 8 ? sizeof(OnesweepSmem<K, 8>) : sizeof(OnesweepSmem<K, 4>);
     launch_pdl(kernel, (unsigned)parts, kSortThreads, smem, stream, 
         ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, hist + p * kRadix,
-        lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status);
+        lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status, ranges.first, ranges.block, ranges.n);
     note_launches(1);
     ki = ko;
     vi = vo;
@@ -418,14 +452,15 @@ cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t
                              uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
                              cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist) {
   return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream,
-                            scratch_zeroed, digit_hist);
+                            scratch_zeroed, digit_hist, SortRanges{});
 }
 
 cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in, uint32_t* keys_out,
                              uint32_t* vals_out, int64_t n, int begin_bit, int end_bit, uint32_t* status,
-                             cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist) {
+                             cudaStream_t stream, bool scratch_zeroed, const uint32_t* digit_hist,
+                             SortRanges ranges) {
   return radix_sort_pairs_t(ws, keys_in, vals_in, keys_out, vals_out, n, begin_bit, end_bit, status, stream,
-                            scratch_zeroed, digit_hist);
+                            scratch_zeroed, digit_hist, ranges);
 }
 
 template <typename K>

@@ -37,11 +37,24 @@ cudaError_t radix_sort_pairs(Carver& ws, const uint64_t* keys_in, const uint32_t
                              uint64_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
                              int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed,
                              const uint32_t* digit_hist = nullptr);
+// Key ranges instead of sorted keys (32-bit keys, at least one pass): the
+// last pass does not write keys_out; for each key value k < n it leaves in
+// first[k] (zeroed beforehand, by the caller) the count of output positions
+// from k's first position to the end (n_pairs - position), 0 when k does not
+// occur, and the same in block[k / kRangesBlock] for the first key of each
+// block of kRangesBlock key values.
+constexpr int kRangesBlock = 256;
+struct SortRanges {
+  int32_t* first = nullptr;
+  int32_t* block = nullptr;
+  int64_t n = 0;
+};
+
 // 32-bit keys (end_bit <= 32): 8 bytes per pair moved per pass instead of 12.
 cudaError_t radix_sort_pairs(Carver& ws, const uint32_t* keys_in, const uint32_t* vals_in,
                              uint32_t* keys_out, uint32_t* vals_out, int64_t n, int begin_bit,
                              int end_bit, uint32_t* status, cudaStream_t stream, bool scratch_zeroed,
-                             const uint32_t* digit_hist = nullptr);
+                             const uint32_t* digit_hist = nullptr, SortRanges ranges = SortRanges{});
 
 // The words a radix_sort_pairs call carved from `ws` (at its current offset)
 // needs cleared before it runs (histograms, partition counters, look-back).

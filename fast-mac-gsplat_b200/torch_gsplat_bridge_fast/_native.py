@@ -51,6 +51,7 @@ EXPORTED = (
     "gsb_bin_sort_scan",
     "gsb_bin_emit_workspace_size",
     "gsb_bin_emit",
+    "gsb_bin_emit_ranges",
     "gsb_tile_stats",
     "gsb_render_workspace_size",
     "gsb_render_forward",
@@ -122,6 +123,7 @@ def load() -> C.CDLL:
         "gsb_bin_sort_scan": (C.c_int, [M, p, p, p, p, p, p, p, p, p, p, p, sz, p]),
         "gsb_bin_emit_workspace_size": (sz, [M, i64]),
         "gsb_bin_emit": (C.c_int, [M, p, p, p, i64, p, p, p, p, p, sz, p]),
+        "gsb_bin_emit_ranges": (C.c_int, [M, p, p, p, i64, p, p, p, p, sz, p]),
         "gsb_tile_stats": (C.c_int, [M, p, p, p]),
         "gsb_render_workspace_size": (sz, [M]),
         "gsb_render_forward": (C.c_int, [M, p, p, p, p, p, p, p, p, p, sz, p]),

@@ -219,6 +219,42 @@ def test_emit_without_masks_matches(name):
     assert np.array_equal(keys.cpu().numpy().view(np.uint64), c["keys"])
 
 
+@pytest.mark.parametrize("B,G,H,W,sigma", [
+    (1, 1, 16, 16, (2.0, 3.0)),          # one tile: no sort pass, k_ranges path
+    (1, 7, 17, 33, (0.5, 30.0)),         # 6 tiles, most of them empty: one pass
+    (1, 300, 256, 256, (0.5, 4.0)),      # 256 tiles: one 8-bit pass
+    (1, 60, 1024, 1024, (0.5, 3.0)),     # sparse: long runs of empty tiles
+    (2, 4097, 129, 257, (1.0, 40.0)),
+    (5, 2000, 2048, 2048, (0.5, 6.0)),   # 81,920 tiles: three passes
+    (5, 500, 4096, 4096, (0.5, 3.0)),    # 327,680 tiles, 1,280 blocks of 256
+])
+def test_emit_tile_ranges_without_keys(B, G, H, W, sigma):
+    """gsb_bin_emit_ranges (the host runtime's call for many pairs per tile):
+    the last tile-sort pass records each tile's and each 256-tile block's
+    first pair and k_ranges_fix fills the offsets (empty tiles and empty
+    blocks included); ids and offsets must equal gsb_bin_emit's and the
+    oracle's."""
+    s = make_2d(B, G, H, W, seed=B * 7 + G, sigma=sigma)
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV).contiguous() for t in s.tensors()))
+    L = N.load()
+    T = st.tile_offsets.numel() - 1
+    ids = torch.full((max(st.P, 1),), -7, dtype=torch.int32, device=DEV)
+    toff = torch.full((T + 1,), -7, dtype=torch.int32, device=DEV)
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    wsb = int(L.gsb_bin_emit_workspace_size(st.meta, st.P))
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=DEV)
+    N.check(L.gsb_bin_emit_ranges(st.meta, N.ptr(st.rec), N.ptr(st.pair_offsets), None, st.P, N.ptr(ids),
+                                  N.ptr(toff), N.ptr(status), N.ptr(ws), wsb, N.stream_ptr(DEV)),
+            "gsb_bin_emit_ranges")
+    torch.cuda.synchronize()
+    assert int(status[N.GSB_STATUS_ERROR]) == 0
+    assert torch.equal(ids[:st.P], st.binned_ids) and torch.equal(toff, st.tile_offsets)
+    c = cpu_bin(s)
+    assert np.array_equal(ids[:st.P].cpu().numpy(), c["ids"])
+    assert np.array_equal(toff.cpu().numpy(), c["tile_offsets"])
+
+
 @pytest.mark.parametrize("sigma,G,H,W", [
     ((20.0, 120.0), 600, 512, 640),   # hundreds to thousands of candidate tiles per splat: hit bits
     ((150.0, 300.0), 300, 1024, 1024),  # every splat covers the frame: the bit region (8 words a splat) fills up
