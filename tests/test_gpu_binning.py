@@ -255,6 +255,27 @@ def test_emit_tile_ranges_without_keys(B, G, H, W, sigma):
     assert np.array_equal(toff.cpu().numpy(), c["tile_offsets"])
 
 
+def test_emit_tile_ranges_without_pairs():
+    """No visible splat: gsb_bin_emit_ranges writes all-zero tile offsets."""
+    s = make_2d(2, 64, 40, 70, seed=5, sigma=(1.0, 4.0))
+    s.opacities.zero_()
+    cfg = tgb.RasterConfig(s.height, s.width)
+    st = _bin(cfg, *(t.to(DEV).contiguous() for t in s.tensors()))
+    assert st.P == 0
+    L = N.load()
+    T = st.tile_offsets.numel() - 1
+    ids = torch.empty(1, dtype=torch.int32, device=DEV)
+    toff = torch.full((T + 1,), -7, dtype=torch.int32, device=DEV)
+    status = torch.zeros(N.GSB_STATUS_WORDS, dtype=torch.int32, device=DEV)
+    wsb = int(L.gsb_bin_emit_workspace_size(st.meta, 0))
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=DEV)
+    N.check(L.gsb_bin_emit_ranges(st.meta, N.ptr(st.rec), N.ptr(st.pair_offsets), None, 0, N.ptr(ids),
+                                  N.ptr(toff), N.ptr(status), N.ptr(ws), wsb, N.stream_ptr(DEV)),
+            "gsb_bin_emit_ranges")
+    torch.cuda.synchronize()
+    assert int(toff.abs().sum()) == 0
+
+
 @pytest.mark.parametrize("sigma,G,H,W", [
     ((20.0, 120.0), 600, 512, 640),   # hundreds to thousands of candidate tiles per splat: hit bits
     ((150.0, 300.0), 300, 1024, 1024),  # every splat covers the frame: the bit region (8 words a splat) fills up
