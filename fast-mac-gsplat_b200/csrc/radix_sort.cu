@@ -143,14 +143,17 @@ __device__ __forceinline__ void rank_items(const K (&k)[ITEMS], uint32_t (&rank)
 // first[] (zeroed beforehand) ends up holding n - (the key's first position),
 // 0 for a key value that does not occur; block[] gets the same per block of
 // kRangesBlock key values.
-template <typename K, int ITEMS, bool kRanges = false>
+// kPrefix (the first pass of a long sort, see rs_part_counts): partition
+// blockIdx.x reads its per-digit exclusive prefix over the partitions before it
+// from prefix[] instead of resolving it by look-back.
+template <typename K, int ITEMS, bool kRanges = false, bool kPrefix = false>
 __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
     rs_onesweep(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                 K* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
                 int shift, int bits, const uint32_t* __restrict__ hist,
                 uint32_t* __restrict__ lookback, uint32_t* __restrict__ part_counter,
                 uint32_t* __restrict__ status, int32_t* __restrict__ first, int32_t* __restrict__ block,
-                int64_t first_n) {
+                int64_t first_n, const uint32_t* __restrict__ prefix) {
   pdl_wait();
   pdl_trigger();
   constexpr int kTile = kSortThreads * ITEMS;
@@ -159,7 +162,7 @@ __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) sm.part = atomicAdd(part_counter, 1u);
+  if (tid == 0) sm.part = kPrefix ? blockIdx.x : atomicAdd(part_counter, 1u);
   for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&sm.warp_hist[0][0])[i] = 0u;
   __syncthreads();
   const uint32_t part = sm.part;
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
     sum += c;
   }
   uint32_t* my = lookback + (size_t)part * kRadix + t;
-  st_volatile_u32(my, (part == 0 ? kFlagInc : kFlagAgg) | sum);
+  if (!kPrefix) st_volatile_u32(my, (part == 0 ? kFlagInc : kFlagAgg) | sum);
   {
     uint32_t x = sum;
 #pragma unroll
@@ -263,7 +266,9 @@ __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
   }
   // Decoupled look-back for digit t.
   uint32_t exclusive = 0;
-  if (part != 0) {
+  if (kPrefix) {
+    exclusive = prefix[(size_t)part * kRadix + t];
+  } else if (part != 0) {
     // Windowed look-back: read kLookWin predecessors at once, consume them
     // nearest-first until an inclusive prefix is found (one L2 round trip per
     // window instead of one per predecessor).
@@ -325,6 +330,164 @@ __global__ void __launch_bounds__(kSortThreads, (ITEMS >= 16 ? 3 : 0))
   }
 }
 
+// Reduce-then-scan for the first pass of a long sort (n >= kPrefixMinN, two
+// or more passes), in place of that pass's decoupled look-back, whose walk
+// back to an inclusive prefix (about 40 partitions) bound the pass. One CTA
+// per onesweep partition counts its keys' digits for every pass
+// (rs_part_counts, which also replaces the histogram launch); 256-partition
+// groups are summed (rs_group_sums); one CTA scans the group sums of the first
+// pass over the groups and writes every pass's digit totals (rs_group_scan);
+// then each group's partitions get their exclusive prefixes, in place of
+// their first-pass counts (rs_part_prefix). Later passes keep the look-back:
+// their partitions hold the previous pass's output, which exists only after it.
+constexpr int64_t kPrefixMinN = int64_t(1) << 22;
+constexpr int kPrefixGroup = 256;   // partitions per group
+constexpr int kPrefixThreads = 1024;  // 4 threads per digit in the scan kernels
+constexpr int kPrefixSlices = kPrefixThreads / kRadix;
+
+// counts[(p * parts + part) * kRadix + d]: keys of partition `part` (the
+// onesweep partition of ITEMS x 256 keys) with digit d in pass p.
+template <typename K, int ITEMS>
+__global__ void __launch_bounds__(kSortThreads)
+    rs_part_counts(const K* __restrict__ keys, int64_t n, int begin_bit, int passes, int last_bits,
+                   uint32_t* __restrict__ counts, int64_t parts) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t s_cnt[kMaxPasses][kRadix];
+  for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) s_cnt[i / kRadix][i % kRadix] = 0;
+  __syncthreads();
+  const int64_t part = blockIdx.x;
+  const int64_t i0 = part * (int64_t)(kSortThreads * ITEMS) + (int64_t)threadIdx.x * ITEMS;
+  const int cnt = (int)max((int64_t)0, min((int64_t)ITEMS, n - i0));
+  if (cnt > 0) {
+    K k[ITEMS];
+    // ITEMS * sizeof(K) is a multiple of 16, so a 16-byte aligned array gives aligned chunks.
+    const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15u) == 0u;
+    if (cnt == ITEMS && vec) {
+      constexpr int kPer = 16 / sizeof(K);
+#pragma unroll
+      for (int v = 0; v < ITEMS / kPer; ++v) {
+        const uint4 q = reinterpret_cast<const uint4*>(keys + i0)[v];
+        const K* qk = reinterpret_cast<const K*>(&q);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) k[v * kPer + u] = qk[u];
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < ITEMS; ++u) k[u] = u < cnt ? keys[i0 + u] : K(0);
+    }
+    for (int p = 0; p < passes; ++p) {
+      const int bits = (p == passes - 1) ? last_bits : kRadixBits;
+      const int sh = begin_bit + p * kRadixBits;
+      const uint32_t dm = (1u << bits) - 1u;
+      uint32_t run_d = (uint32_t)(k[0] >> sh) & dm, run_n = 1;
+#pragma unroll
+      for (int u = 1; u < ITEMS; ++u) {
+        if (u < cnt) {
+          const uint32_t d = (uint32_t)(k[u] >> sh) & dm;
+          if (d == run_d) {
+            ++run_n;
+          } else {
+            atomicAdd(&s_cnt[p][run_d], run_n);
+            run_d = d;
+            run_n = 1;
+          }
+        }
+      }
+      atomicAdd(&s_cnt[p][run_d], run_n);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) {
+    const int p = i / kRadix, d = i % kRadix;
+    counts[((size_t)p * parts + part) * kRadix + d] = s_cnt[p][d];
+  }
+}
+
+// gsum[(p * groups + g) * kRadix + d]: the counts of group g's partitions.
+__global__ void __launch_bounds__(kPrefixThreads)
+    rs_group_sums(const uint32_t* __restrict__ counts, int64_t parts, uint32_t* __restrict__ gsum, int groups) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t s_part[kPrefixSlices][kRadix];
+  const int g = blockIdx.x, p = blockIdx.y;
+  const int d = threadIdx.x % kRadix, q = threadIdx.x / kRadix;
+  const int64_t r0 = (int64_t)g * kPrefixGroup, r1 = min(parts, r0 + kPrefixGroup);
+  uint32_t s = 0;
+#pragma unroll 8
+  for (int64_t r = r0 + q; r < r1; r += kPrefixSlices) s += counts[((size_t)p * parts + r) * kRadix + d];
+  s_part[q][d] = s;
+  __syncthreads();
+  if (q == 0) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int i = 0; i < kPrefixSlices; ++i) t += s_part[i][d];
+    gsum[((size_t)p * groups + g) * kRadix + d] = t;
+  }
+}
+
+// One CTA: the first pass's group sums become exclusive prefixes over the
+// groups (in place), and hist[p * kRadix + d] receives every pass's totals.
+__global__ void __launch_bounds__(kPrefixThreads)
+    rs_group_scan(uint32_t* __restrict__ gsum, int groups, int passes, uint32_t* __restrict__ hist) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t s_part[kPrefixSlices][kRadix];
+  const int d = threadIdx.x % kRadix, q = threadIdx.x / kRadix;
+  const int per = (groups + kPrefixSlices - 1) / kPrefixSlices;
+  const int g0 = min(groups, q * per), g1 = min(groups, g0 + per);
+  for (int p = 0; p < passes; ++p) {
+    uint32_t* row = gsum + (size_t)p * groups * kRadix;
+    uint32_t s = 0;
+#pragma unroll 8
+    for (int g = g0; g < g1; ++g) s += row[(size_t)g * kRadix + d];
+    s_part[q][d] = s;
+    __syncthreads();
+    uint32_t before = 0, total = 0;
+#pragma unroll
+    for (int i = 0; i < kPrefixSlices; ++i) {
+      before += i < q ? s_part[i][d] : 0u;
+      total += s_part[i][d];
+    }
+    if (p == 0) {
+      for (int g = g0; g < g1; ++g) {
+        const uint32_t v = row[(size_t)g * kRadix + d];
+        row[(size_t)g * kRadix + d] = before;
+        before += v;
+      }
+    }
+    if (q == 0) hist[p * kRadix + d] = total;
+    __syncthreads();  // s_part is reused
+  }
+}
+
+// One CTA per group: the first pass's partition counts of group g become the
+// partitions' exclusive prefixes (group prefix + the group's partitions before).
+__global__ void __launch_bounds__(kPrefixThreads)
+    rs_part_prefix(uint32_t* __restrict__ counts, int64_t parts, const uint32_t* __restrict__ gprefix) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t s_part[kPrefixSlices][kRadix];
+  const int g = blockIdx.x;
+  const int d = threadIdx.x % kRadix, q = threadIdx.x / kRadix;
+  const int64_t r0 = (int64_t)g * kPrefixGroup, r1 = min(parts, r0 + kPrefixGroup);
+  const int64_t per = (r1 - r0 + kPrefixSlices - 1) / kPrefixSlices;
+  const int64_t a = min(r1, r0 + q * per), b = min(r1, a + per);
+  uint32_t s = 0;
+#pragma unroll 8
+  for (int64_t r = a; r < b; ++r) s += counts[(size_t)r * kRadix + d];
+  s_part[q][d] = s;
+  __syncthreads();
+  uint32_t off = gprefix[(size_t)g * kRadix + d];
+#pragma unroll
+  for (int i = 0; i < kPrefixSlices; ++i) off += i < q ? s_part[i][d] : 0u;
+  for (int64_t r = a; r < b; ++r) {
+    const uint32_t v = counts[(size_t)r * kRadix + d];
+    counts[(size_t)r * kRadix + d] = off;
+    off += v;
+  }
+}
+
 template <typename K>
 __global__ void rs_copy(const K* __restrict__ ki, const uint32_t* __restrict__ vi, K* __restrict__ ko,
                         uint32_t* __restrict__ vo, int64_t n) {
@@ -362,6 +525,12 @@ static cudaError_t onesweep_smem_optin() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(rs_onesweep<K, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)sizeof(OnesweepSmem<K, 8>));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(rs_onesweep<K, 16, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(OnesweepSmem<K, 16>));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(rs_onesweep<K, 8, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(OnesweepSmem<K, 8>));
   if constexpr (sizeof(K) == 4) {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(rs_onesweep<K, 16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -382,9 +551,10 @@ static int sort_items(int64_t n) {
   return 4;
 }
 
-template <typename K, bool kRanges>
+template <typename K, bool kRanges, bool kPrefix = false>
 static auto onesweep_kernel(int items) {
-  return items == 16 ? rs_onesweep<K, 16, kRanges> : items == 8 ? rs_onesweep<K, 8, kRanges> : rs_onesweep<K, 4, kRanges>;
+  return items == 16 ? rs_onesweep<K, 16, kRanges, kPrefix>
+                     : items == 8 ? rs_onesweep<K, 8, kRanges, kPrefix> : rs_onesweep<K, 4, kRanges, kPrefix>;
 }
 
 template <typename K>
@@ -405,6 +575,13 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
   uint32_t* hist = digit_hist ? const_cast<uint32_t*>(digit_hist) : zeroed;
   uint32_t* counters = zeroed + (size_t)kMaxPasses * kRadix;
   uint32_t* lookback = counters + kMaxPasses;
+  // Reduce-then-scan for the first pass (rs_part_counts): per-partition counts
+  // of every pass, then group sums. Fully written, never cleared.
+  const bool prefix_mode = n >= kPrefixMinN && passes >= 2;
+  const int groups = (int)((parts + kPrefixGroup - 1) / kPrefixGroup);
+  uint32_t* pcounts = ws.take<uint32_t>(prefix_mode ? (size_t)passes * (size_t)parts * kRadix : 0);
+  uint32_t* gsum = ws.take<uint32_t>(prefix_mode ? (size_t)passes * (size_t)groups * kRadix : 0);
+  if (prefix_mode) hist = zeroed;  // rs_group_scan writes the totals of every pass there
   if (ws.base == nullptr) return cudaSuccess;
   if (n <= 0) return cudaSuccess;
   if (passes == 0) {
@@ -419,7 +596,16 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     e = cudaMemsetAsync(zeroed, 0, sizeof(uint32_t) * zero_words, stream);
     if (e != cudaSuccess) return e;
   }
-  if (!digit_hist) {
+  if (prefix_mode) {
+    auto counts_kernel = items == 16 ? rs_part_counts<K, 16> : items == 8 ? rs_part_counts<K, 8> : rs_part_counts<K, 4>;
+    launch_pdl(counts_kernel, (unsigned)parts, kSortThreads, 0, stream, keys_in, n, begin_bit, passes, last_bits,
+               pcounts, parts);
+    launch_pdl(rs_group_sums, dim3((unsigned)groups, (unsigned)passes), kPrefixThreads, 0, stream,
+               (const uint32_t*)pcounts, parts, gsum, groups);
+    launch_pdl(rs_group_scan, 1, kPrefixThreads, 0, stream, gsum, groups, passes, hist);
+    launch_pdl(rs_part_prefix, (unsigned)groups, kPrefixThreads, 0, stream, pcounts, parts, (const uint32_t*)gsum);
+    note_launches(4);
+  } else if (!digit_hist) {
     launch_pdl(rs_histogram<K>, grid_for((n + kHistItems - 1) / kHistItems, kSortThreads, 148 * 4), kSortThreads, 0,
                stream, keys_in, n, begin_bit, passes, last_bits, hist);
     note_launches(1);
@@ -434,13 +620,15 @@ static cudaError_t radix_sort_pairs_t(Carver& ws, const K* keys_in, const uint32
     uint32_t* vo = to_out ? vals_out : v_tmp;
     const int bits = (p == passes - 1) ? last_bits : kRadixBits;
     auto kernel = onesweep_kernel<K, false>(items);
+    if (prefix_mode && p == 0) kernel = onesweep_kernel<K, false, true>(items);
     if constexpr (sizeof(K) == 4)
       if (ranges.first && p == passes - 1) kernel = onesweep_kernel<K, true>(items);
     const size_t smem = items == 16 ? sizeof(OnesweepSmem<K, 16>)
                                     : items == 8 ? sizeof(OnesweepSmem<K, 8>) : sizeof(OnesweepSmem<K, 4>);
     launch_pdl(kernel, (unsigned)parts, kSortThreads, smem, stream, 
         ki, vi, ko, vo, n, begin_bit + p * kRadixBits, bits, hist + p * kRadix,
-        lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status, ranges.first, ranges.block, ranges.n);
+        lookback + (size_t)p * (size_t)parts * kRadix, counters + p, status, ranges.first, ranges.block, ranges.n,
+        (const uint32_t*)pcounts);
     note_launches(1);
     ki = ko;
     vi = vo;

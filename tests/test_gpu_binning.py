@@ -174,10 +174,13 @@ def _sort(keys: np.ndarray, vals: np.ndarray, begin: int, end: int):
 @pytest.mark.parametrize("n,begin,end", [(1, 0, 8), (4095, 0, 32), (4096, 32, 48), (4097, 5, 19),
                                          (100_000, 0, 64), (1_000_003, 32, 45), (300_000, 0, 0),
                                          (2_000_001, 10, 11), (700_001, 40, 51),
-                                         (28_673, 3, 40), (32_768, 0, 64), (32_769, 0, 33)])
+                                         (28_673, 3, 40), (32_768, 0, 64), (32_769, 0, 33),
+                                         (4_194_304, 0, 16), (4_200_001, 0, 40), (5_000_003, 29, 64)])
 def test_radix_sort_is_stable_and_exact(n, begin, end):
     """Sizes on both sides of the partition sizes (1,024 / 2,048 / 4,096 keys)
-    and of the item-count switches, full and partial last partitions."""
+    and of the item-count switches, full and partial last partitions; from
+    2^22 keys the first pass takes its prefixes from the reduce-then-scan
+    kernels instead of the look-back."""
     rng = np.random.default_rng(n + begin)
     keys = rng.integers(0, 2**63, n, dtype=np.uint64) | (rng.integers(0, 2, n, dtype=np.uint64) << np.uint64(63))
     keys[: n // 3] &= np.uint64(0xFFFF0000FFFF00FF)  # many ties
