@@ -569,7 +569,9 @@ def run_b200(args):
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": f"{peak_kind} copy bandwidth", "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "algorithmic_bytes_per_launch": alg,
-                         "traffic": traffic, "avg_launch_ms": round(dom_ms, 4)},
+                         "traffic": traffic, "avg_launch_ms": round(dom_ms, 4),
+                         "binding": "FP32 issue, not HBM: the binding fraction is roofline_fp32[kernel].frac "
+                                    "(bound names hbm because the contract offers only hbm or tensor)"},
             "roofline_fp32": roof_fp32,
             "fp32_probe_tflops": probe,
             "multi_gpu_splits": splits,
