@@ -230,6 +230,7 @@ def test_emit_without_masks_matches(name):
     (2, 4097, 129, 257, (1.0, 40.0)),
     (5, 2000, 2048, 2048, (0.5, 6.0)),   # 81,920 tiles: three passes
     (5, 500, 4096, 4096, (0.5, 3.0)),    # 327,680 tiles, 1,280 blocks of 256
+    (1, 20000, 4096, 4096, (20.0, 60.0)),  # 4.2M pairs: reduce-then-scan first pass, ranges in the last
 ])
 def test_emit_tile_ranges_without_keys(B, G, H, W, sigma):
     """gsb_bin_emit_ranges (the host runtime's call for many pairs per tile):
