@@ -642,10 +642,71 @@ __global__ void __launch_bounds__(256)
   flush_hist(s_hist, depth_hist, depth_passes * kRadix);
 }
 
+// Reduce-then-scan for the pair offsets of many splats (kScanPrefixMinSplats
+// up to kScanPrefixMaxParts partitions), in place of k_gather_scan's look-back:
+// each partition's count total in rank order (k_scan_part_sums), then one CTA
+// turns the totals into exclusive prefixes (k_scan_part_prefix), both in the
+// look-back array, which that mode does not otherwise use.
+constexpr int kScanPrefixMinSplats = 1 << 18;
+constexpr int kScanPrefixMaxParts = 1 << 16;
+constexpr int kScanPrefixThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads)
+    k_scan_part_sums(int BG, const uint32_t* __restrict__ sorted_vals, const uint32_t* __restrict__ counts,
+                     unsigned long long* __restrict__ psum) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ unsigned long long s_warp[kScanThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r0 = (int64_t)blockIdx.x * kScanTile + (int64_t)tid * kScanItems;
+  unsigned long long t = 0;
+#pragma unroll
+  for (int i = 0; i < kScanItems; ++i)
+    if (r0 + i < BG) t += counts[sorted_vals[r0 + i]];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_down_sync(kFullMask, t, o);
+  if (lane == 0) s_warp[warp] = t;
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long b = 0;
+#pragma unroll
+    for (int w = 0; w < kScanThreads / 32; ++w) b += s_warp[w];
+    psum[blockIdx.x] = b;
+  }
+}
+
+// One CTA, in place: psum[p] becomes the sum of psum[q] for q < p.
+__global__ void __launch_bounds__(kScanPrefixThreads) k_scan_part_prefix(unsigned long long* __restrict__ psum, int parts) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ unsigned long long s_warp[kScanPrefixThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunk = (parts + kScanPrefixThreads - 1) / kScanPrefixThreads;
+  const int lo = min(parts, tid * chunk), hi = min(parts, lo + chunk);
+  unsigned long long t = 0;
+  for (int p = lo; p < hi; ++p) t += psum[p];
+  unsigned long long x = t;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  unsigned long long run = x - t;
+  for (int w = 0; w < warp; ++w) run += s_warp[w];
+  for (int p = lo; p < hi; ++p) {
+    const unsigned long long v = psum[p];
+    psum[p] = run;
+    run += v;
+  }
+}
+
 // Gathers splats into depth-rank order (packed 48-byte records), and turns the
 // per-splat tile counts into exclusive pair offsets with a single-pass chained
-// scan (dynamic partition ids + decoupled look-back).
-template <typename K>
+// scan (dynamic partition ids + decoupled look-back), or, with kPrefix, with
+// the partition prefixes k_scan_part_prefix left in `lookback`.
+template <typename K, bool kPrefix = false>
 __global__ void __launch_bounds__(kScanThreads, 2)
     k_gather_scan(Meta m, const K* __restrict__ sorted_keys,
                   const uint32_t* __restrict__ sorted_vals, const float2* __restrict__ means2d,
@@ -661,7 +722,7 @@ __global__ void __launch_bounds__(kScanThreads, 2)
   __shared__ unsigned long long s_warp[kScanThreads / 32];
   __shared__ unsigned long long s_exclusive;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_part = atomicAdd(part_counter, 1u);
+  if (tid == 0) s_part = kPrefix ? blockIdx.x : atomicAdd(part_counter, 1u);
   __syncthreads();
   const int64_t part = s_part;
   const int64_t r0 = part * kScanTile + (int64_t)tid * kScanItems;
@@ -714,7 +775,9 @@ __global__ void __launch_bounds__(kScanThreads, 2)
 
   if (tid == 0) {
     unsigned long long excl = 0;
-    if (part == 0) {
+    if (kPrefix) {
+      excl = lookback[part];
+    } else if (part == 0) {
       st_volatile_u64(&lookback[0], kScanInc | block_total);
     } else {
       st_volatile_u64(&lookback[part], kScanAgg | block_total);
@@ -1192,6 +1255,17 @@ extern "C" int gsb_bin_count(const gsb_raster_meta* meta, const float* means2d, 
   return cuda_status(cudaGetLastError());
 }
 
+namespace {
+// k_scan_part_sums + k_scan_part_prefix into the look-back array (its words
+// were cleared by k_prepare; both kernels overwrite what they use).
+void launch_scan_prefix(const Meta& m, const PrepareWs& w, int parts, cudaStream_t stream) {
+  launch_pdl(k_scan_part_sums, parts, kScanThreads, 0, stream, m.BG, (const uint32_t*)w.vals_sorted,
+             (const uint32_t*)w.counts, w.lookback);
+  launch_pdl(k_scan_part_prefix, 1, kScanPrefixThreads, 0, stream, w.lookback, parts);
+  note_launches(2);
+}
+}  // namespace
+
 extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means2d, const float* conics,
                                  const float* colors, const float* opacities, const float* depths, int32_t* perm,
                                  float* rec, int32_t* pair_offsets, uint64_t* tile_masks, uint32_t* status,
@@ -1213,6 +1287,9 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
   // k_prepare (gsb_bin_count) cleared the scan's look-back words and counter
   // and the depth sort's scratch.
   const int parts = (m.BG + kScanTile - 1) / kScanTile;
+  // Many splats: the pair-offset prefixes come from a reduce-then-scan
+  // (k_scan_part_sums, k_scan_part_prefix) instead of the scan's look-back.
+  const bool scan_prefix = m.BG >= kScanPrefixMinSplats && parts <= kScanPrefixMaxParts;
   cudaError_t e;
   if (depth_keys32(m)) {
     uint32_t* k32_in = reinterpret_cast<uint32_t*>(w.keys_in);
@@ -1222,7 +1299,8 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
     e = radix_sort_pairs(c, k32_in, w.vals_in, k32_sorted, w.vals_sorted, m.BG, 0, 32, status, stream, true,
                          w.depth_hist);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
-    launch_pdl(k_gather_scan<uint32_t>, parts, kScanThreads, 0, stream, 
+    if (scan_prefix) launch_scan_prefix(m, w, parts, stream);
+    launch_pdl(scan_prefix ? k_gather_scan<uint32_t, true> : k_gather_scan<uint32_t>, parts, kScanThreads, 0, stream,
         m, k32_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities, w.counts,
         w.masks, reinterpret_cast<unsigned long long*>(tile_masks), reinterpret_cast<float4*>(rec), perm,
         pair_offsets, w.lookback, w.counter, status);
@@ -1230,7 +1308,8 @@ extern "C" int gsb_bin_sort_scan(const gsb_raster_meta* meta, const float* means
     e = radix_sort_pairs(c, w.keys_in, w.vals_in, w.keys_sorted, w.vals_sorted, m.BG, 0, depth_sort_end_bit(m),
                          status, stream, true, w.depth_hist);
     if (e != cudaSuccess) return GSB_ERR_CUDA;
-    launch_pdl(k_gather_scan<uint64_t>, parts, kScanThreads, 0, stream, 
+    if (scan_prefix) launch_scan_prefix(m, w, parts, stream);
+    launch_pdl(scan_prefix ? k_gather_scan<uint64_t, true> : k_gather_scan<uint64_t>, parts, kScanThreads, 0, stream,
         m, w.keys_sorted, w.vals_sorted, reinterpret_cast<const float2*>(means2d), conics, colors, opacities,
         w.counts, w.masks, reinterpret_cast<unsigned long long*>(tile_masks), reinterpret_cast<float4*>(rec), perm,
         pair_offsets, w.lookback, w.counter, status);
