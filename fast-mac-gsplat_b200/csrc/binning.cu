@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(256)
 // each partition's count total in rank order (k_scan_part_sums), then one CTA
 // turns the totals into exclusive prefixes (k_scan_part_prefix), both in the
 // look-back array, which that mode does not otherwise use.
-constexpr int kScanPrefixMinSplats = 1 << 18;
+constexpr int kScanPrefixMinSplats = 1 << 16;  // c1/c3 (65,536): prepare -5 us
 constexpr int kScanPrefixMaxParts = 1 << 16;
 constexpr int kScanPrefixThreads = 1024;
 

@@ -60,7 +60,7 @@ def test_binning_bit_exact_configs(name):
     (5, 3000, 31, 47, (0.5, 8.0)),
     (2, 20001, 200, 300, (0.5, 4.0)),
     (1, 65537, 256, 256, (0.5, 2.0)),
-    (1, 300_001, 1024, 1024, (0.5, 2.0)),  # from 2^18 splats: pair offsets by reduce-then-scan
+    (1, 300_001, 1024, 1024, (0.5, 2.0)),  # from 2^16 splats: pair offsets by reduce-then-scan
     (2, 140_001, 512, 768, (0.5, 3.0)),
 ])
 def test_binning_bit_exact_ragged(B, G, H, W, sigma):
