@@ -87,6 +87,24 @@ def test_workspace_queries_without_gpu():
     assert L.gsb_bin_prepare_workspace_size(C.byref(bad)) == 0
 
 
+def test_sort_workspace_carves_prefix_scratch_from_2_22_keys():
+    """From 2^22 keys with two or more passes, the first pass takes its
+    prefixes from the reduce-then-scan kernels, whose per-partition counts
+    (4,096-key partitions, 256 words per pass) and group sums (256-partition
+    groups) are carved after the look-back words; one-pass sorts and shorter
+    inputs carve none."""
+    L = N.load()
+    n = 1 << 22
+    parts, groups = n // 4096, n // 4096 // 256
+    for begin, end, passes in ((0, 16, 2), (3, 40, 5), (0, 64, 8)):
+        grow = L.gsb_radix_sort_pairs_workspace_size(n, begin, end) - \
+            L.gsb_radix_sort_pairs_workspace_size(n - 1, begin, end)
+        scratch = 4 * 256 * passes * (parts + groups)
+        assert scratch <= grow < scratch + 4096, (begin, end, grow, scratch)
+    one = L.gsb_radix_sort_pairs_workspace_size(n, 0, 8) - L.gsb_radix_sort_pairs_workspace_size(n - 1, 0, 8)
+    assert one < 4096
+
+
 def test_argument_validation_without_gpu():
     L = N.load()
     bad = _meta(tile_size=8)
